@@ -1,0 +1,441 @@
+#!/usr/bin/env python
+"""Benchmark of the attention hot path on BASELINE config 4.
+
+Workload (one "step"): 256 independent sequences, each with one Gated DeltaNet
+layer decode step (config-0 shapes: 16/16 heads, d=128, f32 state) and one
+gated-GQA layer decode step over a 32768-token f32 KV cache (8 q heads, 2 kv
+heads, d=256, RoPE on 64 dims, theta 1e7).  The cache grows by one token per
+step.  Sequences are sharded evenly over the N GPUs (strong scaling, no
+inter-GPU traffic on the data path).  Inputs: seeded synthetic N(0,1) data of
+those shapes (no checkpoints or datasets are needed).
+
+value   = layer-steps/s over all GPUs (256 seqs x 2 layers per step),
+          inputs resident in HBM, CUDA events, max over ranks.
+e2e     = the same metric through the public C-ABI calls with the per-step
+          inputs copied from pinned host memory and the outputs copied back
+          inside the timed region.
+roofline: the dominant kernel (GQA flash-decode) -- algorithmic bytes per
+          launch over its CUDA-event duration, against MEASURED_PEAKS.json.
+cpu_baseline: the CPU oracle (restatement of the reference, which is Rust/Burn
+          and cannot be built here) timed on a bounded sample, rank 0, N=1.
+
+--impl reference runs that CPU implementation alone on the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "qwen-3.5_b200"))
+
+# ---- workload constants (dims from text_config.rs) ----
+NSEQ = 256
+HK = HV = 16
+DK = 128
+CONV = 2 * HK * DK + HV * DK  # 6144
+KCONV = 4
+HQ, HKV, D, ROT = 8, 2, 256, 64
+L0 = 32768
+THETA = 1e7
+
+GDN_BYTES_PER_SEQ = (2 * HV * DK * DK * 4          # state read + write
+                     + 2 * CONV * (KCONV - 1) * 4  # conv state read + write
+                     + CONV * 4 + HV * DK * 4 + 2 * HV * 4  # mixed_qkv, z, beta, g
+                     + HV * DK * 4)                # out
+GDN_BYTES_SHARED = CONV * KCONV * 4 + DK * 4     # conv weight + norm weight (read once per launch)
+
+
+def gqa_bytes_per_seq(L):
+    """Algorithmic bytes of one GQA decode step of one sequence whose cache
+    holds L tokens before the append: K and V read for L+1 tokens, the new
+    k/v written, q_gate/k_new/v_new/cos/sin read, output written."""
+    return (2 * HKV * (L + 1) * D * 4 + 2 * HKV * D * 4 + HQ * 2 * D * 4 + 2 * HKV * D * 4 + 2 * ROT * 4
+            + HQ * D * 4)
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out = self.proc.communicate(timeout=5)[0]
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU (oracle) leg
+class CpuWorkload:
+    """The CPU oracle (the reference's attention math restated in C) on one
+    config-4 sequence: a 32768-token KV cache that grows by one token per
+    decode step, plus one Gated DeltaNet layer state.  Every sampled
+    "sequence-step" is one GDN decode + one GQA decode, the same work each of
+    the 256 sequences does per step on the GPU."""
+
+    def __init__(self, threads, max_steps, seed=123):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle  # test infrastructure: the checker / CPU baseline only
+        self.oracle = oracle
+        oracle.set_threads(threads)
+        self.threads = threads
+        rng = np.random.RandomState(seed)
+        f = np.float32
+        cap = L0 + max_steps + 1
+        self.K = np.zeros((1, HKV, cap, D), f)
+        self.V = np.zeros((1, HKV, cap, D), f)
+        fast = np.random.default_rng(seed)
+        self.K[:, :, :L0] = fast.standard_normal((1, HKV, L0, D), dtype=f)
+        self.V[:, :, :L0] = fast.standard_normal((1, HKV, L0, D), dtype=f)
+        self.S = (0.02 * rng.randn(1, HV, DK, DK)).astype(f)
+        self.conv_w = (0.5 * rng.randn(CONV, KCONV)).astype(f)
+        self.norm_w = np.ones(DK, f)
+        self.cst = np.zeros((1, CONV, KCONV - 1), f)
+        self.w0 = np.zeros(D, f)
+        self.lens = np.array([L0], np.int32)
+        self.rng = rng
+
+    def run(self, n):
+        """n sequence-steps; returns the seconds spent inside the oracle calls."""
+        o, f, rng = self.oracle, np.float32, self.rng
+        elapsed = 0.0
+        for _ in range(n):
+            x = rng.randn(1, CONV).astype(f)
+            z = rng.randn(1, HV * DK).astype(f)
+            g = (-np.log1p(np.exp(rng.randn(1, HV)))).astype(f)
+            beta = (1 / (1 + np.exp(-rng.randn(1, HV)))).astype(f)
+            qg = rng.randn(1, HQ, 2 * D).astype(f)
+            kn = rng.randn(1, HKV, D).astype(f)
+            vn = rng.randn(1, HKV, D).astype(f)
+            cos, sin = o.rope_tables(self.lens.astype(np.int64), rot=ROT, theta=THETA)
+            t0 = time.perf_counter()
+            _, self.cst, self.S = o.gdn_decode(x, z, beta, g, self.conv_w, self.norm_w, self.cst, self.S, HK, HV)
+            _, self.K, self.V, self.lens = o.gqa_decode(qg, kn, vn, self.w0, self.w0, cos, sin, self.K, self.V,
+                                                        self.lens, rot=ROT, inplace=True)
+            elapsed += time.perf_counter() - t0
+        return elapsed
+
+    def describe(self, n, elapsed):
+        return (f"{n} sequence-steps of config 4 (each: 1 GDN decode + 1 GQA decode at L~32768), "
+                f"{self.threads} thread(s), {elapsed:.2f} s")
+
+
+def cpu_sample(threads, n=32):
+    w = CpuWorkload(threads, n + 1)
+    w.run(1)  # warm
+    el = w.run(n)
+    return 2 * n / el, w.describe(n, el)
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    w = CpuWorkload(threads, args.warmup + args.steps * args.ref_seqs + 1)
+    for _ in range(args.warmup):
+        w.run(1)
+    vals, tot = [], 0.0
+    for i in range(args.steps):
+        el = w.run(args.ref_seqs)
+        tot += el
+        vals.append(2 * args.ref_seqs / el)
+    value = statistics.median(vals)
+    desc = w.describe(args.ref_seqs, tot / args.steps)
+    line = {
+        "impl": "reference", "metric": "attn layer-steps/s", "value": value, "unit": "layer-steps/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * 2 * NSEQ / value, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config4: 256 seqs x (GDN decode + GQA decode @32K), per-step bounded sample",
+                   "seqs": NSEQ, "kv_len": L0, "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "layer-steps/s", "cores": threads, "kind": "port",
+                         "sample": desc + " (per timed step; median over steps)"},
+        "e2e": {"value": value, "unit": "layer-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is Rust/Burn over wgpu; neither cargo nor a graphics stack exists here, so its "
+                "attention math runs as the C restatement in oracle/ on the host cores",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- GPU leg
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    import q35attn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if NSEQ % world:
+        raise SystemExit("world size must divide 256")
+    B = NSEQ // world
+    K, W = args.steps, args.warmup
+    nsteps = W + K
+    cap = L0 + 2 * nsteps + 16
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+
+    def randn(*shape, scale=1.0):
+        t = torch.empty(*shape, device=dev, dtype=torch.float32)
+        t.normal_(0.0, scale, generator=gen)
+        return t
+
+    # persistent state / caches (resident in HBM)
+    S = randn(B, HV, DK, DK, scale=0.02)
+    cst = randn(B, CONV, KCONV - 1, scale=0.5)
+    conv_w = randn(CONV, KCONV, scale=0.5)
+    norm_w = torch.ones(DK, device=dev)
+    Kc = torch.empty(B, HKV, cap, D, device=dev)
+    Vc = torch.empty(B, HKV, cap, D, device=dev)
+    Kc[:, :, :L0].normal_(generator=gen)
+    Vc[:, :, :L0].normal_(generator=gen)
+    lens = torch.full((B,), L0, dtype=torch.int32, device=dev)
+    qn_w = torch.zeros(D, device=dev)
+    kn_w = torch.zeros(D, device=dev)
+    ws = q35attn.GqaWorkspace(B, HQ, HKV, cap, max_len=cap, device=dev)
+
+    # per-step inputs, resident (device leg)
+    x = randn(nsteps, B, CONV)
+    z = randn(nsteps, B, HV * DK)
+    g = -torch.nn.functional.softplus(randn(nsteps, B, HV))
+    beta = torch.sigmoid(randn(nsteps, B, HV))
+    qg = randn(nsteps, B, HQ, 2 * D)
+    kn = randn(nsteps, B, HKV, D)
+    vn = randn(nsteps, B, HKV, D)
+    pos = torch.arange(L0, L0 + 2 * nsteps + 1, device=dev, dtype=torch.float32)
+    inv_freq = torch.exp(torch.arange(0, ROT, 2, device=dev, dtype=torch.float32) * (-np.log(THETA) / ROT))
+    fr = pos[:, None] * inv_freq[None, :]
+    cos_t = torch.cat([fr.cos(), fr.cos()], -1).contiguous()
+    sin_t = torch.cat([fr.sin(), fr.sin()], -1).contiguous()
+    cos_b = cos_t[:, None, :].expand(-1, B, -1).contiguous()
+    sin_b = sin_t[:, None, :].expand(-1, B, -1).contiguous()
+    out_gdn = torch.empty(B, HV * DK, device=dev)
+    out_gqa = torch.empty(B, HQ * D, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize(dev)
+
+    def step(i, ev=None):
+        q35attn.gdn_decode(x[i], z[i], beta[i], g[i], conv_w, norm_w, cst, S, out_gdn, num_k_heads=HK,
+                           num_v_heads=HV, stream=stream)
+        if ev is not None:
+            ev[0].record(stream)
+        q35attn.gqa_decode(qg[i], kn[i], vn[i], qn_w, kn_w, cos_b[i], sin_b[i], Kc, Vc, lens, out_gqa, workspace=ws,
+                           max_len=cap, stream=stream)
+        if ev is not None:
+            ev[1].record(stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident leg
+    for i in range(W):
+        step(i)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    gdn_evs = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    L_start = L0 + W
+    barrier()
+    q35attn.launch_count(reset=True)
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for k in range(K):
+            gdn_evs[k].record(stream)
+            step(W + k, evs[k])
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+    launches = q35attn.launch_count()
+    barrier()
+    elapsed = max_over_ranks(t0.elapsed_time(t1) / 1000.0)
+    gqa_ms = [evs[k][0].elapsed_time(evs[k][1]) for k in range(K)]
+    gdn_ms = [gdn_evs[k].elapsed_time(evs[k][0]) for k in range(K)]
+    gqa_avg = statistics.mean(gqa_ms) / 1000.0
+    gdn_avg = statistics.mean(gdn_ms) / 1000.0
+    gqa_alg = sum(B * gqa_bytes_per_seq(L_start + k) for k in range(K)) / K
+    gdn_alg = B * GDN_BYTES_PER_SEQ + GDN_BYTES_SHARED
+    value = 2 * NSEQ * K / elapsed
+    peak, peak_kind = load_peaks()
+    gqa_gbs = gqa_alg / gqa_avg / 1e9
+    gdn_gbs = gdn_alg / gdn_avg / 1e9
+    step_bytes_all = (gqa_alg + gdn_alg) * world
+    if lens.min().item() != L0 + W + K or ws.status() != 0:
+        raise SystemExit(f"bench self-check failed: lens {lens.min().item()}..{lens.max().item()}, "
+                         f"status {ws.status()}")
+
+    # ---- end-to-end leg through the public API, host buffers
+    nE = K
+    h_x = torch.empty(nE, B, CONV, pin_memory=True)
+    h_z = torch.empty(nE, B, HV * DK, pin_memory=True)
+    h_b = torch.empty(nE, B, HV, pin_memory=True)
+    h_g = torch.empty(nE, B, HV, pin_memory=True)
+    h_qg = torch.empty(nE, B, HQ, 2 * D, pin_memory=True)
+    h_kn = torch.empty(nE, B, HKV, D, pin_memory=True)
+    h_vn = torch.empty(nE, B, HKV, D, pin_memory=True)
+    h_cos = torch.empty(nE, B, ROT, pin_memory=True)
+    h_sin = torch.empty(nE, B, ROT, pin_memory=True)
+    for hbuf, src in ((h_x, x), (h_z, z), (h_b, beta), (h_g, g), (h_qg, qg), (h_kn, kn), (h_vn, vn)):
+        hbuf.copy_(src[:nE].cpu())
+    h_cos.copy_(cos_b[W + K:W + K + nE].cpu())
+    h_sin.copy_(sin_b[W + K:W + K + nE].cpu())
+    h_out_gdn = torch.empty(nE, B, HV * DK, pin_memory=True)
+    h_out_gqa = torch.empty(nE, B, HQ * D, pin_memory=True)
+    d_in = [torch.empty(B, CONV, device=dev), torch.empty(B, HV * DK, device=dev), torch.empty(B, HV, device=dev),
+            torch.empty(B, HV, device=dev), torch.empty(B, HQ, 2 * D, device=dev), torch.empty(B, HKV, D, device=dev),
+            torch.empty(B, HKV, D, device=dev), torch.empty(B, ROT, device=dev), torch.empty(B, ROT, device=dev)]
+    h_bufs = [h_x, h_z, h_b, h_g, h_qg, h_kn, h_vn, h_cos, h_sin]
+    h2d = sum(t[0].numel() * 4 for t in h_bufs)
+    d2h = (h_out_gdn[0].numel() + h_out_gqa[0].numel()) * 4
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(nE):
+        for dbuf, hbuf in zip(d_in, h_bufs):
+            dbuf.copy_(hbuf[i], non_blocking=True)
+        q35attn.gdn_decode(d_in[0], d_in[1], d_in[2], d_in[3], conv_w, norm_w, cst, S, out_gdn, num_k_heads=HK,
+                           num_v_heads=HV, stream=stream)
+        q35attn.gqa_decode(d_in[4], d_in[5], d_in[6], qn_w, kn_w, d_in[7], d_in[8], Kc, Vc, lens, out_gqa,
+                           workspace=ws, max_len=cap, stream=stream)
+        h_out_gdn[i].copy_(out_gdn, non_blocking=True)
+        h_out_gqa[i].copy_(out_gqa, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_elapsed = max_over_ranks(e0.elapsed_time(e1) / 1000.0)
+    e2e_value = 2 * NSEQ * nE / e2e_elapsed
+    if not (torch.isfinite(h_out_gqa).all() and torch.isfinite(h_out_gdn).all()):
+        raise SystemExit("non-finite outputs")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        v, desc = cpu_sample(threads, n=args.ref_seqs)
+        cpu = {"value": v, "unit": "layer-steps/s", "cores": threads, "kind": "port", "sample": desc}
+
+    if rank == 0:
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "gqa_decode_traffic.json")
+        if os.path.exists(tp):
+            try:
+                with open(tp) as f:
+                    tj = json.load(f)
+                traffic = tj["bytes_per_seq_step"] * B
+            except Exception:
+                traffic = None
+        line = {
+            "metric": "attn layer-steps/s", "value": value, "unit": "layer-steps/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": 1000.0 * elapsed / K, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config4: 256 seqs x (GDN decode + GQA decode @32K ctx) per step",
+                       "seqs": NSEQ, "seqs_per_gpu": B, "kv_len_start": L0, "gdn_heads": [HK, HV, DK],
+                       "gqa_heads": [HQ, HKV, D], "parallelism": f"seq-sharded x{world}",
+                       "l2": "inputs larger than L2 (KV cache %.1f GB per GPU)" % (Kc.numel() * 8 / 1e9)},
+            "hbm_gbs": step_bytes_all / elapsed / 1e9,
+            "hbm_frac_nominal_8tbs": step_bytes_all / elapsed / 1e9 / world / 8000.0,
+            "roofline": {"bound": "hbm", "kernel": "gqa_decode", "achieved": gqa_gbs, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": gqa_gbs / peak, "traffic": traffic,
+                         "alg_bytes_per_launch": gqa_alg, "avg_launch_ms": gqa_avg * 1e3},
+            "gdn_kernel": {"achieved": gdn_gbs, "unit": "GB/s", "frac": gdn_gbs / peak,
+                           "alg_bytes_per_launch": gdn_alg, "avg_launch_ms": gdn_avg * 1e3},
+            "e2e": {"value": e2e_value, "unit": "layer-steps/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ref-seqs", type=int, default=32, help="sequence-steps in each CPU sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

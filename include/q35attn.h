@@ -1,0 +1,184 @@
+/*
+ * q35attn.h -- C ABI of the B200 (sm_100a) attention hot path for the Qwen3.5
+ * hybrid decoder (Gated DeltaNet linear attention + gated GQA full attention).
+ *
+ * Drop-in boundary: each entry point replaces the tensor program between the
+ * input projections and the output projection of one reference module
+ * (inventwithdean/Qwen-3.5, src/text_modules.rs).  Plain pointers and sizes
+ * only; every pointer argument is a DEVICE pointer unless stated otherwise;
+ * `stream` is a cudaStream_t (NULL = legacy default stream).  All tensors are
+ * row-major float32 (the reference casts weights to F32 at load, main.rs:166,
+ * and keeps state/cache in f32, text_config.rs:112).
+ *
+ * Ownership: the caller owns every buffer.  Hot-path entry points never
+ * allocate; where scratch is needed the caller passes a workspace sized by the
+ * matching *_workspace_size query.  State and caches are updated in place.
+ *
+ * Errors: every entry point returns Q35_OK (0) or a Q35_ERR_* code and never
+ * aborts (the reference panics instead, kernels.rs:442,472,580).
+ * q35_last_error() returns a thread-local message for the last failure.
+ * Conditions only the device can see (a cache that is full) are reported
+ * through a status word in the workspace, read with q35_workspace_status().
+ *
+ * Threading: calls are stream-ordered and asynchronous.  Concurrent calls are
+ * safe when they touch disjoint buffers (including disjoint workspaces).
+ */
+#ifndef Q35ATTN_H
+#define Q35ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q35_OK 0
+#define Q35_ERR_INVALID_ARG 1       /* null pointer, negative size, bad flag */
+#define Q35_ERR_UNSUPPORTED 2       /* shape outside the compiled kernel set */
+#define Q35_ERR_CAPACITY 3          /* KV cache capacity exceeded (host-visible) */
+#define Q35_ERR_WORKSPACE 4         /* workspace missing or too small */
+#define Q35_ERR_CUDA 5              /* CUDA runtime error (launch / config) */
+#define Q35_ERR_DEVICE 6            /* no usable sm_100 device */
+
+/* Device-side status bits (q35_workspace_status). */
+#define Q35_STATUS_CACHE_FULL 0x1u    /* lens[b] >= capacity: step skipped for b */
+#define Q35_STATUS_LEN_HINT 0x2u      /* lens[b]+1 > max_len hint: step skipped for b */
+#define Q35_STATUS_WAIT_TIMEOUT 0x4u  /* a bounded in-kernel wait gave up */
+
+/* Gated DeltaNet layer shapes (text_config.rs:95-99, text_modules.rs:670-699).
+ * Qwen3.5-2B: {B, 16, 16, 128, 128, 4, 1e-6}. */
+typedef struct q35_gdn_dims {
+  int32_t batch;        /* B: independent sequences */
+  int32_t num_k_heads;  /* linear_num_key_heads */
+  int32_t num_v_heads;  /* linear_num_value_heads (multiple of num_k_heads) */
+  int32_t head_k_dim;   /* linear_key_head_dim   (128 supported) */
+  int32_t head_v_dim;   /* linear_value_head_dim (128 supported) */
+  int32_t conv_kernel;  /* linear_conv_kernel_dim (2..4 supported) */
+  float eps;            /* rms_norm_eps of the gated output norm */
+} q35_gdn_dims;
+
+/* Gated GQA full-attention shapes (text_config.rs:65,105-108,121-122).
+ * Qwen3.5-2B: {B, 8, 2, 256, 64, cap, 1e-6}. */
+typedef struct q35_gqa_dims {
+  int32_t batch;         /* B */
+  int32_t num_q_heads;   /* num_attention_heads */
+  int32_t num_kv_heads;  /* num_key_value_heads (divides num_q_heads, group <= 8) */
+  int32_t head_dim;      /* 256 supported */
+  int32_t rotary_dim;    /* head_dim * partial_rotary_factor (even, <= head_dim) */
+  int32_t reserved;
+  int64_t capacity;      /* token capacity of the K/V cache per (sequence, kv head) */
+  float eps;             /* rms_norm_eps of q_norm / k_norm */
+} q35_gqa_dims;
+
+/* --------------------------------------------------------------------------
+ * Gated DeltaNet, one decode step (seq_len == 1, conv state present).
+ * Replaces text_modules.rs:515-530 (causal_conv1d_update + SiLU), :554-567
+ * (q/k/v split), :597-615 (k-head expansion), :627-636
+ * (burn_recurrent_gated_delta_rule, :365-443) and :651-660 (RMSNormGated,
+ * :85-117) -- everything between in_proj_* and out_proj of
+ * GatedDeltaNet::forward (:483-667).
+ *   mixed_qkv  [B, C]      in_proj_qkv output, C = 2*Hk*DK + Hv*DV
+ *   z          [B, Hv*DV]  in_proj_z output (gate of the output norm)
+ *   beta, g    [B, Hv]     sigmoid(b) and -exp(A_log)*softplus(a+dt_bias)
+ *   conv_w     [C, K]      depthwise conv weight (Conv1d [C,1,K] squeezed)
+ *   norm_w     [DV]        RMSNormGated weight
+ *   conv_state [B, C, K-1] in/out (cache.conv_states[l])
+ *   rec_state  [B, Hv, DK, DV] in/out, [head][k][v] (cache.recurrent_states[l])
+ *   out        [B, Hv*DV]  input of out_proj
+ */
+int q35_gdn_decode(const q35_gdn_dims *dims, const float *mixed_qkv,
+                   const float *z, const float *beta, const float *g,
+                   const float *conv_w, const float *norm_w, float *conv_state,
+                   float *rec_state, float *out, void *stream);
+
+/* --------------------------------------------------------------------------
+ * Gated DeltaNet chunked prefill (seq_len = T tokens per sequence).
+ * Replaces text_modules.rs:531-552 (causal_conv1d_fn, :164-182, with the
+ * conv-state capture), :554-615 and :637-660 (burn_chunk_gated_delta_rule,
+ * :189-363, chunk 64, then RMSNormGated).
+ *   mixed_qkv [B, T, C], z [B, T, Hv*DV], beta/g [B, T, Hv], out [B, T, Hv*DV]
+ *   conv_state [B, C, K-1]: read when has_prev_conv (prepended history,
+ *              :535-537), always overwritten with the last K-1 inputs.
+ *   rec_state  [B, Hv, DK, DV]: initial state when has_init_state, else zero;
+ *              overwritten with the final state.
+ *   workspace  >= q35_gdn_prefill_workspace_size(dims, T) bytes.
+ */
+size_t q35_gdn_prefill_workspace_size(const q35_gdn_dims *dims, int32_t seq_len);
+int q35_gdn_prefill(const q35_gdn_dims *dims, int32_t seq_len,
+                    const float *mixed_qkv, const float *z, const float *beta,
+                    const float *g, const float *conv_w, const float *norm_w,
+                    float *conv_state, int32_t has_prev_conv, float *rec_state,
+                    int32_t has_init_state, float *out, void *workspace,
+                    size_t workspace_bytes, void *stream);
+
+/* --------------------------------------------------------------------------
+ * beta / g gate projection.  mode 0 replaces kernels.rs:174-247
+ * (gate_proj_kernel: 8-way split partial sums, softplus threshold tested on
+ * the softplus value, called at text_modules.rs:569-576); mode 1 replaces the
+ * prefill branch text_modules.rs:578-595 (threshold on a + dt_bias).
+ *   x [N, in_dim]; w_b, w_a [in_dim, H] (f32, not quantized, main.rs:205-218);
+ *   a_log, dt_bias [H]; beta, g [N, H].
+ */
+int q35_gdn_gate(int32_t n_rows, int32_t in_dim, int32_t num_heads,
+                 const float *x, const float *w_b, const float *w_a,
+                 const float *a_log, const float *dt_bias, float *beta,
+                 float *g, int32_t mode, void *stream);
+
+/* --------------------------------------------------------------------------
+ * Gated GQA, one decode step.  Replaces text_modules.rs:866-936 of
+ * Attention::forward (:842-944): q/gate split of q_proj, q_norm/k_norm
+ * (RMSNorm 1+w, :800-809), partial RoPE (:754-774), KV-cache append
+ * (:899-909, in place instead of cat), repeat_kv (:776-792, as head
+ * grouping, no copy), SDPA (burn::tensor::module::attention, scale
+ * 1/sqrt(head_dim)) and the sigmoid output gate.
+ *   q_gate   [B, Hq, 2*D]   q_proj output: per head [query | gate]
+ *   k_new, v_new [B, Hkv, D] k_proj / v_proj outputs (pre-norm, pre-RoPE)
+ *   qn_w, kn_w [D]          q_norm / k_norm weights (applied as 1 + w)
+ *   cos, sin [B, rotary_dim] rotary tables of the new position
+ *   k_cache, v_cache [B, Hkv, capacity, D] in/out (post-norm, post-RoPE keys)
+ *   lens [B] int32 in/out   valid tokens per sequence; the new token is
+ *                           written at lens[b] and lens[b] is incremented
+ *   out [B, Hq*D]           attention output * sigmoid(gate) (o_proj input)
+ *   max_len                 host upper bound on lens[b]+1 over the batch
+ *                           (sizes the split-K grid; capacity is always safe)
+ *   workspace  >= q35_gqa_decode_workspace_size(dims, max_len) bytes, zeroed
+ *              once by q35_workspace_init before first use; the kernel leaves
+ *              it reusable.  One workspace per concurrently running call.
+ */
+size_t q35_gqa_decode_workspace_size(const q35_gqa_dims *dims, int64_t max_len);
+int q35_workspace_init(void *workspace, size_t workspace_bytes, void *stream);
+int q35_gqa_decode(const q35_gqa_dims *dims, int64_t max_len,
+                   const float *q_gate, const float *k_new, const float *v_new,
+                   const float *qn_w, const float *kn_w, const float *cos,
+                   const float *sin, float *k_cache, float *v_cache,
+                   int32_t *lens, float *out, void *workspace,
+                   size_t workspace_bytes, void *stream);
+
+/* Reads (and with clear != 0 resets) the device-side status word of a
+ * workspace (Q35_STATUS_* bits).  Synchronizes `stream`.  status_out is a
+ * HOST pointer. */
+int q35_workspace_status(void *workspace, uint32_t *status_out, int32_t clear,
+                         void *stream);
+
+/* Test hook: q35_gdn_decode with the per-head column split forced to
+ * split in {1, 2, 4, 8} (the default picks it from the batch size). */
+int q35_gdn_decode_split(const q35_gdn_dims *dims, int32_t split,
+                         const float *mixed_qkv, const float *z,
+                         const float *beta, const float *g,
+                         const float *conv_w, const float *norm_w,
+                         float *conv_state, float *rec_state, float *out,
+                         void *stream);
+
+/* --------------------------------------------------------------------------
+ * Library information. */
+const char *q35_last_error(void);       /* thread-local, never NULL */
+const char *q35_version(void);
+/* Number of kernel launches the library issued on this host thread since
+ * the last reset (test/bench bookkeeping; counts every <<<>>>/cudaLaunch). */
+uint64_t q35_launch_count(int32_t reset);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q35ATTN_H */

@@ -1,0 +1,234 @@
+// capi.cu -- the extern "C" boundary of libq35attn (declared in
+// include/q35attn.h): argument validation, error reporting, workspace
+// management and dispatch to the sm_100a kernels.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+
+namespace q35 {
+
+// kernels (defined in the other translation units)
+int gdn_decode_launch(const q35_gdn_dims *d, const float *mixed_qkv, const float *z, const float *beta,
+                      const float *g, const float *conv_w, const float *norm_w, float *conv_state,
+                      float *rec_state, float *out, cudaStream_t st, int force_split);
+int gdn_gate_launch(int N, int in_dim, int H, const float *x, const float *wb, const float *wa, const float *a_log,
+                    const float *dt_bias, float *beta, float *g, int mode, cudaStream_t st);
+size_t gqa_workspace_bytes(int B, int Hq, int Hkv, long long max_len, int sms);
+int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_gate, const float *k_new,
+                      const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
+                      const float *sin, float *k_cache, float *v_cache, int32_t *lens, float *out,
+                      void *ws, size_t ws_bytes, cudaStream_t st);
+size_t gdn_prefill_workspace_bytes(const q35_gdn_dims *d, int T);
+int gdn_prefill_launch(const q35_gdn_dims *d, int T, const float *mixed_qkv, const float *z, const float *beta,
+                       const float *g, const float *conv_w, const float *norm_w, float *conv_state, int has_prev,
+                       float *rec_state, int has_init, float *out, void *ws, size_t ws_bytes, cudaStream_t st);
+
+namespace {
+thread_local std::string g_last_error = "";
+std::atomic<uint64_t> g_launches{0};
+std::mutex g_sm_mu;
+int g_sm_count[64] = {0};
+int g_sm_major[64] = {0};
+}  // namespace
+
+void set_error(const std::string &msg) { g_last_error = msg; }
+
+int fail(int code, const std::string &msg) {
+  set_error(msg);
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char *what) {
+  if (e == cudaSuccess) return Q35_OK;
+  return fail(Q35_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void note_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+static int query_device(int *sms, int *major) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  std::lock_guard<std::mutex> lk(g_sm_mu);
+  if (g_sm_count[dev] == 0) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return -1;
+    g_sm_count[dev] = prop.multiProcessorCount;
+    g_sm_major[dev] = prop.major;
+  }
+  *sms = g_sm_count[dev];
+  *major = g_sm_major[dev];
+  return 0;
+}
+
+int device_sm_count() {
+  int sms = 148, major = 10;
+  if (query_device(&sms, &major) != 0) return 148;
+  return sms;
+}
+
+int require_sm100() {
+  int sms = 0, major = 0;
+  if (query_device(&sms, &major) != 0) return fail(Q35_ERR_DEVICE, "no CUDA device available");
+  if (major != 10) return fail(Q35_ERR_DEVICE, "libq35attn is built for sm_100a (B200); device major " +
+                                                   std::to_string(major));
+  return Q35_OK;
+}
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int check_gdn_dims(const q35_gdn_dims *d) {
+  Q35_REQUIRE(d != nullptr, Q35_ERR_INVALID_ARG, "dims is NULL");
+  Q35_REQUIRE(d->batch >= 0 && d->num_k_heads > 0 && d->num_v_heads > 0, Q35_ERR_INVALID_ARG,
+              "gdn dims: batch must be >= 0 and head counts > 0");
+  Q35_REQUIRE(d->num_v_heads % d->num_k_heads == 0, Q35_ERR_INVALID_ARG,
+              "gdn dims: num_v_heads must be a multiple of num_k_heads");
+  Q35_REQUIRE(d->head_k_dim == 128 && d->head_v_dim == 128, Q35_ERR_UNSUPPORTED,
+              "gdn dims: head_k_dim = head_v_dim = 128 is the compiled configuration");
+  Q35_REQUIRE(d->conv_kernel >= 2 && d->conv_kernel <= 4, Q35_ERR_UNSUPPORTED, "gdn dims: conv_kernel must be 2..4");
+  Q35_REQUIRE(d->eps >= 0.0f, Q35_ERR_INVALID_ARG, "gdn dims: eps must be >= 0");
+  Q35_REQUIRE(d->batch <= 65535 && d->num_k_heads <= 65535, Q35_ERR_UNSUPPORTED, "gdn dims: batch / heads too large");
+  return Q35_OK;
+}
+
+static int check_gqa_dims(const q35_gqa_dims *d) {
+  Q35_REQUIRE(d != nullptr, Q35_ERR_INVALID_ARG, "dims is NULL");
+  Q35_REQUIRE(d->batch >= 0 && d->num_q_heads > 0 && d->num_kv_heads > 0, Q35_ERR_INVALID_ARG,
+              "gqa dims: batch must be >= 0 and head counts > 0");
+  Q35_REQUIRE(d->num_q_heads % d->num_kv_heads == 0, Q35_ERR_INVALID_ARG,
+              "gqa dims: num_q_heads must be a multiple of num_kv_heads");
+  const int G = d->num_q_heads / d->num_kv_heads;
+  Q35_REQUIRE(G == 1 || G == 2 || G == 4 || G == 8, Q35_ERR_UNSUPPORTED, "gqa dims: group size must be 1, 2, 4 or 8");
+  Q35_REQUIRE(d->head_dim == 256, Q35_ERR_UNSUPPORTED, "gqa dims: head_dim = 256 is the compiled configuration");
+  Q35_REQUIRE(d->rotary_dim >= 0 && d->rotary_dim <= d->head_dim && d->rotary_dim % 2 == 0, Q35_ERR_INVALID_ARG,
+              "gqa dims: rotary_dim must be even and <= head_dim");
+  Q35_REQUIRE(d->capacity > 0 && d->capacity < (1LL << 31), Q35_ERR_INVALID_ARG,
+              "gqa dims: capacity must be in [1, 2^31)");
+  Q35_REQUIRE(d->batch <= 65535 && d->num_kv_heads <= 65535, Q35_ERR_UNSUPPORTED, "gqa dims: batch / heads too large");
+  Q35_REQUIRE(d->eps >= 0.0f, Q35_ERR_INVALID_ARG, "gqa dims: eps must be >= 0");
+  return Q35_OK;
+}
+
+}  // namespace q35
+
+using namespace q35;
+
+#define Q35_PTR(p) Q35_REQUIRE((p) != nullptr, Q35_ERR_INVALID_ARG, #p " is NULL")
+#define Q35_PTR16(p) \
+  Q35_REQUIRE((p) != nullptr && aligned16(p), Q35_ERR_INVALID_ARG, #p " must be a non-NULL 16-byte aligned pointer")
+
+extern "C" {
+
+const char *q35_last_error(void) { return g_last_error.c_str(); }
+
+const char *q35_version(void) { return "q35attn 0.1.0 (sm_100a)"; }
+
+uint64_t q35_launch_count(int32_t reset) {
+  return reset ? g_launches.exchange(0) : g_launches.load();
+}
+
+int q35_gdn_decode(const q35_gdn_dims *dims, const float *mixed_qkv, const float *z, const float *beta,
+                   const float *g, const float *conv_w, const float *norm_w, float *conv_state, float *rec_state,
+                   float *out, void *stream) {
+  if (int rc = check_gdn_dims(dims)) return rc;
+  if (dims->batch == 0) return Q35_OK;
+  Q35_PTR(mixed_qkv); Q35_PTR(z); Q35_PTR(beta); Q35_PTR(g); Q35_PTR(conv_w); Q35_PTR(norm_w);
+  Q35_PTR(conv_state); Q35_PTR(out);
+  Q35_PTR16(rec_state);
+  if (int rc = require_sm100()) return rc;
+  return gdn_decode_launch(dims, mixed_qkv, z, beta, g, conv_w, norm_w, conv_state, rec_state, out,
+                           static_cast<cudaStream_t>(stream), 0);
+}
+
+/* Test hook: same as q35_gdn_decode with the column split forced (1,2,4,8). */
+int q35_gdn_decode_split(const q35_gdn_dims *dims, int32_t split, const float *mixed_qkv, const float *z,
+                         const float *beta, const float *g, const float *conv_w, const float *norm_w,
+                         float *conv_state, float *rec_state, float *out, void *stream) {
+  if (int rc = check_gdn_dims(dims)) return rc;
+  Q35_REQUIRE(split == 1 || split == 2 || split == 4 || split == 8, Q35_ERR_INVALID_ARG, "split must be 1,2,4,8");
+  if (dims->batch == 0) return Q35_OK;
+  Q35_PTR(mixed_qkv); Q35_PTR(z); Q35_PTR(beta); Q35_PTR(g); Q35_PTR(conv_w); Q35_PTR(norm_w);
+  Q35_PTR(conv_state); Q35_PTR(out);
+  Q35_PTR16(rec_state);
+  if (int rc = require_sm100()) return rc;
+  return gdn_decode_launch(dims, mixed_qkv, z, beta, g, conv_w, norm_w, conv_state, rec_state, out,
+                           static_cast<cudaStream_t>(stream), split);
+}
+
+int q35_gdn_gate(int32_t n_rows, int32_t in_dim, int32_t num_heads, const float *x, const float *w_b,
+                 const float *w_a, const float *a_log, const float *dt_bias, float *beta, float *g, int32_t mode,
+                 void *stream) {
+  Q35_REQUIRE(n_rows >= 0 && in_dim > 0 && num_heads > 0, Q35_ERR_INVALID_ARG, "gdn_gate: bad sizes");
+  Q35_REQUIRE(mode == 0 || mode == 1, Q35_ERR_INVALID_ARG, "gdn_gate: mode must be 0 or 1");
+  if (n_rows == 0) return Q35_OK;
+  Q35_PTR(x); Q35_PTR(w_b); Q35_PTR(w_a); Q35_PTR(a_log); Q35_PTR(dt_bias); Q35_PTR(beta); Q35_PTR(g);
+  if (int rc = require_sm100()) return rc;
+  return gdn_gate_launch(n_rows, in_dim, num_heads, x, w_b, w_a, a_log, dt_bias, beta, g, mode,
+                         static_cast<cudaStream_t>(stream));
+}
+
+size_t q35_gqa_decode_workspace_size(const q35_gqa_dims *dims, int64_t max_len) {
+  if (check_gqa_dims(dims) != Q35_OK || max_len <= 0) return 0;
+  return gqa_workspace_bytes(dims->batch, dims->num_q_heads, dims->num_kv_heads, max_len, device_sm_count());
+}
+
+int q35_workspace_init(void *workspace, size_t workspace_bytes, void *stream) {
+  Q35_PTR(workspace);
+  return check_cuda(cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream)),
+                    "workspace init");
+}
+
+int q35_gqa_decode(const q35_gqa_dims *dims, int64_t max_len, const float *q_gate, const float *k_new,
+                   const float *v_new, const float *qn_w, const float *kn_w, const float *cos, const float *sin,
+                   float *k_cache, float *v_cache, int32_t *lens, float *out, void *workspace,
+                   size_t workspace_bytes, void *stream) {
+  if (int rc = check_gqa_dims(dims)) return rc;
+  Q35_REQUIRE(max_len > 0, Q35_ERR_INVALID_ARG, "gqa_decode: max_len must be > 0");
+  Q35_REQUIRE(max_len <= dims->capacity, Q35_ERR_CAPACITY, "gqa_decode: max_len exceeds the cache capacity");
+  if (dims->batch == 0) return Q35_OK;
+  Q35_PTR16(q_gate); Q35_PTR16(k_new); Q35_PTR16(v_new); Q35_PTR16(qn_w); Q35_PTR16(kn_w);
+  Q35_PTR(cos); Q35_PTR(sin); Q35_PTR16(k_cache); Q35_PTR16(v_cache); Q35_PTR(lens); Q35_PTR(out);
+  if (int rc = require_sm100()) return rc;
+  return gqa_decode_launch(dims, max_len, q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, lens, out,
+                           workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int q35_workspace_status(void *workspace, uint32_t *status_out, int32_t clear, void *stream) {
+  Q35_PTR(workspace);
+  Q35_PTR(status_out);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  if (int rc = check_cuda(cudaMemcpyAsync(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost, st), "status read"))
+    return rc;
+  if (int rc = check_cuda(cudaStreamSynchronize(st), "status sync")) return rc;
+  *status_out = v;
+  if (clear) return check_cuda(cudaMemsetAsync(workspace, 0, sizeof(uint32_t), st), "status clear");
+  return Q35_OK;
+}
+
+size_t q35_gdn_prefill_workspace_size(const q35_gdn_dims *dims, int32_t seq_len) {
+  if (check_gdn_dims(dims) != Q35_OK || seq_len <= 0) return 0;
+  return gdn_prefill_workspace_bytes(dims, seq_len);
+}
+
+int q35_gdn_prefill(const q35_gdn_dims *dims, int32_t seq_len, const float *mixed_qkv, const float *z,
+                    const float *beta, const float *g, const float *conv_w, const float *norm_w, float *conv_state,
+                    int32_t has_prev_conv, float *rec_state, int32_t has_init_state, float *out, void *workspace,
+                    size_t workspace_bytes, void *stream) {
+  if (int rc = check_gdn_dims(dims)) return rc;
+  Q35_REQUIRE(seq_len >= 0, Q35_ERR_INVALID_ARG, "gdn_prefill: seq_len must be >= 0");
+  Q35_REQUIRE(has_prev_conv == 0 || has_prev_conv == 1, Q35_ERR_INVALID_ARG, "has_prev_conv must be 0 or 1");
+  Q35_REQUIRE(has_init_state == 0 || has_init_state == 1, Q35_ERR_INVALID_ARG, "has_init_state must be 0 or 1");
+  if (dims->batch == 0 || seq_len == 0) return Q35_OK;
+  Q35_PTR(mixed_qkv); Q35_PTR(z); Q35_PTR(beta); Q35_PTR(g); Q35_PTR(conv_w); Q35_PTR(norm_w);
+  Q35_PTR(conv_state); Q35_PTR(out);
+  Q35_PTR16(rec_state);
+  if (int rc = require_sm100()) return rc;
+  return gdn_prefill_launch(dims, seq_len, mixed_qkv, z, beta, g, conv_w, norm_w, conv_state, has_prev_conv,
+                            rec_state, has_init_state, out, workspace, workspace_bytes,
+                            static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,277 @@
+// gdn_decode.cu -- fused Gated DeltaNet decode step for sm_100a.
+//
+// One kernel replaces the decode branch of GatedDeltaNet::forward between the
+// input and output projections (inventwithdean/Qwen-3.5
+// src/text_modules.rs:515-530 causal_conv1d_update + SiLU, :554-567 q/k/v
+// split, :597-615 k-head expansion, :365-443 burn_recurrent_gated_delta_rule,
+// :651-660 RMSNormGated).
+//
+// Work decomposition.  The delta-rule update is independent per value column
+// v of the [DK x DV] state: kv_mem[v], delta[v], the rank-1 update of column v
+// and o[v] touch column v only.  A thread-block cluster therefore owns one key
+// head (all rf = Hv/Hk value heads that share it) and each CTA of the cluster
+// owns DV/SPLIT columns of one value head.  Inside a CTA every thread holds
+// NP float4 of the state in registers: the state is read from HBM once and
+// written back once, 128-bit coalesced, with streaming cache hints.
+// Reductions over the key dimension use warp shuffles plus one small shared
+// memory pass.  The cluster shares the conv outputs of the q/k channels
+// (computed once, spread over the CTAs) and the per-column sums of squares of
+// the gated RMS norm through distributed shared memory.
+//
+// Race freedom of the in-place conv state: every conv channel is read and
+// rewritten by exactly one thread of one CTA (q/k channels of key head hk are
+// owned by cluster hk; v channels by the CTA owning those columns).
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace q35 {
+namespace {
+
+constexpr int kDK = 128;
+constexpr int kDV = 128;
+
+struct GdnDecodeParams {
+  const float *mixed_qkv, *z, *beta, *g, *conv_w, *norm_w;
+  float *conv_state, *rec_state, *out;
+  int B, Hk, Hv, rf, C;
+  float eps;
+};
+
+template <int SPLIT>
+struct GdnDecodeCfg {
+  static constexpr int CS = kDV / SPLIT;           // state columns per CTA
+  static constexpr int QR = CS / 4;                // float4 quads per row
+  static constexpr int NT = SPLIT <= 2 ? 256 : 128;
+  static constexpr int RP = NT / QR;               // rows covered per pass
+  static constexpr int NP = kDK / RP;              // float4 of state per thread
+  static constexpr int NW = NT / 32;
+  static_assert(QR >= 1 && QR <= 32 && 32 % QR == 0, "quad layout");
+  static_assert(NP * RP == kDK, "row layout");
+};
+
+template <int KC>
+__device__ __forceinline__ float conv_channel(const GdnDecodeParams &p, size_t xrow, int c) {
+  // text_modules.rs:145-161: window = [state..., x]; y = sum_j w[c,j]*win[j];
+  // new state = window[1..]; output silu(y).
+  const float *w = p.conv_w + (size_t)c * KC;
+  float *st = p.conv_state + (xrow + c) * (KC - 1);
+  float win[KC];
+#pragma unroll
+  for (int j = 0; j < KC - 1; ++j) win[j] = st[j];
+  win[KC - 1] = p.mixed_qkv[xrow + c];
+  float acc = 0.0f;
+#pragma unroll
+  for (int j = 0; j < KC; ++j) acc = fmaf(w[j], win[j], acc);
+#pragma unroll
+  for (int j = 0; j < KC - 1; ++j) st[j] = win[j + 1];
+  return siluf_dev(acc);
+}
+
+template <int SPLIT, int KC>
+__global__ void __launch_bounds__(GdnDecodeCfg<SPLIT>::NT)
+    gdn_decode_kernel(const GdnDecodeParams p) {
+  using Cfg = GdnDecodeCfg<SPLIT>;
+  constexpr int CS = Cfg::CS, QR = Cfg::QR, NT = Cfg::NT, RP = Cfg::RP, NP = Cfg::NP, NW = Cfg::NW;
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int ncl = p.rf * SPLIT;  // CTAs per cluster == gridDim.x
+  const int crank = blockIdx.x;
+  const int hk = blockIdx.y, b = blockIdx.z;
+  const int r = crank / SPLIT, s = crank % SPLIT;
+  const int h = hk * p.rf + r;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cq = tid % QR, r0 = tid / QR;
+  const int col0 = s * CS;
+
+  __shared__ float qk_loc[2 * kDK];  // q/k conv outputs owned by this CTA
+  __shared__ float qk_all[2 * kDK];  // full q (0..DK) and k (DK..2DK) of head hk
+  __shared__ float v_loc[CS];
+  __shared__ __align__(16) float red[NW][CS];
+  __shared__ __align__(16) float delta_s[CS];
+  __shared__ float o_s[CS];
+  __shared__ float sq_parts[SPLIT];
+  __shared__ float inv_norm[2];
+
+  // (1) Issue every state load first; they stay in flight during the conv.
+  float *Sp = p.rec_state + ((size_t)b * p.Hv + h) * kDK * kDV + col0 + cq * 4;
+  float4 S[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i)
+    S[i] = __ldcs(reinterpret_cast<const float4 *>(Sp + (size_t)(r0 + i * RP) * kDV));
+
+  // (2) Causal conv update + SiLU.  q/k channels of key head hk are spread
+  // over the cluster (channel i owned by rank i % ncl); v channels of the
+  // CTA's own columns.
+  const size_t xrow = (size_t)b * p.C;
+  for (int i = crank + tid * ncl; i < 2 * kDK; i += NT * ncl) {
+    const int c = i < kDK ? hk * kDK + i : p.Hk * kDK + hk * kDK + (i - kDK);
+    qk_loc[i] = conv_channel<KC>(p, xrow, c);
+  }
+  if (tid < CS) v_loc[tid] = conv_channel<KC>(p, xrow, 2 * p.Hk * kDK + h * kDV + col0 + tid);
+
+  cluster.sync();  // q/k pieces of every rank are in shared memory
+
+  for (int i = tid; i < 2 * kDK; i += NT) {
+    const float *src = cluster.map_shared_rank(&qk_loc[i], i % ncl);
+    qk_all[i] = *src;
+  }
+  __syncthreads();
+
+  // (3) l2norm of q and k (text_modules.rs:184-187, :389-390), eps 1e-6.
+  if (warp < 2) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kDK / 32; ++j) {
+      const float v = qk_all[warp * kDK + lane + 32 * j];
+      ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) inv_norm[warp] = 1.0f / sqrtf(ss + 1e-6f);
+  }
+  __syncthreads();
+
+  const float qscale = rsqrtf((float)kDK);  // 128^-0.5 is exact in f32
+  const float inv_q = inv_norm[0], inv_k = inv_norm[1];
+  float kr[NP], qr[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int row = r0 + i * RP;
+    kr[i] = qk_all[kDK + row] * inv_k;
+    qr[i] = (qk_all[row] * inv_q) * qscale;
+  }
+
+  // (4) Delta rule (text_modules.rs:412-430).
+  const float decay = expf(p.g[(size_t)b * p.Hv + h]);
+  const float bt = p.beta[(size_t)b * p.Hv + h];
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    S[i].x *= decay; S[i].y *= decay; S[i].z *= decay; S[i].w *= decay;
+    acc = f4_fma(kr[i], S[i], acc);
+  }
+#pragma unroll
+  for (int off = QR; off < 32; off <<= 1) {
+    acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off);
+    acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off);
+    acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
+    acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
+  }
+  if (lane < QR) *reinterpret_cast<float4 *>(&red[warp][cq * 4]) = acc;
+  __syncthreads();
+  if (tid < CS) {
+    float kv = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) kv += red[w][tid];
+    delta_s[tid] = (v_loc[tid] - kv) * bt;
+  }
+  __syncthreads();
+
+  const float4 dl = *reinterpret_cast<const float4 *>(&delta_s[cq * 4]);
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    S[i] = f4_fma(kr[i], dl, S[i]);
+    o = f4_fma(qr[i], S[i], o);
+    __stcs(reinterpret_cast<float4 *>(Sp + (size_t)(r0 + i * RP) * kDV), S[i]);
+  }
+#pragma unroll
+  for (int off = QR; off < 32; off <<= 1) {
+    o.x += __shfl_xor_sync(0xffffffffu, o.x, off);
+    o.y += __shfl_xor_sync(0xffffffffu, o.y, off);
+    o.z += __shfl_xor_sync(0xffffffffu, o.z, off);
+    o.w += __shfl_xor_sync(0xffffffffu, o.w, off);
+  }
+  if (lane < QR) *reinterpret_cast<float4 *>(&red[warp][cq * 4]) = o;
+  __syncthreads();
+  if (tid < CS) {
+    float ov = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) ov += red[w][tid];
+    o_s[tid] = ov;
+  }
+  __syncthreads();
+
+  // (5) RMSNormGated over the DV outputs of head h (text_modules.rs:93-101):
+  // the SPLIT CTAs of head h exchange their partial sums of squares.
+  if (warp == 0) {
+    float ss = 0.0f;
+    for (int c = lane; c < CS; c += 32) ss = fmaf(o_s[c], o_s[c], ss);
+    ss = warp_sum(ss);
+    if (lane < SPLIT) *cluster.map_shared_rank(&sq_parts[s], r * SPLIT + lane) = ss;
+  }
+  cluster.sync();
+  if (tid < CS) {
+    float tot = 0.0f;
+#pragma unroll
+    for (int j = 0; j < SPLIT; ++j) tot += sq_parts[j];
+    const float inv = 1.0f / sqrtf(tot / (float)kDV + p.eps);
+    const int col = col0 + tid;
+    const size_t oidx = ((size_t)b * p.Hv + h) * kDV + col;
+    p.out[oidx] = (p.norm_w[col] * (o_s[tid] * inv)) * siluf_dev(p.z[oidx]);
+  }
+}
+
+template <int SPLIT, int KC>
+cudaError_t launch(const GdnDecodeParams &p, int ncl, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ncl, p.Hk, p.B);
+  cfg.blockDim = dim3(GdnDecodeCfg<SPLIT>::NT, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ncl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  note_launch();
+  return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<SPLIT, KC>, p);
+}
+
+template <int KC>
+cudaError_t launch_split(const GdnDecodeParams &p, int split, cudaStream_t st) {
+  const int ncl = split * p.rf;
+  switch (split) {
+    case 1: return launch<1, KC>(p, ncl, st);
+    case 2: return launch<2, KC>(p, ncl, st);
+    case 4: return launch<4, KC>(p, ncl, st);
+    default: return launch<8, KC>(p, ncl, st);
+  }
+}
+
+}  // namespace
+
+// Column split per head: enough CTAs to cover every SM twice, at most 8 CTAs
+// per cluster (portable cluster size).
+int gdn_decode_split(int B, int Hv, int rf, int sms) {
+  int split = 1;
+  while (split < 8 && (long long)B * Hv * split < 2LL * sms) split *= 2;
+  while (split > 1 && split * rf > 8) split /= 2;
+  return split;
+}
+
+int gdn_decode_launch(const q35_gdn_dims *d, const float *mixed_qkv, const float *z, const float *beta,
+                      const float *g, const float *conv_w, const float *norm_w, float *conv_state,
+                      float *rec_state, float *out, cudaStream_t st, int force_split) {
+  GdnDecodeParams p;
+  p.mixed_qkv = mixed_qkv; p.z = z; p.beta = beta; p.g = g; p.conv_w = conv_w; p.norm_w = norm_w;
+  p.conv_state = conv_state; p.rec_state = rec_state; p.out = out;
+  p.B = d->batch; p.Hk = d->num_k_heads; p.Hv = d->num_v_heads; p.rf = p.Hv / p.Hk;
+  p.C = 2 * p.Hk * kDK + p.Hv * kDV;
+  p.eps = d->eps;
+  const int split = force_split > 0 ? force_split : gdn_decode_split(p.B, p.Hv, p.rf, device_sm_count());
+  Q35_REQUIRE(split * p.rf <= 8, Q35_ERR_UNSUPPORTED, "gdn_decode: num_v_heads/num_k_heads * split must be <= 8");
+  cudaError_t e;
+  switch (d->conv_kernel) {
+    case 2: e = launch_split<2>(p, split, st); break;
+    case 3: e = launch_split<3>(p, split, st); break;
+    default: e = launch_split<4>(p, split, st); break;
+  }
+  return check_cuda(e, "gdn_decode launch");
+}
+
+}  // namespace q35

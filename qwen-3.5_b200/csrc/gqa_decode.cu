@@ -1,0 +1,462 @@
+// gqa_decode.cu -- fused gated-GQA decode step (split-K flash-decode) for sm_100a.
+//
+// Replaces Attention::forward between the projections for seq_len == 1
+// (inventwithdean/Qwen-3.5 src/text_modules.rs:866-936): q/gate split, q_norm /
+// k_norm (RMSNorm with 1 + w, :800-809), partial RoPE (:754-774), the KV-cache
+// append (:899-909, here in place at lens[b]), repeat_kv (:776-792, as head
+// grouping with no copy), scaled-dot-product attention and the sigmoid gate.
+//
+// Grid (nsplit, Hkv, B); one CTA streams keys [s*kps, min((s+1)*kps, L)) of one
+// (sequence, kv head) for all G = Hq/Hkv query heads of the group, so each K/V
+// byte is read from HBM exactly once.  Warp roles:
+//   * warp NW (producer): writes the new token's normalised, rotated key and
+//     its value into the cache (only the CTA whose range holds position
+//     lens[b]), then streams K and V tiles with bulk TMA copies
+//     (cp.async.bulk + mbarrier complete_tx) into an NS-stage ring, with an
+//     evict-first L2 policy;
+//   * warps 0..NW-1 (consumers): each keeps its own online-softmax state
+//     (running max / sum per head, G x 8 output accumulators per lane) over
+//     KPW keys of every tile; a lane owns 8 of the 256 dims, q.k partial dots
+//     are finished with a butterfly reduce-scatter across the warp.
+// The CTA merges its warps in shared memory, writes an (m, l, o) partial to
+// the workspace, and the last CTA of each (sequence, kv head) to arrive
+// (atomic ticket, no spin-wait) merges the splits, applies sigmoid(gate) and
+// writes the output.  The last pair of each sequence increments lens[b].
+#include "common.cuh"
+
+namespace q35 {
+namespace {
+
+constexpr int kD = 256;
+constexpr int kNW = 8;            // consumer warps
+constexpr int kThreads = (kNW + 1) * 32;
+constexpr int kTK = 16;           // keys per pipeline stage
+constexpr int kNS = 3;            // pipeline stages
+constexpr int kKPW = kTK / kNW;   // keys per consumer warp per stage
+
+struct GqaParams {
+  const float *q_gate, *k_new, *v_new, *qn_w, *kn_w, *cos, *sin;
+  float *k_cache, *v_cache;
+  int32_t *lens;
+  float *out;
+  float *part_o;       // [B, Hkv, nsplit, G, D]
+  float *part_ml;      // [B, Hkv, nsplit, G, 2]
+  uint32_t *pair_cnt;  // [B * Hkv]
+  uint32_t *seq_cnt;   // [B]
+  uint32_t *status;
+  long long cap;
+  int B, Hq, Hkv, rot, nsplit, kps;
+  float eps, qscale_log2;
+};
+
+struct GqaSmem {
+  float k[kNS][kTK][kD];
+  float v[kNS][kTK][kD];
+};
+
+// RMSNorm(1+w) + partial RoPE of one head vector held as 8 floats per lane
+// (dims 4*lane..4*lane+3 and 128+4*lane..128+4*lane+3); `tmp` is a 256-float
+// shared scratch for the rotate-half partner exchange.  Returns the result in
+// x0/x1 (same layout).
+__device__ __forceinline__ void norm_rope(float4 &x0, float4 &x1, const float *w, const float *cs,
+                                          const float *sn, int rot, float eps, float *tmp, int lane) {
+  float ss = x0.x * x0.x + x0.y * x0.y + x0.z * x0.z + x0.w * x0.w;
+  ss += x1.x * x1.x + x1.y * x1.y + x1.z * x1.z + x1.w * x1.w;
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / (float)kD + eps);
+  const float4 w0 = *reinterpret_cast<const float4 *>(w + 4 * lane);
+  const float4 w1 = *reinterpret_cast<const float4 *>(w + 128 + 4 * lane);
+  x0 = make_float4((x0.x * inv) * (1.0f + w0.x), (x0.y * inv) * (1.0f + w0.y), (x0.z * inv) * (1.0f + w0.z),
+                   (x0.w * inv) * (1.0f + w0.w));
+  x1 = make_float4((x1.x * inv) * (1.0f + w1.x), (x1.y * inv) * (1.0f + w1.y), (x1.z * inv) * (1.0f + w1.z),
+                   (x1.w * inv) * (1.0f + w1.w));
+  *reinterpret_cast<float4 *>(tmp + 4 * lane) = x0;
+  *reinterpret_cast<float4 *>(tmp + 128 + 4 * lane) = x1;
+  __syncwarp();
+  const int half = rot >> 1;
+  float r[8];
+  const float xin[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int d = (e < 4 ? 4 * lane : 128 + 4 * lane) + (e & 3);
+    if (d < rot) {
+      const float rh = d < half ? -tmp[d + half] : tmp[d - half];
+      r[e] = xin[e] * cs[d] + rh * sn[d];
+    } else {
+      r[e] = xin[e];
+    }
+  }
+  __syncwarp();
+  x0 = make_float4(r[0], r[1], r[2], r[3]);
+  x1 = make_float4(r[4], r[5], r[6], r[7]);
+}
+
+// Butterfly reduce-scatter of V = 2^m partial sums across the warp: on return
+// v[0] holds the full sum of value index (lane >> (5 - m)).
+template <int V>
+__device__ __forceinline__ void reduce_scatter(float (&v)[V], int lane) {
+#pragma unroll
+  for (int lvl = 0; lvl < 5; ++lvl) {
+    const int off = 16 >> lvl;
+    const int cnt = V >> lvl;
+    if (cnt >= 2) {
+      const bool upper = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < cnt / 2; ++i) {
+        const float send = upper ? v[i] : v[i + cnt / 2];
+        const float keep = upper ? v[i + cnt / 2] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    }
+  }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(const GqaParams p) {
+  constexpr int V = kKPW * G;  // (key, head) dots per warp per stage
+  constexpr int LOGV = V == 1 ? 0 : V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : V == 16 ? 4 : 5;
+  static_assert((1 << LOGV) == V && V <= 32, "V must be a power of two <= 32");
+
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  GqaSmem &sm = *reinterpret_cast<GqaSmem *>(smem_raw);
+  __shared__ __align__(16) float q_s[G][kD];
+  __shared__ __align__(16) float tmp_s[kNW + 1][kD];
+  __shared__ __align__(8) uint64_t full_bar[kNS], empty_bar[kNS];
+  __shared__ int last_flag;
+
+  const int s = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  const int len = p.lens[b];
+  if (len >= p.cap) {
+    if (s == 0 && kvh == 0 && tid == 0) atomicOr(p.status, Q35_STATUS_CACHE_FULL);
+    return;
+  }
+  const int L = len + 1;
+  if (L > p.nsplit * p.kps) {
+    if (s == 0 && kvh == 0 && tid == 0) atomicOr(p.status, Q35_STATUS_LEN_HINT);
+    return;
+  }
+  const int kbeg = s * p.kps;
+  const int kend = min(kbeg + p.kps, L);
+  const int nkeys = max(kend - kbeg, 0);
+  const int ntiles = (nkeys + kTK - 1) / kTK;
+  const size_t pair = (size_t)b * p.Hkv + kvh;
+  float *Kc = p.k_cache + pair * (size_t)p.cap * kD;
+  float *Vc = p.v_cache + pair * (size_t)p.cap * kD;
+
+  if (tid == 0) {
+    for (int i = 0; i < kNS; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], kNW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kNW) {
+    // ---------------------------------------------------------- producer
+    if (len >= kbeg && len < kend) {
+      // This CTA owns the new position: k_norm + RoPE, append k and v.
+      const float *kin = p.k_new + pair * kD;
+      const float *vin = p.v_new + pair * kD;
+      float4 x0 = *reinterpret_cast<const float4 *>(kin + 4 * lane);
+      float4 x1 = *reinterpret_cast<const float4 *>(kin + 128 + 4 * lane);
+      norm_rope(x0, x1, p.kn_w, p.cos + (size_t)b * p.rot, p.sin + (size_t)b * p.rot, p.rot, p.eps,
+                tmp_s[kNW], lane);
+      float *kd = Kc + (size_t)len * kD;
+      float *vd = Vc + (size_t)len * kD;
+      *reinterpret_cast<float4 *>(kd + 4 * lane) = x0;
+      *reinterpret_cast<float4 *>(kd + 128 + 4 * lane) = x1;
+      *reinterpret_cast<float4 *>(vd + 4 * lane) = *reinterpret_cast<const float4 *>(vin + 4 * lane);
+      *reinterpret_cast<float4 *>(vd + 128 + 4 * lane) = *reinterpret_cast<const float4 *>(vin + 128 + 4 * lane);
+      fence_proxy_async_global();
+      __syncwarp();
+    }
+    if (lane == 0 && ntiles > 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      for (int t = 0; t < ntiles; ++t) {
+        const int st = t % kNS;
+        if (t >= kNS && !mbar_wait(&empty_bar[st], ((t / kNS) - 1) & 1)) {
+          atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
+          break;
+        }
+        const int k0 = kbeg + t * kTK;
+        const int nk = min(kTK, kend - k0);
+        const uint32_t bytes = (uint32_t)nk * kD * sizeof(float);
+        mbar_arrive_expect_tx(&full_bar[st], 2 * bytes);
+        bulk_g2s(&sm.k[st][0][0], Kc + (size_t)k0 * kD, bytes, &full_bar[st], pol);
+        bulk_g2s(&sm.v[st][0][0], Vc + (size_t)k0 * kD, bytes, &full_bar[st], pol);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  // q prologue: warp g < G normalises + rotates query head g of the group.
+  if (warp < G) {
+    const int h = kvh * G + warp;
+    const float *qin = p.q_gate + ((size_t)b * p.Hq + h) * 2 * kD;
+    float4 x0 = *reinterpret_cast<const float4 *>(qin + 4 * lane);
+    float4 x1 = *reinterpret_cast<const float4 *>(qin + 128 + 4 * lane);
+    norm_rope(x0, x1, p.qn_w, p.cos + (size_t)b * p.rot, p.sin + (size_t)b * p.rot, p.rot, p.eps,
+              tmp_s[warp], lane);
+    const float sc = p.qscale_log2;
+    *reinterpret_cast<float4 *>(&q_s[warp][4 * lane]) = make_float4(x0.x * sc, x0.y * sc, x0.z * sc, x0.w * sc);
+    *reinterpret_cast<float4 *>(&q_s[warp][128 + 4 * lane]) =
+        make_float4(x1.x * sc, x1.y * sc, x1.z * sc, x1.w * sc);
+  }
+  named_bar_sync(1, kNW * 32);
+
+  float4 q0[G], q1[G], a0[G], a1[G];
+  float m_run[G], l_run[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    q0[g] = *reinterpret_cast<const float4 *>(&q_s[g][4 * lane]);
+    q1[g] = *reinterpret_cast<const float4 *>(&q_s[g][128 + 4 * lane]);
+    a0[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    a1[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    m_run[g] = -INFINITY;
+    l_run[g] = 0.0f;
+  }
+
+  bool ok = true;
+  for (int t = 0; t < ntiles && ok; ++t) {
+    const int st = t % kNS;
+    if (!mbar_wait(&full_bar[st], (t / kNS) & 1)) {
+      if (lane == 0) atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
+      ok = false;
+      break;
+    }
+    const int nk = min(kTK, kend - (kbeg + t * kTK));
+    float sv[V];
+#pragma unroll
+    for (int kk = 0; kk < kKPW; ++kk) {
+      const int j = warp * kKPW + kk;
+      if (j < nk) {
+        const float4 k0 = *reinterpret_cast<const float4 *>(&sm.k[st][j][4 * lane]);
+        const float4 k1 = *reinterpret_cast<const float4 *>(&sm.k[st][j][128 + 4 * lane]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float d = q0[g].x * k0.x;
+          d = fmaf(q0[g].y, k0.y, d); d = fmaf(q0[g].z, k0.z, d); d = fmaf(q0[g].w, k0.w, d);
+          d = fmaf(q1[g].x, k1.x, d); d = fmaf(q1[g].y, k1.y, d); d = fmaf(q1[g].z, k1.z, d);
+          d = fmaf(q1[g].w, k1.w, d);
+          sv[kk * G + g] = d;
+        }
+      } else {
+#pragma unroll
+        for (int g = 0; g < G; ++g) sv[kk * G + g] = 0.0f;
+      }
+    }
+    reduce_scatter<V>(sv, lane);
+    // broadcast the V finished dots; invalid keys become -inf
+    float sc[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      sc[i] = __shfl_sync(0xffffffffu, sv[0], i << (5 - LOGV));
+      if (warp * kKPW + i / G >= nk) sc[i] = -INFINITY;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float mt = sc[g];
+#pragma unroll
+      for (int kk = 1; kk < kKPW; ++kk) mt = fmaxf(mt, sc[kk * G + g]);
+      if (mt > m_run[g]) {  // warp-uniform: every lane holds the same scores
+        const float alpha = exp2f(m_run[g] - mt);  // exp2(-inf) = 0 on the first key
+        l_run[g] *= alpha;
+        a0[g].x *= alpha; a0[g].y *= alpha; a0[g].z *= alpha; a0[g].w *= alpha;
+        a1[g].x *= alpha; a1[g].y *= alpha; a1[g].z *= alpha; a1[g].w *= alpha;
+        m_run[g] = mt;
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < kKPW; ++kk) {
+      const int j = warp * kKPW + kk;
+      if (j < nk) {
+        const float4 v0 = *reinterpret_cast<const float4 *>(&sm.v[st][j][4 * lane]);
+        const float4 v1 = *reinterpret_cast<const float4 *>(&sm.v[st][j][128 + 4 * lane]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float pr = exp2f(sc[kk * G + g] - m_run[g]);
+          l_run[g] += pr;
+          a0[g] = f4_fma(pr, v0, a0[g]);
+          a1[g] = f4_fma(pr, v1, a1[g]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[st]);
+  }
+
+  // ---- merge the NW warps of this CTA (stage buffers are drained: reuse)
+  named_bar_sync(1, kNW * 32);
+  float *wacc = &sm.k[0][0][0];            // [NW][G][D]
+  float *wml = wacc + kNW * G * kD;        // [NW][G][2]
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    *reinterpret_cast<float4 *>(wacc + ((size_t)warp * G + g) * kD + 4 * lane) = a0[g];
+    *reinterpret_cast<float4 *>(wacc + ((size_t)warp * G + g) * kD + 128 + 4 * lane) = a1[g];
+    if (lane == 0) {
+      wml[(warp * G + g) * 2 + 0] = m_run[g];
+      wml[(warp * G + g) * 2 + 1] = l_run[g];
+    }
+  }
+  named_bar_sync(1, kNW * 32);
+
+  const bool single = p.nsplit == 1;
+  float *po = p.part_o + (pair * p.nsplit + s) * G * kD;
+  float *pml = p.part_ml + (pair * p.nsplit + s) * G * 2;
+  for (int i = tid; i < G * kD; i += kNW * 32) {
+    const int g = i / kD, d = i % kD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) M = fmaxf(M, wml[(w * G + g) * 2]);
+    float Ls = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) {
+      const float mw = wml[(w * G + g) * 2];
+      const float sc = mw == -INFINITY ? 0.0f : exp2f(mw - M);
+      Ls = fmaf(wml[(w * G + g) * 2 + 1], sc, Ls);
+      O = fmaf(wacc[((size_t)w * G + g) * kD + d], sc, O);
+    }
+    if (single) {
+      const int h = kvh * G + g;
+      const float gate = p.q_gate[((size_t)b * p.Hq + h) * 2 * kD + kD + d];
+      p.out[((size_t)b * p.Hq + h) * kD + d] = (O / Ls) * sigmoidf_dev(gate);
+    } else {
+      __stcg(po + i, O);
+      if (d == 0) {
+        __stcg(pml + g * 2 + 0, M);
+        __stcg(pml + g * 2 + 1, Ls);
+      }
+    }
+  }
+
+  // ---- cross-CTA combine by the last split to arrive (no spin-wait)
+  if (!single) {
+    __threadfence();
+    named_bar_sync(1, kNW * 32);
+    if (tid == 0) {
+      const uint32_t ticket = atomicAdd(&p.pair_cnt[pair], 1u);
+      last_flag = ticket == (uint32_t)(p.nsplit - 1);
+    }
+    named_bar_sync(1, kNW * 32);
+    if (!last_flag) return;
+    __threadfence();
+    const float *pob = p.part_o + pair * p.nsplit * G * kD;
+    const float *pmlb = p.part_ml + pair * p.nsplit * G * 2;
+    for (int i = tid; i < G * kD; i += kNW * 32) {
+      const int g = i / kD, d = i % kD;
+      float M = -INFINITY;
+      for (int j = 0; j < p.nsplit; ++j) M = fmaxf(M, __ldcg(pmlb + (j * G + g) * 2));
+      float Ls = 0.0f, O = 0.0f;
+      for (int j = 0; j < p.nsplit; ++j) {
+        const float mj = __ldcg(pmlb + (j * G + g) * 2);
+        const float sc = mj == -INFINITY ? 0.0f : exp2f(mj - M);
+        Ls = fmaf(__ldcg(pmlb + (j * G + g) * 2 + 1), sc, Ls);
+        O = fmaf(__ldcg(pob + ((size_t)j * G + g) * kD + d), sc, O);
+      }
+      const int h = kvh * G + g;
+      const float gate = p.q_gate[((size_t)b * p.Hq + h) * 2 * kD + kD + d];
+      p.out[((size_t)b * p.Hq + h) * kD + d] = (O / Ls) * sigmoidf_dev(gate);
+    }
+    if (tid == 0) p.pair_cnt[pair] = 0u;
+  }
+  // ---- the last (sequence, kv head) pair of sequence b advances lens[b]
+  if (tid == 0) {
+    __threadfence();
+    const uint32_t t2 = atomicAdd(&p.seq_cnt[b], 1u);
+    if (t2 == (uint32_t)(p.Hkv - 1)) {
+      p.seq_cnt[b] = 0u;
+      p.lens[b] = len + 1;
+    }
+  }
+}
+
+template <int G>
+cudaError_t launch_g(const GqaParams &p, cudaStream_t st) {
+  const size_t smem = sizeof(GqaSmem);
+  static bool configured = false;  // per-process attribute set-up
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gqa_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  dim3 grid(p.nsplit, p.Hkv, p.B);
+  note_launch();
+  gqa_decode_kernel<G><<<grid, kThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// Keys per split.  Large problems (many tiles per SM) use long splits so the
+// combine traffic stays negligible; small ones are cut so that about one full
+// wave of CTAs (2 per SM) is resident.
+int gqa_keys_per_split(int B, int Hkv, long long max_len, int sms) {
+  const long long pairs = (long long)B * Hkv;
+  const long long slots = 2LL * sms;
+  const long long long_kps = 2048;
+  if (pairs * ((max_len + long_kps - 1) / long_kps) >= 8 * slots) return (int)long_kps;
+  long long per = (max_len * pairs + slots - 1) / slots;
+  per = (per + kTK - 1) / kTK * kTK;
+  if (per < 4 * kTK) per = 4 * kTK;
+  if (per > long_kps) per = long_kps;
+  return (int)per;
+}
+
+size_t gqa_workspace_bytes(int B, int Hq, int Hkv, long long max_len, int sms) {
+  const int kps = gqa_keys_per_split(B, Hkv, max_len, sms);
+  const long long nsplit = (max_len + kps - 1) / kps;
+  const int G = Hq / Hkv;
+  size_t off = 256;                                                   // status word
+  off += ((size_t)B * Hkv + B) * sizeof(uint32_t);                    // counters
+  off = (off + 255) / 256 * 256;
+  off += (size_t)B * Hkv * nsplit * G * kD * sizeof(float);           // part_o
+  off += (size_t)B * Hkv * nsplit * G * 2 * sizeof(float);            // part_ml
+  return (off + 255) / 256 * 256;
+}
+
+int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_gate, const float *k_new,
+                      const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
+                      const float *sin, float *k_cache, float *v_cache, int32_t *lens, float *out,
+                      void *ws, size_t ws_bytes, cudaStream_t st) {
+  const int sms = device_sm_count();
+  GqaParams p = {};
+  p.B = d->batch; p.Hq = d->num_q_heads; p.Hkv = d->num_kv_heads; p.rot = d->rotary_dim;
+  p.cap = d->capacity; p.eps = d->eps;
+  p.kps = gqa_keys_per_split(p.B, p.Hkv, max_len, sms);
+  p.nsplit = (int)((max_len + p.kps - 1) / p.kps);
+  const size_t need = gqa_workspace_bytes(p.B, p.Hq, p.Hkv, max_len, sms);
+  Q35_REQUIRE(ws != nullptr && ws_bytes >= need, Q35_ERR_WORKSPACE,
+              "gqa_decode: workspace too small (need " + std::to_string(need) + " bytes)");
+  Q35_REQUIRE(p.nsplit <= 65535, Q35_ERR_UNSUPPORTED, "gqa_decode: max_len too large for the split grid");
+  p.q_gate = q_gate; p.k_new = k_new; p.v_new = v_new; p.qn_w = qn_w; p.kn_w = kn_w; p.cos = cos; p.sin = sin;
+  p.k_cache = k_cache; p.v_cache = v_cache; p.lens = lens; p.out = out;
+  p.qscale_log2 = (1.0f / sqrtf((float)kD)) * kLog2e;
+  unsigned char *base = static_cast<unsigned char *>(ws);
+  p.status = reinterpret_cast<uint32_t *>(base);
+  p.pair_cnt = reinterpret_cast<uint32_t *>(base + 256);
+  p.seq_cnt = p.pair_cnt + (size_t)p.B * p.Hkv;
+  size_t off = 256 + ((size_t)p.B * p.Hkv + p.B) * sizeof(uint32_t);
+  off = (off + 255) / 256 * 256;
+  const int G = p.Hq / p.Hkv;
+  p.part_o = reinterpret_cast<float *>(base + off);
+  off += (size_t)p.B * p.Hkv * p.nsplit * G * kD * sizeof(float);
+  p.part_ml = reinterpret_cast<float *>(base + off);
+  cudaError_t e;
+  switch (G) {
+    case 1: e = launch_g<1>(p, st); break;
+    case 2: e = launch_g<2>(p, st); break;
+    case 4: e = launch_g<4>(p, st); break;
+    case 8: e = launch_g<8>(p, st); break;
+    default: return fail(Q35_ERR_UNSUPPORTED, "gqa_decode: group size must be 1, 2, 4 or 8");
+  }
+  return check_cuda(e, "gqa_decode launch");
+}
+
+}  // namespace q35

@@ -1,0 +1,12 @@
+"""q35attn -- B200 (sm_100a) attention hot path of the Qwen3.5 hybrid decoder.
+
+Gated DeltaNet (decode, chunked prefill, gate projection) and gated GQA
+flash-decode, behind the C ABI of include/q35attn.h.  The Python layer is a
+thin ctypes binding over device pointers; all math runs in libq35attn.so.
+"""
+from ._lib import (GdnDims, GqaDims, LIB_PATH, Q35Error, STATUS_CACHE_FULL, STATUS_LEN_HINT,  # noqa: F401
+                   STATUS_WAIT_TIMEOUT, load)
+from .ops import (GqaWorkspace, gdn_decode, gdn_gate, gdn_prefill, gdn_prefill_workspace,  # noqa: F401
+                  gqa_decode, launch_count)
+
+__version__ = "0.1.0"

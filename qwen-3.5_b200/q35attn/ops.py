@@ -1,0 +1,140 @@
+"""Torch-facing wrappers of the C ABI (device tensors in, device tensors out).
+
+PyTorch is used only for device memory and streams; every computation runs in
+libq35attn's sm_100a kernels.  Inputs must be contiguous float32 CUDA tensors
+(int32 for ``lens``); anything else raises instead of being converted.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from ._lib import GdnDims, GqaDims, Q35Error, check, load
+
+__all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_workspace", "gdn_gate", "GqaWorkspace", "gqa_decode",
+           "launch_count", "Q35Error"]
+
+
+def _req(t: torch.Tensor, name: str, dtype=torch.float32) -> int:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must live on a CUDA device (got {t.device})")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype} (got {t.dtype})")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t.data_ptr()
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def launch_count(reset: bool = False) -> int:
+    return int(load().q35_launch_count(1 if reset else 0))
+
+
+def gdn_dims(batch, num_k_heads, num_v_heads, conv_kernel=4, eps=1e-6, head_dim=128) -> GdnDims:
+    return GdnDims(batch, num_k_heads, num_v_heads, head_dim, head_dim, conv_kernel, eps)
+
+
+def gdn_decode(mixed_qkv, z, beta, g, conv_w, norm_w, conv_state, rec_state, out=None, *, num_k_heads,
+               num_v_heads, eps=1e-6, split=0, stream=None):
+    """One decode step of the Gated DeltaNet core; conv_state / rec_state are
+    updated in place.  Returns ``out`` [B, Hv*128]."""
+    B = mixed_qkv.shape[0]
+    if out is None:
+        out = torch.empty(B, num_v_heads * 128, device=mixed_qkv.device, dtype=torch.float32)
+    d = gdn_dims(B, num_k_heads, num_v_heads, conv_w.shape[1], eps)
+    ptrs = [_req(t, n) for t, n in ((mixed_qkv, "mixed_qkv"), (z, "z"), (beta, "beta"), (g, "g"),
+                                     (conv_w, "conv_w"), (norm_w, "norm_w"), (conv_state, "conv_state"),
+                                     (rec_state, "rec_state"), (out, "out"))]
+    lib = load()
+    if split:
+        check(lib.q35_gdn_decode_split(C.byref(d), int(split), *ptrs, _stream(stream)))
+    else:
+        check(lib.q35_gdn_decode(C.byref(d), *ptrs, _stream(stream)))
+    return out
+
+
+def gdn_prefill_workspace(B, T, num_k_heads, num_v_heads, conv_kernel=4, device="cuda"):
+    d = gdn_dims(B, num_k_heads, num_v_heads, conv_kernel)
+    n = int(load().q35_gdn_prefill_workspace_size(C.byref(d), int(T)))
+    return torch.empty(max(n, 16), dtype=torch.uint8, device=device)
+
+
+def gdn_prefill(mixed_qkv, z, beta, g, conv_w, norm_w, conv_state, rec_state, out=None, *, num_k_heads,
+                num_v_heads, has_prev_conv=False, has_init_state=False, workspace=None, eps=1e-6, stream=None):
+    """Chunked prefill over T tokens; conv_state / rec_state updated in place.
+    Returns ``out`` [B, T, Hv*128]."""
+    B, T = mixed_qkv.shape[:2]
+    if out is None:
+        out = torch.empty(B, T, num_v_heads * 128, device=mixed_qkv.device, dtype=torch.float32)
+    if workspace is None:
+        workspace = gdn_prefill_workspace(B, T, num_k_heads, num_v_heads, conv_w.shape[1], mixed_qkv.device)
+    d = gdn_dims(B, num_k_heads, num_v_heads, conv_w.shape[1], eps)
+    lib = load()
+    check(lib.q35_gdn_prefill(C.byref(d), int(T), _req(mixed_qkv, "mixed_qkv"), _req(z, "z"), _req(beta, "beta"),
+                              _req(g, "g"), _req(conv_w, "conv_w"), _req(norm_w, "norm_w"),
+                              _req(conv_state, "conv_state"), int(bool(has_prev_conv)), _req(rec_state, "rec_state"),
+                              int(bool(has_init_state)), _req(out, "out"), _req(workspace, "workspace", torch.uint8),
+                              workspace.numel(), _stream(stream)))
+    return out
+
+
+def gdn_gate(x, w_b, w_a, a_log, dt_bias, mode=0, beta=None, g=None, stream=None):
+    N, in_dim = x.shape
+    H = w_b.shape[1]
+    if beta is None:
+        beta = torch.empty(N, H, device=x.device, dtype=torch.float32)
+    if g is None:
+        g = torch.empty(N, H, device=x.device, dtype=torch.float32)
+    check(load().q35_gdn_gate(N, in_dim, H, _req(x, "x"), _req(w_b, "w_b"), _req(w_a, "w_a"), _req(a_log, "a_log"),
+                              _req(dt_bias, "dt_bias"), _req(beta, "beta"), _req(g, "g"), int(mode),
+                              _stream(stream)))
+    return beta, g
+
+
+def gqa_dims(batch, num_q_heads, num_kv_heads, capacity, rotary_dim=64, eps=1e-6, head_dim=256) -> GqaDims:
+    return GqaDims(batch, num_q_heads, num_kv_heads, head_dim, rotary_dim, 0, capacity, eps)
+
+
+class GqaWorkspace:
+    """Scratch for the split-K partials and arrival counters of q35_gqa_decode,
+    zeroed once at creation (the kernel leaves it reusable)."""
+
+    def __init__(self, batch, num_q_heads, num_kv_heads, capacity, max_len=None, device="cuda", stream=None):
+        self.dims = gqa_dims(batch, num_q_heads, num_kv_heads, capacity)
+        self.max_len = int(max_len or capacity)
+        n = int(load().q35_gqa_decode_workspace_size(C.byref(self.dims), self.max_len))
+        if n == 0:
+            raise Q35Error(1, "invalid GQA dims for workspace")
+        self.buf = torch.empty(n, dtype=torch.uint8, device=device)
+        check(load().q35_workspace_init(self.buf.data_ptr(), n, _stream(stream)))
+
+    def status(self, clear=False, stream=None) -> int:
+        v = C.c_uint32(0)
+        check(load().q35_workspace_status(self.buf.data_ptr(), C.byref(v), int(clear), _stream(stream)))
+        return int(v.value)
+
+
+def gqa_decode(q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, lens, out=None, *, workspace,
+               max_len=None, rotary_dim=None, eps=1e-6, stream=None):
+    """One gated-GQA decode step; appends to k_cache/v_cache at lens[b] and
+    increments lens.  Returns ``out`` [B, Hq*256]."""
+    B, Hq, _ = q_gate.shape
+    Hkv, cap = k_cache.shape[1], k_cache.shape[2]
+    rot = int(rotary_dim if rotary_dim is not None else cos.shape[-1])
+    if out is None:
+        out = torch.empty(B, Hq * 256, device=q_gate.device, dtype=torch.float32)
+    d = gqa_dims(B, Hq, Hkv, cap, rot, eps)
+    ml = int(max_len if max_len is not None else workspace.max_len)
+    check(load().q35_gqa_decode(C.byref(d), ml, _req(q_gate, "q_gate"), _req(k_new, "k_new"), _req(v_new, "v_new"),
+                                _req(qn_w, "qn_w"), _req(kn_w, "kn_w"), _req(cos, "cos"), _req(sin, "sin"),
+                                _req(k_cache, "k_cache"), _req(v_cache, "v_cache"), _req(lens, "lens", torch.int32),
+                                _req(out, "out"), workspace.buf.data_ptr(), workspace.buf.numel(), _stream(stream)))
+    return out

@@ -1,0 +1,96 @@
+"""CPU checks of the C ABI library: it loads, exports every symbol the header
+declares, the ctypes table matches the header, and host-side argument
+validation rejects bad calls before any device work."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import pytest
+
+import q35attn
+from q35attn import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADERS = [os.path.join(ROOT, "include", f) for f in os.listdir(os.path.join(ROOT, "include")) if f.endswith(".h")]
+
+
+def declared_functions():
+    names = set()
+    for h in HEADERS:
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"\b(q35_\w+)\s*\(", src):
+            names.add(m.group(1))
+    return names
+
+
+def exported_symbols():
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True, check=True)
+    return {line.split()[-1] for line in out.stdout.splitlines() if line.strip()}
+
+
+def test_library_loads():
+    lib = q35attn.load()
+    assert lib.q35_version().decode().startswith("q35attn")
+
+
+def test_every_declared_symbol_is_exported():
+    decl = declared_functions()
+    assert len(decl) >= 10
+    missing = decl - exported_symbols()
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+
+
+def test_ctypes_table_covers_header():
+    assert declared_functions() == set(_lib.SIGNATURES)
+
+
+def test_validation_errors_without_device():
+    lib = q35attn.load()
+    # NULL dims
+    assert lib.q35_gdn_decode(None, *([None] * 10)) == _lib.ERR_INVALID_ARG
+    assert "NULL" in lib.q35_last_error().decode()
+    # unsupported head dim
+    d = _lib.GdnDims(1, 16, 16, 64, 64, 4, 1e-6)
+    assert lib.q35_gdn_decode(C.byref(d), *([None] * 10)) == _lib.ERR_UNSUPPORTED
+    # Hv not a multiple of Hk
+    d = _lib.GdnDims(1, 3, 16, 128, 128, 4, 1e-6)
+    assert lib.q35_gdn_decode(C.byref(d), *([None] * 10)) == _lib.ERR_INVALID_ARG
+    # batch 0 is a no-op
+    d = _lib.GdnDims(0, 16, 16, 128, 128, 4, 1e-6)
+    assert lib.q35_gdn_decode(C.byref(d), *([None] * 10)) == _lib.OK
+    # GQA: group size 3 unsupported, max_len beyond capacity rejected on the host
+    g = _lib.GqaDims(1, 6, 2, 256, 64, 0, 100, 1e-6)
+    assert lib.q35_gqa_decode(C.byref(g), 10, *([None] * 12), 0, None) == _lib.ERR_UNSUPPORTED
+    g = _lib.GqaDims(1, 8, 2, 256, 64, 0, 100, 1e-6)
+    assert lib.q35_gqa_decode(C.byref(g), 101, *([None] * 12), 0, None) == _lib.ERR_CAPACITY
+    assert lib.q35_gqa_decode(C.byref(g), 10, *([None] * 12), 0, None) == _lib.ERR_INVALID_ARG
+    # odd rotary dim
+    g = _lib.GqaDims(1, 8, 2, 256, 63, 0, 100, 1e-6)
+    assert lib.q35_gqa_decode(C.byref(g), 10, *([None] * 12), 0, None) == _lib.ERR_INVALID_ARG
+    # gate: bad mode
+    assert lib.q35_gdn_gate(1, 64, 16, *([None] * 7), 2, None) == _lib.ERR_INVALID_ARG
+    # prefill flags
+    d = _lib.GdnDims(1, 16, 16, 128, 128, 4, 1e-6)
+    assert lib.q35_gdn_prefill(C.byref(d), 8, *([None] * 7), 2, None, 0, None, None, 0, None) == _lib.ERR_INVALID_ARG
+
+
+def test_workspace_sizes_are_positive_and_monotone():
+    lib = q35attn.load()
+    g = _lib.GqaDims(256, 8, 2, 256, 64, 0, 40000, 1e-6)
+    a = lib.q35_gqa_decode_workspace_size(C.byref(g), 4097)
+    b = lib.q35_gqa_decode_workspace_size(C.byref(g), 32769)
+    assert 0 < a <= b
+    d = _lib.GdnDims(1, 16, 16, 128, 128, 4, 1e-6)
+    assert lib.q35_gdn_prefill_workspace_size(C.byref(d), 8192) == 16 * 128 * (4 * 64 * 128 + 64 * 64 + 16) * 4
+    assert lib.q35_gdn_prefill_workspace_size(C.byref(d), 0) == 0
+
+
+def test_python_wrappers_refuse_cpu_tensors():
+    import torch
+    x = torch.zeros(1, 6144)
+    with pytest.raises(ValueError):
+        q35attn.gdn_decode(x, torch.zeros(1, 2048), torch.zeros(1, 16), torch.zeros(1, 16), torch.zeros(6144, 4),
+                           torch.ones(128), torch.zeros(1, 6144, 3), torch.zeros(1, 16, 128, 128),
+                           out=torch.zeros(1, 2048), num_k_heads=16, num_v_heads=16)

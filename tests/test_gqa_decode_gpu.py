@@ -1,0 +1,124 @@
+"""Parity of q35_gqa_decode (fused q/k norm + RoPE + cache append + split-K
+flash-decode + sigmoid gate) against the CPU oracle, through the C ABI.
+Tolerance: max rel err <= 1e-3 per tensor (outputs every step, cache, lens)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import q35attn
+from conftest import max_rel_err
+from gdn_data import gqa_inputs
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def rope(pos, rot=64):
+    return oracle.rope_tables(np.asarray(pos, np.int64), rot=rot, theta=1e7)
+
+
+def run_gqa(B, Hq, Hkv, steps, lens0, cap, seed, wscale=0.0, rot=64, max_len=None, check_every=1):
+    lens0 = np.asarray(lens0, np.int32)
+    d = gqa_inputs(seed, B, Hq, Hkv, steps, int(lens0.max()), cap, wscale=wscale)
+    for b in range(B):  # ragged: zero the tail beyond each sequence's length
+        d["K"][b, :, lens0[b]:] = 0
+        d["V"][b, :, lens0[b]:] = 0
+    dev = torch.device("cuda:0")
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    Kc, Vc, lens = T(d["K"]), T(d["V"]), T(lens0)
+    ws = q35attn.GqaWorkspace(B, Hq, Hkv, cap, max_len=max_len or cap)
+    oK, oV, olens = d["K"].copy(), d["V"].copy(), lens0.copy()
+    worst = 0.0
+    for t in range(steps):
+        cos, sin = rope(olens, rot)
+        out = q35attn.gqa_decode(T(d["qg"][t]), T(d["kn"][t]), T(d["vn"][t]), T(d["qn_w"]), T(d["kn_w"]), T(cos),
+                                 T(sin), Kc, Vc, lens, workspace=ws, rotary_dim=rot)
+        ref, oK, oV, olens = oracle.gqa_decode(d["qg"][t], d["kn"][t], d["vn"][t], d["qn_w"], d["kn_w"], cos, sin,
+                                               oK, oV, olens, rot=rot)
+        if t % check_every == 0 or t == steps - 1:
+            worst = max(worst, max_rel_err(out.cpu().numpy(), ref))
+    torch.cuda.synchronize()
+    assert ws.status() == 0
+    np.testing.assert_array_equal(lens.cpu().numpy(), olens)
+    return worst, max_rel_err(Kc.cpu().numpy(), oK), max_rel_err(Vc.cpu().numpy(), oV)
+
+
+def test_config1_4096_context_128_steps():
+    """8 q heads, 2 kv heads, d=256, RoPE on 64 dims
+    (theta 1e7), 4096 cached tokens, 128 decode steps."""
+    e_out, e_k, e_v = run_gqa(1, 8, 2, 128, [4096], 4096 + 128, seed=1, check_every=1)
+    print(f"config1: out {e_out:.2e} K {e_k:.2e} V {e_v:.2e}")
+    assert e_out <= TOL and e_k <= TOL and e_v == 0.0
+
+
+def test_config1_with_norm_weights():
+    e_out, e_k, e_v = run_gqa(1, 8, 2, 16, [4096], 4200, seed=2, wscale=0.1)
+    assert e_out <= TOL and e_k <= TOL and e_v == 0.0
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(8, 2), (4, 4), (16, 2), (4, 2)])
+def test_ragged_batch_and_group_sizes(Hq, Hkv):
+    """Ragged lengths, including an empty cache (L=0 -> output is the gated
+    new value) and lengths that straddle split boundaries."""
+    lens0 = [0, 1, 17, 300, 2049]
+    e_out, e_k, e_v = run_gqa(5, Hq, Hkv, 3, lens0, 2100, seed=3 + Hq)
+    assert e_out <= TOL and e_k <= TOL and e_v == 0.0
+
+
+def test_partial_rotary_dims():
+    for rot in (0, 32, 256):
+        e_out, e_k, e_v = run_gqa(2, 8, 2, 2, [40, 7], 64, seed=40 + rot, rot=rot)
+        assert e_out <= TOL and e_k <= TOL and e_v == 0.0
+
+
+def test_tight_max_len_hint():
+    e_out, e_k, e_v = run_gqa(2, 8, 2, 4, [100, 90], 4096, seed=5, max_len=104)
+    assert e_out <= TOL and e_k <= TOL and e_v == 0.0
+
+
+def test_empty_cache_returns_gated_value():
+    """L = 0: softmax over the single new key is 1, so out = v * sigmoid(gate)."""
+    B, Hq, Hkv, D, cap = 1, 8, 2, 256, 8
+    rng = np.random.RandomState(9)
+    dev = torch.device("cuda:0")
+    qg = torch.from_numpy(rng.randn(B, Hq, 2 * D).astype(np.float32)).to(dev)
+    kn = torch.from_numpy(rng.randn(B, Hkv, D).astype(np.float32)).to(dev)
+    vn = torch.from_numpy(rng.randn(B, Hkv, D).astype(np.float32)).to(dev)
+    w = torch.zeros(D, device=dev)
+    cos, sin = rope([0])
+    Kc = torch.zeros(B, Hkv, cap, D, device=dev)
+    Vc = torch.zeros(B, Hkv, cap, D, device=dev)
+    lens = torch.zeros(B, dtype=torch.int32, device=dev)
+    ws = q35attn.GqaWorkspace(B, Hq, Hkv, cap)
+    out = q35attn.gqa_decode(qg, kn, vn, w, w, torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev), Kc, Vc,
+                             lens, workspace=ws)
+    exp = (vn.repeat_interleave(Hq // Hkv, dim=1) * torch.sigmoid(qg[:, :, D:])).reshape(B, Hq * D)
+    assert max_rel_err(out.cpu().numpy(), exp.cpu().numpy()) <= 1e-6
+    assert int(lens.item()) == 1
+
+
+def test_full_cache_sets_status_and_skips():
+    """A sequence whose cache is full is skipped on the device (status bit,
+    lens, cache and output untouched) while the others proceed."""
+    B, Hq, Hkv, D, cap = 2, 8, 2, 256, 16
+    dev = torch.device("cuda:0")
+    rng = np.random.RandomState(11)
+    qg = torch.from_numpy(rng.randn(B, Hq, 2 * D).astype(np.float32)).to(dev)
+    kn = torch.from_numpy(rng.randn(B, Hkv, D).astype(np.float32)).to(dev)
+    vn = torch.from_numpy(rng.randn(B, Hkv, D).astype(np.float32)).to(dev)
+    w = torch.zeros(D, device=dev)
+    cos, sin = rope([16, 5])
+    Kc = torch.randn(B, Hkv, cap, D, device=dev)
+    Vc = torch.randn(B, Hkv, cap, D, device=dev)
+    K0 = Kc.clone()
+    lens = torch.tensor([cap, 5], dtype=torch.int32, device=dev)
+    out = torch.full((B, Hq * D), 7.0, device=dev)
+    ws = q35attn.GqaWorkspace(B, Hq, Hkv, cap)
+    q35attn.gqa_decode(qg, kn, vn, w, w, torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev), Kc, Vc, lens,
+                       out, workspace=ws)
+    assert ws.status(clear=True) & q35attn.STATUS_CACHE_FULL
+    assert ws.status() == 0
+    assert lens.cpu().tolist() == [cap, 6]
+    assert torch.all(out[0] == 7.0) and not torch.all(out[1] == 7.0)
+    assert torch.equal(Kc[0], K0[0])
