@@ -72,27 +72,36 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons; only samples
+    stamped inside [mark_start, mark_end] (the timed region) are summarised."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.t0 = self.t1 = None
+        self.out = ""
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.5)  # let the sampler start before the timed region
         except Exception:
             self.proc = None
         return self
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
     def __exit__(self, *a):
-        self.out = ""
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -101,22 +110,27 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        import datetime
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in (self.out or "").splitlines():
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = max(mx, float(f[2]))
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                clk, cmax = float(f[2]), float(f[3])
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+            mx = max(mx, cmax)
+            if self.t0 is not None and not (self.t0 - 0.06 <= ts <= (self.t1 or ts) + 0.06):
+                continue
+            sm.append(clk)
+            for n, v in zip(names, f[6:10]):
                 if v.lower() == "active":
                     reasons.add(n)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": mx or None, "reasons": ["unsampled"], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
@@ -231,8 +245,9 @@ def run_gpu(args):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    NSEQ = args.seqs
     if NSEQ % world:
-        raise SystemExit("world size must divide 256")
+        raise SystemExit("world size must divide the number of sequences")
     B = NSEQ // world
     K, W = args.steps, args.warmup
     nsteps = W + K
@@ -311,12 +326,14 @@ def run_gpu(args):
     barrier()
     q35attn.launch_count(reset=True)
     with ClockSampler(local) as clk:
+        clk.mark_start()
         t0.record(stream)
         for k in range(K):
             gdn_evs[k].record(stream)
             step(W + k, evs[k])
         t1.record(stream)
         torch.cuda.synchronize(dev)
+        clk.mark_end()
     launches = q35attn.launch_count()
     barrier()
     elapsed = max_over_ranks(t0.elapsed_time(t1) / 1000.0)
@@ -377,6 +394,11 @@ def run_gpu(args):
     if not (torch.isfinite(h_out_gqa).all() and torch.isfinite(h_out_gdn).all()):
         raise SystemExit("non-finite outputs")
 
+    extras = None
+    if rank == 0 and world == 1 and not args.no_extras:
+        del x, z, g, beta, qg, kn, vn
+        extras = run_extras(dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -401,8 +423,9 @@ def run_gpu(args):
                        "seqs": NSEQ, "seqs_per_gpu": B, "kv_len_start": L0, "gdn_heads": [HK, HV, DK],
                        "gqa_heads": [HQ, HKV, D], "parallelism": f"seq-sharded x{world}",
                        "l2": "inputs larger than L2 (KV cache %.1f GB per GPU)" % (Kc.numel() * 8 / 1e9)},
-            "hbm_gbs": step_bytes_all / elapsed / 1e9,
-            "hbm_frac_nominal_8tbs": step_bytes_all / elapsed / 1e9 / world / 8000.0,
+            "hbm_gbs": step_bytes_all * K / elapsed / 1e9,
+            "hbm_frac_measured": step_bytes_all * K / elapsed / 1e9 / world / peak,
+            "hbm_frac_nominal_8tbs": step_bytes_all * K / elapsed / 1e9 / world / 8000.0,
             "roofline": {"bound": "hbm", "kernel": "gqa_decode", "achieved": gqa_gbs, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": gqa_gbs / peak, "traffic": traffic,
                          "alg_bytes_per_launch": gqa_alg, "avg_launch_ms": gqa_avg * 1e3},
@@ -413,12 +436,121 @@ def run_gpu(args):
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "configs": extras,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     return 0
+
+
+# --------------------------------------------------------------------------- side measurements
+def run_extras(dev, reps=3):
+    """Per-step latency of BASELINE configs 0, 1 and 2 and of the single
+    32K-context sequence on one GPU.  Decode loops are captured in one CUDA
+    graph per configuration (each replay = the config's full step count), so
+    the numbers exclude host launch overhead; the eager per-step time of
+    config 0 is reported beside it."""
+    import torch
+
+    import q35attn
+    res = {}
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+
+    def randn(*shape, scale=1.0):
+        t = torch.empty(*shape, device=dev, dtype=torch.float32)
+        t.normal_(0.0, scale, generator=gen)
+        return t
+
+    def timed_graph(fn, reps):
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            fn()  # warm (also configures kernel attributes outside capture)
+        torch.cuda.synchronize(dev)
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph, stream=st):
+            fn()
+        gph.replay()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            gph.replay()
+        b.record()
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / 1000.0 / reps
+
+    # config 0: GDN decode, B=1, 256 steps
+    n0 = 256
+    x, z = randn(n0, 1, CONV), randn(n0, 1, HV * DK)
+    g = -torch.nn.functional.softplus(randn(n0, 1, HV))
+    beta = torch.sigmoid(randn(n0, 1, HV))
+    S, cst = randn(1, HV, DK, DK, scale=0.02), randn(1, CONV, KCONV - 1, scale=0.5)
+    conv_w, norm_w = randn(CONV, KCONV, scale=0.5), torch.ones(DK, device=dev)
+    o = torch.empty(1, HV * DK, device=dev)
+
+    def cfg0():
+        for i in range(n0):
+            q35attn.gdn_decode(x[i], z[i], beta[i], g[i], conv_w, norm_w, cst, S, o, num_k_heads=HK, num_v_heads=HV)
+    t = timed_graph(cfg0, reps) / n0
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    cfg0()
+    b.record()
+    torch.cuda.synchronize(dev)
+    t_eager = a.elapsed_time(b) / 1000.0 / n0
+    by0 = GDN_BYTES_PER_SEQ + GDN_BYTES_SHARED
+    res["config0_gdn_decode_b1"] = {"us_per_step_graph": t * 1e6, "us_per_step_eager": t_eager * 1e6,
+                                    "layer_steps_per_s": 1.0 / t, "alg_bytes_per_step": by0,
+                                    "achieved_gbs": by0 / t / 1e9}
+
+    # config 1 and the single 32K sequence: GQA decode, B=1
+    for name, L0c, n1 in (("config1_gqa_decode_b1_L4096", 4096, 128), ("single_seq_gqa_decode_L32768", 32768, 64)):
+        cap = L0c + n1 * (reps + 2) + 1
+        Kc, Vc = torch.empty(1, HKV, cap, D, device=dev), torch.empty(1, HKV, cap, D, device=dev)
+        Kc[:, :, :L0c].normal_(generator=gen)
+        Vc[:, :, :L0c].normal_(generator=gen)
+        lens = torch.full((1,), L0c, dtype=torch.int32, device=dev)
+        qg, kn, vn = randn(n1, 1, HQ, 2 * D), randn(n1, 1, HKV, D), randn(n1, 1, HKV, D)
+        cs, sn = randn(n1, 1, ROT), randn(n1, 1, ROT)
+        w0 = torch.zeros(D, device=dev)
+        o1 = torch.empty(1, HQ * D, device=dev)
+        ws = q35attn.GqaWorkspace(1, HQ, HKV, cap, device=dev)
+
+        def cfg1():
+            for i in range(n1):
+                q35attn.gqa_decode(qg[i], kn[i], vn[i], w0, w0, cs[i], sn[i], Kc, Vc, lens, o1, workspace=ws,
+                                   max_len=cap)
+        t = timed_graph(cfg1, reps) / n1
+        Lmid = L0c + n1 * 2 + n1 * reps // 2
+        by1 = gqa_bytes_per_seq(Lmid)
+        res[name] = {"us_per_step_graph": t * 1e6, "layer_steps_per_s": 1.0 / t, "alg_bytes_per_step": by1,
+                     "achieved_gbs": by1 / t / 1e9, "status": ws.status()}
+        del Kc, Vc
+
+    # config 2: GDN chunked prefill, T=8192
+    T2 = 8192
+    xp, zp = randn(1, T2, CONV), randn(1, T2, HV * DK)
+    gp = -torch.nn.functional.softplus(randn(1, T2, HV))
+    bp = torch.sigmoid(randn(1, T2, HV))
+    S2, c2 = torch.zeros(1, HV, DK, DK, device=dev), torch.zeros(1, CONV, KCONV - 1, device=dev)
+    op = torch.empty(1, T2, HV * DK, device=dev)
+    wsp = q35attn.gdn_prefill_workspace(1, T2, HK, HV, device=dev)
+
+    def cfg2():
+        q35attn.gdn_prefill(xp, zp, bp, gp, conv_w, norm_w, c2, S2, op, num_k_heads=HK, num_v_heads=HV,
+                            workspace=wsp)
+    t = timed_graph(cfg2, reps)
+    by2 = 271.6e6
+    fl2 = 23.97e9
+    res["config2_gdn_prefill_T8192"] = {"ms": t * 1e3, "tokens_per_s": T2 / t, "alg_bytes": by2,
+                                        "achieved_gbs": by2 / t / 1e9, "alg_gflop": fl2 / 1e9,
+                                        "achieved_tflops": fl2 / t / 1e12}
+    return res
 
 
 def main():
@@ -429,6 +561,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ref-seqs", type=int, default=32, help="sequence-steps in each CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seqs", type=int, default=NSEQ, help="total sequences (256 = config 4; smaller for ncu)")
+    ap.add_argument("--no-extras", action="store_true", help="skip the config 0/1/2 side measurements")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -189,7 +189,11 @@ int q35_gqa_decode(const q35_gqa_dims *dims, int64_t max_len, const float *q_gat
   Q35_REQUIRE(max_len <= dims->capacity, Q35_ERR_CAPACITY, "gqa_decode: max_len exceeds the cache capacity");
   if (dims->batch == 0) return Q35_OK;
   Q35_PTR16(q_gate); Q35_PTR16(k_new); Q35_PTR16(v_new); Q35_PTR16(qn_w); Q35_PTR16(kn_w);
-  Q35_PTR(cos); Q35_PTR(sin); Q35_PTR16(k_cache); Q35_PTR16(v_cache); Q35_PTR(lens); Q35_PTR(out);
+  if (dims->rotary_dim > 0) {
+    Q35_PTR(cos);
+    Q35_PTR(sin);
+  }
+  Q35_PTR16(k_cache); Q35_PTR16(v_cache); Q35_PTR(lens); Q35_PTR(out);
   if (int rc = require_sm100()) return rc;
   return gqa_decode_launch(dims, max_len, q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, lens, out,
                            workspace, workspace_bytes, static_cast<cudaStream_t>(stream));

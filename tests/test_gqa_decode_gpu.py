@@ -122,3 +122,39 @@ def test_full_cache_sets_status_and_skips():
     assert lens.cpu().tolist() == [cap, 6]
     assert torch.all(out[0] == 7.0) and not torch.all(out[1] == 7.0)
     assert torch.equal(Kc[0], K0[0])
+
+
+def test_config4_shapes_long_splits():
+    """Config-4 GQA shapes at full context (32K cached tokens) with a batch
+    large enough to take the long-split (2048 keys per CTA) schedule; a sample
+    of sequences is checked against the oracle on every step."""
+    B, L0, steps, Hq, Hkv, D = 96, 32768, 2, 8, 2, 256
+    cap = L0 + steps + 1
+    dev = torch.device("cuda:0")
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4)
+    Kc = torch.empty(B, Hkv, cap, D, device=dev)
+    Vc = torch.empty(B, Hkv, cap, D, device=dev)
+    Kc.normal_(generator=gen)
+    Vc.normal_(generator=gen)
+    sample = [0, 47, 95]
+    oK = Kc[sample].cpu().numpy()
+    oV = Vc[sample].cpu().numpy()
+    lens = torch.full((B,), L0, dtype=torch.int32, device=dev)
+    olens = np.full(len(sample), L0, np.int32)
+    w = torch.zeros(D, device=dev)
+    ws = q35attn.GqaWorkspace(B, Hq, Hkv, cap)
+    rng = np.random.RandomState(8)
+    for t in range(steps):
+        qg = rng.randn(B, Hq, 2 * D).astype(np.float32)
+        kn = rng.randn(B, Hkv, D).astype(np.float32)
+        vn = rng.randn(B, Hkv, D).astype(np.float32)
+        cos, sin = rope(np.full(B, L0 + t))
+        T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        out = q35attn.gqa_decode(T(qg), T(kn), T(vn), w, w, T(cos), T(sin), Kc, Vc, lens, workspace=ws).cpu().numpy()
+        ref, oK, oV, olens = oracle.gqa_decode(qg[sample], kn[sample], vn[sample], np.zeros(D, np.float32),
+                                               np.zeros(D, np.float32), cos[sample], sin[sample], oK, oV, olens)
+        assert max_rel_err(out[sample], ref) <= TOL
+    assert ws.status() == 0
+    assert (lens.cpu().numpy() == L0 + steps).all()
+    assert max_rel_err(Kc[sample][:, :, L0:L0 + steps].cpu().numpy(), oK[:, :, L0:L0 + steps]) <= TOL
