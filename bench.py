@@ -532,6 +532,25 @@ def run_extras(dev, reps=3):
                      "achieved_gbs": by1 / t / 1e9, "status": ws.status()}
         del Kc, Vc
 
+    # GDN decode at the config-4 batch (256 sequences): column-split sweep
+    Bs = 256
+    xs, zs = randn(Bs, CONV), randn(Bs, HV * DK)
+    gs = -torch.nn.functional.softplus(randn(Bs, HV))
+    bs = torch.sigmoid(randn(Bs, HV))
+    Ss, cs_ = randn(Bs, HV, DK, DK, scale=0.02), randn(Bs, CONV, KCONV - 1, scale=0.5)
+    os_ = torch.empty(Bs, HV * DK, device=dev)
+    sweep = {}
+    for split in (1, 2, 4, 8):
+        def gdn_b():
+            for _ in range(10):
+                q35attn.gdn_decode(xs, zs, bs, gs, conv_w, norm_w, cs_, Ss, os_, num_k_heads=HK, num_v_heads=HV,
+                                   split=split)
+        t = timed_graph(gdn_b, reps) / 10
+        byb = Bs * GDN_BYTES_PER_SEQ + GDN_BYTES_SHARED
+        sweep[str(split)] = {"us": t * 1e6, "achieved_gbs": byb / t / 1e9}
+    res["gdn_decode_b256_split_sweep"] = sweep
+    del Ss
+
     # config 2: GDN chunked prefill, T=8192
     T2 = 8192
     xp, zp = randn(1, T2, CONV), randn(1, T2, HV * DK)

@@ -70,14 +70,17 @@ __device__ __forceinline__ float conv_channel(const GdnDecodeParams &p, size_t x
   return siluf_dev(acc);
 }
 
-template <int SPLIT, int KC>
+// SOLO: one CTA per key head (SPLIT == 1 and rf == 1), launched without a
+// cluster, so no cluster barrier (whose release semantics would wait for the
+// in-flight state loads) is needed.
+template <int SPLIT, int KC, bool SOLO>
 __global__ void __launch_bounds__(GdnDecodeCfg<SPLIT>::NT)
     gdn_decode_kernel(const GdnDecodeParams p) {
   using Cfg = GdnDecodeCfg<SPLIT>;
   constexpr int CS = Cfg::CS, QR = Cfg::QR, NT = Cfg::NT, RP = Cfg::RP, NP = Cfg::NP, NW = Cfg::NW;
+  static_assert(!SOLO || SPLIT == 1, "SOLO implies one CTA per head");
 
-  cg::cluster_group cluster = cg::this_cluster();
-  const int ncl = p.rf * SPLIT;  // CTAs per cluster == gridDim.x
+  const int ncl = SOLO ? 1 : p.rf * SPLIT;  // CTAs per cluster == gridDim.x
   const int crank = blockIdx.x;
   const int hk = blockIdx.y, b = blockIdx.z;
   const int r = crank / SPLIT, s = crank % SPLIT;
@@ -108,17 +111,21 @@ __global__ void __launch_bounds__(GdnDecodeCfg<SPLIT>::NT)
   const size_t xrow = (size_t)b * p.C;
   for (int i = crank + tid * ncl; i < 2 * kDK; i += NT * ncl) {
     const int c = i < kDK ? hk * kDK + i : p.Hk * kDK + hk * kDK + (i - kDK);
-    qk_loc[i] = conv_channel<KC>(p, xrow, c);
+    (SOLO ? qk_all : qk_loc)[i] = conv_channel<KC>(p, xrow, c);
   }
   if (tid < CS) v_loc[tid] = conv_channel<KC>(p, xrow, 2 * p.Hk * kDK + h * kDV + col0 + tid);
 
-  cluster.sync();  // q/k pieces of every rank are in shared memory
-
-  for (int i = tid; i < 2 * kDK; i += NT) {
-    const float *src = cluster.map_shared_rank(&qk_loc[i], i % ncl);
-    qk_all[i] = *src;
+  if constexpr (SOLO) {
+    __syncthreads();
+  } else {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();  // q/k pieces of every rank are in shared memory
+    for (int i = tid; i < 2 * kDK; i += NT) {
+      const float *src = cluster.map_shared_rank(&qk_loc[i], i % ncl);
+      qk_all[i] = *src;
+    }
+    __syncthreads();
   }
-  __syncthreads();
 
   // (3) l2norm of q and k (text_modules.rs:184-187, :389-390), eps 1e-6.
   if (warp < 2) {
@@ -200,9 +207,17 @@ __global__ void __launch_bounds__(GdnDecodeCfg<SPLIT>::NT)
     float ss = 0.0f;
     for (int c = lane; c < CS; c += 32) ss = fmaf(o_s[c], o_s[c], ss);
     ss = warp_sum(ss);
-    if (lane < SPLIT) *cluster.map_shared_rank(&sq_parts[s], r * SPLIT + lane) = ss;
+    if constexpr (SOLO) {
+      if (lane == 0) sq_parts[0] = ss;
+    } else {
+      if (lane < SPLIT) *cg::this_cluster().map_shared_rank(&sq_parts[s], r * SPLIT + lane) = ss;
+    }
   }
-  cluster.sync();
+  if constexpr (SOLO) {
+    __syncthreads();
+  } else {
+    cg::this_cluster().sync();
+  }
   if (tid < CS) {
     float tot = 0.0f;
 #pragma unroll
@@ -216,6 +231,13 @@ __global__ void __launch_bounds__(GdnDecodeCfg<SPLIT>::NT)
 
 template <int SPLIT, int KC>
 cudaError_t launch(const GdnDecodeParams &p, int ncl, cudaStream_t st) {
+  if constexpr (SPLIT == 1) {
+    if (ncl == 1) {
+      note_launch();
+      gdn_decode_kernel<1, KC, true><<<dim3(1, p.Hk, p.B), GdnDecodeCfg<1>::NT, 0, st>>>(p);
+      return cudaGetLastError();
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ncl, p.Hk, p.B);
   cfg.blockDim = dim3(GdnDecodeCfg<SPLIT>::NT, 1, 1);
@@ -229,7 +251,7 @@ cudaError_t launch(const GdnDecodeParams &p, int ncl, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   note_launch();
-  return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<SPLIT, KC>, p);
+  return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<SPLIT, KC, false>, p);
 }
 
 template <int KC>

@@ -113,6 +113,72 @@ __device__ __forceinline__ void reduce_scatter(float (&v)[V], int lane) {
   }
 }
 
+// Merge the nsplit (m, l, o) partials of one (sequence, kv head) pair and
+// write out = o / l * sigmoid(gate).  Run by the 256 consumer threads of the
+// last CTA to arrive.  Warp w takes splits w, w+NW, ...; a lane owns G*2
+// float4 columns of the [G][D] output, so every lane keeps G*2 independent
+// 16-byte loads in flight per split.  Per-head maxima come first (lanes stride
+// over splits), the warps' partial sums are merged through shared memory.
+template <int G>
+__device__ __forceinline__ void combine_splits(const GqaParams &p, size_t pair, int kvh, int b, float *scratch,
+                                               int warp, int lane, int tid) {
+  constexpr int F = G * kD / 4 / 32;  // float4 per lane
+  float *Mh = scratch + kNW * G * kD;  // [G] global max, [G] sum of l
+  const float *pml = p.part_ml + pair * p.nsplit * G * 2;
+  const float4 *po = reinterpret_cast<const float4 *>(p.part_o + pair * p.nsplit * G * kD);
+  if (warp < G) {
+    const int g = warp;
+    float M = -INFINITY;
+    for (int j = lane; j < p.nsplit; j += 32) M = fmaxf(M, __ldcg(pml + (j * G + g) * 2));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float Ls = 0.0f;
+    for (int j = lane; j < p.nsplit; j += 32) {
+      const float mj = __ldcg(pml + (j * G + g) * 2);
+      if (mj != -INFINITY) Ls = fmaf(__ldcg(pml + (j * G + g) * 2 + 1), exp2f(mj - M), Ls);
+    }
+    Ls = warp_sum(Ls);
+    if (lane == 0) {
+      Mh[g] = M;
+      Mh[G + g] = Ls;
+    }
+  }
+  named_bar_sync(1, kNW * 32);
+  float Mg[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) Mg[g] = Mh[g];
+  float4 acc[F];
+#pragma unroll
+  for (int f = 0; f < F; ++f) acc[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = warp; j < p.nsplit; j += kNW) {
+    float wgt[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float mj = __ldcg(pml + (j * G + g) * 2);
+      wgt[g] = mj == -INFINITY ? 0.0f : exp2f(mj - Mg[g]);
+    }
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      const int q = lane + 32 * f;            // float4 index in [G][D/4]
+      const float4 v = __ldcg(po + (size_t)j * (G * kD / 4) + q);
+      acc[f] = f4_fma(wgt[(32 * f) / (kD / 4)], v, acc[f]);  // lane < 32: head is f / 2
+    }
+  }
+#pragma unroll
+  for (int f = 0; f < F; ++f)
+    reinterpret_cast<float4 *>(scratch)[(size_t)warp * (G * kD / 4) + lane + 32 * f] = acc[f];
+  named_bar_sync(1, kNW * 32);
+  for (int i = tid; i < G * kD; i += kNW * 32) {
+    const int g = i / kD, d = i % kD;
+    float O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) O += scratch[(size_t)w * G * kD + i];
+    const int h = kvh * G + g;
+    const float gate = p.q_gate[((size_t)b * p.Hq + h) * 2 * kD + kD + d];
+    p.out[((size_t)b * p.Hq + h) * kD + d] = (O / Mh[G + g]) * sigmoidf_dev(gate);
+  }
+}
+
 template <int G>
 __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(const GqaParams p) {
   constexpr int V = kKPW * G;  // (key, head) dots per warp per stage
@@ -346,23 +412,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
     named_bar_sync(1, kNW * 32);
     if (!last_flag) return;
     __threadfence();
-    const float *pob = p.part_o + pair * p.nsplit * G * kD;
-    const float *pmlb = p.part_ml + pair * p.nsplit * G * 2;
-    for (int i = tid; i < G * kD; i += kNW * 32) {
-      const int g = i / kD, d = i % kD;
-      float M = -INFINITY;
-      for (int j = 0; j < p.nsplit; ++j) M = fmaxf(M, __ldcg(pmlb + (j * G + g) * 2));
-      float Ls = 0.0f, O = 0.0f;
-      for (int j = 0; j < p.nsplit; ++j) {
-        const float mj = __ldcg(pmlb + (j * G + g) * 2);
-        const float sc = mj == -INFINITY ? 0.0f : exp2f(mj - M);
-        Ls = fmaf(__ldcg(pmlb + (j * G + g) * 2 + 1), sc, Ls);
-        O = fmaf(__ldcg(pob + ((size_t)j * G + g) * kD + d), sc, O);
-      }
-      const int h = kvh * G + g;
-      const float gate = p.q_gate[((size_t)b * p.Hq + h) * 2 * kD + kD + d];
-      p.out[((size_t)b * p.Hq + h) * kD + d] = (O / Ls) * sigmoidf_dev(gate);
-    }
+    combine_splits<G>(p, pair, kvh, b, wacc, warp, lane, tid);
     if (tid == 0) p.pair_cnt[pair] = 0u;
   }
   // ---- the last (sequence, kv head) pair of sequence b advances lens[b]
