@@ -540,7 +540,7 @@ def run_extras(dev, reps=3):
     Ss, cs_ = randn(Bs, HV, DK, DK, scale=0.02), randn(Bs, CONV, KCONV - 1, scale=0.5)
     os_ = torch.empty(Bs, HV * DK, device=dev)
     sweep = {}
-    for split in (1, 2, 4, 8):
+    for split in (-1, 1, 2, 4, 8):
         def gdn_b():
             for _ in range(10):
                 q35attn.gdn_decode(xs, zs, bs, gs, conv_w, norm_w, cs_, Ss, os_, num_k_heads=HK, num_v_heads=HV,

@@ -161,8 +161,9 @@ int q35_gqa_decode(const q35_gqa_dims *dims, int64_t max_len,
 int q35_workspace_status(void *workspace, uint32_t *status_out, int32_t clear,
                          void *stream);
 
-/* Test hook: q35_gdn_decode with the per-head column split forced to
- * split in {1, 2, 4, 8} (the default picks it from the batch size). */
+/* Test hook: q35_gdn_decode with the kernel schedule forced: split in
+ * {1, 2, 4, 8} selects the cluster kernel with that per-head column split,
+ * -1 the persistent streaming kernel (the default picks from the batch). */
 int q35_gdn_decode_split(const q35_gdn_dims *dims, int32_t split,
                          const float *mixed_qkv, const float *z,
                          const float *beta, const float *g,

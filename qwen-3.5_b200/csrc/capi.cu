@@ -147,7 +147,8 @@ int q35_gdn_decode_split(const q35_gdn_dims *dims, int32_t split, const float *m
                          const float *beta, const float *g, const float *conv_w, const float *norm_w,
                          float *conv_state, float *rec_state, float *out, void *stream) {
   if (int rc = check_gdn_dims(dims)) return rc;
-  Q35_REQUIRE(split == 1 || split == 2 || split == 4 || split == 8, Q35_ERR_INVALID_ARG, "split must be 1,2,4,8");
+  Q35_REQUIRE(split == -1 || split == 1 || split == 2 || split == 4 || split == 8, Q35_ERR_INVALID_ARG,
+              "split must be -1 (streaming kernel) or 1, 2, 4, 8");
   if (dims->batch == 0) return Q35_OK;
   Q35_PTR(mixed_qkv); Q35_PTR(z); Q35_PTR(beta); Q35_PTR(g); Q35_PTR(conv_w); Q35_PTR(norm_w);
   Q35_PTR(conv_state); Q35_PTR(out);

@@ -229,6 +229,215 @@ __global__ void __launch_bounds__(GdnDecodeCfg<SPLIT>::NT)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Streaming variant for large batches: persistent CTAs (one per SM) walk a
+// static list of (sequence, key head) items; each item has rf value-head
+// tiles.  A producer thread moves every 64 KB state tile (contiguous in HBM)
+// plus the tile's conv inputs and gate into a 3-stage shared-memory ring with
+// bulk TMA copies (mbarrier complete_tx); 8 consumer warps run the delta rule
+// out of shared memory, write the updated tile back in place, and one thread
+// returns it to HBM with a bulk TMA store while the next tiles are already in
+// flight.  The q/k conv and l2norm of a key head are computed on its first
+// tile (r == 0) and reused by the other rf - 1 tiles of the item.
+constexpr int kStages = 3;
+constexpr int kCons = 256;                 // consumer threads (8 warps)
+constexpr int kStreamThreads = kCons + 32; // + producer warp
+
+template <int KC>
+struct StreamStage {
+  float S[kDK * kDV];
+  float xqk[2 * kDK];
+  float cqk[2 * kDK * (KC - 1)];
+  float xv[kDV];
+  float cv[kDV * (KC - 1)];
+  float z[kDV];
+};
+
+template <int KC>
+__global__ void __launch_bounds__(kStreamThreads, 1) gdn_decode_stream_kernel(const GdnDecodeParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  StreamStage<KC> *stg = reinterpret_cast<StreamStage<KC> *>(smem_raw);
+  __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
+  __shared__ __align__(16) float qkn[2 * kDK];   // normalised q (scaled) | k of the current key head
+  __shared__ __align__(16) float red[8][kDV];
+  __shared__ __align__(16) float delta_s[kDV];
+  __shared__ float v_loc[kDV];
+  __shared__ float sq[4];
+  __shared__ float inv_norm[2];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int items = p.B * p.Hk;
+  const int n_my_items = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int ntiles = n_my_items * p.rf;
+  constexpr uint32_t kStBytes = (KC - 1) * kDK * sizeof(float);
+
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kCons / 32) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      for (int t = 0; t < ntiles; ++t) {
+        const int sidx = t % kStages;
+        if (t >= kStages && !mbar_wait(&empty_bar[sidx], ((t / kStages) - 1) & 1)) break;
+        const int item = blockIdx.x + (t / p.rf) * gridDim.x;
+        const int r = t % p.rf;
+        const int b = item / p.Hk, hk = item % p.Hk, h = hk * p.rf + r;
+        StreamStage<KC> &sg = stg[sidx];
+        const size_t xrow = (size_t)b * p.C;
+        const int cq0 = hk * kDK, ck0 = p.Hk * kDK + hk * kDK, cv0 = 2 * p.Hk * kDK + h * kDV;
+        uint32_t bytes = sizeof(sg.S) + 2 * kDV * sizeof(float) + kStBytes;
+        if (r == 0) bytes += 2 * kDK * sizeof(float) + 2 * kStBytes;
+        mbar_arrive_expect_tx(&full_bar[sidx], bytes);
+        bulk_g2s(sg.S, p.rec_state + ((size_t)b * p.Hv + h) * kDK * kDV, sizeof(sg.S), &full_bar[sidx], pol);
+        if (r == 0) {
+          bulk_g2s(sg.xqk, p.mixed_qkv + xrow + cq0, kDK * sizeof(float), &full_bar[sidx], pol);
+          bulk_g2s(sg.xqk + kDK, p.mixed_qkv + xrow + ck0, kDK * sizeof(float), &full_bar[sidx], pol);
+          bulk_g2s(sg.cqk, p.conv_state + (xrow + cq0) * (KC - 1), kStBytes, &full_bar[sidx], pol);
+          bulk_g2s(sg.cqk + kDK * (KC - 1), p.conv_state + (xrow + ck0) * (KC - 1), kStBytes, &full_bar[sidx], pol);
+        }
+        bulk_g2s(sg.xv, p.mixed_qkv + xrow + cv0, kDV * sizeof(float), &full_bar[sidx], pol);
+        bulk_g2s(sg.cv, p.conv_state + (xrow + cv0) * (KC - 1), kStBytes, &full_bar[sidx], pol);
+        bulk_g2s(sg.z, p.z + ((size_t)b * p.Hv + h) * kDV, kDV * sizeof(float), &full_bar[sidx], pol);
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const float qscale = rsqrtf((float)kDK);
+  for (int t = 0; t < ntiles; ++t) {
+    const int sidx = t % kStages;
+    const int item = blockIdx.x + (t / p.rf) * gridDim.x;
+    const int r = t % p.rf;
+    const int b = item / p.Hk, hk = item % p.Hk, h = hk * p.rf + r;
+    const size_t xrow = (size_t)b * p.C;
+    const float decay = expf(__ldg(p.g + (size_t)b * p.Hv + h));
+    const float bt = __ldg(p.beta + (size_t)b * p.Hv + h);
+    StreamStage<KC> &sg = stg[sidx];
+    if (!mbar_wait(&full_bar[sidx], (t / kStages) & 1)) break;
+
+    // causal conv update + SiLU (text_modules.rs:145-161) from the staged inputs
+    auto conv = [&](const float *win_state, float xin, int c, float &y) {
+      const float *w = p.conv_w + (size_t)c * KC;
+      float win[KC];
+#pragma unroll
+      for (int j = 0; j < KC - 1; ++j) win[j] = win_state[j];
+      win[KC - 1] = xin;
+      float acc = 0.0f;
+#pragma unroll
+      for (int j = 0; j < KC; ++j) acc = fmaf(__ldg(w + j), win[j], acc);
+      float *dst = p.conv_state + (xrow + c) * (KC - 1);
+#pragma unroll
+      for (int j = 0; j < KC - 1; ++j) dst[j] = win[j + 1];
+      y = siluf_dev(acc);
+    };
+    if (r == 0) {
+      const int i = tid;  // 256 q|k channels
+      const int c = i < kDK ? hk * kDK + i : p.Hk * kDK + hk * kDK + (i - kDK);
+      float y;
+      conv(sg.cqk + i * (KC - 1), sg.xqk[i], c, y);
+      qkn[i] = y;
+    }
+    if (tid < kDV) {
+      float y;
+      conv(sg.cv + tid * (KC - 1), sg.xv[tid], 2 * p.Hk * kDK + h * kDV + tid, y);
+      v_loc[tid] = y;
+    }
+    named_bar_sync(1, kCons);
+    if (r == 0) {
+      if (warp < 2) {  // l2norm of q and k (text_modules.rs:184-187)
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kDK / 32; ++j) {
+          const float v = qkn[warp * kDK + lane + 32 * j];
+          ss = fmaf(v, v, ss);
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) inv_norm[warp] = 1.0f / sqrtf(ss + 1e-6f);
+      }
+      named_bar_sync(1, kCons);
+      const float v = qkn[tid];
+      qkn[tid] = tid < kDK ? (v * inv_norm[0]) * qscale : v * inv_norm[1];
+      named_bar_sync(1, kCons);
+    }
+
+    // delta rule (text_modules.rs:412-430): lane owns 4 columns, warp owns rows warp + 8i
+    float4 Sv[16];
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int row = warp + 8 * i;
+      Sv[i] = *reinterpret_cast<const float4 *>(&sg.S[row * kDV + 4 * lane]);
+      Sv[i].x *= decay; Sv[i].y *= decay; Sv[i].z *= decay; Sv[i].w *= decay;
+      acc = f4_fma(qkn[kDK + row], Sv[i], acc);
+    }
+    *reinterpret_cast<float4 *>(&red[warp][4 * lane]) = acc;
+    named_bar_sync(1, kCons);
+    if (tid < kDV) {
+      float kv = 0.0f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) kv += red[w][tid];
+      delta_s[tid] = (v_loc[tid] - kv) * bt;
+    }
+    named_bar_sync(1, kCons);
+    const float4 dl = *reinterpret_cast<const float4 *>(&delta_s[4 * lane]);
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int row = warp + 8 * i;
+      Sv[i] = f4_fma(qkn[kDK + row], dl, Sv[i]);
+      o = f4_fma(qkn[row], Sv[i], o);
+      *reinterpret_cast<float4 *>(&sg.S[row * kDV + 4 * lane]) = Sv[i];
+    }
+    *reinterpret_cast<float4 *>(&red[warp][4 * lane]) = o;
+    fence_proxy_async_smem();
+    named_bar_sync(1, kCons);
+    if (tid == 0) {
+      bulk_s2g(p.rec_state + ((size_t)b * p.Hv + h) * kDK * kDV, sg.S, sizeof(sg.S));
+      bulk_commit();
+      if (t > 0) {
+        bulk_wait_read<1>();  // the previous tile's store has left shared memory
+        mbar_arrive(&empty_bar[(t - 1) % kStages]);
+      }
+    }
+    // RMSNormGated over the 128 outputs of head h (text_modules.rs:93-101)
+    float ov = 0.0f;
+    if (tid < kDV) {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) ov += red[w][tid];
+      const float ss = warp_sum(ov * ov);
+      if (lane == 0) sq[warp] = ss;
+    }
+    named_bar_sync(1, kCons);
+    if (tid < kDV) {
+      const float inv = 1.0f / sqrtf((sq[0] + sq[1] + sq[2] + sq[3]) / (float)kDV + p.eps);
+      p.out[((size_t)b * p.Hv + h) * kDV + tid] = (p.norm_w[tid] * (ov * inv)) * siluf_dev(sg.z[tid]);
+    }
+  }
+  if (tid == 0) bulk_wait_read<0>();
+}
+
+template <int KC>
+cudaError_t launch_stream(const GdnDecodeParams &p, int sms, cudaStream_t st) {
+  const size_t smem = kStages * sizeof(StreamStage<KC>);
+  cudaError_t e = cudaFuncSetAttribute(gdn_decode_stream_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  const int items = p.B * p.Hk;
+  const int grid = items < sms ? items : sms;
+  note_launch();
+  gdn_decode_stream_kernel<KC><<<grid, kStreamThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
 template <int SPLIT, int KC>
 cudaError_t launch(const GdnDecodeParams &p, int ncl, cudaStream_t st) {
   if constexpr (SPLIT == 1) {
@@ -285,7 +494,23 @@ int gdn_decode_launch(const q35_gdn_dims *d, const float *mixed_qkv, const float
   p.B = d->batch; p.Hk = d->num_k_heads; p.Hv = d->num_v_heads; p.rf = p.Hv / p.Hk;
   p.C = 2 * p.Hk * kDK + p.Hv * kDV;
   p.eps = d->eps;
-  const int split = force_split > 0 ? force_split : gdn_decode_split(p.B, p.Hv, p.rf, device_sm_count());
+  const int sms = device_sm_count();
+  // Large batches stream persistent tiles through shared memory; small ones
+  // split each head's columns over a cluster to occupy every SM.
+  const bool stream = force_split < 0 || (force_split == 0 && (long long)p.B * p.Hv >= 4LL * sms);
+  if (stream) {
+    Q35_REQUIRE((reinterpret_cast<uintptr_t>(mixed_qkv) & 15u) == 0 && (reinterpret_cast<uintptr_t>(z) & 15u) == 0 &&
+                    (reinterpret_cast<uintptr_t>(conv_state) & 15u) == 0,
+                Q35_ERR_INVALID_ARG, "gdn_decode: mixed_qkv, z and conv_state must be 16-byte aligned");
+    cudaError_t e;
+    switch (d->conv_kernel) {
+      case 2: e = launch_stream<2>(p, sms, st); break;
+      case 3: e = launch_stream<3>(p, sms, st); break;
+      default: e = launch_stream<4>(p, sms, st); break;
+    }
+    return check_cuda(e, "gdn_decode (stream) launch");
+  }
+  const int split = force_split > 0 ? force_split : gdn_decode_split(p.B, p.Hv, p.rf, sms);
   Q35_REQUIRE(split * p.rf <= 8, Q35_ERR_UNSUPPORTED, "gdn_decode: num_v_heads/num_k_heads * split must be <= 8");
   cudaError_t e;
   switch (d->conv_kernel) {

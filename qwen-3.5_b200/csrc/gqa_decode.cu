@@ -126,18 +126,28 @@ __device__ __forceinline__ void combine_splits(const GqaParams &p, size_t pair, 
   float *Mh = scratch + kNW * G * kD;  // [G] global max, [G] sum of l
   const float *pml = p.part_ml + pair * p.nsplit * G * 2;
   const float4 *po = reinterpret_cast<const float4 *>(p.part_o + pair * p.nsplit * G * kD);
-  if (warp < G) {
+  if (warp < G) {  // per-head global max and rescaled sum of l, one online pass
     const int g = warp;
-    float M = -INFINITY;
-    for (int j = lane; j < p.nsplit; j += 32) M = fmaxf(M, __ldcg(pml + (j * G + g) * 2));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    float Ls = 0.0f;
+    float M = -INFINITY, Ls = 0.0f;
+#pragma unroll 4
     for (int j = lane; j < p.nsplit; j += 32) {
       const float mj = __ldcg(pml + (j * G + g) * 2);
-      if (mj != -INFINITY) Ls = fmaf(__ldcg(pml + (j * G + g) * 2 + 1), exp2f(mj - M), Ls);
+      const float lj = __ldcg(pml + (j * G + g) * 2 + 1);
+      if (mj > M) {
+        Ls = Ls * exp2f(M - mj) + lj;  // exp2(-inf) = 0 when M is still -inf
+        M = mj;
+      } else if (mj != -INFINITY) {
+        Ls = fmaf(lj, exp2f(mj - M), Ls);
+      }
     }
-    Ls = warp_sum(Ls);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float Mo = __shfl_xor_sync(0xffffffffu, M, o);
+      const float Lo = __shfl_xor_sync(0xffffffffu, Ls, o);
+      const float Mn = fmaxf(M, Mo);
+      Ls = (M == -INFINITY ? 0.0f : Ls * exp2f(M - Mn)) + (Mo == -INFINITY ? 0.0f : Lo * exp2f(Mo - Mn));
+      M = Mn;
+    }
     if (lane == 0) {
       Mh[g] = M;
       Mh[G + g] = Ls;
@@ -150,6 +160,7 @@ __device__ __forceinline__ void combine_splits(const GqaParams &p, size_t pair, 
   float4 acc[F];
 #pragma unroll
   for (int f = 0; f < F; ++f) acc[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
   for (int j = warp; j < p.nsplit; j += kNW) {
     float wgt[G];
 #pragma unroll

@@ -42,13 +42,13 @@ def test_config0_256_steps():
     assert e_out <= TOL and e_S <= TOL and e_conv <= 1e-6
 
 
-@pytest.mark.parametrize("split", [1, 2, 4, 8])
+@pytest.mark.parametrize("split", [-1, 1, 2, 4, 8])
 def test_every_column_split(split):
     e_out, e_S, e_conv = run_gdn(3, 16, 16, 12, seed=10 + split, split=split)
     assert e_out <= TOL and e_S <= TOL and e_conv <= 1e-6
 
 
-@pytest.mark.parametrize("Hk,Hv,split", [(8, 16, 0), (8, 16, 4), (4, 16, 2), (8, 24, 1)])
+@pytest.mark.parametrize("Hk,Hv,split", [(8, 16, 0), (8, 16, 4), (4, 16, 2), (8, 24, 1), (8, 16, -1), (8, 24, -1)])
 def test_value_heads_share_key_heads(Hk, Hv, split):
     """num_v_heads > num_k_heads: k-head h//rf expanded as text_modules.rs:597-615."""
     e_out, e_S, e_conv = run_gdn(2, Hk, Hv, 8, seed=20 + Hv + split, split=split)
@@ -56,8 +56,9 @@ def test_value_heads_share_key_heads(Hk, Hv, split):
 
 
 @pytest.mark.parametrize("K", [2, 3])
-def test_short_conv_kernels(K):
-    e_out, e_S, e_conv = run_gdn(2, 16, 16, 6, seed=30 + K, K=K)
+@pytest.mark.parametrize("split", [0, -1])
+def test_short_conv_kernels(K, split):
+    e_out, e_S, e_conv = run_gdn(2, 16, 16, 6, seed=30 + K, K=K, split=split)
     assert e_out <= TOL and e_S <= TOL and e_conv <= 1e-6
 
 
