@@ -33,19 +33,23 @@ constexpr int kThreads = (kNW + 1) * 32;
 constexpr int kTK = 16;           // keys per pipeline stage
 constexpr int kNS = 3;            // pipeline stages
 constexpr int kKPW = kTK / kNW;   // keys per consumer warp per stage
+constexpr int kFanIn = 8;         // partials merged per node of the combine tree
 
 struct GqaParams {
   const float *q_gate, *k_new, *v_new, *qn_w, *kn_w, *cos, *sin;
   float *k_cache, *v_cache;
   int32_t *lens;
   float *out;
-  float *part_o;       // [B, Hkv, nsplit, G, D]
-  float *part_ml;      // [B, Hkv, nsplit, G, 2]
+  float *part_o;       // level 0: [B, Hkv, nsplit, G, D]
+  float *part_ml;      // level 0: [B, Hkv, nsplit, G, 2]
+  float *grp_o;        // level 1: [B, Hkv, ngroups, G, D]
+  float *grp_ml;       // level 1: [B, Hkv, ngroups, G, 2]
+  uint32_t *grp_cnt;   // [B * Hkv * ngroups]
   uint32_t *pair_cnt;  // [B * Hkv]
   uint32_t *seq_cnt;   // [B]
   uint32_t *status;
   long long cap;
-  int B, Hq, Hkv, rot, nsplit, kps;
+  int B, Hq, Hkv, rot, nsplit, kps, ngroups;
   float eps, qscale_log2;
 };
 
@@ -113,28 +117,30 @@ __device__ __forceinline__ void reduce_scatter(float (&v)[V], int lane) {
   }
 }
 
-// Merge the nsplit (m, l, o) partials of one (sequence, kv head) pair and
-// write out = o / l * sigmoid(gate).  Run by the 256 consumer threads of the
-// last CTA to arrive.  Warp w takes splits w, w+NW, ...; a lane owns G*2
-// float4 columns of the [G][D] output, so every lane keeps G*2 independent
-// 16-byte loads in flight per split.  Per-head maxima come first (lanes stride
-// over splits), the warps' partial sums are merged through shared memory.
+// Merge n (m, l, o) partials (m in log2 units, o unnormalised) laid out as
+// pml [n][G][2], po [n][G][D].  With out_ml == nullptr the result is final:
+// out = o / l * sigmoid(gate); otherwise it is written as one partial of the
+// same format to (out_ml, out_o).  Run by the 256 consumer threads.  Warp w
+// takes partials w, w+NW, ...; a lane owns G*2 float4 of the [G][D] output, so
+// it keeps G*2 independent 16-byte loads in flight per partial.  The per-head
+// maxima come first (one online pass, lanes striding over partials); the
+// warps' sums are merged through shared memory.
 template <int G>
-__device__ __forceinline__ void combine_splits(const GqaParams &p, size_t pair, int kvh, int b, float *scratch,
+__device__ __forceinline__ void merge_partials(const GqaParams &p, const float *pml, const float *po_f, int n,
+                                               float *out_ml, float *out_o, int kvh, int b, float *scratch,
                                                int warp, int lane, int tid) {
   constexpr int F = G * kD / 4 / 32;  // float4 per lane
   float *Mh = scratch + kNW * G * kD;  // [G] global max, [G] sum of l
-  const float *pml = p.part_ml + pair * p.nsplit * G * 2;
-  const float4 *po = reinterpret_cast<const float4 *>(p.part_o + pair * p.nsplit * G * kD);
-  if (warp < G) {  // per-head global max and rescaled sum of l, one online pass
+  const float4 *po = reinterpret_cast<const float4 *>(po_f);
+  if (warp < G) {
     const int g = warp;
     float M = -INFINITY, Ls = 0.0f;
 #pragma unroll 4
-    for (int j = lane; j < p.nsplit; j += 32) {
+    for (int j = lane; j < n; j += 32) {
       const float mj = __ldcg(pml + (j * G + g) * 2);
       const float lj = __ldcg(pml + (j * G + g) * 2 + 1);
       if (mj > M) {
-        Ls = Ls * exp2f(M - mj) + lj;  // exp2(-inf) = 0 when M is still -inf
+        Ls = Ls * exp2f(M - mj) + lj;  // exp2(-inf) = 0 while M is still -inf
         M = mj;
       } else if (mj != -INFINITY) {
         Ls = fmaf(lj, exp2f(mj - M), Ls);
@@ -160,8 +166,8 @@ __device__ __forceinline__ void combine_splits(const GqaParams &p, size_t pair, 
   float4 acc[F];
 #pragma unroll
   for (int f = 0; f < F; ++f) acc[f] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 2
-  for (int j = warp; j < p.nsplit; j += kNW) {
+#pragma unroll 1
+  for (int j = warp; j < n; j += kNW) {
     float wgt[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -170,8 +176,7 @@ __device__ __forceinline__ void combine_splits(const GqaParams &p, size_t pair, 
     }
 #pragma unroll
     for (int f = 0; f < F; ++f) {
-      const int q = lane + 32 * f;            // float4 index in [G][D/4]
-      const float4 v = __ldcg(po + (size_t)j * (G * kD / 4) + q);
+      const float4 v = __ldcg(po + (size_t)j * (G * kD / 4) + lane + 32 * f);
       acc[f] = f4_fma(wgt[(32 * f) / (kD / 4)], v, acc[f]);  // lane < 32: head is f / 2
     }
   }
@@ -184,9 +189,17 @@ __device__ __forceinline__ void combine_splits(const GqaParams &p, size_t pair, 
     float O = 0.0f;
 #pragma unroll
     for (int w = 0; w < kNW; ++w) O += scratch[(size_t)w * G * kD + i];
-    const int h = kvh * G + g;
-    const float gate = p.q_gate[((size_t)b * p.Hq + h) * 2 * kD + kD + d];
-    p.out[((size_t)b * p.Hq + h) * kD + d] = (O / Mh[G + g]) * sigmoidf_dev(gate);
+    if (out_ml == nullptr) {
+      const int h = kvh * G + g;
+      const float gate = p.q_gate[((size_t)b * p.Hq + h) * 2 * kD + kD + d];
+      p.out[((size_t)b * p.Hq + h) * kD + d] = (O / Mh[G + g]) * sigmoidf_dev(gate);
+    } else {
+      __stcg(out_o + i, O);
+      if (d == 0) {
+        __stcg(out_ml + g * 2 + 0, Mh[g]);
+        __stcg(out_ml + g * 2 + 1, Mh[G + g]);
+      }
+    }
   }
 }
 
@@ -412,19 +425,38 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
     }
   }
 
-  // ---- cross-CTA combine by the last split to arrive (no spin-wait)
+  // ---- cross-CTA combine: a two-level ticket tree (fan-in 8, no spin-wait).
+  // The last split of each group of 8 to arrive merges the group; the last
+  // group to finish merges the group partials into the output.
   if (!single) {
     __threadfence();
     named_bar_sync(1, kNW * 32);
-    if (tid == 0) {
-      const uint32_t ticket = atomicAdd(&p.pair_cnt[pair], 1u);
-      last_flag = ticket == (uint32_t)(p.nsplit - 1);
-    }
+    const int grp = s / kFanIn;
+    const int gsize = min(kFanIn, p.nsplit - grp * kFanIn);
+    uint32_t *gc = p.grp_cnt + pair * p.ngroups + grp;
+    if (tid == 0) last_flag = atomicAdd(gc, 1u) == (uint32_t)(gsize - 1);
     named_bar_sync(1, kNW * 32);
     if (!last_flag) return;
     __threadfence();
-    combine_splits<G>(p, pair, kvh, b, wacc, warp, lane, tid);
-    if (tid == 0) p.pair_cnt[pair] = 0u;
+    const float *gml = p.part_ml + (pair * p.nsplit + grp * kFanIn) * G * 2;
+    const float *go = p.part_o + (pair * p.nsplit + grp * kFanIn) * G * kD;
+    if (p.ngroups == 1) {
+      merge_partials<G>(p, gml, go, gsize, nullptr, nullptr, kvh, b, wacc, warp, lane, tid);
+      if (tid == 0) *gc = 0u;
+    } else {
+      merge_partials<G>(p, gml, go, gsize, p.grp_ml + (pair * p.ngroups + grp) * G * 2,
+                        p.grp_o + (pair * p.ngroups + grp) * G * kD, kvh, b, wacc, warp, lane, tid);
+      if (tid == 0) *gc = 0u;
+      __threadfence();
+      named_bar_sync(1, kNW * 32);
+      if (tid == 0) last_flag = atomicAdd(&p.pair_cnt[pair], 1u) == (uint32_t)(p.ngroups - 1);
+      named_bar_sync(1, kNW * 32);
+      if (!last_flag) return;
+      __threadfence();
+      merge_partials<G>(p, p.grp_ml + pair * p.ngroups * G * 2, p.grp_o + pair * p.ngroups * G * kD, p.ngroups,
+                        nullptr, nullptr, kvh, b, wacc, warp, lane, tid);
+      if (tid == 0) p.pair_cnt[pair] = 0u;
+    }
   }
   // ---- the last (sequence, kv head) pair of sequence b advances lens[b]
   if (tid == 0) {
@@ -470,16 +502,32 @@ int gqa_keys_per_split(int B, int Hkv, long long max_len, int sms) {
   return (int)per;
 }
 
+struct GqaWsLayout {
+  size_t status, grp_cnt, pair_cnt, seq_cnt, part_o, part_ml, grp_o, grp_ml, total;
+  int kps, nsplit, ngroups;
+};
+
+GqaWsLayout gqa_ws_layout(int B, int Hq, int Hkv, long long max_len, int sms) {
+  GqaWsLayout l;
+  l.kps = gqa_keys_per_split(B, Hkv, max_len, sms);
+  l.nsplit = (int)((max_len + l.kps - 1) / l.kps);
+  l.ngroups = (l.nsplit + kFanIn - 1) / kFanIn;
+  const size_t G = (size_t)(Hq / Hkv), pairs = (size_t)B * Hkv;
+  auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+  l.status = 0;
+  l.grp_cnt = 256;
+  l.pair_cnt = l.grp_cnt + pairs * l.ngroups * sizeof(uint32_t);
+  l.seq_cnt = l.pair_cnt + pairs * sizeof(uint32_t);
+  l.part_o = up(l.seq_cnt + (size_t)B * sizeof(uint32_t));
+  l.part_ml = up(l.part_o + pairs * l.nsplit * G * kD * sizeof(float));
+  l.grp_o = up(l.part_ml + pairs * l.nsplit * G * 2 * sizeof(float));
+  l.grp_ml = up(l.grp_o + pairs * l.ngroups * G * kD * sizeof(float));
+  l.total = up(l.grp_ml + pairs * l.ngroups * G * 2 * sizeof(float));
+  return l;
+}
+
 size_t gqa_workspace_bytes(int B, int Hq, int Hkv, long long max_len, int sms) {
-  const int kps = gqa_keys_per_split(B, Hkv, max_len, sms);
-  const long long nsplit = (max_len + kps - 1) / kps;
-  const int G = Hq / Hkv;
-  size_t off = 256;                                                   // status word
-  off += ((size_t)B * Hkv + B) * sizeof(uint32_t);                    // counters
-  off = (off + 255) / 256 * 256;
-  off += (size_t)B * Hkv * nsplit * G * kD * sizeof(float);           // part_o
-  off += (size_t)B * Hkv * nsplit * G * 2 * sizeof(float);            // part_ml
-  return (off + 255) / 256 * 256;
+  return gqa_ws_layout(B, Hq, Hkv, max_len, sms).total;
 }
 
 int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_gate, const float *k_new,
@@ -490,25 +538,28 @@ int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_g
   GqaParams p = {};
   p.B = d->batch; p.Hq = d->num_q_heads; p.Hkv = d->num_kv_heads; p.rot = d->rotary_dim;
   p.cap = d->capacity; p.eps = d->eps;
-  p.kps = gqa_keys_per_split(p.B, p.Hkv, max_len, sms);
-  p.nsplit = (int)((max_len + p.kps - 1) / p.kps);
-  const size_t need = gqa_workspace_bytes(p.B, p.Hq, p.Hkv, max_len, sms);
-  Q35_REQUIRE(ws != nullptr && ws_bytes >= need, Q35_ERR_WORKSPACE,
-              "gqa_decode: workspace too small (need " + std::to_string(need) + " bytes)");
+  const GqaWsLayout lay = gqa_ws_layout(p.B, p.Hq, p.Hkv, max_len, sms);
+  p.kps = lay.kps;
+  p.nsplit = lay.nsplit;
+  p.ngroups = lay.ngroups;
+  Q35_REQUIRE(ws != nullptr && ws_bytes >= lay.total && (reinterpret_cast<uintptr_t>(ws) & 255u) == 0,
+              Q35_ERR_WORKSPACE,
+              "gqa_decode: workspace missing, not 256-byte aligned or too small (need " +
+                  std::to_string(lay.total) + " bytes)");
   Q35_REQUIRE(p.nsplit <= 65535, Q35_ERR_UNSUPPORTED, "gqa_decode: max_len too large for the split grid");
   p.q_gate = q_gate; p.k_new = k_new; p.v_new = v_new; p.qn_w = qn_w; p.kn_w = kn_w; p.cos = cos; p.sin = sin;
   p.k_cache = k_cache; p.v_cache = v_cache; p.lens = lens; p.out = out;
   p.qscale_log2 = (1.0f / sqrtf((float)kD)) * kLog2e;
   unsigned char *base = static_cast<unsigned char *>(ws);
-  p.status = reinterpret_cast<uint32_t *>(base);
-  p.pair_cnt = reinterpret_cast<uint32_t *>(base + 256);
-  p.seq_cnt = p.pair_cnt + (size_t)p.B * p.Hkv;
-  size_t off = 256 + ((size_t)p.B * p.Hkv + p.B) * sizeof(uint32_t);
-  off = (off + 255) / 256 * 256;
+  p.status = reinterpret_cast<uint32_t *>(base + lay.status);
+  p.grp_cnt = reinterpret_cast<uint32_t *>(base + lay.grp_cnt);
+  p.pair_cnt = reinterpret_cast<uint32_t *>(base + lay.pair_cnt);
+  p.seq_cnt = reinterpret_cast<uint32_t *>(base + lay.seq_cnt);
+  p.part_o = reinterpret_cast<float *>(base + lay.part_o);
+  p.part_ml = reinterpret_cast<float *>(base + lay.part_ml);
+  p.grp_o = reinterpret_cast<float *>(base + lay.grp_o);
+  p.grp_ml = reinterpret_cast<float *>(base + lay.grp_ml);
   const int G = p.Hq / p.Hkv;
-  p.part_o = reinterpret_cast<float *>(base + off);
-  off += (size_t)p.B * p.Hkv * p.nsplit * G * kD * sizeof(float);
-  p.part_ml = reinterpret_cast<float *>(base + off);
   cudaError_t e;
   switch (G) {
     case 1: e = launch_g<1>(p, st); break;
