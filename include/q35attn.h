@@ -155,6 +155,23 @@ int q35_gqa_decode(const q35_gqa_dims *dims, int64_t max_len,
                    int32_t *lens, float *out, void *workspace,
                    size_t workspace_bytes, void *stream);
 
+/* q35_gqa_decode for callers that cannot allocate device memory (no entry
+ * in the reference: its Burn host always allocates).  Same arguments and
+ * semantics minus the workspace: the split-K scratch lives in a fixed 16 MiB
+ * array inside the library, held on every GPU that loads it until exit.
+ * Calls needing more (q35_gqa_decode_workspace_size > 16 MiB, e.g. 256
+ * sequences at 32K context) fail with Q35_ERR_WORKSPACE.  All calls share the
+ * array, so calls that overlap on the GPU race; each call first clears the
+ * array's counters with a memset on `stream`.  The first call on a device
+ * looks up the array's device address and should come before any stream
+ * capture.  Device-side skips (full cache) leave lens[b] unchanged. */
+int q35_gqa_decode_noalloc(const q35_gqa_dims *dims, int64_t max_len,
+                           const float *q_gate, const float *k_new,
+                           const float *v_new, const float *qn_w,
+                           const float *kn_w, const float *cos,
+                           const float *sin, float *k_cache, float *v_cache,
+                           int32_t *lens, float *out, void *stream);
+
 /* Reads (and with clear != 0 resets) the device-side status word of a
  * workspace (Q35_STATUS_* bits).  Synchronizes `stream`.  status_out is a
  * HOST pointer. */

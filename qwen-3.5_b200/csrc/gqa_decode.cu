@@ -530,6 +530,11 @@ size_t gqa_workspace_bytes(int B, int Hq, int Hkv, long long max_len, int sms) {
   return gqa_ws_layout(B, Hq, Hkv, max_len, sms).total;
 }
 
+// Bytes at the front of the workspace holding the status word and counters.
+size_t gqa_workspace_counter_bytes(int B, int Hq, int Hkv, long long max_len, int sms) {
+  return gqa_ws_layout(B, Hq, Hkv, max_len, sms).part_o;
+}
+
 int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_gate, const float *k_new,
                       const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
                       const float *sin, float *k_cache, float *v_cache, int32_t *lens, float *out,

@@ -53,6 +53,7 @@ SIGNATURES = {
     "q35_workspace_init": (C.c_int, [_P, _SZ, _P]),
     "q35_gqa_decode": (C.c_int, [C.POINTER(GqaDims), _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "q35_workspace_status": (C.c_int, [_P, C.POINTER(C.c_uint32), _I32, _P]),
+    "q35_gqa_decode_noalloc": (C.c_int, [C.POINTER(GqaDims), _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "q35_last_error": (C.c_char_p, []),
     "q35_version": (C.c_char_p, []),
     "q35_launch_count": (C.c_uint64, [_I32]),
