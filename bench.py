@@ -395,6 +395,10 @@ def run_gpu(args):
         raise SystemExit("non-finite outputs")
 
     extras = None
+    if world > 1 and not args.no_extras:
+        del x, z, g, beta, qg, kn, vn
+        cp = run_single_seq_cp(dev, world, rank)
+        extras = {"single_seq_context_parallel": cp}
     if rank == 0 and world == 1 and not args.no_extras:
         del x, z, g, beta, qg, kn, vn
         extras = run_extras(dev)
@@ -570,6 +574,81 @@ def run_extras(dev, reps=3):
                                         "achieved_gbs": by2 / t / 1e9, "alg_gflop": fl2 / 1e9,
                                         "achieved_tflops": fl2 / t / 1e12}
     return res
+
+
+def run_single_seq_cp(dev, world, rank, steps=64, warmup=3):
+    """BASELINE config 4's single 32K-context sequence decoded across all
+    ranks: GDN heads-parallel, GQA KV length split, NCCL all-gather of the
+    per-rank GQA softmax partials and GDN head outputs (q35attn.parallel).
+    Collective on every rank; returns the per-step time (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    import q35attn
+    from q35attn.parallel import ShardPlan
+
+    plan = ShardPlan(world, rank, HK, HV, L0)
+    lo, hi = plan.kv_tokens
+    n_loc = hi - lo
+    cap = n_loc + (steps + warmup + 2 if plan.holds_tail else 0) + 1
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(777 + rank)
+
+    def randn(*shape, scale=1.0):
+        t = torch.empty(*shape, device=dev, dtype=torch.float32)
+        t.normal_(0.0, scale, generator=gen)
+        return t
+
+    Kc, Vc = randn(1, HKV, cap, D), randn(1, HKV, cap, D)
+    lens = torch.full((1,), n_loc, dtype=torch.int32, device=dev)
+    ws = q35attn.GqaWorkspace(1, HQ, HKV, cap, device=dev)
+    hk_l = HK // world
+    hv_l = HV // world
+    c_loc = 2 * hk_l * DK + hv_l * DK
+    S = randn(1, hv_l, DK, DK, scale=0.02)
+    cst = randn(1, c_loc, KCONV - 1, scale=0.5)
+    conv_w = randn(c_loc, KCONV, scale=0.5)
+    norm_w = torch.ones(DK, device=dev)
+    w0 = torch.zeros(D, device=dev)
+    nst = steps + warmup
+    x, z = randn(nst, 1, c_loc), randn(nst, 1, hv_l * DK)
+    g = -torch.nn.functional.softplus(randn(nst, 1, hv_l))
+    beta = torch.sigmoid(randn(nst, 1, hv_l))
+    qg, kn, vn = randn(nst, 1, HQ, 2 * D), randn(nst, 1, HKV, D), randn(nst, 1, HKV, D)
+    cs, sn = randn(nst, 1, ROT), randn(nst, 1, ROT)
+    part = torch.empty(1, HQ, D + 2, device=dev)
+    parts = torch.empty(world, 1, HQ, D + 2, device=dev)
+    out_l = torch.empty(1, hv_l * DK, device=dev)
+    gdn_all = torch.empty(world, 1, hv_l * DK, device=dev)
+    out = torch.empty(1, HQ * D, device=dev)
+    tail = plan.holds_tail
+
+    def step(i):
+        q35attn.gdn_decode(x[i], z[i], beta[i], g[i], conv_w, norm_w, cst, S, out_l, num_k_heads=hk_l,
+                           num_v_heads=hv_l)
+        q35attn.gqa_decode_partial(qg[i], kn[i] if tail else None, vn[i] if tail else None, w0, w0, cs[i], sn[i],
+                                   Kc, Vc, lens, part, workspace=ws, max_len=cap)
+        dist.all_gather_into_tensor(parts, part)
+        q35attn.gqa_combine_partials(parts, qg[i], out)
+        dist.all_gather_into_tensor(gdn_all, out_l)
+
+    for i in range(warmup):
+        step(i)
+    dist.barrier(device_ids=[dev.index])
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(warmup, nst):
+        step(i)
+    b.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([a.elapsed_time(b) / 1000.0 / steps], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t = float(t.item())
+    by = gqa_bytes_per_seq(L0 + warmup + steps // 2) + GDN_BYTES_PER_SEQ + GDN_BYTES_SHARED
+    return {"us_per_step": t * 1e6, "layer_steps_per_s": 2.0 / t, "alg_bytes_per_step_all_gpus": by,
+            "achieved_gbs_all_gpus": by / t / 1e9, "collectives_per_step": 2,
+            "partitioning": f"GDN heads {HV}/{world} per rank, GQA KV length {L0}/{world} per rank"}
 
 
 def main():

@@ -155,6 +155,33 @@ int q35_gqa_decode(const q35_gqa_dims *dims, int64_t max_len,
                    int32_t *lens, float *out, void *workspace,
                    size_t workspace_bytes, void *stream);
 
+/* Context-parallel form of q35_gqa_decode for one shard of a KV cache split
+ * along its length across GPUs (text_modules.rs:899-928 with the keys
+ * partitioned; no reference counterpart for the partitioning itself).
+ * Writes, per (sequence, query head), the unnormalised partial
+ * partial_out[B, Hq, D+2] = [o (D) | m | l] of the softmax over this shard's
+ * keys, m in log2 units (scores * log2(e)), o = sum_j 2^(s_j - m) v_j.
+ * k_new / v_new NULL: attend the cached keys [0, lens[b]) only, no append,
+ * lens unchanged (every shard but the last).  Non-NULL: append at lens[b] as
+ * q35_gqa_decode does and attend [0, lens[b]] (the shard holding the tail).
+ * cos / sin are the tables of the token's global position. */
+int q35_gqa_decode_partial(const q35_gqa_dims *dims, int64_t max_len,
+                           const float *q_gate, const float *k_new,
+                           const float *v_new, const float *qn_w,
+                           const float *kn_w, const float *cos,
+                           const float *sin, float *k_cache, float *v_cache,
+                           int32_t *lens, float *partial_out, void *workspace,
+                           size_t workspace_bytes, void *stream);
+
+/* Merges n_parts shard partials parts[n_parts, B, Hq, D+2] (as written by
+ * q35_gqa_decode_partial, gathered from every shard) into
+ * out[B, Hq*D] = (sum o 2^(m-M)) / (sum l 2^(m-M)) * sigmoid(gate), the gate
+ * taken from q_gate[B, Hq, 2*D] (text_modules.rs:930-936). */
+int q35_gqa_combine_partials(int32_t batch, int32_t num_q_heads,
+                             int32_t head_dim, int32_t n_parts,
+                             const float *parts, const float *q_gate,
+                             float *out, void *stream);
+
 /* q35_gqa_decode for callers that cannot allocate device memory (no entry
  * in the reference: its Burn host always allocates).  Same arguments and
  * semantics minus the workspace: the split-K scratch lives in a fixed 16 MiB

@@ -20,7 +20,9 @@ size_t gqa_workspace_bytes(int B, int Hq, int Hkv, long long max_len, int sms);
 int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_gate, const float *k_new,
                       const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
                       const float *sin, float *k_cache, float *v_cache, int32_t *lens, float *out,
-                      void *ws, size_t ws_bytes, cudaStream_t st);
+                      void *ws, size_t ws_bytes, cudaStream_t st, float *part_out);
+int gqa_combine_launch(int B, int Hq, int n_parts, const float *parts, const float *q_gate, float *out,
+                       cudaStream_t st);
 size_t gdn_prefill_workspace_bytes(const q35_gdn_dims *d, int T);
 int gdn_prefill_launch(const q35_gdn_dims *d, int T, const float *mixed_qkv, const float *z, const float *beta,
                        const float *g, const float *conv_w, const float *norm_w, float *conv_state, int has_prev,
@@ -197,7 +199,41 @@ int q35_gqa_decode(const q35_gqa_dims *dims, int64_t max_len, const float *q_gat
   Q35_PTR16(k_cache); Q35_PTR16(v_cache); Q35_PTR(lens); Q35_PTR(out);
   if (int rc = require_sm100()) return rc;
   return gqa_decode_launch(dims, max_len, q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, lens, out,
-                           workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+                           workspace, workspace_bytes, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int q35_gqa_decode_partial(const q35_gqa_dims *dims, int64_t max_len, const float *q_gate, const float *k_new,
+                           const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
+                           const float *sin, float *k_cache, float *v_cache, int32_t *lens, float *partial_out,
+                           void *workspace, size_t workspace_bytes, void *stream) {
+  if (int rc = check_gqa_dims(dims)) return rc;
+  Q35_REQUIRE(max_len > 0, Q35_ERR_INVALID_ARG, "gqa_decode_partial: max_len must be > 0");
+  Q35_REQUIRE(max_len <= dims->capacity, Q35_ERR_CAPACITY, "gqa_decode_partial: max_len exceeds the capacity");
+  Q35_REQUIRE((k_new == nullptr) == (v_new == nullptr), Q35_ERR_INVALID_ARG,
+              "gqa_decode_partial: k_new and v_new must both be set (append) or both be NULL");
+  if (dims->batch == 0) return Q35_OK;
+  Q35_PTR16(q_gate); Q35_PTR16(qn_w);
+  if (k_new != nullptr) {
+    Q35_PTR16(k_new); Q35_PTR16(v_new); Q35_PTR16(kn_w);
+  }
+  if (dims->rotary_dim > 0) {
+    Q35_PTR(cos);
+    Q35_PTR(sin);
+  }
+  Q35_PTR16(k_cache); Q35_PTR16(v_cache); Q35_PTR(lens); Q35_PTR(partial_out);
+  if (int rc = require_sm100()) return rc;
+  return gqa_decode_launch(dims, max_len, q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, lens,
+                           nullptr, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), partial_out);
+}
+
+int q35_gqa_combine_partials(int32_t batch, int32_t num_q_heads, int32_t head_dim, int32_t n_parts,
+                             const float *parts, const float *q_gate, float *out, void *stream) {
+  Q35_REQUIRE(batch >= 0 && num_q_heads > 0 && n_parts > 0, Q35_ERR_INVALID_ARG, "gqa_combine: bad sizes");
+  Q35_REQUIRE(head_dim == 256, Q35_ERR_UNSUPPORTED, "gqa_combine: head_dim = 256 is the compiled configuration");
+  if (batch == 0) return Q35_OK;
+  Q35_PTR(parts); Q35_PTR(q_gate); Q35_PTR(out);
+  if (int rc = require_sm100()) return rc;
+  return gqa_combine_launch(batch, num_q_heads, n_parts, parts, q_gate, out, static_cast<cudaStream_t>(stream));
 }
 
 int q35_workspace_status(void *workspace, uint32_t *status_out, int32_t clear, void *stream) {

@@ -40,6 +40,7 @@ struct GqaParams {
   float *k_cache, *v_cache;
   int32_t *lens;
   float *out;
+  float *part_out;     // optional [B, Hq, D+2] (o unnormalised | m (log2 units) | l) instead of `out`
   float *part_o;       // level 0: [B, Hkv, nsplit, G, D]
   float *part_ml;      // level 0: [B, Hkv, nsplit, G, 2]
   float *grp_o;        // level 1: [B, Hkv, ngroups, G, D]
@@ -117,6 +118,23 @@ __device__ __forceinline__ void reduce_scatter(float (&v)[V], int lane) {
   }
 }
 
+// Final value of output element (head h, dim d): the gated, normalised
+// attention output, or -- for a context-parallel caller -- the unnormalised
+// (o, m, l) triple that q35_gqa_combine_partials merges across GPUs.
+__device__ __forceinline__ void write_final(const GqaParams &p, int b, int h, int d, float O, float M, float Ls) {
+  if (p.part_out != nullptr) {
+    float *dst = p.part_out + ((size_t)b * p.Hq + h) * (kD + 2);
+    dst[d] = O;
+    if (d == 0) {
+      dst[kD] = M;
+      dst[kD + 1] = Ls;
+    }
+  } else {
+    const float gate = p.q_gate[((size_t)b * p.Hq + h) * 2 * kD + kD + d];
+    p.out[((size_t)b * p.Hq + h) * kD + d] = (O / Ls) * sigmoidf_dev(gate);
+  }
+}
+
 // Merge n (m, l, o) partials (m in log2 units, o unnormalised) laid out as
 // pml [n][G][2], po [n][G][D].  With out_ml == nullptr the result is final:
 // out = o / l * sigmoid(gate); otherwise it is written as one partial of the
@@ -190,9 +208,7 @@ __device__ __forceinline__ void merge_partials(const GqaParams &p, const float *
 #pragma unroll
     for (int w = 0; w < kNW; ++w) O += scratch[(size_t)w * G * kD + i];
     if (out_ml == nullptr) {
-      const int h = kvh * G + g;
-      const float gate = p.q_gate[((size_t)b * p.Hq + h) * 2 * kD + kD + d];
-      p.out[((size_t)b * p.Hq + h) * kD + d] = (O / Mh[G + g]) * sigmoidf_dev(gate);
+      write_final(p, b, kvh * G + g, d, O, Mh[g], Mh[G + g]);
     } else {
       __stcg(out_o + i, O);
       if (d == 0) {
@@ -220,11 +236,12 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   const int len = p.lens[b];
-  if (len >= p.cap) {
+  const bool append = p.k_new != nullptr;  // false: attend the cached keys only (context-parallel shard)
+  if (append && len >= p.cap) {
     if (s == 0 && kvh == 0 && tid == 0) atomicOr(p.status, Q35_STATUS_CACHE_FULL);
     return;
   }
-  const int L = len + 1;
+  const int L = append ? len + 1 : len;
   if (L > p.nsplit * p.kps) {
     if (s == 0 && kvh == 0 && tid == 0) atomicOr(p.status, Q35_STATUS_LEN_HINT);
     return;
@@ -248,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
 
   if (warp == kNW) {
     // ---------------------------------------------------------- producer
-    if (len >= kbeg && len < kend) {
+    if (append && len >= kbeg && len < kend) {
       // This CTA owns the new position: k_norm + RoPE, append k and v.
       const float *kin = p.k_new + pair * kD;
       const float *vin = p.v_new + pair * kD;
@@ -413,9 +430,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
       O = fmaf(wacc[((size_t)w * G + g) * kD + d], sc, O);
     }
     if (single) {
-      const int h = kvh * G + g;
-      const float gate = p.q_gate[((size_t)b * p.Hq + h) * 2 * kD + kD + d];
-      p.out[((size_t)b * p.Hq + h) * kD + d] = (O / Ls) * sigmoidf_dev(gate);
+      write_final(p, b, kvh * G + g, d, O, M, Ls);
     } else {
       __stcg(po + i, O);
       if (d == 0) {
@@ -464,9 +479,29 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
     const uint32_t t2 = atomicAdd(&p.seq_cnt[b], 1u);
     if (t2 == (uint32_t)(p.Hkv - 1)) {
       p.seq_cnt[b] = 0u;
-      p.lens[b] = len + 1;
+      if (append) p.lens[b] = len + 1;
     }
   }
+}
+
+// out[b, h, :] = (sum_r o_r 2^(m_r - M)) / (sum_r l_r 2^(m_r - M)) * sigmoid(gate),
+// M = max_r m_r, over n_parts partials [n][B][Hq][D+2] (one per context shard).
+__global__ void gqa_combine_kernel(int B, int Hq, int n_parts, const float *__restrict__ parts,
+                                   const float *__restrict__ q_gate, float *__restrict__ out) {
+  const int bh = blockIdx.x, d = threadIdx.x;
+  const size_t stride = (size_t)B * Hq * (kD + 2);
+  const float *base = parts + (size_t)bh * (kD + 2);
+  float M = -INFINITY;
+  for (int r = 0; r < n_parts; ++r) M = fmaxf(M, base[r * stride + kD]);
+  float Ls = 0.0f, O = 0.0f;
+  for (int r = 0; r < n_parts; ++r) {
+    const float mr = base[r * stride + kD];
+    const float sc = mr == -INFINITY ? 0.0f : exp2f(mr - M);
+    Ls = fmaf(base[r * stride + kD + 1], sc, Ls);
+    O = fmaf(base[r * stride + d], sc, O);
+  }
+  const float gate = q_gate[(size_t)bh * 2 * kD + kD + d];
+  out[(size_t)bh * kD + d] = (O / Ls) * sigmoidf_dev(gate);
 }
 
 template <int G>
@@ -535,10 +570,18 @@ size_t gqa_workspace_counter_bytes(int B, int Hq, int Hkv, long long max_len, in
   return gqa_ws_layout(B, Hq, Hkv, max_len, sms).part_o;
 }
 
+int gqa_combine_launch(int B, int Hq, int n_parts, const float *parts, const float *q_gate, float *out,
+                       cudaStream_t st) {
+  if (B == 0) return Q35_OK;
+  note_launch();
+  gqa_combine_kernel<<<B * Hq, kD, 0, st>>>(B, Hq, n_parts, parts, q_gate, out);
+  return check_cuda(cudaGetLastError(), "gqa_combine launch");
+}
+
 int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_gate, const float *k_new,
                       const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
                       const float *sin, float *k_cache, float *v_cache, int32_t *lens, float *out,
-                      void *ws, size_t ws_bytes, cudaStream_t st) {
+                      void *ws, size_t ws_bytes, cudaStream_t st, float *part_out) {
   const int sms = device_sm_count();
   GqaParams p = {};
   p.B = d->batch; p.Hq = d->num_q_heads; p.Hkv = d->num_kv_heads; p.rot = d->rotary_dim;
@@ -553,7 +596,7 @@ int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_g
                   std::to_string(lay.total) + " bytes)");
   Q35_REQUIRE(p.nsplit <= 65535, Q35_ERR_UNSUPPORTED, "gqa_decode: max_len too large for the split grid");
   p.q_gate = q_gate; p.k_new = k_new; p.v_new = v_new; p.qn_w = qn_w; p.kn_w = kn_w; p.cos = cos; p.sin = sin;
-  p.k_cache = k_cache; p.v_cache = v_cache; p.lens = lens; p.out = out;
+  p.k_cache = k_cache; p.v_cache = v_cache; p.lens = lens; p.out = out; p.part_out = part_out;
   p.qscale_log2 = (1.0f / sqrtf((float)kD)) * kLog2e;
   unsigned char *base = static_cast<unsigned char *>(ws);
   p.status = reinterpret_cast<uint32_t *>(base + lay.status);

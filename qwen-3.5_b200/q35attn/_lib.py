@@ -53,6 +53,9 @@ SIGNATURES = {
     "q35_workspace_init": (C.c_int, [_P, _SZ, _P]),
     "q35_gqa_decode": (C.c_int, [C.POINTER(GqaDims), _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "q35_workspace_status": (C.c_int, [_P, C.POINTER(C.c_uint32), _I32, _P]),
+    "q35_gqa_decode_partial": (C.c_int, [C.POINTER(GqaDims), _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                         _SZ, _P]),
+    "q35_gqa_combine_partials": (C.c_int, [_I32, _I32, _I32, _I32, _P, _P, _P, _P]),
     "q35_gqa_decode_noalloc": (C.c_int, [C.POINTER(GqaDims), _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "q35_last_error": (C.c_char_p, []),
     "q35_version": (C.c_char_p, []),

@@ -138,3 +138,35 @@ def gqa_decode(q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, len
                                 _req(k_cache, "k_cache"), _req(v_cache, "v_cache"), _req(lens, "lens", torch.int32),
                                 _req(out, "out"), workspace.buf.data_ptr(), workspace.buf.numel(), _stream(stream)))
     return out
+
+
+def gqa_decode_partial(q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, lens, partial_out=None, *,
+                       workspace, max_len=None, rotary_dim=None, eps=1e-6, stream=None):
+    """Context-parallel shard of a GQA decode step: writes the unnormalised
+    softmax partial [B, Hq, 256+2] = [o | m (log2 units) | l] over this shard's
+    keys.  k_new / v_new None: attend cached keys only (no append)."""
+    B, Hq, _ = q_gate.shape
+    Hkv, cap = k_cache.shape[1], k_cache.shape[2]
+    rot = int(rotary_dim if rotary_dim is not None else cos.shape[-1])
+    if partial_out is None:
+        partial_out = torch.empty(B, Hq, 256 + 2, device=q_gate.device, dtype=torch.float32)
+    d = gqa_dims(B, Hq, Hkv, cap, rot, eps)
+    ml = int(max_len if max_len is not None else workspace.max_len)
+    kp = _req(k_new, "k_new") if k_new is not None else None
+    vp = _req(v_new, "v_new") if v_new is not None else None
+    check(load().q35_gqa_decode_partial(C.byref(d), ml, _req(q_gate, "q_gate"), kp, vp, _req(qn_w, "qn_w"),
+                                        _req(kn_w, "kn_w"), _req(cos, "cos"), _req(sin, "sin"),
+                                        _req(k_cache, "k_cache"), _req(v_cache, "v_cache"),
+                                        _req(lens, "lens", torch.int32), _req(partial_out, "partial_out"),
+                                        workspace.buf.data_ptr(), workspace.buf.numel(), _stream(stream)))
+    return partial_out
+
+
+def gqa_combine_partials(parts, q_gate, out=None, stream=None):
+    """parts [n, B, Hq, 258] -> out [B, Hq*256] = merged softmax * sigmoid(gate)."""
+    n, B, Hq, _ = parts.shape
+    if out is None:
+        out = torch.empty(B, Hq * 256, device=parts.device, dtype=torch.float32)
+    check(load().q35_gqa_combine_partials(B, Hq, 256, n, _req(parts, "parts"), _req(q_gate, "q_gate"),
+                                          _req(out, "out"), _stream(stream)))
+    return out
