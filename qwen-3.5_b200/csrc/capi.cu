@@ -263,9 +263,8 @@ int q35_gdn_prefill(const q35_gdn_dims *dims, int32_t seq_len, const float *mixe
   Q35_REQUIRE(has_prev_conv == 0 || has_prev_conv == 1, Q35_ERR_INVALID_ARG, "has_prev_conv must be 0 or 1");
   Q35_REQUIRE(has_init_state == 0 || has_init_state == 1, Q35_ERR_INVALID_ARG, "has_init_state must be 0 or 1");
   if (dims->batch == 0 || seq_len == 0) return Q35_OK;
-  Q35_PTR(mixed_qkv); Q35_PTR(z); Q35_PTR(beta); Q35_PTR(g); Q35_PTR(conv_w); Q35_PTR(norm_w);
-  Q35_PTR(conv_state); Q35_PTR(out);
-  Q35_PTR16(rec_state);
+  Q35_PTR(mixed_qkv); Q35_PTR(beta); Q35_PTR(g); Q35_PTR(conv_w); Q35_PTR(conv_state);
+  Q35_PTR16(z); Q35_PTR16(norm_w); Q35_PTR16(out); Q35_PTR16(rec_state);
   if (int rc = require_sm100()) return rc;
   return gdn_prefill_launch(dims, seq_len, mixed_qkv, z, beta, g, conv_w, norm_w, conv_state, has_prev_conv,
                             rec_state, has_init_state, out, workspace, workspace_bytes,

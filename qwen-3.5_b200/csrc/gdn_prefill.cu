@@ -50,9 +50,11 @@ struct ChunkSmem {
   float q[kC][kLd];
   float k[kC][kLd];
   float v[kC][kLd];
-  float A[kC][kC + 1];
-  float Aqk[kC][kC + 1];
-  float gam[kC], bet[kC], row[kC];
+  float A[kC][kC + 4];    // -tril((k*beta) k^T o D, -1), then T = (I - A)^-1
+  float Aqk[kC][kC + 4];  // tril((q k^T) o D)
+  float Tb[kC][kC + 4];   // T[i][j] * beta_j
+  float Te[kC][kC + 4];   // T[i][j] * beta_j * e^gamma_j
+  float gam[kC], bet[kC];
 };
 
 template <int KC>
@@ -64,31 +66,45 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_chunk_kernel(const Prefi
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int t0 = c * kC;
 
-  // (1) causal conv + SiLU (text_modules.rs:164-182); tokens >= T are the
-  // zero padding of :224-236 (q, k, v, beta, g all zero).
-  for (int idx = tid; idx < kC * 3 * kD; idx += kThreads) {
-    const int i = idx / (3 * kD), ch = idx % (3 * kD);
-    const int t = t0 + i;
-    float y = 0.0f;
-    if (t < p.T) {
-      int cg_;
-      if (ch < kD) cg_ = hk * kD + ch;
-      else if (ch < 2 * kD) cg_ = p.Hk * kD + hk * kD + (ch - kD);
-      else cg_ = 2 * p.Hk * kD + h * kD + (ch - 2 * kD);
-      const float *w = p.conv_w + (size_t)cg_ * KC;
-      float acc = 0.0f;
+  // (1) causal conv + SiLU (text_modules.rs:164-182) as a sliding window per
+  // channel: the K-1 history values (previous chunk, cached conv state or
+  // zeros) then 64 tokens loaded 8 at a time.  Tokens >= T are the zero
+  // padding of :224-236.
+  for (int ch = tid; ch < 3 * kD; ch += kThreads) {
+    int cgl;
+    if (ch < kD) cgl = hk * kD + ch;
+    else if (ch < 2 * kD) cgl = p.Hk * kD + hk * kD + (ch - kD);
+    else cgl = 2 * p.Hk * kD + h * kD + (ch - 2 * kD);
+    float w[KC];
 #pragma unroll
-      for (int j = 0; j < KC; ++j) {
-        const int tau = t - (KC - 1) + j;
-        float xv;
-        if (tau >= 0) xv = p.x[((size_t)b * p.T + tau) * p.C + cg_];
-        else xv = p.has_prev ? p.conv_state[((size_t)b * p.C + cg_) * (KC - 1) + (KC - 1) + tau] : 0.0f;
-        acc = fmaf(w[j], xv, acc);
-      }
-      y = siluf_dev(acc);
+    for (int j = 0; j < KC; ++j) w[j] = __ldg(p.conv_w + (size_t)cgl * KC + j);
+    float hist[KC - 1];
+#pragma unroll
+    for (int j = 0; j < KC - 1; ++j) {
+      const int tau = t0 - (KC - 1) + j;
+      hist[j] = tau >= 0 ? (tau < p.T ? __ldg(p.x + ((size_t)b * p.T + tau) * p.C + cgl) : 0.0f)
+                         : (p.has_prev ? p.conv_state[((size_t)b * p.C + cgl) * (KC - 1) + (KC - 1) + tau] : 0.0f);
     }
-    float *dst = ch < kD ? &sm.q[i][ch] : ch < 2 * kD ? &sm.k[i][ch - kD] : &sm.v[i][ch - 2 * kD];
-    *dst = y;
+    float *dst = ch < kD ? &sm.q[0][ch] : ch < 2 * kD ? &sm.k[0][ch - kD] : &sm.v[0][ch - 2 * kD];
+    for (int i0 = 0; i0 < kC; i0 += 8) {
+      float xv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int t = t0 + i0 + u;
+        xv[u] = t < p.T ? __ldg(p.x + ((size_t)b * p.T + t) * p.C + cgl) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int j = 0; j < KC - 1; ++j) acc = fmaf(w[j], hist[j], acc);
+        acc = fmaf(w[KC - 1], xv[u], acc);
+#pragma unroll
+        for (int j = 0; j < KC - 2; ++j) hist[j] = hist[j + 1];
+        hist[KC - 2] = xv[u];
+        dst[(size_t)(i0 + u) * kLd] = (t0 + i0 + u) < p.T ? siluf_dev(acc) : 0.0f;
+      }
+    }
   }
   if (tid < kC) {
     const int t = t0 + tid;
@@ -126,101 +142,167 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_chunk_kernel(const Prefi
   __syncthreads();
 
   // (3) A = -tril((k*beta) k^T o D, -1), Aqk = tril((q k^T) o D) (:259-279).
+  // Thread (iq, jq) owns rows iq + 16 ri and columns jq + 16 rj; blocks with
+  // rj > ri are zero and skipped.
   {
-    const int i = tid / 4, jq = tid % 4;
-    float aA[16], aQ[16];
+    const int iq = tid / 16, jq = tid % 16;
+    float aA[10], aQ[10];
 #pragma unroll
-    for (int m = 0; m < 16; ++m) aA[m] = aQ[m] = 0.0f;
-    const float bi = sm.bet[i];
-    for (int d = 0; d < kD; ++d) {
-      const float qi = sm.q[i][d];
-      const float kbi = sm.k[i][d] * bi;
+    for (int e = 0; e < 10; ++e) aA[e] = aQ[e] = 0.0f;
+    for (int d = 0; d < kD; d += 4) {
+      float4 qi[4], ki[4], kj[4];
 #pragma unroll
-      for (int m = 0; m < 16; ++m) {
-        const float kj = sm.k[jq + 4 * m][d];
-        aA[m] = fmaf(kbi, kj, aA[m]);
-        aQ[m] = fmaf(qi, kj, aQ[m]);
+      for (int r = 0; r < 4; ++r) {
+        qi[r] = *reinterpret_cast<const float4 *>(&sm.q[iq + 16 * r][d]);
+        ki[r] = *reinterpret_cast<const float4 *>(&sm.k[iq + 16 * r][d]);
+        kj[r] = *reinterpret_cast<const float4 *>(&sm.k[jq + 16 * r][d]);
       }
-    }
-    const float gi = sm.gam[i];
+      int e = 0;
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const int j = jq + 4 * m;
-      const float dec = j <= i ? expf(gi - sm.gam[j]) : 0.0f;
-      sm.A[i][j] = j < i ? -(aA[m] * dec) : 0.0f;
-      sm.Aqk[i][j] = aQ[m] * dec;
+      for (int ri = 0; ri < 4; ++ri)
+#pragma unroll
+        for (int rj = 0; rj <= ri; ++rj, ++e) {
+          aA[e] = dot4(ki[ri], kj[rj], aA[e]);
+          aQ[e] = dot4(qi[ri], kj[rj], aQ[e]);
+        }
     }
+    int e = 0;
+#pragma unroll
+    for (int ri = 0; ri < 4; ++ri)
+#pragma unroll
+      for (int rj = 0; rj < 4; ++rj) {
+        const int i = iq + 16 * ri, j = jq + 16 * rj;
+        float va = 0.0f, vq = 0.0f;
+        if (rj <= ri) {
+          const float dec = j <= i ? expf(sm.gam[i] - sm.gam[j]) : 0.0f;
+          va = j < i ? -((aA[e] * sm.bet[i]) * dec) : 0.0f;
+          vq = aQ[e] * dec;
+          ++e;
+        }
+        sm.A[i][j] = va;
+        sm.Aqk[i][j] = vq;
+      }
   }
   __syncthreads();
 
-  // (4) forward substitution, row by row (:280-287):
-  //     A[i,:i] <- A[i,:i] + A[i,:i] @ A[:i,:i]
-  for (int i = 1; i < kC; ++i) {
-    float nv = 0.0f;
-    if (tid < i) {
-      const int j = tid;
-      float s = 0.0f;
-      for (int m = j + 1; m < i; ++m) s = fmaf(sm.A[i][m], sm.A[m][j], s);
-      nv = sm.A[i][j] + s;
-    }
-    __syncthreads();
-    if (tid < i) sm.A[i][tid] = nv;
-    __syncthreads();
-  }
-  if (tid < kC) sm.A[tid][tid] = 1.0f;  // T = A + I (:289-290)
-  __syncthreads();
-
-  // (5) U = T (v*beta), W = T (k*beta*e^gamma) (:292-293), q' and k' (:303-311)
   float *rec = p.ws + (((size_t)b * p.Hv + h) * p.NC + c) * kRec;
   float *U = rec, *W = rec + kC * kD, *Qp = rec + 2 * kC * kD, *Kp = rec + 3 * kC * kD;
   float *Aq = rec + 4 * kC * kD;
+  const float glast = sm.gam[kC - 1];
+
+  if (warp < 2) {
+    // (4) T = (I - A)^-1 column by column (the row recursion of :280-287 solves
+    // (I - A) T = I; column j: c[j] = 1, c[i] = sum_{m<i} A[i][m] c[m] for i > j).
+    const int j = tid;
+    float cv[kC];
+#pragma unroll
+    for (int m = 0; m < kC; ++m) cv[m] = m == j ? 1.0f : 0.0f;
+#pragma unroll
+    for (int i = 1; i < kC; ++i) {
+      float s = 0.0f;
+#pragma unroll
+      for (int m4 = 0; m4 < i / 4; ++m4) {
+        const float4 a = *reinterpret_cast<const float4 *>(&sm.A[i][4 * m4]);
+        s = fmaf(a.x, cv[4 * m4 + 0], s);
+        s = fmaf(a.y, cv[4 * m4 + 1], s);
+        s = fmaf(a.z, cv[4 * m4 + 2], s);
+        s = fmaf(a.w, cv[4 * m4 + 3], s);
+      }
+#pragma unroll
+      for (int m = (i / 4) * 4; m < i; ++m) s = fmaf(sm.A[i][m], cv[m], s);
+      if (i > j) cv[i] = s;
+    }
+    const float bj = sm.bet[j], ej = bj * expf(sm.gam[j]);
+#pragma unroll
+    for (int i = 0; i < kC; ++i) {
+      sm.Tb[i][j] = cv[i] * bj;
+      sm.Te[i][j] = cv[i] * ej;
+    }
+  } else {
+    // meanwhile: q' = q e^gamma, k' = k e^(gamma_last - gamma) (:303-311) and Aqk
+    for (int idx = tid - 64; idx < kC * kD / 4; idx += kThreads - 64) {
+      const int i = idx / (kD / 4), d4 = idx % (kD / 4);
+      const float eq = expf(sm.gam[i]), ek = expf(glast - sm.gam[i]);
+      float4 qv = *reinterpret_cast<const float4 *>(&sm.q[i][4 * d4]);
+      float4 kv = *reinterpret_cast<const float4 *>(&sm.k[i][4 * d4]);
+      qv = make_float4(qv.x * eq, qv.y * eq, qv.z * eq, qv.w * eq);
+      kv = make_float4(kv.x * ek, kv.y * ek, kv.z * ek, kv.w * ek);
+      reinterpret_cast<float4 *>(Qp)[idx] = qv;
+      reinterpret_cast<float4 *>(Kp)[idx] = kv;
+    }
+    for (int idx = tid - 64; idx < kC * kC / 4; idx += kThreads - 64) {
+      const int i = idx / (kC / 4), j4 = idx % (kC / 4);
+      reinterpret_cast<float4 *>(Aq)[idx] = *reinterpret_cast<const float4 *>(&sm.Aqk[i][4 * j4]);
+    }
+    if (tid == 64) Aq[kC * kC] = expf(glast);
+  }
+  __syncthreads();
+
+  // (5) U = T (v*beta), W = T (k*beta*e^gamma) (:292-293); thread (iq, dq)
+  // owns rows iq + 16 ri and float4 columns 4 dq + 64 rd.
   {
-    const int i = tid / 4, dq = tid % 4;
-    float u[32], w[32];
+    const int iq = tid / 16, dq = tid % 16;
+    float4 u[4][2], w[4][2];
 #pragma unroll
-    for (int m = 0; m < 32; ++m) u[m] = w[m] = 0.0f;
-    for (int j = 0; j <= i; ++j) {
-      const float tij = sm.A[i][j];
-      const float bj = sm.bet[j];
-      const float ej = bj * expf(sm.gam[j]);
+    for (int ri = 0; ri < 4; ++ri)
 #pragma unroll
-      for (int m = 0; m < 32; ++m) {
-        const int d = dq + 4 * m;
-        u[m] = fmaf(tij, sm.v[j][d] * bj, u[m]);
-        w[m] = fmaf(tij, sm.k[j][d] * ej, w[m]);
+      for (int rd = 0; rd < 2; ++rd) u[ri][rd] = w[ri][rd] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int jb = 0; jb < 4; ++jb) {
+      for (int jj = 0; jj < 16; ++jj) {
+        const int j = 16 * jb + jj;
+        float4 vv[2], kk[2];
+#pragma unroll
+        for (int rd = 0; rd < 2; ++rd) {
+          vv[rd] = *reinterpret_cast<const float4 *>(&sm.v[j][4 * dq + 64 * rd]);
+          kk[rd] = *reinterpret_cast<const float4 *>(&sm.k[j][4 * dq + 64 * rd]);
+        }
+#pragma unroll
+        for (int ri = jb; ri < 4; ++ri) {
+          const float tb = sm.Tb[iq + 16 * ri][j], te = sm.Te[iq + 16 * ri][j];
+#pragma unroll
+          for (int rd = 0; rd < 2; ++rd) {
+            u[ri][rd] = f4_fma(tb, vv[rd], u[ri][rd]);
+            w[ri][rd] = f4_fma(te, kk[rd], w[ri][rd]);
+          }
+        }
       }
     }
 #pragma unroll
-    for (int m = 0; m < 32; ++m) {
-      const int d = dq + 4 * m;
-      U[i * kD + d] = u[m];
-      W[i * kD + d] = w[m];
-    }
+    for (int ri = 0; ri < 4; ++ri)
+#pragma unroll
+      for (int rd = 0; rd < 2; ++rd) {
+        const size_t o = (size_t)(iq + 16 * ri) * kD + 4 * dq + 64 * rd;
+        *reinterpret_cast<float4 *>(U + o) = u[ri][rd];
+        *reinterpret_cast<float4 *>(W + o) = w[ri][rd];
+      }
   }
-  const float glast = sm.gam[kC - 1];
-  for (int idx = tid; idx < kC * kD; idx += kThreads) {
-    const int i = idx / kD, d = idx % kD;
-    Qp[idx] = sm.q[i][d] * expf(sm.gam[i]);
-    Kp[idx] = sm.k[i][d] * expf(glast - sm.gam[i]);
-  }
-  for (int idx = tid; idx < kC * kC; idx += kThreads) {
-    const int i = idx / kC, j = idx % kC;
-    Aq[idx] = j <= i ? sm.Aqk[i][j] : 0.0f;
-  }
-  if (tid == 0) Aq[kC * kC] = expf(glast);
 }
 
 struct StateSmem {
-  float W[kC][kLd];
+  float W[2][kC][kLd];  // double-buffered: chunk c+1 is fetched during chunk c
+  float U[2][kC][kCS];
   float Q[kC][kLd];
   float K[kC][kD];
   float Aq[kC][kC + 4];
-  float U[kC][kCS];
   float Vn[kC][kCS];
   float S[kD][kCS];
   float sq[2][kSplit][kC];
   float decay;
 };
+
+// Issue the cp.async copies of chunk c's W and U columns into buffer `buf`.
+__device__ __forceinline__ void fetch_wu(StateSmem &sm, const float *rec, int col0, int buf, int tid) {
+  const float *W = rec + kC * kD;
+  for (int idx = tid; idx < kC * kD / 4; idx += kThreads) {
+    const int r = idx / (kD / 4), q4 = idx % (kD / 4);
+    cp_async16(&sm.W[buf][r][4 * q4], W + (size_t)idx * 4);
+  }
+  for (int idx = tid; idx < kC * kCS / 4; idx += kThreads) {
+    const int r = idx / (kCS / 4), q4 = idx % (kCS / 4);
+    cp_async16(&sm.U[buf][r][4 * q4], rec + (size_t)r * kD + col0 + 4 * q4);
+  }
+}
 
 template <int KC>
 __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const PrefillParams p) {
@@ -231,46 +313,51 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
   const int tid = threadIdx.x;
   const int col0 = s * kCS;
   float *Sg = p.rec_state + ((size_t)b * p.Hv + h) * kD * kD;
+  const float *rec0 = p.ws + ((size_t)b * p.Hv + h) * p.NC * kRec;
 
   for (int idx = tid; idx < kD * kCS; idx += kThreads) {
     const int r = idx / kCS, cc = idx % kCS;
     sm.S[r][cc] = p.has_init ? Sg[(size_t)r * kD + col0 + cc] : 0.0f;
   }
+  fetch_wu(sm, rec0, col0, 0, tid);
+  cp_async_commit();
 
   const int i = tid / 4, cq = tid % 4;  // output row / float4 column group
   for (int c = 0; c < p.NC; ++c) {
-    const float *rec = p.ws + (((size_t)b * p.Hv + h) * p.NC + c) * kRec;
-    const float *U = rec, *W = rec + kC * kD, *Qp = rec + 2 * kC * kD, *Kp = rec + 3 * kC * kD;
-    const float *Aq = rec + 4 * kC * kD;
-    __syncthreads();  // previous chunk is done with every smem tile
+    const int buf = c & 1;
+    const float *rec = rec0 + (size_t)c * kRec;
+    const float *Qp = rec + 2 * kC * kD, *Kp = rec + 3 * kC * kD, *Aq = rec + 4 * kC * kD;
+    cp_async_wait<0>();  // W, U of chunk c
+    __syncthreads();     // ... visible to all; previous chunk done with Q, K, Aq, Vn
+    // group A: q', k', Aqk of chunk c (needed after v')
     for (int idx = tid; idx < kC * kD / 4; idx += kThreads) {
       const int r = idx / (kD / 4), q4 = idx % (kD / 4);
-      *reinterpret_cast<float4 *>(&sm.W[r][4 * q4]) = __ldcg(reinterpret_cast<const float4 *>(W) + idx);
-      *reinterpret_cast<float4 *>(&sm.Q[r][4 * q4]) = __ldcg(reinterpret_cast<const float4 *>(Qp) + idx);
-      *reinterpret_cast<float4 *>(&sm.K[r][4 * q4]) = __ldcg(reinterpret_cast<const float4 *>(Kp) + idx);
+      cp_async16(&sm.Q[r][4 * q4], Qp + (size_t)idx * 4);
+      cp_async16(&sm.K[r][4 * q4], Kp + (size_t)idx * 4);
     }
     for (int idx = tid; idx < kC * kC / 4; idx += kThreads) {
       const int r = idx / (kC / 4), q4 = idx % (kC / 4);
-      *reinterpret_cast<float4 *>(&sm.Aq[r][4 * q4]) = __ldcg(reinterpret_cast<const float4 *>(Aq) + idx);
+      cp_async16(&sm.Aq[r][4 * q4], Aq + (size_t)idx * 4);
     }
-    for (int idx = tid; idx < kC * kCS / 4; idx += kThreads) {
-      const int r = idx / (kCS / 4), q4 = idx % (kCS / 4);
-      *reinterpret_cast<float4 *>(&sm.U[r][4 * q4]) =
-          __ldcg(reinterpret_cast<const float4 *>(U + (size_t)r * kD + col0) + q4);
-    }
+    cp_async_commit();
+    // group B: W, U of chunk c+1 into the other buffer
+    if (c + 1 < p.NC) fetch_wu(sm, rec + kRec, col0, buf ^ 1, tid);
+    cp_async_commit();
     if (tid == 0) sm.decay = __ldcg(Aq + kC * kC);
-    __syncthreads();
 
     // v' = U - W S  (:315-324)
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < kD; ++k) acc = f4_fma(sm.W[i][k], *reinterpret_cast<const float4 *>(&sm.S[k][4 * cq]), acc);
-    const float4 u = *reinterpret_cast<const float4 *>(&sm.U[i][4 * cq]);
-    *reinterpret_cast<float4 *>(&sm.Vn[i][4 * cq]) =
-        make_float4(u.x - acc.x, u.y - acc.y, u.z - acc.z, u.w - acc.w);
+#pragma unroll 8
+    for (int k = 0; k < kD; ++k)
+      acc = f4_fma(sm.W[buf][i][k], *reinterpret_cast<const float4 *>(&sm.S[k][4 * cq]), acc);
+    const float4 u = *reinterpret_cast<const float4 *>(&sm.U[buf][i][4 * cq]);
+    *reinterpret_cast<float4 *>(&sm.Vn[i][4 * cq]) = make_float4(u.x - acc.x, u.y - acc.y, u.z - acc.z, u.w - acc.w);
+    cp_async_wait<1>();  // group A has landed (group B may still be in flight)
     __syncthreads();
 
     // o = q' S + Aqk v'  (:325-341)
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
     for (int k = 0; k < kD; ++k) o = f4_fma(sm.Q[i][k], *reinterpret_cast<const float4 *>(&sm.S[k][4 * cq]), o);
     float4 o2 = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j <= i; ++j) o2 = f4_fma(sm.Aq[i][j], *reinterpret_cast<const float4 *>(&sm.Vn[j][4 * cq]), o2);
@@ -281,13 +368,10 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
     float ss = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
     ss += __shfl_xor_sync(0xffffffffu, ss, 1);
     ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    if (cq < kSplit / 2) {
-      // lanes cq = 0..3 each push to two of the eight ranks
-      *cluster.map_shared_rank(&sm.sq[c & 1][s][i], 2 * cq) = ss;
-      *cluster.map_shared_rank(&sm.sq[c & 1][s][i], 2 * cq + 1) = ss;
-    }
+    *cluster.map_shared_rank(&sm.sq[c & 1][s][i], 2 * cq) = ss;
+    *cluster.map_shared_rank(&sm.sq[c & 1][s][i], 2 * cq + 1) = ss;
 
-    // S <- S * decay + k'^T v'  (:342-349); rows r and r + 64
+    // S <- S * decay + k'^T v'  (:342-349); rows i and i + 64
     float4 ns[2];
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -295,6 +379,7 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
       float4 a = *reinterpret_cast<const float4 *>(&sm.S[r][4 * cq]);
       a = make_float4(a.x * sm.decay, a.y * sm.decay, a.z * sm.decay, a.w * sm.decay);
       float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
       for (int t = 0; t < kC; ++t) kv = f4_fma(sm.K[t][r], *reinterpret_cast<const float4 *>(&sm.Vn[t][4 * cq]), kv);
       ns[hh] = make_float4(a.x + kv.x, a.y + kv.y, a.z + kv.z, a.w + kv.w);
     }
@@ -310,14 +395,17 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
       for (int j = 0; j < kSplit; ++j) tot += sm.sq[c & 1][j][i];
       const float inv = 1.0f / sqrtf(tot / (float)kD + p.eps);
       const size_t obase = ((size_t)b * p.T + t) * p.Hv * kD + (size_t)h * kD + col0 + 4 * cq;
-      const float ov[4] = {o.x, o.y, o.z, o.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int col = col0 + 4 * cq + e;
-        p.out[obase + e] = (p.norm_w[col] * (ov[e] * inv)) * siluf_dev(p.z[obase + e]);
-      }
+      const float4 zv = *reinterpret_cast<const float4 *>(p.z + obase);
+      const float4 wv = *reinterpret_cast<const float4 *>(p.norm_w + col0 + 4 * cq);
+      float4 r;
+      r.x = (wv.x * (o.x * inv)) * siluf_dev(zv.x);
+      r.y = (wv.y * (o.y * inv)) * siluf_dev(zv.y);
+      r.z = (wv.z * (o.z * inv)) * siluf_dev(zv.z);
+      r.w = (wv.w * (o.w * inv)) * siluf_dev(zv.w);
+      *reinterpret_cast<float4 *>(p.out + obase) = r;
     }
   }
+  cp_async_wait<0>();
   __syncthreads();
   for (int idx = tid; idx < kD * kCS; idx += kThreads) {
     const int r = idx / kCS, cc = idx % kCS;
