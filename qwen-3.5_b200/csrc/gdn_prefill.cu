@@ -17,9 +17,13 @@
 //  (2) gdn_prefill_state_kernel, grid (8, Hv, B) with 8-CTA clusters, walks
 //      the chunks in order; each CTA keeps 16 of the 128 value columns of the
 //      state in shared memory: v' = U - W S, o = q' S + Aqk v',
-//      S <- S e^(gamma_last) + k'^T v'.  The cluster exchanges per-token sums
-//      of squares through distributed shared memory for the gated RMS norm,
-//      and the kernel finally stores the state and the new conv state.
+//      S <- S e^(gamma_last) + k'^T v', as 4 x 4 register tiles over the
+//      transposed operands (W^T, q'^T, Aqk^T written by kernel 1) with the
+//      contraction split across thread groups.  The next chunk's W^T and U are
+//      prefetched with cp.async during the current one.  The cluster
+//      exchanges per-token sums of squares through distributed shared memory
+//      for the gated RMS norm, and the kernel finally stores the state and the
+//      new conv state.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -185,9 +189,10 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_chunk_kernel(const Prefi
   }
   __syncthreads();
 
+  // workspace record: U [64][128] | Wt [128][64] | Qt [128][64] | Kp [64][128] | AqT [64][64] | decay
   float *rec = p.ws + (((size_t)b * p.Hv + h) * p.NC + c) * kRec;
-  float *U = rec, *W = rec + kC * kD, *Qp = rec + 2 * kC * kD, *Kp = rec + 3 * kC * kD;
-  float *Aq = rec + 4 * kC * kD;
+  float *U = rec, *Wt = rec + kC * kD, *Qt = rec + 2 * kC * kD, *Kp = rec + 3 * kC * kD;
+  float *AqT = rec + 4 * kC * kD;
   const float glast = sm.gam[kC - 1];
 
   if (warp < 2) {
@@ -219,22 +224,27 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_chunk_kernel(const Prefi
       sm.Te[i][j] = cv[i] * ej;
     }
   } else {
-    // meanwhile: q' = q e^gamma, k' = k e^(gamma_last - gamma) (:303-311) and Aqk
+    // meanwhile: q' = q e^gamma (stored transposed, Qt[k][i]), k' = k e^(gamma_last - gamma)
+    // (:303-311) and Aqk (stored transposed, AqT[j][i])
     for (int idx = tid - 64; idx < kC * kD / 4; idx += kThreads - 64) {
+      const int kk = idx / (kC / 4), i4 = idx % (kC / 4);
+      float4 qv;
+      qv.x = sm.q[4 * i4 + 0][kk] * expf(sm.gam[4 * i4 + 0]);
+      qv.y = sm.q[4 * i4 + 1][kk] * expf(sm.gam[4 * i4 + 1]);
+      qv.z = sm.q[4 * i4 + 2][kk] * expf(sm.gam[4 * i4 + 2]);
+      qv.w = sm.q[4 * i4 + 3][kk] * expf(sm.gam[4 * i4 + 3]);
+      reinterpret_cast<float4 *>(Qt)[idx] = qv;
       const int i = idx / (kD / 4), d4 = idx % (kD / 4);
-      const float eq = expf(sm.gam[i]), ek = expf(glast - sm.gam[i]);
-      float4 qv = *reinterpret_cast<const float4 *>(&sm.q[i][4 * d4]);
+      const float ek = expf(glast - sm.gam[i]);
       float4 kv = *reinterpret_cast<const float4 *>(&sm.k[i][4 * d4]);
-      qv = make_float4(qv.x * eq, qv.y * eq, qv.z * eq, qv.w * eq);
-      kv = make_float4(kv.x * ek, kv.y * ek, kv.z * ek, kv.w * ek);
-      reinterpret_cast<float4 *>(Qp)[idx] = qv;
-      reinterpret_cast<float4 *>(Kp)[idx] = kv;
+      reinterpret_cast<float4 *>(Kp)[idx] = make_float4(kv.x * ek, kv.y * ek, kv.z * ek, kv.w * ek);
     }
     for (int idx = tid - 64; idx < kC * kC / 4; idx += kThreads - 64) {
-      const int i = idx / (kC / 4), j4 = idx % (kC / 4);
-      reinterpret_cast<float4 *>(Aq)[idx] = *reinterpret_cast<const float4 *>(&sm.Aqk[i][4 * j4]);
+      const int j = idx / (kC / 4), i4 = idx % (kC / 4);
+      reinterpret_cast<float4 *>(AqT)[idx] =
+          make_float4(sm.Aqk[4 * i4][j], sm.Aqk[4 * i4 + 1][j], sm.Aqk[4 * i4 + 2][j], sm.Aqk[4 * i4 + 3][j]);
     }
-    if (tid == 64) Aq[kC * kC] = expf(glast);
+    if (tid == 64) AqT[kC * kC] = expf(glast);
   }
   __syncthreads();
 
@@ -268,40 +278,60 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_chunk_kernel(const Prefi
         }
       }
     }
+    // W goes out transposed (Wt[k][i]) through shared memory (q is free now):
+    // staging rows of 65 floats keep the scattered writes at 2-way conflicts.
+    float *wt_s = &sm.q[0][0];
 #pragma unroll
     for (int ri = 0; ri < 4; ++ri)
 #pragma unroll
       for (int rd = 0; rd < 2; ++rd) {
-        const size_t o = (size_t)(iq + 16 * ri) * kD + 4 * dq + 64 * rd;
-        *reinterpret_cast<float4 *>(U + o) = u[ri][rd];
-        *reinterpret_cast<float4 *>(W + o) = w[ri][rd];
+        const int i = iq + 16 * ri, d0 = 4 * dq + 64 * rd;
+        *reinterpret_cast<float4 *>(U + (size_t)i * kD + d0) = u[ri][rd];
+        wt_s[(d0 + 0) * (kC + 1) + i] = w[ri][rd].x;
+        wt_s[(d0 + 1) * (kC + 1) + i] = w[ri][rd].y;
+        wt_s[(d0 + 2) * (kC + 1) + i] = w[ri][rd].z;
+        wt_s[(d0 + 3) * (kC + 1) + i] = w[ri][rd].w;
       }
+    __syncthreads();
+    for (int idx = tid; idx < kD * kC / 4; idx += kThreads) {
+      const int kk = idx / (kC / 4), i4 = idx % (kC / 4);
+      const float *src = wt_s + kk * (kC + 1) + 4 * i4;
+      reinterpret_cast<float4 *>(Wt)[idx] = make_float4(src[0], src[1], src[2], src[3]);
+    }
   }
 }
 
 struct StateSmem {
-  float W[2][kC][kLd];  // double-buffered: chunk c+1 is fetched during chunk c
+  float Wt[2][kD][kC];  // double-buffered: chunk c+1 is fetched during chunk c
   float U[2][kC][kCS];
-  float Q[kC][kLd];
-  float K[kC][kD];
-  float Aq[kC][kC + 4];
+  float Qt[kD][kC];
+  float Kp[kC][kD];
+  float AqT[kC][kC];
   float Vn[kC][kCS];
   float S[kD][kCS];
+  float Pv[4][kC][kCS];  // k-split partials of W S, then of q' S + Aqk v'
+  float Ps[2][kD][kCS];  // t-split partials of k'^T v'
   float sq[2][kSplit][kC];
   float decay;
 };
 
-// Issue the cp.async copies of chunk c's W and U columns into buffer `buf`.
+// Issue the cp.async copies of chunk c's Wt and U columns into buffer `buf`.
 __device__ __forceinline__ void fetch_wu(StateSmem &sm, const float *rec, int col0, int buf, int tid) {
-  const float *W = rec + kC * kD;
-  for (int idx = tid; idx < kC * kD / 4; idx += kThreads) {
-    const int r = idx / (kD / 4), q4 = idx % (kD / 4);
-    cp_async16(&sm.W[buf][r][4 * q4], W + (size_t)idx * 4);
-  }
+  const float4 *Wt = reinterpret_cast<const float4 *>(rec + kC * kD);
+  float4 *dst = reinterpret_cast<float4 *>(&sm.Wt[buf][0][0]);
+  for (int idx = tid; idx < kD * kC / 4; idx += kThreads) cp_async16(dst + idx, Wt + idx);
   for (int idx = tid; idx < kC * kCS / 4; idx += kThreads) {
     const int r = idx / (kCS / 4), q4 = idx % (kCS / 4);
     cp_async16(&sm.U[buf][r][4 * q4], rec + (size_t)r * kD + col0 + 4 * q4);
   }
+}
+
+// acc[r] += a[r] * s for a 4 x 4 register tile (rows in a, columns in s).
+__device__ __forceinline__ void tile4(float4 (&acc)[4], float4 a, float4 s) {
+  acc[0] = f4_fma(a.x, s, acc[0]);
+  acc[1] = f4_fma(a.y, s, acc[1]);
+  acc[2] = f4_fma(a.z, s, acc[2]);
+  acc[3] = f4_fma(a.w, s, acc[3]);
 }
 
 template <int KC>
@@ -322,77 +352,120 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
   fetch_wu(sm, rec0, col0, 0, tid);
   cp_async_commit();
 
-  const int i = tid / 4, cq = tid % 4;  // output row / float4 column group
+  // thread roles: (kq, iq, cq) for the 64 x 16 products with a 4-way split of
+  // the contraction; (h2, rq, cq) for the 128 x 16 state update (2-way split)
+  const int kq = tid >> 6, iq = (tid & 63) >> 2, cq = tid & 3;
+  const int h2 = tid >> 7, rq = (tid & 127) >> 2;
+  const int ri = tid >> 2;  // row of the reductions (64 rows x 4 column quads)
   for (int c = 0; c < p.NC; ++c) {
     const int buf = c & 1;
     const float *rec = rec0 + (size_t)c * kRec;
-    const float *Qp = rec + 2 * kC * kD, *Kp = rec + 3 * kC * kD, *Aq = rec + 4 * kC * kD;
-    cp_async_wait<0>();  // W, U of chunk c
-    __syncthreads();     // ... visible to all; previous chunk done with Q, K, Aq, Vn
-    // group A: q', k', Aqk of chunk c (needed after v')
-    for (int idx = tid; idx < kC * kD / 4; idx += kThreads) {
-      const int r = idx / (kD / 4), q4 = idx % (kD / 4);
-      cp_async16(&sm.Q[r][4 * q4], Qp + (size_t)idx * 4);
-      cp_async16(&sm.K[r][4 * q4], Kp + (size_t)idx * 4);
+    cp_async_wait<0>();  // Wt, U of chunk c
+    __syncthreads();     // ... visible to all; previous chunk done with every tile
+    {  // group A: q'^T, k', Aqk^T of chunk c (needed after v')
+      const float4 *Qt = reinterpret_cast<const float4 *>(rec + 2 * kC * kD);
+      const float4 *Kp = reinterpret_cast<const float4 *>(rec + 3 * kC * kD);
+      const float4 *AqT = reinterpret_cast<const float4 *>(rec + 4 * kC * kD);
+      for (int idx = tid; idx < kC * kD / 4; idx += kThreads) {
+        cp_async16(reinterpret_cast<float4 *>(&sm.Qt[0][0]) + idx, Qt + idx);
+        cp_async16(reinterpret_cast<float4 *>(&sm.Kp[0][0]) + idx, Kp + idx);
+      }
+      for (int idx = tid; idx < kC * kC / 4; idx += kThreads)
+        cp_async16(reinterpret_cast<float4 *>(&sm.AqT[0][0]) + idx, AqT + idx);
+      cp_async_commit();
     }
-    for (int idx = tid; idx < kC * kC / 4; idx += kThreads) {
-      const int r = idx / (kC / 4), q4 = idx % (kC / 4);
-      cp_async16(&sm.Aq[r][4 * q4], Aq + (size_t)idx * 4);
-    }
-    cp_async_commit();
-    // group B: W, U of chunk c+1 into the other buffer
+    // group B: Wt, U of chunk c+1 into the other buffer
     if (c + 1 < p.NC) fetch_wu(sm, rec + kRec, col0, buf ^ 1, tid);
     cp_async_commit();
-    if (tid == 0) sm.decay = __ldcg(Aq + kC * kC);
+    if (tid == 0) sm.decay = __ldcg(rec + 4 * kC * kD + kC * kC);
 
-    // v' = U - W S  (:315-324)
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    // v' = U - W S  (:315-324), contraction k split 4 ways
+    {
+      float4 acc[4] = {};
 #pragma unroll 8
-    for (int k = 0; k < kD; ++k)
-      acc = f4_fma(sm.W[buf][i][k], *reinterpret_cast<const float4 *>(&sm.S[k][4 * cq]), acc);
-    const float4 u = *reinterpret_cast<const float4 *>(&sm.U[buf][i][4 * cq]);
-    *reinterpret_cast<float4 *>(&sm.Vn[i][4 * cq]) = make_float4(u.x - acc.x, u.y - acc.y, u.z - acc.z, u.w - acc.w);
+      for (int kk = 0; kk < kD / 4; ++kk) {
+        const int k = (kD / 4) * kq + kk;
+        tile4(acc, *reinterpret_cast<const float4 *>(&sm.Wt[buf][k][4 * iq]),
+              *reinterpret_cast<const float4 *>(&sm.S[k][4 * cq]));
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) *reinterpret_cast<float4 *>(&sm.Pv[kq][4 * iq + r][4 * cq]) = acc[r];
+    }
+    __syncthreads();
+    {
+      float4 v = *reinterpret_cast<const float4 *>(&sm.U[buf][ri][4 * cq]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 pv = *reinterpret_cast<const float4 *>(&sm.Pv[q][ri][4 * cq]);
+        v = make_float4(v.x - pv.x, v.y - pv.y, v.z - pv.z, v.w - pv.w);
+      }
+      *reinterpret_cast<float4 *>(&sm.Vn[ri][4 * cq]) = v;
+    }
     cp_async_wait<1>();  // group A has landed (group B may still be in flight)
     __syncthreads();
 
-    // o = q' S + Aqk v'  (:325-341)
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    // o = q' S + Aqk v'  (:325-341) and k'^T v'  (:342-349)
+    {
+      float4 acc[4] = {};
 #pragma unroll 8
-    for (int k = 0; k < kD; ++k) o = f4_fma(sm.Q[i][k], *reinterpret_cast<const float4 *>(&sm.S[k][4 * cq]), o);
-    float4 o2 = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j <= i; ++j) o2 = f4_fma(sm.Aq[i][j], *reinterpret_cast<const float4 *>(&sm.Vn[j][4 * cq]), o2);
-    o = make_float4(o.x + o2.x, o.y + o2.y, o.z + o2.z, o.w + o2.w);
+      for (int kk = 0; kk < kD / 4; ++kk) {
+        const int k = (kD / 4) * kq + kk;
+        tile4(acc, *reinterpret_cast<const float4 *>(&sm.Qt[k][4 * iq]),
+              *reinterpret_cast<const float4 *>(&sm.S[k][4 * cq]));
+      }
+#pragma unroll 8
+      for (int jj = 0; jj < kC / 4; ++jj) {
+        const int j = (kC / 4) * kq + jj;
+        tile4(acc, *reinterpret_cast<const float4 *>(&sm.AqT[j][4 * iq]),
+              *reinterpret_cast<const float4 *>(&sm.Vn[j][4 * cq]));
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) *reinterpret_cast<float4 *>(&sm.Pv[kq][4 * iq + r][4 * cq]) = acc[r];
+      float4 acs[4] = {};
+#pragma unroll 8
+      for (int tt = 0; tt < kC / 2; ++tt) {
+        const int t = (kC / 2) * h2 + tt;
+        tile4(acs, *reinterpret_cast<const float4 *>(&sm.Kp[t][4 * rq]),
+              *reinterpret_cast<const float4 *>(&sm.Vn[t][4 * cq]));
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) *reinterpret_cast<float4 *>(&sm.Ps[h2][4 * rq + r][4 * cq]) = acs[r];
+    }
+    __syncthreads();
+
+    // S <- S * decay + k'^T v'
+    const float dec = sm.decay;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int idx = tid + kThreads * e, r = idx >> 2, q4 = idx & 3;
+      float4 a = *reinterpret_cast<const float4 *>(&sm.S[r][4 * q4]);
+      const float4 p0 = *reinterpret_cast<const float4 *>(&sm.Ps[0][r][4 * q4]);
+      const float4 p1 = *reinterpret_cast<const float4 *>(&sm.Ps[1][r][4 * q4]);
+      a = make_float4(a.x * dec + (p0.x + p1.x), a.y * dec + (p0.y + p1.y), a.z * dec + (p0.z + p1.z),
+                      a.w * dec + (p0.w + p1.w));
+      *reinterpret_cast<float4 *>(&sm.S[r][4 * q4]) = a;
+    }
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 pv = *reinterpret_cast<const float4 *>(&sm.Pv[q][ri][4 * cq]);
+      o = make_float4(o.x + pv.x, o.y + pv.y, o.z + pv.z, o.w + pv.w);
+    }
 
     // per-token partial sum of squares over this CTA's 16 columns -> every
     // CTA of the cluster (double-buffered by chunk parity)
     float ss = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
     ss += __shfl_xor_sync(0xffffffffu, ss, 1);
     ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    *cluster.map_shared_rank(&sm.sq[c & 1][s][i], 2 * cq) = ss;
-    *cluster.map_shared_rank(&sm.sq[c & 1][s][i], 2 * cq + 1) = ss;
-
-    // S <- S * decay + k'^T v'  (:342-349); rows i and i + 64
-    float4 ns[2];
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int r = i + 64 * hh;
-      float4 a = *reinterpret_cast<const float4 *>(&sm.S[r][4 * cq]);
-      a = make_float4(a.x * sm.decay, a.y * sm.decay, a.z * sm.decay, a.w * sm.decay);
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-      for (int t = 0; t < kC; ++t) kv = f4_fma(sm.K[t][r], *reinterpret_cast<const float4 *>(&sm.Vn[t][4 * cq]), kv);
-      ns[hh] = make_float4(a.x + kv.x, a.y + kv.y, a.z + kv.z, a.w + kv.w);
-    }
-    __syncthreads();  // every thread finished reading S for this chunk
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) *reinterpret_cast<float4 *>(&sm.S[i + 64 * hh][4 * cq]) = ns[hh];
+    *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq) = ss;
+    *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq + 1) = ss;
 
     cluster.sync();  // all sums of squares of this chunk have arrived
-    const int t = c * kC + i;
+    const int t = c * kC + ri;
     if (t < p.T) {
       float tot = 0.0f;
 #pragma unroll
-      for (int j = 0; j < kSplit; ++j) tot += sm.sq[c & 1][j][i];
+      for (int j = 0; j < kSplit; ++j) tot += sm.sq[c & 1][j][ri];
       const float inv = 1.0f / sqrtf(tot / (float)kD + p.eps);
       const size_t obase = ((size_t)b * p.T + t) * p.Hv * kD + (size_t)h * kD + col0 + 4 * cq;
       const float4 zv = *reinterpret_cast<const float4 *>(p.z + obase);
