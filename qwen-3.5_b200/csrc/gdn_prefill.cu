@@ -306,25 +306,15 @@ struct StateSmem {
   float U[2][kC][kCS];
   float Qt[kD][kC];
   float Kp[kC][kD];
-  float AqT[kC][kC];
+  float AqT[kC * kC + 4];  // Aqk^T followed by the chunk decay
+  float Z[kC][kCS];        // gate z of this CTA's 16 columns
   float Vn[kC][kCS];
   float S[kD][kCS];
   float Pv[4][kC][kCS];  // k-split partials of W S, then of q' S + Aqk v'
   float Ps[2][kD][kCS];  // t-split partials of k'^T v'
   float sq[2][kSplit][kC];
-  float decay;
+  uint64_t barW[2], barA;
 };
-
-// Issue the cp.async copies of chunk c's Wt and U columns into buffer `buf`.
-__device__ __forceinline__ void fetch_wu(StateSmem &sm, const float *rec, int col0, int buf, int tid) {
-  const float4 *Wt = reinterpret_cast<const float4 *>(rec + kC * kD);
-  float4 *dst = reinterpret_cast<float4 *>(&sm.Wt[buf][0][0]);
-  for (int idx = tid; idx < kD * kC / 4; idx += kThreads) cp_async16(dst + idx, Wt + idx);
-  for (int idx = tid; idx < kC * kCS / 4; idx += kThreads) {
-    const int r = idx / (kCS / 4), q4 = idx % (kCS / 4);
-    cp_async16(&sm.U[buf][r][4 * q4], rec + (size_t)r * kD + col0 + 4 * q4);
-  }
-}
 
 // acc[r] += a[r] * s for a 4 x 4 register tile (rows in a, columns in s).
 __device__ __forceinline__ void tile4(float4 (&acc)[4], float4 a, float4 s) {
@@ -334,9 +324,24 @@ __device__ __forceinline__ void tile4(float4 (&acc)[4], float4 a, float4 s) {
   acc[3] = f4_fma(a.w, s, acc[3]);
 }
 
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Bulk copies of chunk c's W^T and U columns into buffer `buf` (one thread).
+__device__ __forceinline__ void fetch_wu(StateSmem &sm, const float *rec, int col0, int buf, uint64_t pol) {
+  mbar_arrive_expect_tx(&sm.barW[buf], sizeof(sm.Wt[0]) + sizeof(sm.U[0]));
+  bulk_g2s(&sm.Wt[buf][0][0], rec + kC * kD, sizeof(sm.Wt[0]), &sm.barW[buf], pol);
+  for (int r = 0; r < kC; ++r)
+    bulk_g2s(&sm.U[buf][r][0], rec + (size_t)r * kD + col0, kCS * sizeof(float), &sm.barW[buf], pol);
+}
+
 template <int KC>
 __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const PrefillParams p) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   StateSmem &sm = *reinterpret_cast<StateSmem *>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
   const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -344,40 +349,51 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
   const int col0 = s * kCS;
   float *Sg = p.rec_state + ((size_t)b * p.Hv + h) * kD * kD;
   const float *rec0 = p.ws + ((size_t)b * p.Hv + h) * p.NC * kRec;
+  const float *zrow0 = p.z + (size_t)b * p.T * p.Hv * kD + (size_t)h * kD + col0;  // token 0
+  const size_t zstride = (size_t)p.Hv * kD;
+  uint64_t pol = 0;
 
   for (int idx = tid; idx < kD * kCS; idx += kThreads) {
     const int r = idx / kCS, cc = idx % kCS;
     sm.S[r][cc] = p.has_init ? Sg[(size_t)r * kD + col0 + cc] : 0.0f;
   }
-  fetch_wu(sm, rec0, col0, 0, tid);
-  cp_async_commit();
+  if (tid == 0) {
+    mbar_init(&sm.barW[0], 1);
+    mbar_init(&sm.barW[1], 1);
+    mbar_init(&sm.barA, 1);
+    fence_mbar_init();
+    pol = l2_policy_evict_first();
+    fetch_wu(sm, rec0, col0, 0, pol);
+  }
+  __syncthreads();
 
   // thread roles: (kq, iq, cq) for the 64 x 16 products with a 4-way split of
   // the contraction; (h2, rq, cq) for the 128 x 16 state update (2-way split)
   const int kq = tid >> 6, iq = (tid & 63) >> 2, cq = tid & 3;
   const int h2 = tid >> 7, rq = (tid & 127) >> 2;
   const int ri = tid >> 2;  // row of the reductions (64 rows x 4 column quads)
+  // A wait that gives up (ok = false) stops this thread waiting and issuing
+  // copies, but every barrier below is still executed, so no CTA of the
+  // cluster is left behind at a cluster barrier; the output is then poisoned.
+  bool ok = true;
   for (int c = 0; c < p.NC; ++c) {
     const int buf = c & 1;
     const float *rec = rec0 + (size_t)c * kRec;
-    cp_async_wait<0>();  // Wt, U of chunk c
-    __syncthreads();     // ... visible to all; previous chunk done with every tile
-    {  // group A: q'^T, k', Aqk^T of chunk c (needed after v')
-      const float4 *Qt = reinterpret_cast<const float4 *>(rec + 2 * kC * kD);
-      const float4 *Kp = reinterpret_cast<const float4 *>(rec + 3 * kC * kD);
-      const float4 *AqT = reinterpret_cast<const float4 *>(rec + 4 * kC * kD);
-      for (int idx = tid; idx < kC * kD / 4; idx += kThreads) {
-        cp_async16(reinterpret_cast<float4 *>(&sm.Qt[0][0]) + idx, Qt + idx);
-        cp_async16(reinterpret_cast<float4 *>(&sm.Kp[0][0]) + idx, Kp + idx);
-      }
-      for (int idx = tid; idx < kC * kC / 4; idx += kThreads)
-        cp_async16(reinterpret_cast<float4 *>(&sm.AqT[0][0]) + idx, AqT + idx);
-      cp_async_commit();
+    if (ok && !mbar_wait(&sm.barW[buf], (c >> 1) & 1)) ok = false;  // Wt, U of chunk c
+    __syncthreads();  // previous chunk done with every tile (Qt, Kp, AqT, Z, Wt[buf ^ 1])
+    if (tid == 0 && ok) {
+      // q'^T, k', Aqk^T + decay and z of chunk c (needed after v'), then the
+      // next chunk's W^T and U into the other buffer
+      const int ntok = min(kC, p.T - c * kC);
+      mbar_arrive_expect_tx(&sm.barA, sizeof(sm.Qt) + sizeof(sm.Kp) + sizeof(sm.AqT) +
+                                          (uint32_t)ntok * kCS * sizeof(float));
+      bulk_g2s(&sm.Qt[0][0], rec + 2 * kC * kD, sizeof(sm.Qt), &sm.barA, pol);
+      bulk_g2s(&sm.Kp[0][0], rec + 3 * kC * kD, sizeof(sm.Kp), &sm.barA, pol);
+      bulk_g2s(&sm.AqT[0], rec + 4 * kC * kD, sizeof(sm.AqT), &sm.barA, pol);
+      for (int r = 0; r < ntok; ++r)
+        bulk_g2s(&sm.Z[r][0], zrow0 + (size_t)(c * kC + r) * zstride, kCS * sizeof(float), &sm.barA, pol);
+      if (c + 1 < p.NC) fetch_wu(sm, rec + kRec, col0, buf ^ 1, pol);
     }
-    // group B: Wt, U of chunk c+1 into the other buffer
-    if (c + 1 < p.NC) fetch_wu(sm, rec + kRec, col0, buf ^ 1, tid);
-    cp_async_commit();
-    if (tid == 0) sm.decay = __ldcg(rec + 4 * kC * kD + kC * kC);
 
     // v' = U - W S  (:315-324), contraction k split 4 ways
     {
@@ -401,7 +417,7 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
       }
       *reinterpret_cast<float4 *>(&sm.Vn[ri][4 * cq]) = v;
     }
-    cp_async_wait<1>();  // group A has landed (group B may still be in flight)
+    if (ok && !mbar_wait(&sm.barA, c & 1)) ok = false;  // q'^T, k', Aqk^T, z of chunk c
     __syncthreads();
 
     // o = q' S + Aqk v'  (:325-341) and k'^T v'  (:342-349)
@@ -416,7 +432,7 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
 #pragma unroll 8
       for (int jj = 0; jj < kC / 4; ++jj) {
         const int j = (kC / 4) * kq + jj;
-        tile4(acc, *reinterpret_cast<const float4 *>(&sm.AqT[j][4 * iq]),
+        tile4(acc, *reinterpret_cast<const float4 *>(&sm.AqT[j * kC + 4 * iq]),
               *reinterpret_cast<const float4 *>(&sm.Vn[j][4 * cq]));
       }
 #pragma unroll
@@ -433,8 +449,24 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
     }
     __syncthreads();
 
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 pv = *reinterpret_cast<const float4 *>(&sm.Pv[q][ri][4 * cq]);
+      o = make_float4(o.x + pv.x, o.y + pv.y, o.z + pv.z, o.w + pv.w);
+    }
+    // per-token partial sum of squares over this CTA's 16 columns -> every
+    // CTA of the cluster (double-buffered by chunk parity); the cluster
+    // barrier is split so the state update runs while it completes
+    float ss = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq) = ss;
+    *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq + 1) = ss;
+    cluster_arrive_release();
+
     // S <- S * decay + k'^T v'
-    const float dec = sm.decay;
+    const float dec = sm.AqT[kC * kC];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int idx = tid + kThreads * e, r = idx >> 2, q4 = idx & 3;
@@ -445,22 +477,8 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
                       a.w * dec + (p0.w + p1.w));
       *reinterpret_cast<float4 *>(&sm.S[r][4 * q4]) = a;
     }
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float4 pv = *reinterpret_cast<const float4 *>(&sm.Pv[q][ri][4 * cq]);
-      o = make_float4(o.x + pv.x, o.y + pv.y, o.z + pv.z, o.w + pv.w);
-    }
 
-    // per-token partial sum of squares over this CTA's 16 columns -> every
-    // CTA of the cluster (double-buffered by chunk parity)
-    float ss = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq) = ss;
-    *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq + 1) = ss;
-
-    cluster.sync();  // all sums of squares of this chunk have arrived
+    cluster_wait_acquire();  // all sums of squares of this chunk have arrived
     const int t = c * kC + ri;
     if (t < p.T) {
       float tot = 0.0f;
@@ -468,7 +486,7 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
       for (int j = 0; j < kSplit; ++j) tot += sm.sq[c & 1][j][ri];
       const float inv = 1.0f / sqrtf(tot / (float)kD + p.eps);
       const size_t obase = ((size_t)b * p.T + t) * p.Hv * kD + (size_t)h * kD + col0 + 4 * cq;
-      const float4 zv = *reinterpret_cast<const float4 *>(p.z + obase);
+      const float4 zv = *reinterpret_cast<const float4 *>(&sm.Z[ri][4 * cq]);
       const float4 wv = *reinterpret_cast<const float4 *>(p.norm_w + col0 + 4 * cq);
       float4 r;
       r.x = (wv.x * (o.x * inv)) * siluf_dev(zv.x);
@@ -478,7 +496,7 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
       *reinterpret_cast<float4 *>(p.out + obase) = r;
     }
   }
-  cp_async_wait<0>();
+  if (!ok) p.out[0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison the output
   __syncthreads();
   for (int idx = tid; idx < kD * kCS; idx += kThreads) {
     const int r = idx / kCS, cc = idx % kCS;
