@@ -40,6 +40,7 @@ constexpr int kLd = kD + kPad;
 constexpr int kCS = 16;     // value columns per CTA in the state kernel
 constexpr int kSplit = kD / kCS;
 constexpr int kThreads = 256;
+constexpr int kStateThreads = 512;  // state pass: 16 warps hide the shared-memory latency
 // workspace record per (b, h, chunk): U, W, q', k' [64x128] + Aqk [64x64] + decay
 constexpr size_t kRec = 4 * (size_t)kC * kD + (size_t)kC * kC + 16;
 
@@ -63,7 +64,7 @@ struct ChunkSmem {
 
 template <int KC>
 __global__ void __launch_bounds__(kThreads) gdn_prefill_chunk_kernel(const PrefillParams p) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   ChunkSmem &sm = *reinterpret_cast<ChunkSmem *>(smem_raw);
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / p.rf;
@@ -310,8 +311,8 @@ struct StateSmem {
   float Z[kC][kCS];        // gate z of this CTA's 16 columns
   float Vn[kC][kCS];
   float S[kD][kCS];
-  float Pv[4][kC][kCS];  // k-split partials of W S, then of q' S + Aqk v'
-  float Ps[2][kD][kCS];  // t-split partials of k'^T v'
+  float Pv[8][kC][kCS];  // k-split partials of W S, then of q' S + Aqk v'
+                         // (the t-split partials of k'^T v' reuse Wt[buf] once W S is done)
   float sq[2][kSplit][kC];
   uint64_t barW[2], barA;
 };
@@ -331,16 +332,22 @@ __device__ __forceinline__ void cluster_wait_acquire() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Bulk copies of chunk c's W^T and U columns into buffer `buf` (one thread).
-__device__ __forceinline__ void fetch_wu(StateSmem &sm, const float *rec, int col0, int buf, uint64_t pol) {
-  mbar_arrive_expect_tx(&sm.barW[buf], sizeof(sm.Wt[0]) + sizeof(sm.U[0]));
-  bulk_g2s(&sm.Wt[buf][0][0], rec + kC * kD, sizeof(sm.Wt[0]), &sm.barW[buf], pol);
-  for (int r = 0; r < kC; ++r)
-    bulk_g2s(&sm.U[buf][r][0], rec + (size_t)r * kD + col0, kCS * sizeof(float), &sm.barW[buf], pol);
+// Chunk c's W^T (one bulk copy by thread 0) and U columns (one 16-byte
+// cp.async per thread: 64 rows x 4) into buffer `buf`.
+__device__ __forceinline__ void fetch_wu(StateSmem &sm, const float *rec, int col0, int buf, uint64_t pol,
+                                         int tid) {
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&sm.barW[buf], sizeof(sm.Wt[0]));
+    bulk_g2s(&sm.Wt[buf][0][0], rec + kC * kD, sizeof(sm.Wt[0]), &sm.barW[buf], pol);
+  }
+  if (tid < kC * kCS / 4) {
+    const int r = tid >> 2, q4 = tid & 3;
+    cp_async16(&sm.U[buf][r][4 * q4], rec + (size_t)r * kD + col0 + 4 * q4);
+  }
 }
 
 template <int KC>
-__global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const PrefillParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   StateSmem &sm = *reinterpret_cast<StateSmem *>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
@@ -353,7 +360,7 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
   const size_t zstride = (size_t)p.Hv * kD;
   uint64_t pol = 0;
 
-  for (int idx = tid; idx < kD * kCS; idx += kThreads) {
+  for (int idx = tid; idx < kD * kCS; idx += kStateThreads) {
     const int r = idx / kCS, cc = idx % kCS;
     sm.S[r][cc] = p.has_init ? Sg[(size_t)r * kD + col0 + cc] : 0.0f;
   }
@@ -363,15 +370,18 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
     mbar_init(&sm.barA, 1);
     fence_mbar_init();
     pol = l2_policy_evict_first();
-    fetch_wu(sm, rec0, col0, 0, pol);
   }
   __syncthreads();
+  fetch_wu(sm, rec0, col0, 0, pol, tid);
+  cp_async_commit();
 
-  // thread roles: (kq, iq, cq) for the 64 x 16 products with a 4-way split of
-  // the contraction; (h2, rq, cq) for the 128 x 16 state update (2-way split)
+  // thread roles: (kq, iq, cq) for the 64 x 16 products with an 8-way split of
+  // the contraction; (h4, rq, cq) for the 128 x 16 state update (4-way split);
+  // threads < 256 also own one (row, column quad) of the 64 x 16 reductions
   const int kq = tid >> 6, iq = (tid & 63) >> 2, cq = tid & 3;
-  const int h2 = tid >> 7, rq = (tid & 127) >> 2;
-  const int ri = tid >> 2;  // row of the reductions (64 rows x 4 column quads)
+  const int h4 = tid >> 7, rq = (tid & 127) >> 2;
+  const int ri = (tid & 255) >> 2;
+  const bool red = tid < kC * kCS / 4;
   // A wait that gives up (ok = false) stops this thread waiting and issuing
   // copies, but every barrier below is still executed, so no CTA of the
   // cluster is left behind at a cluster barrier; the output is then poisoned.
@@ -379,28 +389,31 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
   for (int c = 0; c < p.NC; ++c) {
     const int buf = c & 1;
     const float *rec = rec0 + (size_t)c * kRec;
-    if (ok && !mbar_wait(&sm.barW[buf], (c >> 1) & 1)) ok = false;  // Wt, U of chunk c
+    if (ok && !mbar_wait(&sm.barW[buf], (c >> 1) & 1)) ok = false;  // W^T of chunk c
+    cp_async_wait<0>();                                                 // U of chunk c
     __syncthreads();  // previous chunk done with every tile (Qt, Kp, AqT, Z, Wt[buf ^ 1])
     if (tid == 0 && ok) {
-      // q'^T, k', Aqk^T + decay and z of chunk c (needed after v'), then the
-      // next chunk's W^T and U into the other buffer
-      const int ntok = min(kC, p.T - c * kC);
-      mbar_arrive_expect_tx(&sm.barA, sizeof(sm.Qt) + sizeof(sm.Kp) + sizeof(sm.AqT) +
-                                          (uint32_t)ntok * kCS * sizeof(float));
+      // q'^T, k', Aqk^T + decay of chunk c (needed after v')
+      mbar_arrive_expect_tx(&sm.barA, sizeof(sm.Qt) + sizeof(sm.Kp) + sizeof(sm.AqT));
       bulk_g2s(&sm.Qt[0][0], rec + 2 * kC * kD, sizeof(sm.Qt), &sm.barA, pol);
       bulk_g2s(&sm.Kp[0][0], rec + 3 * kC * kD, sizeof(sm.Kp), &sm.barA, pol);
       bulk_g2s(&sm.AqT[0], rec + 4 * kC * kD, sizeof(sm.AqT), &sm.barA, pol);
-      for (int r = 0; r < ntok; ++r)
-        bulk_g2s(&sm.Z[r][0], zrow0 + (size_t)(c * kC + r) * zstride, kCS * sizeof(float), &sm.barA, pol);
-      if (c + 1 < p.NC) fetch_wu(sm, rec + kRec, col0, buf ^ 1, pol);
+    }
+    {  // z of chunk c (used by the output), then the next chunk's W^T and U
+      const int r = tid >> 2, q4 = tid & 3;
+      if (red && c * kC + r < p.T)
+        cp_async16(&sm.Z[r][4 * q4], zrow0 + (size_t)(c * kC + r) * zstride + 4 * q4);
+      cp_async_commit();
+      if (c + 1 < p.NC && ok) fetch_wu(sm, rec + kRec, col0, buf ^ 1, pol, tid);
+      cp_async_commit();
     }
 
-    // v' = U - W S  (:315-324), contraction k split 4 ways
+    // v' = U - W S  (:315-324), contraction k split 8 ways
     {
       float4 acc[4] = {};
 #pragma unroll 8
-      for (int kk = 0; kk < kD / 4; ++kk) {
-        const int k = (kD / 4) * kq + kk;
+      for (int kk = 0; kk < kD / 8; ++kk) {
+        const int k = (kD / 8) * kq + kk;
         tile4(acc, *reinterpret_cast<const float4 *>(&sm.Wt[buf][k][4 * iq]),
               *reinterpret_cast<const float4 *>(&sm.S[k][4 * cq]));
       }
@@ -408,10 +421,10 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
       for (int r = 0; r < 4; ++r) *reinterpret_cast<float4 *>(&sm.Pv[kq][4 * iq + r][4 * cq]) = acc[r];
     }
     __syncthreads();
-    {
+    if (red) {
       float4 v = *reinterpret_cast<const float4 *>(&sm.U[buf][ri][4 * cq]);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 8; ++q) {
         const float4 pv = *reinterpret_cast<const float4 *>(&sm.Pv[q][ri][4 * cq]);
         v = make_float4(v.x - pv.x, v.y - pv.y, v.z - pv.z, v.w - pv.w);
       }
@@ -421,17 +434,18 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
     __syncthreads();
 
     // o = q' S + Aqk v'  (:325-341) and k'^T v'  (:342-349)
+    float(*Ps)[kD][kCS] = reinterpret_cast<float(*)[kD][kCS]>(&sm.Wt[buf][0][0]);  // [4][128][16]
     {
       float4 acc[4] = {};
 #pragma unroll 8
-      for (int kk = 0; kk < kD / 4; ++kk) {
-        const int k = (kD / 4) * kq + kk;
+      for (int kk = 0; kk < kD / 8; ++kk) {
+        const int k = (kD / 8) * kq + kk;
         tile4(acc, *reinterpret_cast<const float4 *>(&sm.Qt[k][4 * iq]),
               *reinterpret_cast<const float4 *>(&sm.S[k][4 * cq]));
       }
 #pragma unroll 8
-      for (int jj = 0; jj < kC / 4; ++jj) {
-        const int j = (kC / 4) * kq + jj;
+      for (int jj = 0; jj < kC / 8; ++jj) {
+        const int j = (kC / 8) * kq + jj;
         tile4(acc, *reinterpret_cast<const float4 *>(&sm.AqT[j * kC + 4 * iq]),
               *reinterpret_cast<const float4 *>(&sm.Vn[j][4 * cq]));
       }
@@ -439,19 +453,19 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
       for (int r = 0; r < 4; ++r) *reinterpret_cast<float4 *>(&sm.Pv[kq][4 * iq + r][4 * cq]) = acc[r];
       float4 acs[4] = {};
 #pragma unroll 8
-      for (int tt = 0; tt < kC / 2; ++tt) {
-        const int t = (kC / 2) * h2 + tt;
+      for (int tt = 0; tt < kC / 4; ++tt) {
+        const int t = (kC / 4) * h4 + tt;
         tile4(acs, *reinterpret_cast<const float4 *>(&sm.Kp[t][4 * rq]),
               *reinterpret_cast<const float4 *>(&sm.Vn[t][4 * cq]));
       }
 #pragma unroll
-      for (int r = 0; r < 4; ++r) *reinterpret_cast<float4 *>(&sm.Ps[h2][4 * rq + r][4 * cq]) = acs[r];
+      for (int r = 0; r < 4; ++r) *reinterpret_cast<float4 *>(&Ps[h4][4 * rq + r][4 * cq]) = acs[r];
     }
     __syncthreads();
 
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < 8; ++q) {
       const float4 pv = *reinterpret_cast<const float4 *>(&sm.Pv[q][ri][4 * cq]);
       o = make_float4(o.x + pv.x, o.y + pv.y, o.z + pv.z, o.w + pv.w);
     }
@@ -461,26 +475,32 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
     float ss = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
     ss += __shfl_xor_sync(0xffffffffu, ss, 1);
     ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq) = ss;
-    *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq + 1) = ss;
+    if (red) {
+      *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq) = ss;
+      *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq + 1) = ss;
+    }
     cluster_arrive_release();
 
-    // S <- S * decay + k'^T v'
-    const float dec = sm.AqT[kC * kC];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int idx = tid + kThreads * e, r = idx >> 2, q4 = idx & 3;
+    // S <- S * decay + k'^T v'  (one float4 of the 128 x 16 state per thread)
+    {
+      const float dec = sm.AqT[kC * kC];
+      const int r = tid >> 2, q4 = tid & 3;
       float4 a = *reinterpret_cast<const float4 *>(&sm.S[r][4 * q4]);
-      const float4 p0 = *reinterpret_cast<const float4 *>(&sm.Ps[0][r][4 * q4]);
-      const float4 p1 = *reinterpret_cast<const float4 *>(&sm.Ps[1][r][4 * q4]);
-      a = make_float4(a.x * dec + (p0.x + p1.x), a.y * dec + (p0.y + p1.y), a.z * dec + (p0.z + p1.z),
-                      a.w * dec + (p0.w + p1.w));
+      float4 ps = *reinterpret_cast<const float4 *>(&Ps[0][r][4 * q4]);
+#pragma unroll
+      for (int q = 1; q < 4; ++q) {
+        const float4 pq = *reinterpret_cast<const float4 *>(&Ps[q][r][4 * q4]);
+        ps = make_float4(ps.x + pq.x, ps.y + pq.y, ps.z + pq.z, ps.w + pq.w);
+      }
+      a = make_float4(a.x * dec + ps.x, a.y * dec + ps.y, a.z * dec + ps.z, a.w * dec + ps.w);
       *reinterpret_cast<float4 *>(&sm.S[r][4 * q4]) = a;
+      fence_proxy_async_smem();  // Ps (in Wt[buf]) is refilled by a bulk copy next chunk
     }
 
+    cp_async_wait<1>();      // z of this chunk (the next chunk's U may still be in flight)
     cluster_wait_acquire();  // all sums of squares of this chunk have arrived
     const int t = c * kC + ri;
-    if (t < p.T) {
+    if (red && t < p.T) {
       float tot = 0.0f;
 #pragma unroll
       for (int j = 0; j < kSplit; ++j) tot += sm.sq[c & 1][j][ri];
@@ -497,8 +517,9 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_state_kernel(const Prefi
     }
   }
   if (!ok) p.out[0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison the output
+  cp_async_wait<0>();
   __syncthreads();
-  for (int idx = tid; idx < kD * kCS; idx += kThreads) {
+  for (int idx = tid; idx < kD * kCS; idx += kStateThreads) {
     const int r = idx / kCS, cc = idx % kCS;
     Sg[(size_t)r * kD + col0 + cc] = sm.S[r][cc];
   }
@@ -540,7 +561,7 @@ int launch_kc(const PrefillParams &p, cudaStream_t st) {
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kSplit, p.Hv, p.B);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(kStateThreads, 1, 1);
   cfg.dynamicSmemBytes = s2;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
