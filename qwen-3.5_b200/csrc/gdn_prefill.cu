@@ -13,7 +13,9 @@
 //      A = -tril((k*beta) k^T o D, -1) and Aqk = (q k^T) o D, the 63-row
 //      forward substitution (text_modules.rs:280-287), T = A + I,
 //      U = T (v*beta), W = T (k*beta*e^gamma), q' = q e^gamma,
-//      k' = k e^(gamma_last - gamma).  Results go to the workspace.
+//      k' = k e^(gamma_last - gamma).  The four contractions run on the
+//      tcgen05 tensor cores (3xTF32, TMEM accumulators).  Results go to the
+//      workspace.
 //  (2) gdn_prefill_state_kernel, grid (8, Hv, B) with 8-CTA clusters, walks
 //      the chunks in order; each CTA keeps 16 of the 128 value columns of the
 //      state in shared memory: v' = U - W S, o = q' S + Aqk v',
@@ -27,6 +29,7 @@
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "umma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -51,63 +54,105 @@ struct PrefillParams {
   float eps;
 };
 
+// ---------------------------------------------------------------------------
+// Kernel 1 on the 5th-generation tensor cores.  The four intra-chunk
+// contractions run as tcgen05 kind::tf32 MMAs with f32 accumulators in TMEM,
+// as 3xTF32 (hi*hi + hi*lo + lo*hi; the f32 buffer is the hi term because the
+// tensor core reads f32 as truncated tf32) so the result keeps f32 accuracy:
+//   G12 : D[128 x 64] = [k ; q] k^T           (rows 0-63: k k^T, 64-127: q k^T)
+//   GU  : D[128 x 64] = v^T (T diag(beta))^T   = U^T
+//   GW  : D[128 x 64] = k^T (T diag(beta e^g))^T = W^T
+// All operands are K-major in the 8x4-blocked layout of umma.cuh.  Every
+// shared-memory pass maps one warp onto one 8x4 core matrix (lane = row*4 +
+// column), which keeps the blocked layout free of bank conflicts.
 struct ChunkSmem {
-  float q[kC][kLd];
-  float k[kC][kLd];
-  float v[kC][kLd];
-  float A[kC][kC + 4];    // -tril((k*beta) k^T o D, -1), then T = (I - A)^-1
-  float Aqk[kC][kC + 4];  // tril((q k^T) o D)
-  float Tb[kC][kC + 4];   // T[i][j] * beta_j
-  float Te[kC][kC + 4];   // T[i][j] * beta_j * e^gamma_j
-  float gam[kC], bet[kC];
+  float r1[4][kC * kD];  // k | q | k_lo | q_lo  (blocked [64 x 128]); after G12:
+                         // Tb+Tb_lo | kT | Te+Te_lo | kT_lo  (kT blocked [128 x 64])
+  float vT[kD * kC];     // v^T blocked [128 x 64]
+  float vT_lo[kD * kC];
+  float Am[kC][kC + 4];  // A = -tril(diag(beta) k k^T o D, -1), then T = (I - A)^-1
+  float gam[kC], bet[kC], eg[kC], ek[kC];
+  float stage[kThreads / 32][8][36];  // per-warp conv staging tile (rows padded to 36: conflict-free both ways)
+  uint32_t tbase;
+  uint64_t bar1, bar2;
 };
 
 template <int KC>
-__global__ void __launch_bounds__(kThreads) gdn_prefill_chunk_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const PrefillParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   ChunkSmem &sm = *reinterpret_cast<ChunkSmem *>(smem_raw);
+  float *kS = sm.r1[0], *qS = sm.r1[1], *kL = sm.r1[2], *qL = sm.r1[3];
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / p.rf;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lr = lane >> 2, lc = lane & 3;  // (row, column) inside an 8 x 4 core matrix
   const int t0 = c * kC;
+  using umma::blk_off;
 
-  // (1) causal conv + SiLU (text_modules.rs:164-182) as a sliding window per
-  // channel: the K-1 history values (previous chunk, cached conv state or
-  // zeros) then 64 tokens loaded 8 at a time.  Tokens >= T are the zero
-  // padding of :224-236.
-  for (int ch = tid; ch < 3 * kD; ch += kThreads) {
-    int cgl;
-    if (ch < kD) cgl = hk * kD + ch;
-    else if (ch < 2 * kD) cgl = p.Hk * kD + hk * kD + (ch - kD);
-    else cgl = 2 * p.Hk * kD + h * kD + (ch - 2 * kD);
-    float w[KC];
+  if (warp == 0) {
+    umma::tmem_alloc(&sm.tbase, 256);
+    umma::tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&sm.bar1, 1);
+    mbar_init(&sm.bar2, 1);
+    fence_mbar_init();
+  }
+
+  // (1) causal conv + SiLU (text_modules.rs:164-182).  A warp takes 32
+  // consecutive channels (one per lane: every token row is one coalesced
+  // 128-byte load) over half of the chunk's tokens as a sliding window, 8
+  // tokens at a time; each 8 x 32 output tile goes through a padded staging
+  // tile into the blocked layouts (q, k: [token x channel]; v: [channel x
+  // token]).  Tokens >= T are the zero padding of :224-236.
+  {
+    float(*stg)[36] = sm.stage[warp];
+    for (int item = warp; item < 2 * (3 * kD / 32); item += kThreads / 32) {
+      const int cgrp = item >> 1, half = item & 1;
+      const int ch = 32 * cgrp + lane;  // 0..383 over q | k | v
+      int cgl;
+      if (ch < kD) cgl = hk * kD + ch;
+      else if (ch < 2 * kD) cgl = p.Hk * kD + hk * kD + (ch - kD);
+      else cgl = 2 * p.Hk * kD + h * kD + (ch - 2 * kD);
+      float w[KC];
 #pragma unroll
-    for (int j = 0; j < KC; ++j) w[j] = __ldg(p.conv_w + (size_t)cgl * KC + j);
-    float hist[KC - 1];
+      for (int j = 0; j < KC; ++j) w[j] = __ldg(p.conv_w + (size_t)cgl * KC + j);
+      float hist[KC - 1];
 #pragma unroll
-    for (int j = 0; j < KC - 1; ++j) {
-      const int tau = t0 - (KC - 1) + j;
-      hist[j] = tau >= 0 ? (tau < p.T ? __ldg(p.x + ((size_t)b * p.T + tau) * p.C + cgl) : 0.0f)
-                         : (p.has_prev ? p.conv_state[((size_t)b * p.C + cgl) * (KC - 1) + (KC - 1) + tau] : 0.0f);
-    }
-    float *dst = ch < kD ? &sm.q[0][ch] : ch < 2 * kD ? &sm.k[0][ch - kD] : &sm.v[0][ch - 2 * kD];
-    for (int i0 = 0; i0 < kC; i0 += 8) {
-      float xv[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int t = t0 + i0 + u;
-        xv[u] = t < p.T ? __ldg(p.x + ((size_t)b * p.T + t) * p.C + cgl) : 0.0f;
+      for (int j = 0; j < KC - 1; ++j) {
+        const int tau = t0 + 32 * half - (KC - 1) + j;
+        if (tau >= 0) hist[j] = tau < p.T ? __ldg(p.x + ((size_t)b * p.T + tau) * p.C + cgl) : 0.0f;
+        else hist[j] = p.has_prev ? p.conv_state[((size_t)b * p.C + cgl) * (KC - 1) + (KC - 1) + tau] : 0.0f;
       }
+      for (int tg = 0; tg < 4; ++tg) {
+        const int i0 = 32 * half + 8 * tg;
+        float xv[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        float acc = 0.0f;
+        for (int u = 0; u < 8; ++u) {
+          const int t = t0 + i0 + u;
+          xv[u] = t < p.T ? __ldg(p.x + ((size_t)b * p.T + t) * p.C + cgl) : 0.0f;
+        }
+        __syncwarp();
 #pragma unroll
-        for (int j = 0; j < KC - 1; ++j) acc = fmaf(w[j], hist[j], acc);
-        acc = fmaf(w[KC - 1], xv[u], acc);
+        for (int u = 0; u < 8; ++u) {
+          float acc = 0.0f;
 #pragma unroll
-        for (int j = 0; j < KC - 2; ++j) hist[j] = hist[j + 1];
-        hist[KC - 2] = xv[u];
-        dst[(size_t)(i0 + u) * kLd] = (t0 + i0 + u) < p.T ? siluf_dev(acc) : 0.0f;
+          for (int j = 0; j < KC - 1; ++j) acc = fmaf(w[j], hist[j], acc);
+          acc = fmaf(w[KC - 1], xv[u], acc);
+#pragma unroll
+          for (int j = 0; j < KC - 2; ++j) hist[j] = hist[j + 1];
+          hist[KC - 2] = xv[u];
+          stg[u][lane] = (t0 + i0 + u) < p.T ? siluf_dev(acc) : 0.0f;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int cq = 0; cq < 8; ++cq) {
+          const float v = stg[lr][4 * cq + lc];
+          const int i = i0 + lr, chl = 32 * cgrp + 4 * cq + lc;
+          if (cgrp < kD / 32) qS[blk_off(i, chl, kD)] = v;
+          else if (cgrp < 2 * kD / 32) kS[blk_off(i, chl - kD, kD)] = v;
+          else sm.vT[blk_off(chl - 2 * kD, i, kC)] = v;
+        }
       }
     }
   }
@@ -117,26 +162,6 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_chunk_kernel(const Prefi
     sm.gam[tid] = t < p.T ? p.g[((size_t)b * p.T + t) * p.Hv + h] : 0.0f;
   }
   __syncthreads();
-
-  // (2) l2norm of q and k per token, q scaled by DK^-0.5 (:218-222).
-  const float qscale = rsqrtf((float)kD);
-  for (int i = warp; i < kC; i += kThreads / 32) {
-    float sq = 0.f, sk = 0.f;
-#pragma unroll
-    for (int j = 0; j < kD / 32; ++j) {
-      const float a = sm.q[i][lane + 32 * j], bb = sm.k[i][lane + 32 * j];
-      sq = fmaf(a, a, sq);
-      sk = fmaf(bb, bb, sk);
-    }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    const float iq = 1.0f / sqrtf(sq + 1e-6f), ik = 1.0f / sqrtf(sk + 1e-6f);
-#pragma unroll
-    for (int j = 0; j < kD / 32; ++j) {
-      sm.q[i][lane + 32 * j] = (sm.q[i][lane + 32 * j] * iq) * qscale;
-      sm.k[i][lane + 32 * j] = sm.k[i][lane + 32 * j] * ik;
-    }
-  }
   if (tid == 0) {  // cum_decay = cumsum(decay), sequential (:255)
     float a = 0.0f;
     for (int i = 0; i < kC; ++i) {
@@ -144,61 +169,123 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_chunk_kernel(const Prefi
       sm.gam[i] = a;
     }
   }
-  __syncthreads();
 
-  // (3) A = -tril((k*beta) k^T o D, -1), Aqk = tril((q k^T) o D) (:259-279).
-  // Thread (iq, jq) owns rows iq + 16 ri and columns jq + 16 rj; blocks with
-  // rj > ri are zero and skipped.
-  {
-    const int iq = tid / 16, jq = tid % 16;
-    float aA[10], aQ[10];
-#pragma unroll
-    for (int e = 0; e < 10; ++e) aA[e] = aQ[e] = 0.0f;
-    for (int d = 0; d < kD; d += 4) {
-      float4 qi[4], ki[4], kj[4];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        qi[r] = *reinterpret_cast<const float4 *>(&sm.q[iq + 16 * r][d]);
-        ki[r] = *reinterpret_cast<const float4 *>(&sm.k[iq + 16 * r][d]);
-        kj[r] = *reinterpret_cast<const float4 *>(&sm.k[jq + 16 * r][d]);
-      }
-      int e = 0;
-#pragma unroll
-      for (int ri = 0; ri < 4; ++ri)
-#pragma unroll
-        for (int rj = 0; rj <= ri; ++rj, ++e) {
-          aA[e] = dot4(ki[ri], kj[rj], aA[e]);
-          aQ[e] = dot4(qi[ri], kj[rj], aQ[e]);
-        }
+  // (2) l2norm of q and k rows, q scaled by DK^-0.5 (:218-222), and the lo
+  // terms; one warp per 8-row group (16 groups).
+  const float qscale = rsqrtf((float)kD);
+  for (int grp = warp; grp < 16; grp += kThreads / 32) {
+    float *M = grp < 8 ? qS : kS, *ML = grp < 8 ? qL : kL;
+    const int i = 8 * (grp & 7) + lr;
+    float ss = 0.0f;
+#pragma unroll 8
+    for (int jj = 0; jj < kD / 4; ++jj) {
+      const float v = M[blk_off(i, 4 * jj + lc, kD)];
+      ss = fmaf(v, v, ss);
     }
-    int e = 0;
-#pragma unroll
-    for (int ri = 0; ri < 4; ++ri)
-#pragma unroll
-      for (int rj = 0; rj < 4; ++rj) {
-        const int i = iq + 16 * ri, j = jq + 16 * rj;
-        float va = 0.0f, vq = 0.0f;
-        if (rj <= ri) {
-          const float dec = j <= i ? expf(sm.gam[i] - sm.gam[j]) : 0.0f;
-          va = j < i ? -((aA[e] * sm.bet[i]) * dec) : 0.0f;
-          vq = aQ[e] * dec;
-          ++e;
-        }
-        sm.A[i][j] = va;
-        sm.Aqk[i][j] = vq;
-      }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    const float inv = 1.0f / sqrtf(ss + 1e-6f);
+    const float sc = grp < 8 ? qscale : 1.0f;
+#pragma unroll 8
+    for (int jj = 0; jj < kD / 4; ++jj) {
+      const int off = blk_off(i, 4 * jj + lc, kD);
+      const float v = (M[off] * inv) * sc;
+      M[off] = v;
+      ML[off] = umma::tf32_lo(v);
+    }
   }
+  for (int e = tid; e < kD * kC; e += kThreads) sm.vT_lo[e] = umma::tf32_lo(sm.vT[e]);
+  fence_proxy_async_smem();
+  umma::fence_before_sync();
   __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tb = sm.tbase;
+  if (tid < kC) {
+    sm.eg[tid] = expf(sm.gam[tid]);
+    sm.ek[tid] = expf(sm.gam[kC - 1] - sm.gam[tid]);
+  }
+
+  // (3) G12 (thread 0): D12 = [k ; q] k^T, K = 128 in 16 steps of 8
+  if (tid == 0) {
+    const uint32_t id = umma::idesc_tf32(128, 64, 0, 0);
+    for (int st = 0; st < kD / 8; ++st) {
+      const uint64_t hi = umma::smem_desc(kS + st * 64, 128, (kD / 4) * 128);
+      const uint64_t lo = umma::smem_desc(kL + st * 64, 128, (kD / 4) * 128);
+      umma::mma_tf32(tb, hi, hi, id, st > 0);
+      umma::mma_tf32(tb, hi, lo, id, 1);
+      umma::mma_tf32(tb, lo, hi, id, 1);
+    }
+    umma::commit(&sm.bar1);
+  }
+  __syncthreads();  // eg / ek ready
 
   // workspace record: U [64][128] | Wt [128][64] | Qt [128][64] | Kp [64][128] | AqT [64][64] | decay
   float *rec = p.ws + (((size_t)b * p.Hv + h) * p.NC + c) * kRec;
   float *U = rec, *Wt = rec + kC * kD, *Qt = rec + 2 * kC * kD, *Kp = rec + 3 * kC * kD;
   float *AqT = rec + 4 * kC * kD;
-  const float glast = sm.gam[kC - 1];
 
+  // meanwhile: q' = q e^gamma, stored transposed (Qt[d][i]) (:303-307)
+  for (int cm = warp; cm < (kC / 8) * (kD / 4); cm += kThreads / 32) {
+    const int i = 8 * (cm / (kD / 4)) + lr, d = 4 * (cm % (kD / 4)) + lc;
+    Qt[(size_t)d * kC + i] = qS[blk_off(i, d, kD)] * sm.eg[i];
+  }
+  if (tid == 0) AqT[kC * kC] = expf(sm.gam[kC - 1]);
+
+  const bool g12_ok = mbar_wait(&sm.bar1, 0);
+  umma::fence_after_sync();
+
+  // (4) epilogue of G12: TMEM lane = row of [k k^T ; q k^T]; warps w and w+4
+  // read columns 0-31 and 32-63 of lane quadrant w % 4.
+  {
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = 32 * quad + lane;
+    float v[32];
+    umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + 32 * half, *reinterpret_cast<float(*)[16]>(&v[0]));
+    umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + 32 * half + 16,
+                        *reinterpret_cast<float(*)[16]>(&v[16]));
+    umma::wait_ld();
+    if (row < kC) {  // A = -tril(diag(beta) k k^T o D, -1) (:259-279)
+      const int i = row;
+      const float bi = sm.bet[i], gi = sm.gam[i];
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = 32 * half + jj;
+        sm.Am[i][j] = j < i ? -((v[jj] * bi) * expf(gi - sm.gam[j])) : 0.0f;
+      }
+    } else {  // Aqk = tril(q k^T o D), stored transposed (AqT[j][i])
+      const int i = row - kC;
+      const float gi = sm.gam[i];
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = 32 * half + jj;
+        AqT[(size_t)j * kC + i] = j <= i ? v[jj] * expf(gi - sm.gam[j]) : 0.0f;
+      }
+    }
+    if (!g12_ok && tid == 0) p.out[0] = __int_as_float(0x7fc00000);
+  }
+  __syncthreads();  // every warp is done reading q (q'^T above) before k^T overwrites its slot
+
+  // (5) k^T (blocked [128 x 64]) + lo into the free q / q_lo slots, and
+  // k' = k e^(gamma_last - gamma) (:308-311) to the workspace
+  float *kT = sm.r1[1], *kTL = sm.r1[3];
+  for (int cm = warp; cm < (kD / 8) * (kC / 4); cm += kThreads / 32) {
+    const int d = 8 * (cm / (kC / 4)) + lr, i = 4 * (cm % (kC / 4)) + lc;
+    const float v = kS[blk_off(i, d, kD)];
+    kT[blk_off(d, i, kC)] = v;
+    kTL[blk_off(d, i, kC)] = umma::tf32_lo(v);
+  }
+  for (int it = warp; it < (kC / 8) * (kD / 16); it += kThreads / 32) {
+    const int r = lane & 7, c4 = lane >> 3;
+    const int i = 8 * (it / (kD / 16)) + r, d0 = 16 * (it % (kD / 16)) + 4 * c4;
+    const float4 v = *reinterpret_cast<const float4 *>(&kS[blk_off(i, d0, kD)]);
+    const float e = sm.ek[i];
+    *reinterpret_cast<float4 *>(Kp + (size_t)i * kD + d0) = make_float4(v.x * e, v.y * e, v.z * e, v.w * e);
+  }
+  __syncthreads();
+
+  // (6) T = (I - A)^-1 column by column (the row recursion of :280-287
+  // solves (I - A) T = I; column j: c[j] = 1, c[i] = sum_{m<i} A[i][m] c[m]).
   if (warp < 2) {
-    // (4) T = (I - A)^-1 column by column (the row recursion of :280-287 solves
-    // (I - A) T = I; column j: c[j] = 1, c[i] = sum_{m<i} A[i][m] c[m] for i > j).
     const int j = tid;
     float cv[kC];
 #pragma unroll
@@ -208,98 +295,81 @@ __global__ void __launch_bounds__(kThreads) gdn_prefill_chunk_kernel(const Prefi
       float s = 0.0f;
 #pragma unroll
       for (int m4 = 0; m4 < i / 4; ++m4) {
-        const float4 a = *reinterpret_cast<const float4 *>(&sm.A[i][4 * m4]);
+        const float4 a = *reinterpret_cast<const float4 *>(&sm.Am[i][4 * m4]);
         s = fmaf(a.x, cv[4 * m4 + 0], s);
         s = fmaf(a.y, cv[4 * m4 + 1], s);
         s = fmaf(a.z, cv[4 * m4 + 2], s);
         s = fmaf(a.w, cv[4 * m4 + 3], s);
       }
 #pragma unroll
-      for (int m = (i / 4) * 4; m < i; ++m) s = fmaf(sm.A[i][m], cv[m], s);
+      for (int m = (i / 4) * 4; m < i; ++m) s = fmaf(sm.Am[i][m], cv[m], s);
       if (i > j) cv[i] = s;
     }
-    const float bj = sm.bet[j], ej = bj * expf(sm.gam[j]);
+    named_bar_sync(2, 64);  // both warps finished reading A
 #pragma unroll
-    for (int i = 0; i < kC; ++i) {
-      sm.Tb[i][j] = cv[i] * bj;
-      sm.Te[i][j] = cv[i] * ej;
-    }
-  } else {
-    // meanwhile: q' = q e^gamma (stored transposed, Qt[k][i]), k' = k e^(gamma_last - gamma)
-    // (:303-311) and Aqk (stored transposed, AqT[j][i])
-    for (int idx = tid - 64; idx < kC * kD / 4; idx += kThreads - 64) {
-      const int kk = idx / (kC / 4), i4 = idx % (kC / 4);
-      float4 qv;
-      qv.x = sm.q[4 * i4 + 0][kk] * expf(sm.gam[4 * i4 + 0]);
-      qv.y = sm.q[4 * i4 + 1][kk] * expf(sm.gam[4 * i4 + 1]);
-      qv.z = sm.q[4 * i4 + 2][kk] * expf(sm.gam[4 * i4 + 2]);
-      qv.w = sm.q[4 * i4 + 3][kk] * expf(sm.gam[4 * i4 + 3]);
-      reinterpret_cast<float4 *>(Qt)[idx] = qv;
-      const int i = idx / (kD / 4), d4 = idx % (kD / 4);
-      const float ek = expf(glast - sm.gam[i]);
-      float4 kv = *reinterpret_cast<const float4 *>(&sm.k[i][4 * d4]);
-      reinterpret_cast<float4 *>(Kp)[idx] = make_float4(kv.x * ek, kv.y * ek, kv.z * ek, kv.w * ek);
-    }
-    for (int idx = tid - 64; idx < kC * kC / 4; idx += kThreads - 64) {
-      const int j = idx / (kC / 4), i4 = idx % (kC / 4);
-      reinterpret_cast<float4 *>(AqT)[idx] =
-          make_float4(sm.Aqk[4 * i4][j], sm.Aqk[4 * i4 + 1][j], sm.Aqk[4 * i4 + 2][j], sm.Aqk[4 * i4 + 3][j]);
-    }
-    if (tid == 64) AqT[kC * kC] = expf(glast);
+    for (int i = 0; i < kC; ++i) sm.Am[i][j] = cv[i];  // T, column j
   }
   __syncthreads();
-
-  // (5) U = T (v*beta), W = T (k*beta*e^gamma) (:292-293); thread (iq, dq)
-  // owns rows iq + 16 ri and float4 columns 4 dq + 64 rd.
-  {
-    const int iq = tid / 16, dq = tid % 16;
-    float4 u[4][2], w[4][2];
-#pragma unroll
-    for (int ri = 0; ri < 4; ++ri)
-#pragma unroll
-      for (int rd = 0; rd < 2; ++rd) u[ri][rd] = w[ri][rd] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int jb = 0; jb < 4; ++jb) {
-      for (int jj = 0; jj < 16; ++jj) {
-        const int j = 16 * jb + jj;
-        float4 vv[2], kk[2];
-#pragma unroll
-        for (int rd = 0; rd < 2; ++rd) {
-          vv[rd] = *reinterpret_cast<const float4 *>(&sm.v[j][4 * dq + 64 * rd]);
-          kk[rd] = *reinterpret_cast<const float4 *>(&sm.k[j][4 * dq + 64 * rd]);
-        }
-#pragma unroll
-        for (int ri = jb; ri < 4; ++ri) {
-          const float tb = sm.Tb[iq + 16 * ri][j], te = sm.Te[iq + 16 * ri][j];
-#pragma unroll
-          for (int rd = 0; rd < 2; ++rd) {
-            u[ri][rd] = f4_fma(tb, vv[rd], u[ri][rd]);
-            w[ri][rd] = f4_fma(te, kk[rd], w[ri][rd]);
-          }
-        }
-      }
-    }
-    // W goes out transposed (Wt[k][i]) through shared memory (q is free now):
-    // staging rows of 65 floats keep the scattered writes at 2-way conflicts.
-    float *wt_s = &sm.q[0][0];
-#pragma unroll
-    for (int ri = 0; ri < 4; ++ri)
-#pragma unroll
-      for (int rd = 0; rd < 2; ++rd) {
-        const int i = iq + 16 * ri, d0 = 4 * dq + 64 * rd;
-        *reinterpret_cast<float4 *>(U + (size_t)i * kD + d0) = u[ri][rd];
-        wt_s[(d0 + 0) * (kC + 1) + i] = w[ri][rd].x;
-        wt_s[(d0 + 1) * (kC + 1) + i] = w[ri][rd].y;
-        wt_s[(d0 + 2) * (kC + 1) + i] = w[ri][rd].z;
-        wt_s[(d0 + 3) * (kC + 1) + i] = w[ri][rd].w;
-      }
-    __syncthreads();
-    for (int idx = tid; idx < kD * kC / 4; idx += kThreads) {
-      const int kk = idx / (kC / 4), i4 = idx % (kC / 4);
-      const float *src = wt_s + kk * (kC + 1) + 4 * i4;
-      reinterpret_cast<float4 *>(Wt)[idx] = make_float4(src[0], src[1], src[2], src[3]);
-    }
+  // T diag(beta) and T diag(beta e^gamma) (+ lo) blocked [64 (i) x 64 (j)]
+  float *Tb = sm.r1[0], *TbL = sm.r1[0] + kC * kC, *Te = sm.r1[2], *TeL = sm.r1[2] + kC * kC;
+  for (int cm = warp; cm < (kC / 8) * (kC / 4); cm += kThreads / 32) {
+    const int i = 8 * (cm / (kC / 4)) + lr, j = 4 * (cm % (kC / 4)) + lc;
+    const float t = sm.Am[i][j];
+    const float tbv = t * sm.bet[j], tev = t * (sm.bet[j] * sm.eg[j]);
+    const int off = blk_off(i, j, kC);
+    Tb[off] = tbv;
+    TbL[off] = umma::tf32_lo(tbv);
+    Te[off] = tev;
+    TeL[off] = umma::tf32_lo(tev);
   }
+  fence_proxy_async_smem();
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+
+  // (7) GU and GW (thread 0): K = 64 tokens in 8 steps
+  if (tid == 0) {
+    const uint32_t id = umma::idesc_tf32(128, 64, 0, 0);
+    constexpr uint32_t sbo = (kC / 4) * 128;
+    for (int st = 0; st < kC / 8; ++st) {
+      const uint64_t vh = umma::smem_desc(sm.vT + st * 64, 128, sbo), vl = umma::smem_desc(sm.vT_lo + st * 64, 128, sbo);
+      const uint64_t bh = umma::smem_desc(Tb + st * 64, 128, sbo), bl = umma::smem_desc(TbL + st * 64, 128, sbo);
+      umma::mma_tf32(tb + 64, vh, bh, id, st > 0);
+      umma::mma_tf32(tb + 64, vh, bl, id, 1);
+      umma::mma_tf32(tb + 64, vl, bh, id, 1);
+      const uint64_t kh = umma::smem_desc(kT + st * 64, 128, sbo), kl = umma::smem_desc(kTL + st * 64, 128, sbo);
+      const uint64_t eh = umma::smem_desc(Te + st * 64, 128, sbo), el = umma::smem_desc(TeL + st * 64, 128, sbo);
+      umma::mma_tf32(tb + 128, kh, eh, id, st > 0);
+      umma::mma_tf32(tb + 128, kh, el, id, 1);
+      umma::mma_tf32(tb + 128, kl, eh, id, 1);
+    }
+    umma::commit(&sm.bar2);
+  }
+  const bool g2_ok = mbar_wait(&sm.bar2, 0);
+  umma::fence_after_sync();
+
+  // (8) epilogue: TMEM lane = d.  U[i][d] from U^T (warps 0-3), Wt[d][i] = W^T (warps 4-7)
+  {
+    const int quad = warp & 3, d = 32 * quad + lane;
+#pragma unroll
+    for (int cb = 0; cb < kC / 16; ++cb) {
+      float v[16];
+      umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + (warp < 4 ? 64 : 128) + 16 * cb, v);
+      umma::wait_ld();
+      if (warp < 4) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) U[(size_t)(16 * cb + e) * kD + d] = v[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; e += 4)
+          *reinterpret_cast<float4 *>(Wt + (size_t)d * kC + 16 * cb + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+      }
+    }
+    if (!g2_ok && tid == 0) p.out[0] = __int_as_float(0x7fc00000);
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tb, 256);
 }
 
 struct StateSmem {
