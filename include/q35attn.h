@@ -103,6 +103,7 @@ int q35_gdn_decode(const q35_gdn_dims *dims, const float *mixed_qkv,
  *   rec_state  [B, Hv, DK, DV]: initial state when has_init_state, else zero;
  *              overwritten with the final state.
  *   workspace  >= q35_gdn_prefill_workspace_size(dims, T) bytes.
+ *   mixed_qkv, z, norm_w, rec_state and out must be 16-byte aligned.
  */
 size_t q35_gdn_prefill_workspace_size(const q35_gdn_dims *dims, int32_t seq_len);
 int q35_gdn_prefill(const q35_gdn_dims *dims, int32_t seq_len,

@@ -91,7 +91,7 @@ static int check_gdn_dims(const q35_gdn_dims *d) {
               "gdn dims: head_k_dim = head_v_dim = 128 is the compiled configuration");
   Q35_REQUIRE(d->conv_kernel >= 2 && d->conv_kernel <= 4, Q35_ERR_UNSUPPORTED, "gdn dims: conv_kernel must be 2..4");
   Q35_REQUIRE(d->eps >= 0.0f, Q35_ERR_INVALID_ARG, "gdn dims: eps must be >= 0");
-  Q35_REQUIRE(d->batch <= 65535 && d->num_k_heads <= 65535, Q35_ERR_UNSUPPORTED, "gdn dims: batch / heads too large");
+  Q35_REQUIRE(d->batch <= 65535 && d->num_v_heads <= 65535, Q35_ERR_UNSUPPORTED, "gdn dims: batch / heads too large");
   return Q35_OK;
 }
 
@@ -263,8 +263,8 @@ int q35_gdn_prefill(const q35_gdn_dims *dims, int32_t seq_len, const float *mixe
   Q35_REQUIRE(has_prev_conv == 0 || has_prev_conv == 1, Q35_ERR_INVALID_ARG, "has_prev_conv must be 0 or 1");
   Q35_REQUIRE(has_init_state == 0 || has_init_state == 1, Q35_ERR_INVALID_ARG, "has_init_state must be 0 or 1");
   if (dims->batch == 0 || seq_len == 0) return Q35_OK;
-  Q35_PTR(mixed_qkv); Q35_PTR(beta); Q35_PTR(g); Q35_PTR(conv_w); Q35_PTR(conv_state);
-  Q35_PTR16(z); Q35_PTR16(norm_w); Q35_PTR16(out); Q35_PTR16(rec_state);
+  Q35_PTR(beta); Q35_PTR(g); Q35_PTR(conv_w); Q35_PTR(conv_state);
+  Q35_PTR16(mixed_qkv); Q35_PTR16(z); Q35_PTR16(norm_w); Q35_PTR16(out); Q35_PTR16(rec_state);
   if (int rc = require_sm100()) return rc;
   return gdn_prefill_launch(dims, seq_len, mixed_qkv, z, beta, g, conv_w, norm_w, conv_state, has_prev_conv,
                             rec_state, has_init_state, out, workspace, workspace_bytes,

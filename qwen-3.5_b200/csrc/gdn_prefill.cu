@@ -6,7 +6,7 @@
 // :189-363 burn_chunk_gated_delta_rule, :651-660 RMSNormGated).
 //
 // Two kernels:
-//  (1) gdn_prefill_chunk_kernel, grid (chunks, Hv, B), fully parallel: causal
+//  (1) gdn_prefill_chunk_kernel, grid (Hv, chunks, B), fully parallel: causal
 //      conv + SiLU of the chunk's q/k/v channels (3-token halo from the
 //      previous chunk or the cached conv state), l2norm, beta scaling,
 //      cumulative decay gamma, the strictly-lower system
@@ -38,11 +38,9 @@ namespace {
 
 constexpr int kC = 64;      // chunk length (text_modules.rs:645)
 constexpr int kD = 128;     // head_k_dim == head_v_dim
-constexpr int kPad = 4;     // row padding (floats) of [64][128] smem tiles
-constexpr int kLd = kD + kPad;
 constexpr int kCS = 16;     // value columns per CTA in the state kernel
 constexpr int kSplit = kD / kCS;
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;  // 16 warps: the chunk phases are latency-bound
 constexpr int kStateThreads = 512;  // state pass: 16 warps hide the shared-memory latency
 // workspace record per (b, h, chunk): U, W, q', k' [64x128] + Aqk [64x64] + decay
 constexpr size_t kRec = 4 * (size_t)kC * kD + (size_t)kC * kC + 16;
@@ -72,7 +70,6 @@ struct ChunkSmem {
   float vT_lo[kD * kC];
   float Am[kC][kC + 4];  // A = -tril(diag(beta) k k^T o D, -1), then T = (I - A)^-1
   float gam[kC], bet[kC], eg[kC], ek[kC];
-  float stage[kThreads / 32][8][36];  // per-warp conv staging tile (rows padded to 36: conflict-free both ways)
   uint32_t tbase;
   uint64_t bar1, bar2;
 };
@@ -82,7 +79,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
   extern __shared__ __align__(128) unsigned char smem_raw[];
   ChunkSmem &sm = *reinterpret_cast<ChunkSmem *>(smem_raw);
   float *kS = sm.r1[0], *qS = sm.r1[1], *kL = sm.r1[2], *qL = sm.r1[3];
-  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // heads vary fastest: one wave then reads every head's channel columns of
+  // its token rows instead of one 512-byte column group at the row stride
+  const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
   const int hk = h / p.rf;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lr = lane >> 2, lc = lane & 3;  // (row, column) inside an 8 x 4 core matrix
@@ -99,59 +98,92 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
     fence_mbar_init();
   }
 
-  // (1) causal conv + SiLU (text_modules.rs:164-182).  A warp takes 32
-  // consecutive channels (one per lane: every token row is one coalesced
-  // 128-byte load) over half of the chunk's tokens as a sliding window, 8
-  // tokens at a time; each 8 x 32 output tile goes through a padded staging
-  // tile into the blocked layouts (q, k: [token x channel]; v: [channel x
-  // token]).  Tokens >= T are the zero padding of :224-236.
+  // (1) causal conv + SiLU (text_modules.rs:164-182).  The chunk's raw q, k
+  // and v rows (64 tokens x 128 channels each) are all requested at once with
+  // 16-byte cp.async copies (96 KB in flight per SM) into the k_lo, q_lo and
+  // v_lo slots, which are free until step (2); the 16-byte column groups of
+  // row t are XOR-swizzled by t % 8 so that the conv reads below are free of
+  // bank conflicts.  Rows >= T are zero-filled (the padding of :224-236).  The
+  // K-1 history rows (previous chunk, or the cached conv state before the
+  // first chunk) and the weights go to the A slot.
   {
-    float(*stg)[36] = sm.stage[warp];
-    for (int item = warp; item < 2 * (3 * kD / 32); item += kThreads / 32) {
-      const int cgrp = item >> 1, half = item & 1;
-      const int ch = 32 * cgrp + lane;  // 0..383 over q | k | v
-      int cgl;
-      if (ch < kD) cgl = hk * kD + ch;
-      else if (ch < 2 * kD) cgl = p.Hk * kD + hk * kD + (ch - kD);
-      else cgl = 2 * p.Hk * kD + h * kD + (ch - 2 * kD);
-      float w[KC];
-#pragma unroll
-      for (int j = 0; j < KC; ++j) w[j] = __ldg(p.conv_w + (size_t)cgl * KC + j);
-      float hist[KC - 1];
-#pragma unroll
-      for (int j = 0; j < KC - 1; ++j) {
-        const int tau = t0 + 32 * half - (KC - 1) + j;
-        if (tau >= 0) hist[j] = tau < p.T ? __ldg(p.x + ((size_t)b * p.T + tau) * p.C + cgl) : 0.0f;
-        else hist[j] = p.has_prev ? p.conv_state[((size_t)b * p.C + cgl) * (KC - 1) + (KC - 1) + tau] : 0.0f;
+    auto raw = [&](int sl) { return sl == 0 ? qL : (sl == 1 ? kL : sm.vT_lo); };
+    float *hist = &sm.Am[0][0];              // [KC-1][3*128]
+    float *wts = hist + (KC - 1) * 3 * kD;   // [3*128][KC]
+    auto cbase = [&](int sl) {
+      return sl == 0 ? (size_t)hk * kD : (sl == 1 ? (size_t)(p.Hk + hk) * kD : (size_t)2 * p.Hk * kD + (size_t)h * kD);
+    };
+#pragma unroll 4
+    for (int e = tid; e < 3 * kC * (kD / 4); e += kThreads) {
+      const int sl = e / (kC * (kD / 4)), rem = e % (kC * (kD / 4));
+      const int t = rem >> 5, q4 = rem & 31;
+      const bool in = t0 + t < p.T;
+      const float *src = p.x + ((size_t)b * p.T + (in ? t0 + t : 0)) * p.C + cbase(sl) + 4 * q4;
+      cp_async16_zfill(raw(sl) + t * kD + ((q4 ^ (t & 7)) << 2), src, in ? 16u : 0u);
+    }
+    if (t0 > 0) {  // history rows t0-KC+1 .. t0-1 of the three column slices
+      for (int e = tid; e < (KC - 1) * 3 * (kD / 4); e += kThreads) {
+        const int j = e / (3 * (kD / 4)), r = e % (3 * (kD / 4));
+        const float *src = p.x + ((size_t)b * p.T + t0 - (KC - 1) + j) * p.C + cbase(r / (kD / 4)) + 4 * (r % (kD / 4));
+        cp_async16(hist + j * 3 * kD + 4 * r, src);
       }
-      for (int tg = 0; tg < 4; ++tg) {
-        const int i0 = 32 * half + 8 * tg;
-        float xv[8];
+    } else {  // before the first chunk: the cached conv state, or zeros
+      for (int e = tid; e < (KC - 1) * 3 * kD; e += kThreads) {
+        const int j = e / (3 * kD), r = e % (3 * kD);
+        const size_t cgl = cbase(r / kD) + (r % kD);
+        hist[e] = p.has_prev ? p.conv_state[((size_t)b * p.C + cgl) * (KC - 1) + j] : 0.0f;
+      }
+    }
+    for (int e = tid; e < 3 * kD * KC; e += kThreads) {
+      const int r = e / KC, j = e % KC;
+      cp_async4(wts + e, p.conv_w + (cbase(r / kD) + (r % kD)) * KC + j);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    // Lane (lr, lc) of warp w computes tokens 8 tg + lr (tg = w / 8 mod 2) of
+    // channels 4 (w8 + 8 m) + lc, w8 = w % 8, m < 4: per store one whole 8 x 4
+    // core matrix.  The swizzle only touches the low 3 bits of the column
+    // group w8 + 8 m, so the read offset of row tau is
+    // ((w8 ^ (tau % 8)) * 4 + lc) + 32 m.
+    const int w8 = warp & 7;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int t = t0 + i0 + u;
-          xv[u] = t < p.T ? __ldg(p.x + ((size_t)b * p.T + t) * p.C + cgl) : 0.0f;
+    for (int sl = 0; sl < 3; ++sl) {
+      const float *rs = raw(sl);
+      float wv[4][KC];
+#pragma unroll
+      for (int m = 0; m < 4; ++m)
+#pragma unroll
+        for (int j = 0; j < KC; ++j) wv[m][j] = wts[(sl * kD + 4 * (w8 + 8 * m) + lc) * KC + j];
+      int coff[KC];
+#pragma unroll
+      for (int j = 0; j < KC; ++j) coff[j] = ((w8 ^ ((lr - (KC - 1) + j) & 7)) << 2) + lc;
+#pragma unroll 2
+      for (int tg = warp >> 3; tg < kC / 8; tg += 2) {
+        const int i = 8 * tg + lr;
+        float xin[KC][4];
+#pragma unroll
+        for (int j = 0; j < KC; ++j) {
+          const int tau = i - (KC - 1) + j;
+          if (tau >= 0) {
+#pragma unroll
+            for (int m = 0; m < 4; ++m) xin[j][m] = rs[tau * kD + coff[j] + 32 * m];
+          } else {
+#pragma unroll
+            for (int m = 0; m < 4; ++m) xin[j][m] = hist[(KC - 1 + tau) * 3 * kD + sl * kD + 4 * (w8 + 8 * m) + lc];
+          }
         }
-        __syncwarp();
+        const bool live = t0 + i < p.T;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int m = 0; m < 4; ++m) {
           float acc = 0.0f;
 #pragma unroll
-          for (int j = 0; j < KC - 1; ++j) acc = fmaf(w[j], hist[j], acc);
-          acc = fmaf(w[KC - 1], xv[u], acc);
-#pragma unroll
-          for (int j = 0; j < KC - 2; ++j) hist[j] = hist[j + 1];
-          hist[KC - 2] = xv[u];
-          stg[u][lane] = (t0 + i0 + u) < p.T ? siluf_dev(acc) : 0.0f;
-        }
-        __syncwarp();
-#pragma unroll
-        for (int cq = 0; cq < 8; ++cq) {
-          const float v = stg[lr][4 * cq + lc];
-          const int i = i0 + lr, chl = 32 * cgrp + 4 * cq + lc;
-          if (cgrp < kD / 32) qS[blk_off(i, chl, kD)] = v;
-          else if (cgrp < 2 * kD / 32) kS[blk_off(i, chl - kD, kD)] = v;
-          else sm.vT[blk_off(chl - 2 * kD, i, kC)] = v;
+          for (int j = 0; j < KC; ++j) acc = fmaf(wv[m][j], xin[j][m], acc);
+          const float v = live ? __fdividef(acc, 1.0f + __expf(-acc)) : 0.0f;  // SiLU
+          const int ch = 4 * (w8 + 8 * m) + lc;
+          if (sl == 0) qS[blk_off(i, ch, kD)] = v;
+          else if (sl == 1) kS[blk_off(i, ch, kD)] = v;
+          else sm.vT[blk_off(ch, i, kC)] = v;
         }
       }
     }
@@ -194,7 +226,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
       ML[off] = umma::tf32_lo(v);
     }
   }
-  for (int e = tid; e < kD * kC; e += kThreads) sm.vT_lo[e] = umma::tf32_lo(sm.vT[e]);
+  for (int e = tid; e < kD * kC / 4; e += kThreads) {
+    const float4 v = reinterpret_cast<const float4 *>(sm.vT)[e];
+    reinterpret_cast<float4 *>(sm.vT_lo)[e] =
+        make_float4(umma::tf32_lo(v.x), umma::tf32_lo(v.y), umma::tf32_lo(v.z), umma::tf32_lo(v.w));
+  }
   fence_proxy_async_smem();
   umma::fence_before_sync();
   __syncthreads();
@@ -234,30 +270,28 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
   const bool g12_ok = mbar_wait(&sm.bar1, 0);
   umma::fence_after_sync();
 
-  // (4) epilogue of G12: TMEM lane = row of [k k^T ; q k^T]; warps w and w+4
-  // read columns 0-31 and 32-63 of lane quadrant w % 4.
+  // (4) epilogue of G12: TMEM lane = row of [k k^T ; q k^T]; the four warps
+  // w = quad + 4 qtr of lane quadrant quad read columns 16 qtr .. 16 qtr + 15.
   {
-    const int quad = warp & 3, half = warp >> 2;
+    const int quad = warp & 3, qtr = warp >> 2;
     const int row = 32 * quad + lane;
-    float v[32];
-    umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + 32 * half, *reinterpret_cast<float(*)[16]>(&v[0]));
-    umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + 32 * half + 16,
-                        *reinterpret_cast<float(*)[16]>(&v[16]));
+    float v[16];
+    umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + 16 * qtr, v);
     umma::wait_ld();
     if (row < kC) {  // A = -tril(diag(beta) k k^T o D, -1) (:259-279)
       const int i = row;
       const float bi = sm.bet[i], gi = sm.gam[i];
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int j = 32 * half + jj;
+      for (int jj = 0; jj < 16; ++jj) {
+        const int j = 16 * qtr + jj;
         sm.Am[i][j] = j < i ? -((v[jj] * bi) * expf(gi - sm.gam[j])) : 0.0f;
       }
     } else {  // Aqk = tril(q k^T o D), stored transposed (AqT[j][i])
       const int i = row - kC;
       const float gi = sm.gam[i];
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int j = 32 * half + jj;
+      for (int jj = 0; jj < 16; ++jj) {
+        const int j = 16 * qtr + jj;
         AqT[(size_t)j * kC + i] = j <= i ? v[jj] * expf(gi - sm.gam[j]) : 0.0f;
       }
     }
@@ -266,48 +300,110 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
   __syncthreads();  // every warp is done reading q (q'^T above) before k^T overwrites its slot
 
   // (5) k^T (blocked [128 x 64]) + lo into the free q / q_lo slots, and
-  // k' = k e^(gamma_last - gamma) (:308-311) to the workspace
+  // k' = k e^(gamma_last - gamma) (:308-311) to the workspace, on warps 2-15
+  // while warps 0-1 run level 0 of (6).
+  //
+  // (6) T = (I - A)^-1 (the row recursion of :280-287 solves (I - A) T = I
+  // for the strictly lower A), by 16 x 16 blocks in place in Am.  With
+  // T = [[T0, 0], [X, T1]] for any split, X = T1 A10 T0.  Level 0 solves the
+  // four diagonal blocks column by column; level 1 forms the blocks under
+  // them (16 x 16 products), level 2 the lower-left 32 x 32 block.  The upper
+  // triangle of Am stays zero; products go through the free k slot.
   float *kT = sm.r1[1], *kTL = sm.r1[3];
-  for (int cm = warp; cm < (kD / 8) * (kC / 4); cm += kThreads / 32) {
-    const int d = 8 * (cm / (kC / 4)) + lr, i = 4 * (cm % (kC / 4)) + lc;
-    const float v = kS[blk_off(i, d, kD)];
-    kT[blk_off(d, i, kC)] = v;
-    kTL[blk_off(d, i, kC)] = umma::tf32_lo(v);
-  }
-  for (int it = warp; it < (kC / 8) * (kD / 16); it += kThreads / 32) {
-    const int r = lane & 7, c4 = lane >> 3;
-    const int i = 8 * (it / (kD / 16)) + r, d0 = 16 * (it % (kD / 16)) + 4 * c4;
-    const float4 v = *reinterpret_cast<const float4 *>(&kS[blk_off(i, d0, kD)]);
-    const float e = sm.ek[i];
-    *reinterpret_cast<float4 *>(Kp + (size_t)i * kD + d0) = make_float4(v.x * e, v.y * e, v.z * e, v.w * e);
-  }
-  __syncthreads();
-
-  // (6) T = (I - A)^-1 column by column (the row recursion of :280-287
-  // solves (I - A) T = I; column j: c[j] = 1, c[i] = sum_{m<i} A[i][m] c[m]).
-  if (warp < 2) {
-    const int j = tid;
-    float cv[kC];
-#pragma unroll
-    for (int m = 0; m < kC; ++m) cv[m] = m == j ? 1.0f : 0.0f;
-#pragma unroll
-    for (int i = 1; i < kC; ++i) {
-      float s = 0.0f;
-#pragma unroll
-      for (int m4 = 0; m4 < i / 4; ++m4) {
-        const float4 a = *reinterpret_cast<const float4 *>(&sm.Am[i][4 * m4]);
-        s = fmaf(a.x, cv[4 * m4 + 0], s);
-        s = fmaf(a.y, cv[4 * m4 + 1], s);
-        s = fmaf(a.z, cv[4 * m4 + 2], s);
-        s = fmaf(a.w, cv[4 * m4 + 3], s);
-      }
-#pragma unroll
-      for (int m = (i / 4) * 4; m < i; ++m) s = fmaf(sm.Am[i][m], cv[m], s);
-      if (i > j) cv[i] = s;
+  constexpr int ld = kC + 4;
+  float *Am = &sm.Am[0][0];
+  if (warp >= 2) {
+    constexpr int nw = kThreads / 32 - 2;
+    for (int cm = warp - 2; cm < (kD / 8) * (kC / 4); cm += nw) {
+      const int d = 8 * (cm / (kC / 4)) + lr, i = 4 * (cm % (kC / 4)) + lc;
+      const float v = kS[blk_off(i, d, kD)];
+      kT[blk_off(d, i, kC)] = v;
+      kTL[blk_off(d, i, kC)] = umma::tf32_lo(v);
     }
-    named_bar_sync(2, 64);  // both warps finished reading A
+    for (int it = warp - 2; it < (kC / 8) * (kD / 16); it += nw) {
+      const int r = lane & 7, c4 = lane >> 3;
+      const int i = 8 * (it / (kD / 16)) + r, d0 = 16 * (it % (kD / 16)) + 4 * c4;
+      const float4 v = *reinterpret_cast<const float4 *>(&kS[blk_off(i, d0, kD)]);
+      const float e = sm.ek[i];
+      *reinterpret_cast<float4 *>(Kp + (size_t)i * kD + d0) = make_float4(v.x * e, v.y * e, v.z * e, v.w * e);
+    }
+  } else {  // level 0: block bb, column j
+    const int bb = tid >> 4, j = tid & 15, o = 16 * bb;
+    float cv[16];
 #pragma unroll
-    for (int i = 0; i < kC; ++i) sm.Am[i][j] = cv[i];  // T, column j
+    for (int m = 0; m < 16; ++m) cv[m] = m == j ? 1.0f : 0.0f;
+#pragma unroll
+    for (int i = 1; i < 16; ++i) {
+      const float *arow = Am + (o + i) * ld + o;
+      float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+      for (int m4 = 0; m4 < (i + 3) / 4; ++m4) {
+        const float4 a = *reinterpret_cast<const float4 *>(arow + 4 * m4);  // a[m >= i] is 0
+        s0 = fmaf(a.x, cv[4 * m4 + 0], s0);
+        s1 = fmaf(a.y, cv[4 * m4 + 1], s1);
+        s0 = fmaf(a.z, cv[4 * m4 + 2], s0);
+        s1 = fmaf(a.w, cv[4 * m4 + 3], s1);
+      }
+      if (i > j) cv[i] = s0 + s1;
+    }
+    __syncwarp();  // both blocks of this warp are done reading A
+#pragma unroll
+    for (int i = 0; i < 16; ++i) Am[(o + i) * ld + o + j] = cv[i];
+  }
+  {
+    float *Xs = sm.r1[0];  // [32][36], free once k^T and k' are out
+    constexpr int xld = 36;
+    __syncthreads();
+    // level 1: X_p = A[2p+1][2p] T[2p][2p] -> Xs rows 16p.., then T[2p+1][2p] = T[2p+1][2p+1] X_p
+    const int p1 = (tid >> 6) & 1, i1 = (tid & 63) >> 2, j1 = 4 * (tid & 3);
+    const int o1 = 32 * p1;
+    if (tid < 128) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        const float a = Am[(o1 + 16 + i1) * ld + o1 + m];
+        const float4 t = *reinterpret_cast<const float4 *>(Am + (o1 + m) * ld + o1 + j1);
+        acc = f4_fma(a, t, acc);
+      }
+      *reinterpret_cast<float4 *>(Xs + (16 * p1 + i1) * xld + j1) = acc;
+    }
+    __syncthreads();
+    if (tid < 128) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        const float a = Am[(o1 + 16 + i1) * ld + o1 + 16 + m];
+        const float4 x = *reinterpret_cast<const float4 *>(Xs + (16 * p1 + m) * xld + j1);
+        acc = f4_fma(a, x, acc);
+      }
+      *reinterpret_cast<float4 *>(Am + (o1 + 16 + i1) * ld + o1 + j1) = acc;
+    }
+    __syncthreads();
+    // level 2: X = A[32:][:32] T0 -> Xs, then T[32:][:32] = T1 X (2 columns per thread)
+    const int i2 = tid >> 4, j2 = 2 * (tid & 15);
+    {
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int m = 0; m < 32; ++m) {
+        const float a = Am[(32 + i2) * ld + m];
+        const float2 t = *reinterpret_cast<const float2 *>(Am + m * ld + j2);
+        acc.x = fmaf(a, t.x, acc.x);
+        acc.y = fmaf(a, t.y, acc.y);
+      }
+      *reinterpret_cast<float2 *>(Xs + i2 * xld + j2) = acc;
+    }
+    __syncthreads();
+    {
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int m = 0; m < 32; ++m) {
+        const float a = Am[(32 + i2) * ld + 32 + m];
+        const float2 x = *reinterpret_cast<const float2 *>(Xs + m * xld + j2);
+        acc.x = fmaf(a, x.x, acc.x);
+        acc.y = fmaf(a, x.y, acc.y);
+      }
+      *reinterpret_cast<float2 *>(Am + (32 + i2) * ld + j2) = acc;
+    }
   }
   __syncthreads();
   // T diag(beta) and T diag(beta e^gamma) (+ lo) blocked [64 (i) x 64 (j)]
@@ -348,15 +444,18 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
   const bool g2_ok = mbar_wait(&sm.bar2, 0);
   umma::fence_after_sync();
 
-  // (8) epilogue: TMEM lane = d.  U[i][d] from U^T (warps 0-3), Wt[d][i] = W^T (warps 4-7)
+  // (8) epilogue: TMEM lane = d.  U[i][d] from U^T (warps with (w / 4) % 2 = 0),
+  // Wt[d][i] = W^T (the others); warps w >= 8 take column blocks 2 and 3.
   {
     const int quad = warp & 3, d = 32 * quad + lane;
+    const bool isU = ((warp >> 2) & 1) == 0;
 #pragma unroll
-    for (int cb = 0; cb < kC / 16; ++cb) {
+    for (int cc = 0; cc < 2; ++cc) {
+      const int cb = 2 * (warp >> 3) + cc;
       float v[16];
-      umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + (warp < 4 ? 64 : 128) + 16 * cb, v);
+      umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + (isU ? 64 : 128) + 16 * cb, v);
       umma::wait_ld();
-      if (warp < 4) {
+      if (isU) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) U[(size_t)(16 * cb + e) * kD + d] = v[e];
       } else {
@@ -626,7 +725,7 @@ int launch_kc(const PrefillParams &p, cudaStream_t st) {
     e = cudaFuncSetAttribute(gdn_prefill_state_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2);
   if (e != cudaSuccess) return check_cuda(e, "gdn_prefill attributes");
   note_launch();
-  gdn_prefill_chunk_kernel<KC><<<dim3(p.NC, p.Hv, p.B), kThreads, s1, st>>>(p);
+  gdn_prefill_chunk_kernel<KC><<<dim3(p.Hv, p.NC, p.B), kThreads, s1, st>>>(p);
   if ((e = cudaGetLastError()) != cudaSuccess) return check_cuda(e, "gdn_prefill chunk launch");
 
   cudaLaunchConfig_t cfg = {};
@@ -664,7 +763,7 @@ int gdn_prefill_launch(const q35_gdn_dims *d, int T, const float *mixed_qkv, con
   p.B = d->batch; p.T = T; p.NC = (T + kC - 1) / kC; p.Hk = d->num_k_heads; p.Hv = d->num_v_heads;
   p.rf = p.Hv / p.Hk; p.C = 2 * p.Hk * kD + p.Hv * kD; p.has_prev = has_prev; p.has_init = has_init;
   p.eps = d->eps;
-  Q35_REQUIRE(p.NC <= 2147483647 / 1, Q35_ERR_UNSUPPORTED, "gdn_prefill: too many chunks");
+  Q35_REQUIRE(p.NC <= 65535, Q35_ERR_UNSUPPORTED, "gdn_prefill: seq_len above 65535 chunks of 64");
   switch (d->conv_kernel) {
     case 2: return launch_kc<2>(p, st);
     case 3: return launch_kc<3>(p, st);
