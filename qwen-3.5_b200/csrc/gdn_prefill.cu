@@ -5,33 +5,29 @@
 // causal_conv1d_fn + conv-state capture, :554-615 split/expansion,
 // :189-363 burn_chunk_gated_delta_rule, :651-660 RMSNormGated).
 //
-// Two kernels:
+// Three kernels:
 //  (1) gdn_prefill_chunk_kernel, grid (Hv, chunks, B), fully parallel: causal
 //      conv + SiLU of the chunk's q/k/v channels (3-token halo from the
 //      previous chunk or the cached conv state), l2norm, beta scaling,
 //      cumulative decay gamma, the strictly-lower system
 //      A = -tril((k*beta) k^T o D, -1) and Aqk = (q k^T) o D, the 63-row
-//      forward substitution (text_modules.rs:280-287), T = A + I,
-//      U = T (v*beta), W = T (k*beta*e^gamma), q' = q e^gamma,
-//      k' = k e^(gamma_last - gamma).  The four contractions run on the
-//      tcgen05 tensor cores (3xTF32, TMEM accumulators).  Results go to the
-//      workspace.
-//  (2) gdn_prefill_state_kernel, grid (8, Hv, B) with 8-CTA clusters, walks
-//      the chunks in order; each CTA keeps 16 of the 128 value columns of the
-//      state in shared memory: v' = U - W S, o = q' S + Aqk v',
-//      S <- S e^(gamma_last) + k'^T v', as 4 x 4 register tiles over the
-//      transposed operands (W^T, q'^T, Aqk^T written by kernel 1) with the
-//      contraction split across thread groups.  The next chunk's W^T and U are
-//      prefetched with cp.async during the current one.  The cluster
-//      exchanges per-token sums of squares through distributed shared memory
-//      for the gated RMS norm, and the kernel finally stores the state and the
-//      new conv state.
-#include <cooperative_groups.h>
-
+//      forward substitution (text_modules.rs:280-287) as a blocked inverse,
+//      T = A + I, U = T (v*beta), W = T (k*beta*e^gamma), q' = q e^gamma,
+//      k' = k e^(gamma_last - gamma).  The contractions run on the tcgen05
+//      tensor cores (3xTF32, TMEM accumulators).  Results go to the workspace.
+//  (2) gdn_prefill_state_kernel, grid (8, Hv, B), walks the chunks in order.
+//      The value columns of the state are independent recurrences, so each
+//      CTA keeps 16 of them in shared memory, with no communication:
+//      v' = U - W S, S <- S e^(gamma_last) + k'^T v' as 4 x 4 register tiles
+//      with the contraction split across thread groups, the next chunk's
+//      operands prefetched meanwhile.  It publishes the state at every chunk
+//      start and v', and finally stores the state and the new conv state.
+//  (3) gdn_prefill_output_kernel, grid (Hv, chunks, B), fully parallel:
+//      o = q' S_c + Aqk v' on the tensor cores, then the gated RMS norm.
+//  Only (2) is sequential, and it carries just the two contractions that the
+//  recurrence needs.
 #include "common.cuh"
 #include "umma.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace q35 {
 namespace {
@@ -42,8 +38,20 @@ constexpr int kCS = 16;     // value columns per CTA in the state kernel
 constexpr int kSplit = kD / kCS;
 constexpr int kThreads = 512;  // 16 warps: the chunk phases are latency-bound
 constexpr int kStateThreads = 512;  // state pass: 16 warps hide the shared-memory latency
-// workspace record per (b, h, chunk): U, W, q', k' [64x128] + Aqk [64x64] + decay
-constexpr size_t kRec = 4 * (size_t)kC * kD + (size_t)kC * kC + 16;
+// Workspace record per (b, h, chunk), offsets in floats.  Tiles that the
+// output kernel feeds to the tensor cores are stored in the 8x4-blocked
+// K-major layout of umma.cuh, split into 64-column slabs so that every
+// pipeline stage is one contiguous bulk copy.
+constexpr int kOffU = 0;                  // U [64 t][128 v], row-major
+constexpr int kOffWt = kC * kD;           // W^T [128 k][64 t], row-major
+constexpr int kOffKp = 2 * kC * kD;       // k' [64 t][128 k], row-major
+constexpr int kOffQs = 3 * kC * kD;       // q' [64 t][128 k]: 2 slabs of blocked [64][64]
+constexpr int kOffAq = 4 * kC * kD;       // Aqk [64 i][64 j], blocked
+constexpr int kOffDec = kOffAq + kC * kC; // e^(gamma_last) of the chunk, slot of 64
+constexpr int kOffSc = kOffDec + 64;      // S_c^T [128 v][128 k] (state before the chunk): 2 slabs of blocked [128][64]
+constexpr int kOffVt = kOffSc + kD * kD;  // v'^T [128 v][64 t], blocked
+constexpr size_t kRec = (size_t)kOffVt + (size_t)kD * kC;
+static_assert((kOffSc * 4) % 16 == 0 && (kOffVt * 4) % 16 == 0 && (kRec * 4) % 16 == 0, "16-byte aligned slots");
 
 struct PrefillParams {
   const float *x, *z, *beta, *g, *conv_w, *norm_w;
@@ -255,17 +263,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
   }
   __syncthreads();  // eg / ek ready
 
-  // workspace record: U [64][128] | Wt [128][64] | Qt [128][64] | Kp [64][128] | AqT [64][64] | decay
   float *rec = p.ws + (((size_t)b * p.Hv + h) * p.NC + c) * kRec;
-  float *U = rec, *Wt = rec + kC * kD, *Qt = rec + 2 * kC * kD, *Kp = rec + 3 * kC * kD;
-  float *AqT = rec + 4 * kC * kD;
+  float *U = rec + kOffU, *Wt = rec + kOffWt, *Kp = rec + kOffKp;
 
-  // meanwhile: q' = q e^gamma, stored transposed (Qt[d][i]) (:303-307)
-  for (int cm = warp; cm < (kC / 8) * (kD / 4); cm += kThreads / 32) {
-    const int i = 8 * (cm / (kD / 4)) + lr, d = 4 * (cm % (kD / 4)) + lc;
-    Qt[(size_t)d * kC + i] = qS[blk_off(i, d, kD)] * sm.eg[i];
-  }
-  if (tid == 0) AqT[kC * kC] = expf(sm.gam[kC - 1]);
+  if (tid == 0) rec[kOffDec] = expf(sm.gam[kC - 1]);
 
   const bool g12_ok = mbar_wait(&sm.bar1, 0);
   umma::fence_after_sync();
@@ -286,18 +287,40 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
         const int j = 16 * qtr + jj;
         sm.Am[i][j] = j < i ? -((v[jj] * bi) * expf(gi - sm.gam[j])) : 0.0f;
       }
-    } else {  // Aqk = tril(q k^T o D), stored transposed (AqT[j][i])
+    } else {  // Aqk = tril(q k^T o D), blocked [64 x 64] in the free k_lo slot
       const int i = row - kC;
       const float gi = sm.gam[i];
 #pragma unroll
       for (int jj = 0; jj < 16; ++jj) {
         const int j = 16 * qtr + jj;
-        AqT[(size_t)j * kC + i] = j <= i ? v[jj] * expf(gi - sm.gam[j]) : 0.0f;
+        kL[blk_off(i, j, kC)] = j <= i ? v[jj] * expf(gi - sm.gam[j]) : 0.0f;
       }
     }
-    if (!g12_ok && tid == 0) p.out[0] = __int_as_float(0x7fc00000);
+    if (!g12_ok && tid == 0) rec[kOffDec] = __int_as_float(0x7fc00000);  // poisons state and outputs
   }
-  __syncthreads();  // every warp is done reading q (q'^T above) before k^T overwrites its slot
+  // q' = q e^gamma (:303-307) in place, then q' (as two blocked [64 x 64]
+  // slabs: each 8-row group of the [64 x 128] tile is two 2 KB halves) and
+  // Aqk go to the workspace as bulk copies.  Both slots are overwritten
+  // from (5) on, so thread 0 waits until the copies have read them.
+  for (int f = tid; f < kC * kD / 4; f += kThreads) {
+    const float e = sm.eg[((f >> 8) << 3) + (f & 7)];
+    float4 v = reinterpret_cast<const float4 *>(qS)[f];
+    v = make_float4(v.x * e, v.y * e, v.z * e, v.w * e);
+    reinterpret_cast<float4 *>(qS)[f] = v;
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+#pragma unroll 1
+    for (int rg = 0; rg < kC / 8; ++rg)
+#pragma unroll
+      for (int sl = 0; sl < 2; ++sl)
+        bulk_s2g(rec + kOffQs + sl * kC * 64 + rg * 512, qS + rg * 1024 + sl * 512, 512 * sizeof(float));
+    bulk_s2g(rec + kOffAq, kL, kC * kC * sizeof(float));
+    bulk_commit();
+    bulk_wait_read<0>();
+  }
+  __syncthreads();  // q and the Aqk staging are free from here on
 
   // (5) k^T (blocked [128 x 64]) + lo into the free q / q_lo slots, and
   // k' = k e^(gamma_last - gamma) (:308-311) to the workspace, on warps 2-15
@@ -464,26 +487,33 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
           *reinterpret_cast<float4 *>(Wt + (size_t)d * kC + 16 * cb + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
       }
     }
-    if (!g2_ok && tid == 0) p.out[0] = __int_as_float(0x7fc00000);
+    if (!g2_ok && tid == 0) rec[kOffDec] = __int_as_float(0x7fc00000);
   }
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tb, 256);
+  if (tid == 0) bulk_wait<0>();  // the q' / Aqk copies are complete before the CTA retires
 }
 
+// ---------------------------------------------------------------------------
+// Kernel 2: the sequential pass over the chunks (:314-350 without the output
+// term).  The value columns of the state are independent recurrences, so a
+// CTA owns 16 of them ([128 k x 16 v] in shared memory) and needs no peer:
+//   v' = U - W S,   S <- S e^(gamma_last) + k'^T v'.
+// Per chunk it also publishes, as blocked tiles for the output kernel, the
+// state at the chunk start (S_c^T) and v'^T.  W^T, k' and the decay of the
+// next chunk are fetched by bulk copies (U by cp.async) during the current one.
 struct StateSmem {
-  float Wt[2][kD][kC];  // double-buffered: chunk c+1 is fetched during chunk c
-  float U[2][kC][kCS];
-  float Qt[kD][kC];
-  float Kp[kC][kD];
-  float AqT[kC * kC + 4];  // Aqk^T followed by the chunk decay
-  float Z[kC][kCS];        // gate z of this CTA's 16 columns
-  float Vn[kC][kCS];
-  float S[kD][kCS];
-  float Pv[8][kC][kCS];  // k-split partials of W S, then of q' S + Aqk v'
-                         // (the t-split partials of k'^T v' reuse Wt[buf] once W S is done)
-  float sq[2][kSplit][kC];
-  uint64_t barW[2], barA;
+  float Wt[2][kD][kC];   // W^T of chunks c, c+1
+  float Kp[2][kC][kD];   // k' of chunks c, c+1
+  float U[2][kC][kCS];   // this CTA's 16 columns of U
+  float dec[2][64];      // decay slot of the record
+  float S[kD][kCS];      // the CTA's 16 state columns, [k][v]
+  float Pv[8][kC][kCS];  // k-split partials of W S; then ([4][128][16]) t-split partials of k'^T v'
+  float Vn[kC][kCS];     // v'
+  float Sst[2][2][16 * 64];  // staging of S^T (2 slabs of blocked [16 v x 64 k]), by chunk parity
+  float Vst[2][16 * 64];     // staging of v'^T (blocked [16 v x 64 t]), by chunk parity
+  uint64_t barW[2];
 };
 
 // acc[r] += a[r] * s for a 4 x 4 register tile (rows in a, columns in s).
@@ -494,88 +524,89 @@ __device__ __forceinline__ void tile4(float4 (&acc)[4], float4 a, float4 s) {
   acc[3] = f4_fma(a.w, s, acc[3]);
 }
 
-__device__ __forceinline__ void cluster_arrive_release() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait_acquire() {
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Chunk c's W^T (one bulk copy by thread 0) and U columns (one 16-byte
-// cp.async per thread: 64 rows x 4) into buffer `buf`.
-__device__ __forceinline__ void fetch_wu(StateSmem &sm, const float *rec, int col0, int buf, uint64_t pol,
-                                         int tid) {
+// W^T, k' and the decay of one chunk (bulk copies by thread 0) and this CTA's
+// U columns (one 16-byte cp.async per thread: 64 rows x 4) into buffer `buf`.
+__device__ __forceinline__ void fetch_chunk(StateSmem &sm, const float *rec, int col0, int buf, uint64_t pol,
+                                            int tid) {
   if (tid == 0) {
-    mbar_arrive_expect_tx(&sm.barW[buf], sizeof(sm.Wt[0]));
-    bulk_g2s(&sm.Wt[buf][0][0], rec + kC * kD, sizeof(sm.Wt[0]), &sm.barW[buf], pol);
+    mbar_arrive_expect_tx(&sm.barW[buf], sizeof(sm.Wt[0]) + sizeof(sm.Kp[0]) + sizeof(sm.dec[0]));
+    bulk_g2s(&sm.Wt[buf][0][0], rec + kOffWt, sizeof(sm.Wt[0]), &sm.barW[buf], pol);
+    bulk_g2s(&sm.Kp[buf][0][0], rec + kOffKp, sizeof(sm.Kp[0]), &sm.barW[buf], pol);
+    bulk_g2s(&sm.dec[buf][0], rec + kOffDec, sizeof(sm.dec[0]), &sm.barW[buf], pol);
   }
   if (tid < kC * kCS / 4) {
     const int r = tid >> 2, q4 = tid & 3;
-    cp_async16(&sm.U[buf][r][4 * q4], rec + (size_t)r * kD + col0 + 4 * q4);
+    cp_async16(&sm.U[buf][r][4 * q4], rec + kOffU + (size_t)r * kD + col0 + 4 * q4);
   }
+}
+
+// Thread (r, q4) holds S[r][4 q4 .. 4 q4 + 3]; stage them as S^T rows 4 q4 + e.
+__device__ __forceinline__ void stage_state(float (&st)[2][16 * 64], int r, int q4, float4 a) {
+  using umma::blk_off;
+  float *d = st[r >> 6];
+  const int k = r & 63;
+  d[blk_off(4 * q4 + 0, k, 64)] = a.x;
+  d[blk_off(4 * q4 + 1, k, 64)] = a.y;
+  d[blk_off(4 * q4 + 2, k, 64)] = a.z;
+  d[blk_off(4 * q4 + 3, k, 64)] = a.w;
 }
 
 template <int KC>
 __global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const PrefillParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   StateSmem &sm = *reinterpret_cast<StateSmem *>(smem_raw);
-  cg::cluster_group cluster = cg::this_cluster();
   const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x;
   const int col0 = s * kCS;
   float *Sg = p.rec_state + ((size_t)b * p.Hv + h) * kD * kD;
-  const float *rec0 = p.ws + ((size_t)b * p.Hv + h) * p.NC * kRec;
-  const float *zrow0 = p.z + (size_t)b * p.T * p.Hv * kD + (size_t)h * kD + col0;  // token 0
-  const size_t zstride = (size_t)p.Hv * kD;
+  float *rec0 = p.ws + ((size_t)b * p.Hv + h) * p.NC * kRec;
   uint64_t pol = 0;
 
-  for (int idx = tid; idx < kD * kCS; idx += kStateThreads) {
-    const int r = idx / kCS, cc = idx % kCS;
-    sm.S[r][cc] = p.has_init ? Sg[(size_t)r * kD + col0 + cc] : 0.0f;
-  }
-  if (tid == 0) {
-    mbar_init(&sm.barW[0], 1);
-    mbar_init(&sm.barW[1], 1);
-    mbar_init(&sm.barA, 1);
-    fence_mbar_init();
-    pol = l2_policy_evict_first();
-  }
-  __syncthreads();
-  fetch_wu(sm, rec0, col0, 0, pol, tid);
-  cp_async_commit();
-
-  // thread roles: (kq, iq, cq) for the 64 x 16 products with an 8-way split of
-  // the contraction; (h4, rq, cq) for the 128 x 16 state update (4-way split);
-  // threads < 256 also own one (row, column quad) of the 64 x 16 reductions
+  // thread roles: (kq, iq, cq) for the 64 x 16 product with an 8-way split of
+  // the contraction; (h4, rq, cq) for the 128 x 16 update (4-way split);
+  // threads < 256 also own one (row, column quad) of the 64 x 16 reduction;
+  // (ur, uq) is the float4 of S this thread updates
   const int kq = tid >> 6, iq = (tid & 63) >> 2, cq = tid & 3;
   const int h4 = tid >> 7, rq = (tid & 127) >> 2;
   const int ri = (tid & 255) >> 2;
   const bool red = tid < kC * kCS / 4;
+  const int ur = tid >> 2, uq = tid & 3;
+
+  {  // initial state, also published as S_0 (staging parity 1 = "chunk -1")
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p.has_init) a = *reinterpret_cast<const float4 *>(Sg + (size_t)ur * kD + col0 + 4 * uq);
+    *reinterpret_cast<float4 *>(&sm.S[ur][4 * uq]) = a;
+    stage_state(sm.Sst[1], ur, uq, a);
+  }
+  if (tid == 0) {
+    mbar_init(&sm.barW[0], 1);
+    mbar_init(&sm.barW[1], 1);
+    fence_mbar_init();
+    pol = l2_policy_evict_first();
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    bulk_s2g(rec0 + kOffSc + 16 * 64 * s, sm.Sst[1][0], 16 * 64 * sizeof(float));
+    bulk_s2g(rec0 + kOffSc + kD * 64 + 16 * 64 * s, sm.Sst[1][1], 16 * 64 * sizeof(float));
+    bulk_commit();
+  }
+  fetch_chunk(sm, rec0, col0, 0, pol, tid);
+  cp_async_commit();
+
   // A wait that gives up (ok = false) stops this thread waiting and issuing
-  // copies, but every barrier below is still executed, so no CTA of the
-  // cluster is left behind at a cluster barrier; the output is then poisoned.
+  // copies, but every barrier below is still executed; the final state is
+  // then poisoned.
   bool ok = true;
   for (int c = 0; c < p.NC; ++c) {
     const int buf = c & 1;
-    const float *rec = rec0 + (size_t)c * kRec;
-    if (ok && !mbar_wait(&sm.barW[buf], (c >> 1) & 1)) ok = false;  // W^T of chunk c
+    float *rec = rec0 + (size_t)c * kRec;
+    if (ok && !mbar_wait(&sm.barW[buf], (c >> 1) & 1)) ok = false;  // W^T, k', decay of chunk c
     cp_async_wait<0>();                                                 // U of chunk c
-    __syncthreads();  // previous chunk done with every tile (Qt, Kp, AqT, Z, Wt[buf ^ 1])
-    if (tid == 0 && ok) {
-      // q'^T, k', Aqk^T + decay of chunk c (needed after v')
-      mbar_arrive_expect_tx(&sm.barA, sizeof(sm.Qt) + sizeof(sm.Kp) + sizeof(sm.AqT));
-      bulk_g2s(&sm.Qt[0][0], rec + 2 * kC * kD, sizeof(sm.Qt), &sm.barA, pol);
-      bulk_g2s(&sm.Kp[0][0], rec + 3 * kC * kD, sizeof(sm.Kp), &sm.barA, pol);
-      bulk_g2s(&sm.AqT[0], rec + 4 * kC * kD, sizeof(sm.AqT), &sm.barA, pol);
-    }
-    {  // z of chunk c (used by the output), then the next chunk's W^T and U
-      const int r = tid >> 2, q4 = tid & 3;
-      if (red && c * kC + r < p.T)
-        cp_async16(&sm.Z[r][4 * q4], zrow0 + (size_t)(c * kC + r) * zstride + 4 * q4);
-      cp_async_commit();
-      if (c + 1 < p.NC && ok) fetch_wu(sm, rec + kRec, col0, buf ^ 1, pol, tid);
-      cp_async_commit();
-    }
+    if (tid == 0) bulk_wait_read<1>();  // the stores of chunk c-2 have read staging buffer `buf`
+    __syncthreads();  // chunk c-1 is done with buffer buf ^ 1 and with Pv
+    if (c + 1 < p.NC && ok) fetch_chunk(sm, rec + kRec, col0, buf ^ 1, pol, tid);
+    cp_async_commit();
 
     // v' = U - W S  (:315-324), contraction k split 8 ways
     {
@@ -598,33 +629,22 @@ __global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const 
         v = make_float4(v.x - pv.x, v.y - pv.y, v.z - pv.z, v.w - pv.w);
       }
       *reinterpret_cast<float4 *>(&sm.Vn[ri][4 * cq]) = v;
+      using umma::blk_off;
+      sm.Vst[buf][blk_off(4 * cq + 0, ri, kC)] = v.x;
+      sm.Vst[buf][blk_off(4 * cq + 1, ri, kC)] = v.y;
+      sm.Vst[buf][blk_off(4 * cq + 2, ri, kC)] = v.z;
+      sm.Vst[buf][blk_off(4 * cq + 3, ri, kC)] = v.w;
     }
-    if (ok && !mbar_wait(&sm.barA, c & 1)) ok = false;  // q'^T, k', Aqk^T, z of chunk c
     __syncthreads();
 
-    // o = q' S + Aqk v'  (:325-341) and k'^T v'  (:342-349)
-    float(*Ps)[kD][kCS] = reinterpret_cast<float(*)[kD][kCS]>(&sm.Wt[buf][0][0]);  // [4][128][16]
+    // k'^T v'  (:342-349), contraction t split 4 ways
+    float(*Ps)[kD][kCS] = reinterpret_cast<float(*)[kD][kCS]>(&sm.Pv[0][0][0]);  // [4][128][16]
     {
-      float4 acc[4] = {};
-#pragma unroll 8
-      for (int kk = 0; kk < kD / 8; ++kk) {
-        const int k = (kD / 8) * kq + kk;
-        tile4(acc, *reinterpret_cast<const float4 *>(&sm.Qt[k][4 * iq]),
-              *reinterpret_cast<const float4 *>(&sm.S[k][4 * cq]));
-      }
-#pragma unroll 8
-      for (int jj = 0; jj < kC / 8; ++jj) {
-        const int j = (kC / 8) * kq + jj;
-        tile4(acc, *reinterpret_cast<const float4 *>(&sm.AqT[j * kC + 4 * iq]),
-              *reinterpret_cast<const float4 *>(&sm.Vn[j][4 * cq]));
-      }
-#pragma unroll
-      for (int r = 0; r < 4; ++r) *reinterpret_cast<float4 *>(&sm.Pv[kq][4 * iq + r][4 * cq]) = acc[r];
       float4 acs[4] = {};
 #pragma unroll 8
       for (int tt = 0; tt < kC / 4; ++tt) {
         const int t = (kC / 4) * h4 + tt;
-        tile4(acs, *reinterpret_cast<const float4 *>(&sm.Kp[t][4 * rq]),
+        tile4(acs, *reinterpret_cast<const float4 *>(&sm.Kp[buf][t][4 * rq]),
               *reinterpret_cast<const float4 *>(&sm.Vn[t][4 * cq]));
       }
 #pragma unroll
@@ -632,66 +652,35 @@ __global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const 
     }
     __syncthreads();
 
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 pv = *reinterpret_cast<const float4 *>(&sm.Pv[q][ri][4 * cq]);
-      o = make_float4(o.x + pv.x, o.y + pv.y, o.z + pv.z, o.w + pv.w);
-    }
-    // per-token partial sum of squares over this CTA's 16 columns -> every
-    // CTA of the cluster (double-buffered by chunk parity); the cluster
-    // barrier is split so the state update runs while it completes
-    float ss = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    if (red) {
-      *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq) = ss;
-      *cluster.map_shared_rank(&sm.sq[c & 1][s][ri], 2 * cq + 1) = ss;
-    }
-    cluster_arrive_release();
-
-    // S <- S * decay + k'^T v'  (one float4 of the 128 x 16 state per thread)
+    // S <- S e^(gamma_last) + k'^T v'  (:350); publish it as S_{c+1}
     {
-      const float dec = sm.AqT[kC * kC];
-      const int r = tid >> 2, q4 = tid & 3;
-      float4 a = *reinterpret_cast<const float4 *>(&sm.S[r][4 * q4]);
-      float4 ps = *reinterpret_cast<const float4 *>(&Ps[0][r][4 * q4]);
+      const float dec = sm.dec[buf][0];
+      float4 a = *reinterpret_cast<const float4 *>(&sm.S[ur][4 * uq]);
+      float4 ps = *reinterpret_cast<const float4 *>(&Ps[0][ur][4 * uq]);
 #pragma unroll
       for (int q = 1; q < 4; ++q) {
-        const float4 pq = *reinterpret_cast<const float4 *>(&Ps[q][r][4 * q4]);
+        const float4 pq = *reinterpret_cast<const float4 *>(&Ps[q][ur][4 * uq]);
         ps = make_float4(ps.x + pq.x, ps.y + pq.y, ps.z + pq.z, ps.w + pq.w);
       }
       a = make_float4(a.x * dec + ps.x, a.y * dec + ps.y, a.z * dec + ps.z, a.w * dec + ps.w);
-      *reinterpret_cast<float4 *>(&sm.S[r][4 * q4]) = a;
-      fence_proxy_async_smem();  // Ps (in Wt[buf]) is refilled by a bulk copy next chunk
+      *reinterpret_cast<float4 *>(&sm.S[ur][4 * uq]) = a;
+      if (c + 1 < p.NC) stage_state(sm.Sst[buf], ur, uq, a);
     }
-
-    cp_async_wait<1>();      // z of this chunk (the next chunk's U may still be in flight)
-    cluster_wait_acquire();  // all sums of squares of this chunk have arrived
-    const int t = c * kC + ri;
-    if (red && t < p.T) {
-      float tot = 0.0f;
-#pragma unroll
-      for (int j = 0; j < kSplit; ++j) tot += sm.sq[c & 1][j][ri];
-      const float inv = 1.0f / sqrtf(tot / (float)kD + p.eps);
-      const size_t obase = ((size_t)b * p.T + t) * p.Hv * kD + (size_t)h * kD + col0 + 4 * cq;
-      const float4 zv = *reinterpret_cast<const float4 *>(&sm.Z[ri][4 * cq]);
-      const float4 wv = *reinterpret_cast<const float4 *>(p.norm_w + col0 + 4 * cq);
-      float4 r;
-      r.x = (wv.x * (o.x * inv)) * siluf_dev(zv.x);
-      r.y = (wv.y * (o.y * inv)) * siluf_dev(zv.y);
-      r.z = (wv.z * (o.z * inv)) * siluf_dev(zv.z);
-      r.w = (wv.w * (o.w * inv)) * siluf_dev(zv.w);
-      *reinterpret_cast<float4 *>(p.out + obase) = r;
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      bulk_s2g(rec + kOffVt + 16 * kC * s, sm.Vst[buf], 16 * kC * sizeof(float));
+      if (c + 1 < p.NC) {
+        bulk_s2g(rec + kRec + kOffSc + 16 * 64 * s, sm.Sst[buf][0], 16 * 64 * sizeof(float));
+        bulk_s2g(rec + kRec + kOffSc + kD * 64 + 16 * 64 * s, sm.Sst[buf][1], 16 * 64 * sizeof(float));
+      }
+      bulk_commit();
     }
   }
-  if (!ok) p.out[0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison the output
   cp_async_wait<0>();
-  __syncthreads();
-  for (int idx = tid; idx < kD * kCS; idx += kStateThreads) {
-    const int r = idx / kCS, cc = idx % kCS;
-    Sg[(size_t)r * kD + col0 + cc] = sm.S[r][cc];
-  }
+  *reinterpret_cast<float4 *>(Sg + (size_t)ur * kD + col0 + 4 * uq) =
+      *reinterpret_cast<const float4 *>(&sm.S[ur][4 * uq]);
+  if (!ok && tid == 0) Sg[col0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison the state
 
   // new conv state = last K-1 inputs of [history, x] (:538-540): v channels of
   // this CTA's columns, and (first value head of the key head) 32 of its 256
@@ -713,35 +702,175 @@ __global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const 
     const int li = s * (2 * kD / kSplit) + (tid - 32);
     write_conv(li < kD ? hk * kD + li : p.Hk * kD + hk * kD + (li - kD));
   }
-  cluster.sync();  // keep shared memory alive until all remote stores landed
+  if (tid == 0) bulk_wait<0>();  // every published tile is complete before the CTA retires
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 3: per (chunk, head), fully parallel, on the tensor cores:
+//   o^T [128 v x 64 t] = S_c^T q'^T + v'^T Aqk^T   (:325-341)
+// in three K = 64 stages (S_c^T / q' slab 0, slab 1, then v'^T / Aqk), each a
+// bulk copy into one of two shared-memory buffers; the lo terms of the
+// 3xTF32 split are formed in place.  Epilogue: gated RMS norm over the 128
+// values of each token (:651-660, :85-117) and the output store.
+constexpr int kOutThreads = 256;
+struct OutSmem {
+  float A[2][2][kD * 64];  // [buffer][hi, lo], blocked [128 x 64]
+  float Bm[2][2][kC * 64]; // [buffer][hi, lo], blocked [64 x 64]
+  float part[4][kC];
+  float inv[kC];
+  uint32_t tbase;
+  uint64_t barL[2], barM[2];
+};
+
+__global__ void __launch_bounds__(kOutThreads, 1) gdn_prefill_output_kernel(const PrefillParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  OutSmem &sm = *reinterpret_cast<OutSmem *>(smem_raw);
+  const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t0 = c * kC;
+  const float *rec = p.ws + (((size_t)b * p.Hv + h) * p.NC + c) * kRec;
+  constexpr uint32_t kStageBytes = (kD * 64 + kC * 64) * sizeof(float);
+
+  if (warp == 0) {
+    umma::tmem_alloc(&sm.tbase, 64);
+    umma::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.barL[i], 1);
+      mbar_init(&sm.barM[i], 1);
+    }
+    fence_mbar_init();
+    const uint64_t pol = l2_policy_evict_first();
+    for (int sl = 0; sl < 2; ++sl) {
+      mbar_arrive_expect_tx(&sm.barL[sl], kStageBytes);
+      bulk_g2s(sm.A[sl][0], rec + kOffSc + sl * kD * 64, kD * 64 * sizeof(float), &sm.barL[sl], pol);
+      bulk_g2s(sm.Bm[sl][0], rec + kOffQs + sl * kC * 64, kC * 64 * sizeof(float), &sm.barL[sl], pol);
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tb = sm.tbase;
+  const uint32_t id = umma::idesc_tf32(128, 64, 0, 0);
+  bool ok = true;
+
+#pragma unroll 1
+  for (int st = 0; st < 3; ++st) {
+    const int buf = st & 1;
+    if (ok && !mbar_wait(&sm.barL[buf], st >> 1)) ok = false;
+    {  // lo terms
+      const float4 *ah = reinterpret_cast<const float4 *>(sm.A[buf][0]);
+      float4 *al = reinterpret_cast<float4 *>(sm.A[buf][1]);
+      for (int e = tid; e < kD * 64 / 4; e += kOutThreads) {
+        const float4 v = ah[e];
+        al[e] = make_float4(umma::tf32_lo(v.x), umma::tf32_lo(v.y), umma::tf32_lo(v.z), umma::tf32_lo(v.w));
+      }
+      const float4 *bh = reinterpret_cast<const float4 *>(sm.Bm[buf][0]);
+      float4 *bl = reinterpret_cast<float4 *>(sm.Bm[buf][1]);
+      for (int e = tid; e < kC * 64 / 4; e += kOutThreads) {
+        const float4 v = bh[e];
+        bl[e] = make_float4(umma::tf32_lo(v.x), umma::tf32_lo(v.y), umma::tf32_lo(v.z), umma::tf32_lo(v.w));
+      }
+    }
+    fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    if (tid == 0) {
+      constexpr uint32_t sbo = (64 / 4) * 128;
+#pragma unroll 1
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t ah = umma::smem_desc(sm.A[buf][0] + ks * 64, 128, sbo);
+        const uint64_t al = umma::smem_desc(sm.A[buf][1] + ks * 64, 128, sbo);
+        const uint64_t bh = umma::smem_desc(sm.Bm[buf][0] + ks * 64, 128, sbo);
+        const uint64_t bl = umma::smem_desc(sm.Bm[buf][1] + ks * 64, 128, sbo);
+        umma::mma_tf32(tb, ah, bh, id, (st > 0 || ks > 0) ? 1u : 0u);
+        umma::mma_tf32(tb, ah, bl, id, 1);
+        umma::mma_tf32(tb, al, bh, id, 1);
+      }
+      umma::commit(&sm.barM[buf]);
+      if (st == 0) {  // buffer 0 takes v'^T / Aqk once stage 0's MMAs have read it
+        if (ok && !mbar_wait(&sm.barM[0], 0)) ok = false;
+        if (ok) {
+          const uint64_t pol = l2_policy_evict_first();
+          mbar_arrive_expect_tx(&sm.barL[0], kStageBytes);
+          bulk_g2s(sm.A[0][0], rec + kOffVt, kD * 64 * sizeof(float), &sm.barL[0], pol);
+          bulk_g2s(sm.Bm[0][0], rec + kOffAq, kC * 64 * sizeof(float), &sm.barL[0], pol);
+        }
+      }
+    }
+  }
+  if (ok && !mbar_wait(&sm.barM[0], 1)) ok = false;  // stage 2 (and so every MMA) complete
+  umma::fence_after_sync();
+
+  // epilogue: TMEM lane = value column v; warps w and w + 4 take tokens
+  // 0-31 and 32-63 of lane quadrant w % 4
+  const int quad = warp & 3, half = warp >> 2;
+  const int v = 32 * quad + lane;
+  float o[32];
+  umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + 32 * half, *reinterpret_cast<float(*)[16]>(&o[0]));
+  umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + 32 * half + 16, *reinterpret_cast<float(*)[16]>(&o[16]));
+  umma::wait_ld();
+  {  // per-token sum of squares over the warp's 32 values: reduce-scatter, lane l ends with token 32 half + l
+    float sq[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sq[j] = o[j] * o[j];
+#pragma unroll
+    for (int w = 16; w >= 1; w >>= 1) {
+      const bool upper = (lane & w) != 0;
+#pragma unroll
+      for (int j = 0; j < w; ++j) {
+        const float send = upper ? sq[j] : sq[j + w];
+        const float keep = upper ? sq[j + w] : sq[j];
+        sq[j] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+      }
+    }
+    sm.part[quad][32 * half + lane] = sq[0];
+  }
+  __syncthreads();
+  if (tid < kC) {
+    const float tot = sm.part[0][tid] + sm.part[1][tid] + sm.part[2][tid] + sm.part[3][tid];
+    sm.inv[tid] = 1.0f / sqrtf(tot / (float)kD + p.eps);
+  }
+  __syncthreads();
+  const float wv = p.norm_w[v];
+  const size_t rs = (size_t)p.Hv * kD;
+  const float *zb = p.z + ((size_t)b * p.T + t0 + 32 * half) * rs + (size_t)h * kD + v;
+  float *ob = p.out + ((size_t)b * p.T + t0 + 32 * half) * rs + (size_t)h * kD + v;
+  const int nt = min(32, p.T - t0 - 32 * half);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < nt) {
+      const float zv = zb[(size_t)j * rs];
+      ob[(size_t)j * rs] = (wv * (o[j] * sm.inv[32 * half + j])) * siluf_dev(zv);
+    }
+  }
+  if (!ok && tid == 0 && nt > 0) ob[0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tb, 64);
 }
 
 template <int KC>
 int launch_kc(const PrefillParams &p, cudaStream_t st) {
-  const size_t s1 = sizeof(ChunkSmem), s2 = sizeof(StateSmem);
+  const size_t s1 = sizeof(ChunkSmem), s2 = sizeof(StateSmem), s3 = sizeof(OutSmem);
   cudaError_t e = cudaFuncSetAttribute(gdn_prefill_chunk_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)s1);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(gdn_prefill_state_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s2);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gdn_prefill_output_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s3);
   if (e != cudaSuccess) return check_cuda(e, "gdn_prefill attributes");
   note_launch();
   gdn_prefill_chunk_kernel<KC><<<dim3(p.Hv, p.NC, p.B), kThreads, s1, st>>>(p);
   if ((e = cudaGetLastError()) != cudaSuccess) return check_cuda(e, "gdn_prefill chunk launch");
-
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kSplit, p.Hv, p.B);
-  cfg.blockDim = dim3(kStateThreads, 1, 1);
-  cfg.dynamicSmemBytes = s2;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kSplit;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   note_launch();
-  return check_cuda(cudaLaunchKernelEx(&cfg, gdn_prefill_state_kernel<KC>, p), "gdn_prefill state launch");
+  gdn_prefill_state_kernel<KC><<<dim3(kSplit, p.Hv, p.B), kStateThreads, s2, st>>>(p);
+  if ((e = cudaGetLastError()) != cudaSuccess) return check_cuda(e, "gdn_prefill state launch");
+  note_launch();
+  gdn_prefill_output_kernel<<<dim3(p.Hv, p.NC, p.B), kOutThreads, s3, st>>>(p);
+  return check_cuda(cudaGetLastError(), "gdn_prefill output launch");
 }
 
 }  // namespace
