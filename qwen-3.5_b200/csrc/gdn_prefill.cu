@@ -755,6 +755,18 @@ __global__ void __launch_bounds__(kOutThreads, 1) gdn_prefill_output_kernel(cons
   const uint32_t id = umma::idesc_tf32(128, 64, 0, 0);
   bool ok = true;
 
+  // the gate z of this thread's 32 (token, value) outputs, requested now so
+  // that the loads overlap the contractions: TMEM lane = value column v,
+  // warps w and w + 4 take tokens 0-31 and 32-63 of lane quadrant w % 4
+  const int quad = warp & 3, half = warp >> 2;
+  const int v = 32 * quad + lane;
+  const size_t rs = (size_t)p.Hv * kD;
+  const int nt = min(32, p.T - t0 - 32 * half);
+  const float *__restrict__ zb = p.z + ((size_t)b * p.T + t0 + 32 * half) * rs + (size_t)h * kD + v;
+  float zv[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) zv[j] = j < nt ? __ldg(zb + (size_t)j * rs) : 0.0f;
+
 #pragma unroll 1
   for (int st = 0; st < 3; ++st) {
     const int buf = st & 1;
@@ -804,10 +816,7 @@ __global__ void __launch_bounds__(kOutThreads, 1) gdn_prefill_output_kernel(cons
   if (ok && !mbar_wait(&sm.barM[0], 1)) ok = false;  // stage 2 (and so every MMA) complete
   umma::fence_after_sync();
 
-  // epilogue: TMEM lane = value column v; warps w and w + 4 take tokens
-  // 0-31 and 32-63 of lane quadrant w % 4
-  const int quad = warp & 3, half = warp >> 2;
-  const int v = 32 * quad + lane;
+  // epilogue
   float o[32];
   umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + 32 * half, *reinterpret_cast<float(*)[16]>(&o[0]));
   umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + 32 * half + 16, *reinterpret_cast<float(*)[16]>(&o[16]));
@@ -835,17 +844,10 @@ __global__ void __launch_bounds__(kOutThreads, 1) gdn_prefill_output_kernel(cons
   }
   __syncthreads();
   const float wv = p.norm_w[v];
-  const size_t rs = (size_t)p.Hv * kD;
-  const float *zb = p.z + ((size_t)b * p.T + t0 + 32 * half) * rs + (size_t)h * kD + v;
-  float *ob = p.out + ((size_t)b * p.T + t0 + 32 * half) * rs + (size_t)h * kD + v;
-  const int nt = min(32, p.T - t0 - 32 * half);
+  float *__restrict__ ob = p.out + ((size_t)b * p.T + t0 + 32 * half) * rs + (size_t)h * kD + v;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (j < nt) {
-      const float zv = zb[(size_t)j * rs];
-      ob[(size_t)j * rs] = (wv * (o[j] * sm.inv[32 * half + j])) * siluf_dev(zv);
-    }
-  }
+  for (int j = 0; j < 32; ++j)
+    if (j < nt) ob[(size_t)j * rs] = (wv * (o[j] * sm.inv[32 * half + j])) * siluf_dev(zv[j]);
   if (!ok && tid == 0 && nt > 0) ob[0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison
   umma::fence_before_sync();
   __syncthreads();
