@@ -661,12 +661,60 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seqs", type=int, default=NSEQ, help="total sequences (256 = config 4; smaller for ncu)")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 0/1/2 side measurements")
+    ap.add_argument("--prefill-tokens", type=int, default=0,
+                    help="only run the config-2 GDN prefill at this prompt length (profiling aid)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         return run_reference(args)
+    if args.prefill_tokens > 0:
+        return run_prefill_only(args)
     return run_gpu(args)
+
+
+def run_prefill_only(args):
+    """Config-2 shapes (B=1, 16 heads, conv 4) at --prefill-tokens tokens:
+    --warmup untimed calls, then --steps calls timed with CUDA events.  Prints
+    one JSON line; it is a profiling aid, not the bench line."""
+    import torch
+
+    import q35attn
+    dev = torch.device("cuda:0")
+    T = args.prefill_tokens
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+
+    def randn(*shape, scale=1.0):
+        t = torch.empty(*shape, device=dev, dtype=torch.float32)
+        t.normal_(0.0, scale, generator=gen)
+        return t
+
+    x, z = randn(1, T, CONV), randn(1, T, HV * DK)
+    g = -torch.nn.functional.softplus(randn(1, T, HV))
+    beta = torch.sigmoid(randn(1, T, HV))
+    conv_w, norm_w = randn(CONV, KCONV, scale=0.5), torch.ones(DK, device=dev)
+    S, cst = torch.zeros(1, HV, DK, DK, device=dev), torch.zeros(1, CONV, KCONV - 1, device=dev)
+    out = torch.empty(1, T, HV * DK, device=dev)
+    ws = q35attn.gdn_prefill_workspace(1, T, HK, HV, device=dev)
+
+    def call():
+        q35attn.gdn_prefill(x, z, beta, g, conv_w, norm_w, cst, S, out, num_k_heads=HK, num_v_heads=HV,
+                            workspace=ws)
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        call()
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / args.steps
+    print(json.dumps({"case": "gdn_prefill", "tokens": T, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_call": ms, "tokens_per_s": T / ms * 1e3,
+                      "launches_per_call": 3}))
+    return 0
 
 
 if __name__ == "__main__":
