@@ -573,6 +573,30 @@ def run_extras(dev, reps=3):
     res["config2_gdn_prefill_T8192"] = {"ms": t * 1e3, "tokens_per_s": T2 / t, "alg_bytes": by2,
                                         "achieved_gbs": by2 / t / 1e9, "alg_gflop": fl2 / 1e9,
                                         "achieved_tflops": fl2 / t / 1e12}
+    del xp, zp, gp, bp, op, wsp
+
+    # Q8F decode GEMV (kernels.rs:103-165) at the 2B projection shapes; the
+    # timed calls rotate over enough weight copies to exceed L2 (126 MB)
+    gemv = {}
+    for name, ind, outd in (("in_proj_qkv", 2048, 6144), ("o_proj", 2048, 2048), ("down_proj", 6144, 2048),
+                            ("lm_head", 2048, 248320)):
+        wbytes = ind * outd + ind * (outd // 64) * 4
+        ncopy = max(1, -(-(256 << 20) // wbytes))
+        ws_ = [torch.randint(-2**31, 2**31 - 1, (ind, outd // 4), dtype=torch.int32, device=dev)
+               for _ in range(ncopy)]
+        ss_ = [torch.rand(ind, outd // 64, device=dev) * 0.01 for _ in range(ncopy)]
+        xg, yg = randn(ind), torch.empty(outd, device=dev)
+        calls = 64
+
+        def gcall():
+            for i in range(calls):
+                q35attn.q8_gemv(xg, ws_[i % ncopy], ss_[i % ncopy], yg, mode=0)
+        tg = timed_graph(gcall, reps) / calls
+        by = wbytes + 4 * (ind + outd)
+        gemv[name] = {"in": ind, "out": outd, "us": tg * 1e6, "alg_bytes": by, "achieved_gbs": by / tg / 1e9,
+                      "weight_copies": ncopy}
+        del ws_, ss_
+    res["q8_gemv"] = gemv
     return res
 
 

@@ -127,6 +127,27 @@ int q35_gdn_gate(int32_t n_rows, int32_t in_dim, int32_t num_heads,
                  float *g, int32_t mode, void *stream);
 
 /* --------------------------------------------------------------------------
+ * Q8F split-K GEMV y = x^T W, the decode projections of both layer types.
+ * Replaces q8_gemv_partial_sum_kernel + q8_gemv_sum_reduction_kernel
+ * (kernels.rs:103-165; host side :495-537, called from text_modules.rs:498,
+ * 505, 662, 856, 877, 886, 939, 1003-1005).
+ *   x       [in_dim] f32
+ *   w       [in_dim, out_dim/4] u32: byte j (little-endian) of word c is the
+ *           int8 weight of column 4c + j
+ *   scales  [in_dim, out_dim/64] f32, one per (input row, 64-column block)
+ *   y       [out_dim] f32
+ *   mode    0: every input row.  1: only the rows the reference's kernel
+ *           covers (per split s: rows s*chunk .. s*chunk + (chunk/8)*8 - 1,
+ *           chunk = in_dim/splits, splits = clamp(25000/out_dim, 1,
+ *           max(in_dim/80, 1)); kernels.rs:119-131, :504).
+ * out_dim must be a multiple of 64; w must be 16-byte aligned.  No workspace:
+ * the split-K partial sums are added inside a thread-block cluster.
+ */
+int q35_q8_gemv(int32_t in_dim, int32_t out_dim, const float *x,
+                const uint32_t *w, const float *scales, float *y,
+                int32_t mode, void *stream);
+
+/* --------------------------------------------------------------------------
  * Gated GQA, one decode step.  Replaces text_modules.rs:866-936 of
  * Attention::forward (:842-944): q/gate split of q_proj, q_norm/k_norm
  * (RMSNorm 1+w, :800-809), partial RoPE (:754-774), KV-cache append

@@ -24,6 +24,8 @@ int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_g
 int gqa_combine_launch(int B, int Hq, int n_parts, const float *parts, const float *q_gate, float *out,
                        cudaStream_t st);
 size_t gdn_prefill_workspace_bytes(const q35_gdn_dims *d, int T);
+int q8_gemv_launch(int in_dim, int out_dim, const float *x, const uint32_t *w, const float *scales, float *y,
+                   int mode, cudaStream_t st);
 int gdn_prefill_launch(const q35_gdn_dims *d, int T, const float *mixed_qkv, const float *z, const float *beta,
                        const float *g, const float *conv_w, const float *norm_w, float *conv_state, int has_prev,
                        float *rec_state, int has_init, float *out, void *ws, size_t ws_bytes, cudaStream_t st);
@@ -170,6 +172,16 @@ int q35_gdn_gate(int32_t n_rows, int32_t in_dim, int32_t num_heads, const float 
   if (int rc = require_sm100()) return rc;
   return gdn_gate_launch(n_rows, in_dim, num_heads, x, w_b, w_a, a_log, dt_bias, beta, g, mode,
                          static_cast<cudaStream_t>(stream));
+}
+
+int q35_q8_gemv(int32_t in_dim, int32_t out_dim, const float *x, const uint32_t *w, const float *scales, float *y,
+                int32_t mode, void *stream) {
+  Q35_REQUIRE(in_dim > 0 && out_dim > 0, Q35_ERR_INVALID_ARG, "q8_gemv: in_dim and out_dim must be > 0");
+  Q35_REQUIRE(out_dim % 64 == 0, Q35_ERR_UNSUPPORTED, "q8_gemv: out_dim must be a multiple of 64 (Q8F block)");
+  Q35_REQUIRE(mode == 0 || mode == 1, Q35_ERR_INVALID_ARG, "q8_gemv: mode must be 0 or 1");
+  Q35_PTR(x); Q35_PTR16(w); Q35_PTR(scales); Q35_PTR(y);
+  if (int rc = require_sm100()) return rc;
+  return q8_gemv_launch(in_dim, out_dim, x, w, scales, y, mode, static_cast<cudaStream_t>(stream));
 }
 
 size_t q35_gqa_decode_workspace_size(const q35_gqa_dims *dims, int64_t max_len) {

@@ -1,12 +1,13 @@
 """q35attn -- B200 (sm_100a) attention hot path of the Qwen3.5 hybrid decoder.
 
-Gated DeltaNet (decode, chunked prefill, gate projection) and gated GQA
-flash-decode, behind the C ABI of include/q35attn.h.  The Python layer is a
+Gated DeltaNet (decode, chunked prefill, gate projection), gated GQA
+flash-decode and the Q8F decode GEMV, behind the C ABI of include/q35attn.h.  The Python layer is a
 thin ctypes binding over device pointers; all math runs in libq35attn.so.
 """
 from ._lib import (GdnDims, GqaDims, LIB_PATH, Q35Error, STATUS_CACHE_FULL, STATUS_LEN_HINT,  # noqa: F401
                    STATUS_WAIT_TIMEOUT, load)
-from .ops import (GqaWorkspace, gdn_decode, gdn_gate, gdn_prefill, gdn_prefill_workspace,  # noqa: F401
-                  gqa_combine_partials, gqa_decode, gqa_decode_partial, launch_count)
+from .ops import (GqaWorkspace, gdn_decode, gdn_gate, gdn_prefill,  # noqa: F401
+                  gdn_prefill_workspace, gqa_combine_partials, gqa_decode, gqa_decode_partial, launch_count,
+                  q8_gemv)
 
 __version__ = "0.1.0"

@@ -49,6 +49,7 @@ SIGNATURES = {
     "q35_gdn_prefill": (C.c_int, [C.POINTER(GdnDims), _I32, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _I32, _P, _P, _SZ,
                                   _P]),
     "q35_gdn_gate": (C.c_int, [_I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _I32, _P]),
+    "q35_q8_gemv": (C.c_int, [_I32, _I32, _P, _P, _P, _P, _I32, _P]),
     "q35_gqa_decode_workspace_size": (_SZ, [C.POINTER(GqaDims), _I64]),
     "q35_workspace_init": (C.c_int, [_P, _SZ, _P]),
     "q35_gqa_decode": (C.c_int, [C.POINTER(GqaDims), _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),

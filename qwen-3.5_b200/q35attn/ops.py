@@ -13,7 +13,7 @@ import torch
 from ._lib import GdnDims, GqaDims, Q35Error, check, load
 
 __all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_workspace", "gdn_gate", "GqaWorkspace", "gqa_decode",
-           "launch_count", "Q35Error"]
+           "q8_gemv", "launch_count", "Q35Error"]
 
 
 def _req(t: torch.Tensor, name: str, dtype=torch.float32) -> int:
@@ -97,6 +97,21 @@ def gdn_gate(x, w_b, w_a, a_log, dt_bias, mode=0, beta=None, g=None, stream=None
                               _req(dt_bias, "dt_bias"), _req(beta, "beta"), _req(g, "g"), int(mode),
                               _stream(stream)))
     return beta, g
+
+
+def q8_gemv(x, w, scales, y=None, *, mode=0, stream=None):
+    """y [out] = x [in] @ W for a Q8F matrix: w [in, out/4] int32/uint32 words
+    (4 little-endian int8 columns each), scales [in, out/64].  mode 1 covers
+    only the rows the reference's split-K kernel covers."""
+    in_dim = x.numel()
+    out_dim = w.shape[1] * 4
+    if w.dtype not in (torch.int32, torch.uint32) or not w.is_contiguous() or w.device.type != "cuda":
+        raise TypeError("w must be a contiguous int32/uint32 CUDA tensor")
+    if y is None:
+        y = torch.empty(out_dim, device=x.device, dtype=torch.float32)
+    check(load().q35_q8_gemv(in_dim, out_dim, _req(x, "x"), w.data_ptr(), _req(scales, "scales"), _req(y, "y"),
+                             int(mode), _stream(stream)))
+    return y
 
 
 def gqa_dims(batch, num_q_heads, num_kv_heads, capacity, rotary_dim=64, eps=1e-6, head_dim=256) -> GqaDims:
