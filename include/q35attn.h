@@ -177,6 +177,32 @@ int q35_gqa_decode(const q35_gqa_dims *dims, int64_t max_len,
                    int32_t *lens, float *out, void *workspace,
                    size_t workspace_bytes, void *stream);
 
+/* --------------------------------------------------------------------------
+ * Gated GQA over a prompt of T tokens (prefill).  Replaces Attention::forward
+ * (text_modules.rs:842-944) for seq_len = T: the same per-token steps as
+ * q35_gqa_decode, with the causal mask of model.rs:59-67 (prompt token t sees
+ * keys 0 .. lens[b] + t).  Appends T keys / values at lens[b] and adds T to
+ * lens[b].
+ *   q_gate   [B, T, Hq, 2*D]   k_new, v_new [B, T, Hkv, D]
+ *   cos, sin [B, T, rotary_dim] (NULL allowed when rotary_dim == 0)
+ *   out      [B, T, Hq*D]
+ *   max_len  host upper bound on lens[b] + T over the batch (sizes the
+ *            workspace; sequences beyond it or beyond the capacity are
+ *            skipped and flagged in the workspace status word).
+ *   workspace >= q35_gqa_prefill_workspace_size(dims, T, max_len) bytes,
+ *            256-byte aligned; its first word is the status word read by
+ *            q35_workspace_status.
+ * Requires num_q_heads + num_kv_heads <= 32 and head_dim 256.
+ */
+size_t q35_gqa_prefill_workspace_size(const q35_gqa_dims *dims, int32_t seq_len,
+                                      int64_t max_len);
+int q35_gqa_prefill(const q35_gqa_dims *dims, int32_t seq_len, int64_t max_len,
+                    const float *q_gate, const float *k_new, const float *v_new,
+                    const float *qn_w, const float *kn_w, const float *cos,
+                    const float *sin, float *k_cache, float *v_cache,
+                    int32_t *lens, float *out, void *workspace,
+                    size_t workspace_bytes, void *stream);
+
 /* Context-parallel form of q35_gqa_decode for one shard of a KV cache split
  * along its length across GPUs (text_modules.rs:899-928 with the keys
  * partitioned; no reference counterpart for the partitioning itself).

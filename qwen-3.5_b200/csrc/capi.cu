@@ -21,6 +21,11 @@ int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_g
                       const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
                       const float *sin, float *k_cache, float *v_cache, int32_t *lens, float *out,
                       void *ws, size_t ws_bytes, cudaStream_t st, float *part_out);
+size_t gqa_prefill_workspace_bytes(int B, int T, int Hq, int Hkv, long long max_len);
+int gqa_prefill_launch(const q35_gqa_dims *d, int T, long long max_len, const float *q_gate, const float *k_new,
+                       const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
+                       const float *sin, float *k_cache, float *v_cache, int32_t *lens, float *out, void *ws,
+                       size_t ws_bytes, cudaStream_t st);
 int gqa_combine_launch(int B, int Hq, int n_parts, const float *parts, const float *q_gate, float *out,
                        cudaStream_t st);
 size_t gdn_prefill_workspace_bytes(const q35_gdn_dims *d, int T);
@@ -182,6 +187,32 @@ int q35_q8_gemv(int32_t in_dim, int32_t out_dim, const float *x, const uint32_t 
   Q35_PTR(x); Q35_PTR16(w); Q35_PTR(scales); Q35_PTR(y);
   if (int rc = require_sm100()) return rc;
   return q8_gemv_launch(in_dim, out_dim, x, w, scales, y, mode, static_cast<cudaStream_t>(stream));
+}
+
+size_t q35_gqa_prefill_workspace_size(const q35_gqa_dims *dims, int32_t seq_len, int64_t max_len) {
+  if (check_gqa_dims(dims) != Q35_OK || seq_len <= 0 || max_len < seq_len) return 0;
+  return gqa_prefill_workspace_bytes(dims->batch, seq_len, dims->num_q_heads, dims->num_kv_heads, max_len);
+}
+
+int q35_gqa_prefill(const q35_gqa_dims *dims, int32_t seq_len, int64_t max_len, const float *q_gate,
+                    const float *k_new, const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
+                    const float *sin, float *k_cache, float *v_cache, int32_t *lens, float *out, void *workspace,
+                    size_t workspace_bytes, void *stream) {
+  if (int rc = check_gqa_dims(dims)) return rc;
+  Q35_REQUIRE(seq_len >= 0, Q35_ERR_INVALID_ARG, "gqa_prefill: seq_len must be >= 0");
+  if (dims->batch == 0 || seq_len == 0) return Q35_OK;
+  Q35_REQUIRE(max_len >= seq_len && max_len <= dims->capacity, Q35_ERR_INVALID_ARG,
+              "gqa_prefill: max_len must be in [seq_len, capacity]");
+  Q35_REQUIRE(dims->num_q_heads + dims->num_kv_heads <= 32, Q35_ERR_UNSUPPORTED,
+              "gqa_prefill: num_q_heads + num_kv_heads must be <= 32");
+  Q35_PTR16(q_gate); Q35_PTR16(k_new); Q35_PTR16(v_new); Q35_PTR16(qn_w); Q35_PTR16(kn_w);
+  Q35_PTR16(k_cache); Q35_PTR16(v_cache); Q35_PTR(lens); Q35_PTR16(out);
+  if (dims->rotary_dim > 0) {
+    Q35_PTR(cos); Q35_PTR(sin);
+  }
+  if (int rc = require_sm100()) return rc;
+  return gqa_prefill_launch(dims, seq_len, max_len, q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache,
+                            lens, out, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 size_t q35_gqa_decode_workspace_size(const q35_gqa_dims *dims, int64_t max_len) {

@@ -69,11 +69,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wall-clock bound of one wait: try_wait may suspend the thread for a
+// hardware-defined interval per poll, so the poll count alone does not bound
+// the time.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
 // Bounded wait on an mbarrier phase.  Returns false (and leaves the phase
-// incomplete) after kSpinLimit polls.
+// incomplete) after kWaitLimitNs or kSpinLimit polls, whichever comes first.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
   return false;
 }
 

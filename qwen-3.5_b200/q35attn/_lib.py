@@ -53,6 +53,9 @@ SIGNATURES = {
     "q35_gqa_decode_workspace_size": (_SZ, [C.POINTER(GqaDims), _I64]),
     "q35_workspace_init": (C.c_int, [_P, _SZ, _P]),
     "q35_gqa_decode": (C.c_int, [C.POINTER(GqaDims), _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "q35_gqa_prefill_workspace_size": (_SZ, [C.POINTER(GqaDims), _I32, _I64]),
+    "q35_gqa_prefill": (C.c_int, [C.POINTER(GqaDims), _I32, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                  _SZ, _P]),
     "q35_workspace_status": (C.c_int, [_P, C.POINTER(C.c_uint32), _I32, _P]),
     "q35_gqa_decode_partial": (C.c_int, [C.POINTER(GqaDims), _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                          _SZ, _P]),

@@ -12,7 +12,7 @@ import torch
 
 from ._lib import GdnDims, GqaDims, Q35Error, check, load
 
-__all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_workspace", "gdn_gate", "GqaWorkspace", "gqa_decode",
+__all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_workspace", "gdn_gate", "GqaWorkspace", "gqa_decode", "GqaPrefillWorkspace", "gqa_prefill",
            "q8_gemv", "launch_count", "Q35Error"]
 
 
@@ -152,6 +152,48 @@ def gqa_decode(q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, len
                                 _req(qn_w, "qn_w"), _req(kn_w, "kn_w"), _req(cos, "cos"), _req(sin, "sin"),
                                 _req(k_cache, "k_cache"), _req(v_cache, "v_cache"), _req(lens, "lens", torch.int32),
                                 _req(out, "out"), workspace.buf.data_ptr(), workspace.buf.numel(), _stream(stream)))
+    return out
+
+
+class GqaPrefillWorkspace:
+    """Scratch of q35_gqa_prefill (blocked q / k / v tiles + status word) for
+    prompts of seq_len tokens with lens[b] + seq_len <= max_len."""
+
+    def __init__(self, batch, num_q_heads, num_kv_heads, capacity, seq_len, max_len=None, device="cuda"):
+        self.dims = gqa_dims(batch, num_q_heads, num_kv_heads, capacity)
+        self.seq_len = int(seq_len)
+        self.max_len = int(max_len or capacity)
+        n = int(load().q35_gqa_prefill_workspace_size(C.byref(self.dims), self.seq_len, self.max_len))
+        if n == 0:
+            raise Q35Error(1, "invalid GQA prefill shape for workspace")
+        self.buf = torch.zeros(n, dtype=torch.uint8, device=device)
+
+    def status(self, clear=False, stream=None) -> int:
+        v = C.c_uint32(0)
+        check(load().q35_workspace_status(self.buf.data_ptr(), C.byref(v), int(clear), _stream(stream)))
+        return int(v.value)
+
+
+def gqa_prefill(q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, lens, out=None, *, workspace=None,
+                max_len=None, rotary_dim=None, eps=1e-6, stream=None):
+    """Gated-GQA attention over a prompt: q_gate [B, T, Hq, 512], k_new / v_new
+    [B, T, Hkv, 256], cos / sin [B, T, rot]; appends to the caches at lens[b]
+    and adds T to lens.  Returns ``out`` [B, T, Hq*256]."""
+    B, T, Hq, _ = q_gate.shape
+    Hkv, cap = k_cache.shape[1], k_cache.shape[2]
+    rot = int(rotary_dim if rotary_dim is not None else cos.shape[-1])
+    if out is None:
+        out = torch.empty(B, T, Hq * 256, device=q_gate.device, dtype=torch.float32)
+    if workspace is None:
+        workspace = GqaPrefillWorkspace(B, Hq, Hkv, cap, T, max_len, q_gate.device)
+    d = gqa_dims(B, Hq, Hkv, cap, rot, eps)
+    ml = int(max_len if max_len is not None else workspace.max_len)
+    cp = _req(cos, "cos") if rot > 0 else None
+    sp = _req(sin, "sin") if rot > 0 else None
+    check(load().q35_gqa_prefill(C.byref(d), int(T), ml, _req(q_gate, "q_gate"), _req(k_new, "k_new"),
+                                 _req(v_new, "v_new"), _req(qn_w, "qn_w"), _req(kn_w, "kn_w"), cp, sp,
+                                 _req(k_cache, "k_cache"), _req(v_cache, "v_cache"), _req(lens, "lens", torch.int32),
+                                 _req(out, "out"), workspace.buf.data_ptr(), workspace.buf.numel(), _stream(stream)))
     return out
 
 
