@@ -575,6 +575,27 @@ def run_extras(dev, reps=3):
                                         "achieved_tflops": fl2 / t / 1e12}
     del xp, zp, gp, bp, op, wsp
 
+    # GQA prefill over the config-3 prompt (T = 1024, empty cache); lens is
+    # reset inside the graph so every replay prefills the same prompt
+    T3 = 1024
+    qg3, kn3, vn3 = randn(1, T3, HQ, 2 * D), randn(1, T3, HKV, D), randn(1, T3, HKV, D)
+    w03 = torch.zeros(D, device=dev)
+    inv = 1.0 / (THETA ** (torch.arange(0, ROT, 2, device=dev, dtype=torch.float32) / ROT))
+    ang = torch.arange(T3, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
+    cos3 = torch.cat([ang.cos(), ang.cos()], -1)[None].contiguous()
+    sin3 = torch.cat([ang.sin(), ang.sin()], -1)[None].contiguous()
+    K3, V3 = torch.zeros(1, HKV, T3 + 64, D, device=dev), torch.zeros(1, HKV, T3 + 64, D, device=dev)
+    lens3, out3 = torch.zeros(1, dtype=torch.int32, device=dev), torch.empty(1, T3, HQ * D, device=dev)
+    ws3 = q35attn.GqaPrefillWorkspace(1, HQ, HKV, T3 + 64, T3)
+
+    def cfg3_gqa():
+        lens3.zero_()
+        q35attn.gqa_prefill(qg3, kn3, vn3, w03, w03, cos3, sin3, K3, V3, lens3, out3, workspace=ws3)
+    t = timed_graph(cfg3_gqa, reps)
+    fl3 = 2 * 2 * (T3 * T3 / 2) * D * HQ
+    res["config3_gqa_prefill_T1024"] = {"us": t * 1e6, "causal_gflop": fl3 / 1e9, "achieved_tflops": fl3 / t / 1e12}
+    del qg3, kn3, vn3, K3, V3, ws3
+
     # Q8F decode GEMV (kernels.rs:103-165) at the 2B projection shapes; the
     # timed calls rotate over enough weight copies to exceed L2 (126 MB)
     gemv = {}

@@ -8,14 +8,16 @@
 // causal scaled-dot-product attention (mask model.rs:59-67: query t of the
 // prompt sees keys 0 .. lens[b] + t) and the sigmoid output gate.
 //
-// Four launches:
+// Four launches (five when a key range is split):
 //  (1) qkv: per token, warp per head.  q: norm + RoPE + scale (log2 e / 16),
 //      stored as blocked hi/lo tiles for the tensor cores.  k: norm + RoPE and
 //      v, appended to the cache at lens[b] + t.
 //  (2) kv tiles: the cache rows 0 .. lens[b] + T - 1 of every kv head as
 //      blocked hi/lo tiles, K as [64 keys x 32 dims] chunks and V transposed
 //      as [128 dims x 64 keys] halves (zero past the last key).
-//  (3) attention: CTA = (128-query tile, q head).  A producer warp streams the
+//  (3) attention: CTA = (128-query tile, q head, range of 4 key tiles: the
+//      key range of a query tile is split so the causal triangle spreads over
+//      the SMs).  A producer warp streams the
 //      Q / K chunks and V halves into a 2 x 64 KB shared-memory ring with bulk
 //      copies; an MMA warp issues S = Q K^T (M 128, N 64, K 256 in 32-dim
 //      stages) and O += P V (two N 128 halves, K 64) as 3xTF32 tcgen05 MMAs
@@ -25,7 +27,8 @@
 //      the row max grows by more than 2^8 (the final O / l does not depend on
 //      the reference max).  QK of the next key tile is issued before PV of the
 //      current one, so the softmax overlaps the tensor pipe.  Epilogue:
-//      O / l * sigmoid(gate).
+//      O / l * sigmoid(gate), or, for a split key range, the unnormalised O and
+//      (m, l), which (3b) merges before the gate.
 //  (4) lens[b] += T.
 #include "common.cuh"
 #include "gqa_common.cuh"
@@ -48,6 +51,7 @@ constexpr int kSlot = 2 * kVH;       // ring slot: a V^T half, hi + lo (64 KB)
 constexpr int kAttnThreads = 192;    // warps 0-3 softmax, 4 producer, 5 MMA
 constexpr int kKvThreads = 256;
 constexpr int kKvLd = kD + 4;        // padded row of the kv staging tiles
+constexpr int kKS = 4;               // key tiles per attention CTA (load balance of the causal triangle)
 
 struct PrefillParams {
   const float *q_gate, *k_new, *v_new, *qn_w, *kn_w, *cos, *sin;
@@ -55,9 +59,10 @@ struct PrefillParams {
   int32_t *lens;
   float *out;
   float *qb, *kb, *vb;  // blocked scratch
+  float *po, *pml;      // key-split partials: O [B][ntq][ns][Hq][128][256], (m, l) [..][128][2]
   uint32_t *status;
   long long cap, max_len;  // max_len: host bound on lens[b] + T (sizes the key scratch)
-  int B, T, Hq, Hkv, rot, ntq, nkt;
+  int B, T, Hq, Hkv, rot, ntq, nkt, ns;  // ns: key splits per query tile (grid.z = B * ns)
   float eps, qscale;  // log2(e) / sqrt(D)
 };
 
@@ -173,7 +178,7 @@ struct AttnSmem {
 __global__ void __launch_bounds__(kAttnThreads, 1) gqa_prefill_attn_kernel(const PrefillParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_raw);
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z / p.ns, ks = blockIdx.z % p.ns;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kh = h / (p.Hq / p.Hkv);
   const long long past = p.lens[b];
@@ -181,7 +186,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) gqa_prefill_attn_kernel(const
   const int q0 = qt * kBM, rows = min(kBM, p.T - q0);
   const long long kend = past + p.T;
   const long long klim = min(kend, past + q0 + rows);  // keys seen by the tile's last row
-  const int nt = (int)((klim + kBN - 1) / kBN);
+  const int ntk = (int)((klim + kBN - 1) / kBN);       // key tiles of this query tile
+  const int nsplit = (ntk + kKS - 1) / kKS;
+  const int t0 = ks * kKS;                              // first key tile of this CTA
+  if (t0 >= ntk) return;
+  const int nt = min(kKS, ntk - t0);
   const float *qbase = p.qb + (((size_t)b * p.Hq + h) * p.ntq + qt) * kNQC * 2 * kQC;
   const float *kbase = p.kb + ((size_t)b * p.Hkv + kh) * p.nkt * kNQC * 2 * kKC;
   const float *vbase = p.vb + ((size_t)b * p.Hkv + kh) * p.nkt * 2 * 2 * kVH;
@@ -245,10 +254,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) gqa_prefill_attn_kernel(const
           bulk_g2s(sm.ring[s], vbase + ((size_t)j * 2 + h2) * 2 * kVH, 2 * kVH * sizeof(float), &sm.full[s], pol);
         }
       };
-      qk(0);
+      qk(t0);
       for (int j = 0; j < nt && ok; ++j) {
-        if (j + 1 < nt) qk(j + 1);
-        pv(j);
+        if (j + 1 < nt) qk(t0 + j + 1);
+        pv(t0 + j);
       }
     }
   } else if (warp == 5) {
@@ -343,7 +352,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) gqa_prefill_attn_kernel(const
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kBN; ++c) {
-        const long long kidx = (long long)j * kBN + c;
+        const long long kidx = (long long)(t0 + j) * kBN + c;
         s[c] = kidx < rlim ? s[c] : -INFINITY;
         mx = fmaxf(mx, s[c]);
       }
@@ -372,10 +381,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) gqa_prefill_attn_kernel(const
 #pragma unroll
       for (int c4 = 0; c4 < kBN / 4; ++c4) {
         float4 pv;
-        pv.x = exp2f(s[4 * c4 + 0] - m_use);
-        pv.y = exp2f(s[4 * c4 + 1] - m_use);
-        pv.z = exp2f(s[4 * c4 + 2] - m_use);
-        pv.w = exp2f(s[4 * c4 + 3] - m_use);
+        // a row with no key in this CTA's range so far keeps m = -inf and p = 0
+        const float mu = m_use == -INFINITY ? 0.0f : m_use;
+        pv.x = exp2f(s[4 * c4 + 0] - mu);
+        pv.y = exp2f(s[4 * c4 + 1] - mu);
+        pv.z = exp2f(s[4 * c4 + 2] - mu);
+        pv.w = exp2f(s[4 * c4 + 3] - mu);
         sum += (pv.x + pv.y) + (pv.z + pv.w);
         const int off = blk_off(r, 4 * c4, kBN);
         st4(sm.P[0] + off, pv);
@@ -394,12 +405,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) gqa_prefill_attn_kernel(const
     }
     umma::fence_after_sync();
     // every lane takes part in the warp-collective TMEM loads; rows past the
-    // prompt only skip the stores
+    // prompt only skip the stores.  One key split: the final output; several:
+    // this split's unnormalised O and (m, l) for the combine kernel.
     const bool live = r < rows;
     const size_t tok = (size_t)b * p.T + q0 + (live ? r : 0);
     const float *gate = p.q_gate + (tok * p.Hq + h) * 2 * kD + kD;
-    float *dst = p.out + (tok * p.Hq + h) * kD;
-    const float inv = ok ? 1.0f / l : __int_as_float(0x7fc00000);  // a bounded wait gave up: poison
+    const size_t pidx = ((((size_t)b * p.ntq + qt) * p.ns + ks) * p.Hq + h) * kBM + r;
+    float *dst = nsplit == 1 ? p.out + (tok * p.Hq + h) * kD : p.po + pidx * kD;
+    const float poison = __int_as_float(0x7fc00000);  // a bounded wait gave up
+    const float inv = nsplit == 1 ? (ok ? 1.0f / l : poison) : (ok ? 1.0f : poison);
+    if (nsplit > 1 && live) *reinterpret_cast<float2 *>(p.pml + 2 * pidx) = make_float2(m_use, l);
 #pragma unroll 1
     for (int q = 0; q < kD / 16; ++q) {
       float o[16];
@@ -408,10 +423,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) gqa_prefill_attn_kernel(const
       if (live) {
 #pragma unroll
         for (int e = 0; e < 16; e += 4) {
-          const float4 g = ld4(gate + 16 * q + e);
-          st4(dst + 16 * q + e, make_float4((o[e] * inv) * sigmoidf_dev(g.x), (o[e + 1] * inv) * sigmoidf_dev(g.y),
-                                            (o[e + 2] * inv) * sigmoidf_dev(g.z),
-                                            (o[e + 3] * inv) * sigmoidf_dev(g.w)));
+          float4 v = make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
+          if (nsplit == 1) {
+            const float4 g = ld4(gate + 16 * q + e);
+            v = make_float4(v.x * sigmoidf_dev(g.x), v.y * sigmoidf_dev(g.y), v.z * sigmoidf_dev(g.z),
+                            v.w * sigmoidf_dev(g.w));
+          }
+          st4(dst + 16 * q + e, v);
         }
       }
     }
@@ -423,6 +441,45 @@ __global__ void __launch_bounds__(kAttnThreads, 1) gqa_prefill_attn_kernel(const
   if (tid == 0) atomicAdd(diag + 3, 1u);
 }
 
+// ---------------------------------------------------------------- (3b) combine
+// Query tiles with several key splits: merge the splits' (O, m, l) (base-2
+// exponents) and apply the gate.  Grid (T, B), one warp per q head.
+__global__ void gqa_prefill_combine_kernel(const PrefillParams p) {
+  const int t = blockIdx.x, b = blockIdx.y;
+  const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (h >= p.Hq) return;
+  const long long past = p.lens[b];
+  if (skip_seq(p, past)) return;
+  const int qt = t / kBM, r = t % kBM, q0 = qt * kBM, rows = min(kBM, p.T - q0);
+  const long long klim = min(past + p.T, past + q0 + rows);
+  const int nsplit = (int)((klim + kBN - 1) / kBN + kKS - 1) / kKS;
+  if (nsplit <= 1) return;
+  const size_t base = (((size_t)b * p.ntq + qt) * p.ns * p.Hq + h) * kBM + r;  // split s: + s * Hq * kBM
+  const size_t sstride = (size_t)p.Hq * kBM;
+  float m = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) m = fmaxf(m, p.pml[2 * (base + s * sstride)]);
+  float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+  float l = 0.0f;
+  for (int s = 0; s < nsplit; ++s) {
+    const size_t i = base + s * sstride;
+    const float ms = p.pml[2 * i], ls = p.pml[2 * i + 1];
+    const float w = ms == -INFINITY ? 0.0f : exp2f(ms - m);
+    l = fmaf(ls, w, l);
+    const float4 o0 = ld4(p.po + i * kD + 4 * lane), o1 = ld4(p.po + i * kD + 128 + 4 * lane);
+    a0 = make_float4(fmaf(o0.x, w, a0.x), fmaf(o0.y, w, a0.y), fmaf(o0.z, w, a0.z), fmaf(o0.w, w, a0.w));
+    a1 = make_float4(fmaf(o1.x, w, a1.x), fmaf(o1.y, w, a1.y), fmaf(o1.z, w, a1.z), fmaf(o1.w, w, a1.w));
+  }
+  const float inv = 1.0f / l;
+  const size_t tok = (size_t)b * p.T + t;
+  const float *gate = p.q_gate + (tok * p.Hq + h) * 2 * kD + kD;
+  float *dst = p.out + (tok * p.Hq + h) * kD;
+  const float4 g0 = ld4(gate + 4 * lane), g1 = ld4(gate + 128 + 4 * lane);
+  st4(dst + 4 * lane, make_float4((a0.x * inv) * sigmoidf_dev(g0.x), (a0.y * inv) * sigmoidf_dev(g0.y),
+                                  (a0.z * inv) * sigmoidf_dev(g0.z), (a0.w * inv) * sigmoidf_dev(g0.w)));
+  st4(dst + 128 + 4 * lane, make_float4((a1.x * inv) * sigmoidf_dev(g1.x), (a1.y * inv) * sigmoidf_dev(g1.y),
+                                        (a1.z * inv) * sigmoidf_dev(g1.z), (a1.w * inv) * sigmoidf_dev(g1.w)));
+}
+
 // ---------------------------------------------------------------- (4) lens
 __global__ void gqa_prefill_lens_kernel(const PrefillParams p) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -430,16 +487,21 @@ __global__ void gqa_prefill_lens_kernel(const PrefillParams p) {
 }
 
 struct PrefillWs {
-  size_t qb, kb, vb, total;  // float offsets after the 256-byte status block
+  size_t qb, kb, vb, po, pml, total;  // float offsets after the 256-byte status block
+  int ns;
 };
 
 PrefillWs prefill_ws(int B, int T, int Hq, int Hkv, long long max_len) {
   const size_t ntq = (size_t)(T + kBM - 1) / kBM, nkt = (size_t)((max_len + kBN - 1) / kBN);
   PrefillWs w;
+  w.ns = (int)((nkt + kKS - 1) / kKS);
   w.qb = 64;  // floats: 256-byte status block first
   w.kb = w.qb + (size_t)B * Hq * ntq * kNQC * 2 * kQC;
   w.vb = w.kb + (size_t)B * Hkv * nkt * kNQC * 2 * kKC;
-  w.total = w.vb + (size_t)B * Hkv * nkt * 2 * 2 * kVH;
+  w.po = w.vb + (size_t)B * Hkv * nkt * 2 * 2 * kVH;
+  const size_t nrow = w.ns > 1 ? (size_t)B * ntq * w.ns * Hq * kBM : 0;
+  w.pml = w.po + nrow * kD;
+  w.total = w.pml + 2 * nrow;
   return w;
 }
 
@@ -463,7 +525,8 @@ int gqa_prefill_launch(const q35_gqa_dims *d, int T, long long max_len, const fl
   p.q_gate = q_gate; p.k_new = k_new; p.v_new = v_new; p.qn_w = qn_w; p.kn_w = kn_w; p.cos = cos; p.sin = sin;
   p.k_cache = k_cache; p.v_cache = v_cache; p.lens = lens; p.out = out;
   p.status = static_cast<uint32_t *>(ws);
-  p.qb = wf + w.qb; p.kb = wf + w.kb; p.vb = wf + w.vb;
+  p.qb = wf + w.qb; p.kb = wf + w.kb; p.vb = wf + w.vb; p.po = wf + w.po; p.pml = wf + w.pml;
+  p.ns = w.ns;
   p.cap = d->capacity;
   p.max_len = max_len;
   p.B = d->batch; p.T = T; p.Hq = d->num_q_heads; p.Hkv = d->num_kv_heads; p.rot = d->rotary_dim;
@@ -481,10 +544,12 @@ int gqa_prefill_launch(const q35_gqa_dims *d, int T, long long max_len, const fl
                              (int)sizeof(AttnSmem));
   if (e != cudaSuccess) return check_cuda(e, "gqa_prefill attributes");
   const int nw = p.Hq + p.Hkv;
-  note_launch(4);
+  Q35_REQUIRE((long long)p.B * p.ns <= 65535, Q35_ERR_UNSUPPORTED, "gqa_prefill: batch x key splits too large");
+  note_launch(p.ns > 1 ? 5 : 4);
   gqa_prefill_qkv_kernel<<<dim3(T, p.B), 32 * nw, nw * kD * sizeof(float), st>>>(p);
   gqa_prefill_kv_kernel<<<dim3(p.nkt, p.Hkv, p.B), kKvThreads, 2 * kBN * kKvLd * sizeof(float), st>>>(p);
-  gqa_prefill_attn_kernel<<<dim3(p.ntq, p.Hq, p.B), kAttnThreads, sizeof(AttnSmem), st>>>(p);
+  gqa_prefill_attn_kernel<<<dim3(p.ntq, p.Hq, p.B * p.ns), kAttnThreads, sizeof(AttnSmem), st>>>(p);
+  if (p.ns > 1) gqa_prefill_combine_kernel<<<dim3(T, p.B), 32 * p.Hq, 0, st>>>(p);
   gqa_prefill_lens_kernel<<<(p.B + 127) / 128, 128, 0, st>>>(p);
   return check_cuda(cudaGetLastError(), "gqa_prefill launch");
 }
