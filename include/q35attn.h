@@ -148,6 +148,47 @@ int q35_q8_gemv(int32_t in_dim, int32_t out_dim, const float *x,
                 int32_t mode, void *stream);
 
 /* --------------------------------------------------------------------------
+ * Decoder-stack glue (outside the attention cores; used by the end-to-end
+ * hybrid stack).  All tensors f32 unless stated, row-major, device pointers.
+ *   q35_q8_embedding: kernels.rs:15-45.  table [vocab, dim/4] u32 (Q8F),
+ *     scales [vocab, dim/64]; out [n, dim].  ids outside [0, vocab) give
+ *     zero rows.
+ *   q35_add_rmsnorm: text_modules.rs:800-809 with the residual add of
+ *     :1053-1085: h = x (+ residual if non-NULL), sum_out = h if non-NULL,
+ *     out = h / sqrt(mean(h^2) + eps) * (1 + weight).  [n_rows, dim].
+ *   q35_silu_mul: out = up * silu(gate) (:999-1011), n elements.
+ *   q35_q8_lm_head: kernels.rs:251-291, logits[v] = E[v] . x with the tied
+ *     Q8F embedding E [vocab, dim] (dim 2048).
+ *   q35_argmax: kernels.rs:298-371; ties resolve to the smallest index.
+ *   q35_q8_dequant: the dense f32 weight [rows, cols] of a Q8F matrix (the
+ *     prefill Linear::forward operand).
+ *   q35_rope_gather: cos/sin [B, rot] of each sequence's decode position
+ *     lens[b] from tables [max_pos, rot] (text_modules.rs:30-43 at
+ *     position past_len, model.rs:50-56), so a captured decode step needs
+ *     no host-side position.
+ */
+int q35_q8_embedding(int32_t n, int32_t vocab, int32_t dim, const int32_t *ids,
+                     const uint32_t *table, const float *scales, float *out,
+                     void *stream);
+int q35_add_rmsnorm(int32_t n_rows, int32_t dim, const float *x,
+                    const float *residual, const float *weight, float eps,
+                    float *out, float *sum_out, void *stream);
+int q35_silu_mul(int64_t n, const float *gate, const float *up, float *out,
+                 void *stream);
+int q35_q8_lm_head(int32_t vocab, int32_t dim, const float *x,
+                   const uint32_t *table, const float *scales, float *logits,
+                   void *stream);
+size_t q35_argmax_workspace_size(void);
+int q35_argmax(int32_t n, const float *x, int32_t *out_index, void *workspace,
+               size_t workspace_bytes, void *stream);
+int q35_q8_dequant(int32_t rows, int32_t cols, const uint32_t *w,
+                   const float *scales, float *out, void *stream);
+int q35_rope_gather(int32_t batch, int32_t rot, int32_t max_pos,
+                    const int32_t *lens, const float *table_cos,
+                    const float *table_sin, float *cos_out, float *sin_out,
+                    void *stream);
+
+/* --------------------------------------------------------------------------
  * Gated GQA, one decode step.  Replaces text_modules.rs:866-936 of
  * Attention::forward (:842-944): q/gate split of q_proj, q_norm/k_norm
  * (RMSNorm 1+w, :800-809), partial RoPE (:754-774), KV-cache append

@@ -26,6 +26,18 @@ int gqa_prefill_launch(const q35_gqa_dims *d, int T, long long max_len, const fl
                        const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
                        const float *sin, float *k_cache, float *v_cache, int32_t *lens, float *out, void *ws,
                        size_t ws_bytes, cudaStream_t st);
+int q8_embedding_launch(int n, int vocab, int dim, const int32_t *ids, const uint32_t *table, const float *scales,
+                        float *out, cudaStream_t st);
+int add_rmsnorm_launch(int n, int dim, const float *x, const float *residual, const float *w, float eps, float *out,
+                       float *sum_out, cudaStream_t st);
+int silu_mul_launch(size_t n, const float *gate, const float *up, float *out, cudaStream_t st);
+int q8_lm_head_launch(int vocab, int dim, const float *x, const uint32_t *table, const float *scales, float *logits,
+                      cudaStream_t st);
+size_t argmax_workspace_bytes();
+int argmax_launch(int n, const float *x, int32_t *out, void *ws, cudaStream_t st);
+int q8_dequant_launch(int rows, int cols, const uint32_t *w, const float *scales, float *out, cudaStream_t st);
+int rope_gather_launch(int B, int rot, int max_pos, const int32_t *lens, const float *tc, const float *ts, float *oc,
+                       float *os, cudaStream_t st);
 int gqa_combine_launch(int B, int Hq, int n_parts, const float *parts, const float *q_gate, float *out,
                        cudaStream_t st);
 size_t gdn_prefill_workspace_bytes(const q35_gdn_dims *d, int T);
@@ -213,6 +225,71 @@ int q35_gqa_prefill(const q35_gqa_dims *dims, int32_t seq_len, int64_t max_len, 
   if (int rc = require_sm100()) return rc;
   return gqa_prefill_launch(dims, seq_len, max_len, q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache,
                             lens, out, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int q35_q8_embedding(int32_t n, int32_t vocab, int32_t dim, const int32_t *ids, const uint32_t *table,
+                     const float *scales, float *out, void *stream) {
+  Q35_REQUIRE(n >= 0 && vocab > 0 && dim > 0 && dim % 64 == 0, Q35_ERR_INVALID_ARG,
+              "q8_embedding: n >= 0, vocab > 0, dim a multiple of 64");
+  if (n == 0) return Q35_OK;
+  Q35_PTR(ids); Q35_PTR(table); Q35_PTR(scales); Q35_PTR16(out);
+  if (int rc = require_sm100()) return rc;
+  return q8_embedding_launch(n, vocab, dim, ids, table, scales, out, static_cast<cudaStream_t>(stream));
+}
+
+int q35_add_rmsnorm(int32_t n_rows, int32_t dim, const float *x, const float *residual, const float *weight,
+                    float eps, float *out, float *sum_out, void *stream) {
+  Q35_REQUIRE(n_rows >= 0 && dim > 0 && eps >= 0.0f, Q35_ERR_INVALID_ARG, "add_rmsnorm: bad sizes");
+  if (n_rows == 0) return Q35_OK;
+  Q35_PTR(x); Q35_PTR(weight); Q35_PTR(out);
+  if (int rc = require_sm100()) return rc;
+  return add_rmsnorm_launch(n_rows, dim, x, residual, weight, eps, out, sum_out, static_cast<cudaStream_t>(stream));
+}
+
+int q35_silu_mul(int64_t n, const float *gate, const float *up, float *out, void *stream) {
+  Q35_REQUIRE(n >= 0, Q35_ERR_INVALID_ARG, "silu_mul: n must be >= 0");
+  if (n == 0) return Q35_OK;
+  Q35_PTR(gate); Q35_PTR(up); Q35_PTR(out);
+  if (int rc = require_sm100()) return rc;
+  return silu_mul_launch((size_t)n, gate, up, out, static_cast<cudaStream_t>(stream));
+}
+
+int q35_q8_lm_head(int32_t vocab, int32_t dim, const float *x, const uint32_t *table, const float *scales,
+                   float *logits, void *stream) {
+  Q35_REQUIRE(vocab > 0, Q35_ERR_INVALID_ARG, "q8_lm_head: vocab must be > 0");
+  Q35_PTR16(x); Q35_PTR16(table); Q35_PTR(scales); Q35_PTR(logits);
+  if (int rc = require_sm100()) return rc;
+  return q8_lm_head_launch(vocab, dim, x, table, scales, logits, static_cast<cudaStream_t>(stream));
+}
+
+size_t q35_argmax_workspace_size(void) { return argmax_workspace_bytes(); }
+
+int q35_argmax(int32_t n, const float *x, int32_t *out_index, void *workspace, size_t workspace_bytes,
+               void *stream) {
+  Q35_REQUIRE(n > 0, Q35_ERR_INVALID_ARG, "argmax: n must be > 0");
+  Q35_PTR(x); Q35_PTR(out_index); Q35_PTR(workspace);
+  Q35_REQUIRE(workspace_bytes >= argmax_workspace_bytes(), Q35_ERR_WORKSPACE, "argmax: workspace too small");
+  if (int rc = require_sm100()) return rc;
+  return argmax_launch(n, x, out_index, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int q35_q8_dequant(int32_t rows, int32_t cols, const uint32_t *w, const float *scales, float *out, void *stream) {
+  Q35_REQUIRE(rows >= 0 && cols > 0 && cols % 64 == 0, Q35_ERR_INVALID_ARG,
+              "q8_dequant: rows >= 0, cols a multiple of 64");
+  if (rows == 0) return Q35_OK;
+  Q35_PTR(w); Q35_PTR(scales); Q35_PTR16(out);
+  if (int rc = require_sm100()) return rc;
+  return q8_dequant_launch(rows, cols, w, scales, out, static_cast<cudaStream_t>(stream));
+}
+
+int q35_rope_gather(int32_t batch, int32_t rot, int32_t max_pos, const int32_t *lens, const float *table_cos,
+                    const float *table_sin, float *cos_out, float *sin_out, void *stream) {
+  Q35_REQUIRE(batch >= 0 && rot >= 0 && rot <= 1024 && max_pos > 0, Q35_ERR_INVALID_ARG, "rope_gather: bad sizes");
+  if (batch == 0 || rot == 0) return Q35_OK;
+  Q35_PTR(lens); Q35_PTR(table_cos); Q35_PTR(table_sin); Q35_PTR(cos_out); Q35_PTR(sin_out);
+  if (int rc = require_sm100()) return rc;
+  return rope_gather_launch(batch, rot, max_pos, lens, table_cos, table_sin, cos_out, sin_out,
+                            static_cast<cudaStream_t>(stream));
 }
 
 size_t q35_gqa_decode_workspace_size(const q35_gqa_dims *dims, int64_t max_len) {

@@ -89,6 +89,33 @@ __global__ void gate_prefill_kernel(int N, int in_dim, const float *__restrict__
   }
 }
 
+// Any other head count: one warp per row, one head at a time.
+__global__ void gate_prefill_any_kernel(int N, int in_dim, int H, const float *__restrict__ x,
+                                        const float *__restrict__ wb, const float *__restrict__ wa,
+                                        const float *__restrict__ a_log, const float *__restrict__ dt_bias,
+                                        float *__restrict__ beta, float *__restrict__ g) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= N) return;
+  const float *xr = x + (size_t)warp * in_dim;
+  for (int h = 0; h < H; ++h) {
+    float ab = 0.0f, aa = 0.0f;
+    for (int row = lane; row < in_dim; row += 32) {
+      const float xv = xr[row];
+      ab = fmaf(xv, wb[(size_t)row * H + h], ab);
+      aa = fmaf(xv, wa[(size_t)row * H + h], aa);
+    }
+    ab = warp_sum(ab);
+    aa = warp_sum(aa);
+    if (lane == 0) {
+      const float xg = aa + dt_bias[h];
+      const float sp = xg > 20.0f ? xg : logf(expf(xg) + 1.0f);
+      beta[(size_t)warp * H + h] = sigmoidf_dev(ab);
+      g[(size_t)warp * H + h] = -expf(a_log[h]) * sp;
+    }
+  }
+}
+
 }  // namespace
 
 int gdn_gate_launch(int N, int in_dim, int H, const float *x, const float *wb, const float *wa, const float *a_log,
@@ -109,7 +136,9 @@ int gdn_gate_launch(int N, int in_dim, int H, const float *x, const float *wb, c
     case 32: gate_prefill_kernel<32><<<grid, threads, 0, st>>>(N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
     case 48: gate_prefill_kernel<48><<<grid, threads, 0, st>>>(N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
     case 64: gate_prefill_kernel<64><<<grid, threads, 0, st>>>(N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
-    default: return fail(Q35_ERR_UNSUPPORTED, "gdn_gate mode 1: num_heads must be 16, 32, 48 or 64");
+    default:
+      gate_prefill_any_kernel<<<grid, threads, 0, st>>>(N, in_dim, H, x, wb, wa, a_log, dt_bias, beta, g);
+      break;
   }
   return check_cuda(cudaGetLastError(), "gdn_gate launch");
 }

@@ -50,6 +50,14 @@ SIGNATURES = {
                                   _P]),
     "q35_gdn_gate": (C.c_int, [_I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _I32, _P]),
     "q35_q8_gemv": (C.c_int, [_I32, _I32, _P, _P, _P, _P, _I32, _P]),
+    "q35_q8_embedding": (C.c_int, [_I32, _I32, _I32, _P, _P, _P, _P, _P]),
+    "q35_add_rmsnorm": (C.c_int, [_I32, _I32, _P, _P, _P, C.c_float, _P, _P, _P]),
+    "q35_silu_mul": (C.c_int, [_I64, _P, _P, _P, _P]),
+    "q35_q8_lm_head": (C.c_int, [_I32, _I32, _P, _P, _P, _P, _P]),
+    "q35_argmax_workspace_size": (_SZ, []),
+    "q35_argmax": (C.c_int, [_I32, _P, _P, _P, _SZ, _P]),
+    "q35_q8_dequant": (C.c_int, [_I32, _I32, _P, _P, _P, _P]),
+    "q35_rope_gather": (C.c_int, [_I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),
     "q35_gqa_decode_workspace_size": (_SZ, [C.POINTER(GqaDims), _I64]),
     "q35_workspace_init": (C.c_int, [_P, _SZ, _P]),
     "q35_gqa_decode": (C.c_int, [C.POINTER(GqaDims), _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),

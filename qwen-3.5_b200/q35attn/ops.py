@@ -227,3 +227,63 @@ def gqa_combine_partials(parts, q_gate, out=None, stream=None):
     check(load().q35_gqa_combine_partials(B, Hq, 256, n, _req(parts, "parts"), _req(q_gate, "q_gate"),
                                           _req(out, "out"), _stream(stream)))
     return out
+
+
+# ---------------------------------------------------------------- stack glue
+
+def q8_embedding(ids, table, scales, out=None, stream=None):
+    """out [n, dim] = dequantised rows ids of a Q8F table ([vocab, dim/4] words, [vocab, dim/64] scales)."""
+    n = ids.numel()
+    vocab, dim = table.shape[0], table.shape[1] * 4
+    if out is None:
+        out = torch.empty(n, dim, device=table.device, dtype=torch.float32)
+    check(load().q35_q8_embedding(n, vocab, dim, _req(ids, "ids", torch.int32), table.data_ptr(),
+                                  _req(scales, "scales"), _req(out, "out"), _stream(stream)))
+    return out
+
+
+def add_rmsnorm(x, weight, out, residual=None, sum_out=None, eps=1e-6, stream=None):
+    """out = RMSNorm(x + residual) * (1 + weight) row-wise; sum_out = x + residual."""
+    dim = weight.numel()
+    rows = x.numel() // dim
+    check(load().q35_add_rmsnorm(rows, dim, _req(x, "x"), _req(residual, "residual") if residual is not None else None,
+                                 _req(weight, "weight"), C.c_float(eps), _req(out, "out"),
+                                 _req(sum_out, "sum_out") if sum_out is not None else None, _stream(stream)))
+    return out
+
+
+def silu_mul(gate, up, out, stream=None):
+    check(load().q35_silu_mul(gate.numel(), _req(gate, "gate"), _req(up, "up"), _req(out, "out"), _stream(stream)))
+    return out
+
+
+def q8_lm_head(x, table, scales, logits, stream=None):
+    check(load().q35_q8_lm_head(table.shape[0], x.numel(), _req(x, "x"), table.data_ptr(), _req(scales, "scales"),
+                                _req(logits, "logits"), _stream(stream)))
+    return logits
+
+
+class ArgmaxWorkspace:
+    def __init__(self, device="cuda"):
+        self.buf = torch.empty(int(load().q35_argmax_workspace_size()), dtype=torch.uint8, device=device)
+
+
+def argmax(x, out, workspace, stream=None):
+    check(load().q35_argmax(x.numel(), _req(x, "x"), _req(out, "out", torch.int32), workspace.buf.data_ptr(),
+                            workspace.buf.numel(), _stream(stream)))
+    return out
+
+
+def q8_dequant(words, scales, out, stream=None):
+    rows, cols = words.shape[0], words.shape[1] * 4
+    check(load().q35_q8_dequant(rows, cols, words.data_ptr(), _req(scales, "scales"), _req(out, "out"),
+                                _stream(stream)))
+    return out
+
+
+def rope_gather(lens, table_cos, table_sin, cos_out, sin_out, stream=None):
+    B = lens.numel()
+    max_pos, rot = table_cos.shape
+    check(load().q35_rope_gather(B, rot, max_pos, _req(lens, "lens", torch.int32), _req(table_cos, "table_cos"),
+                                 _req(table_sin, "table_sin"), _req(cos_out, "cos_out"), _req(sin_out, "sin_out"),
+                                 _stream(stream)))

@@ -11,7 +11,7 @@ from conftest import max_rel_err
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("mode,N,H", [(0, 1, 16), (0, 5, 16), (1, 300, 16), (1, 7, 32)])
+@pytest.mark.parametrize("mode,N,H", [(0, 1, 16), (0, 5, 16), (1, 300, 16), (1, 7, 32), (1, 9, 2), (0, 3, 2)])
 def test_gate(mode, N, H):
     rng = np.random.RandomState(mode * 100 + N)
     ind = 2048

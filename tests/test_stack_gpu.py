@@ -1,0 +1,55 @@
+"""End-to-end hybrid decoder stack (config-3 structure: GDN and GQA layers,
+RMSNorm + residual, SwiGLU MLP, Q8F projections, tied Q8F lm_head, greedy
+argmax) on the q35attn kernels, against the CPU reference of oracle/stack_ref.py
+built from the pinned oracle pieces.  A reduced configuration (4 layers, 2-head
+GDN, 2/1-head GQA, vocab 4096) keeps the CPU side fast; hidden stays 2048.
+Logits: max rel err <= 1e-3 per step; the reference is teacher-forced with the
+GPU's tokens, and every GPU token must equal the reference argmax unless the
+reference's top-2 gap is below 1e-4 of its max logit."""
+import numpy as np
+import pytest
+import torch
+
+import q35attn.stack as qs
+from conftest import max_rel_err
+from stack_ref import StackRef
+
+pytestmark = pytest.mark.gpu
+SMALL = qs.StackConfig(layer_types=("linear", "linear", "linear", "full"), gdn_hk=2, gdn_hv=2, gqa_hq=2,
+                       gqa_hkv=1, inter=512, vocab=4096)
+
+
+def _check_token(tok, logits):
+    top = np.sort(logits)[-2:]
+    if top[1] - top[0] > 1e-4 * abs(top[1]):
+        assert tok == int(np.argmax(logits))
+
+
+@pytest.mark.parametrize("gemv_mode", [1, 0])
+def test_small_stack_prefill_and_decode(gemv_mode):
+    st = qs.HybridStack(SMALL, capacity=128, seed=3, gemv_mode=gemv_mode)
+    ids = torch.from_numpy(np.random.RandomState(4).randint(0, SMALL.vocab, 45).astype(np.int32)).cuda()
+    ref = StackRef(st)
+    tok = int(st.prefill(ids).item())
+    rtok, rlog = ref.prefill(ids.cpu().numpy())
+    assert max_rel_err(st.b["logits"].cpu().numpy(), rlog) <= 1e-3
+    _check_token(tok, rlog)
+    st.capture()
+    for step in range(6):
+        st.graph.replay()
+        torch.cuda.synchronize()
+        rtok, rlog = ref.decode(tok)  # teacher-forced with the GPU's token
+        e = max_rel_err(st.b["logits"].cpu().numpy(), rlog)
+        assert e <= 1e-3, (step, e)
+        tok = int(st.b["tok"].item())
+        _check_token(tok, rlog)
+    assert int(st.gqa_layers[0]["lens"].item()) == 45 + 6
+
+
+def test_generate_is_deterministic():
+    st = qs.HybridStack(SMALL, capacity=96, seed=5)
+    ids = torch.arange(30, dtype=torch.int32, device="cuda") * 7
+    a = st.generate(ids, 8).cpu()
+    st.capture()
+    b = st.generate(ids, 8).cpu()
+    assert torch.equal(a, b)
