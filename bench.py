@@ -618,6 +618,34 @@ def run_extras(dev, reps=3):
                       "weight_copies": ncopy}
         del ws_, ss_
     res["q8_gemv"] = gemv
+
+    # config 3: the 2B hybrid stack (24 layers, random Q8F weights), a
+    # 1024-token random prompt, then 512 greedy decode steps (CUDA graph)
+    import q35attn.stack as qs
+    st3 = qs.HybridStack(qs.QWEN35_2B, capacity=1024 + 512 + 16, seed=0, device=dev)
+    ids3 = torch.randint(0, qs.QWEN35_2B.vocab, (1024,), dtype=torch.int32, device=dev, generator=gen)
+    st3.prefill(ids3)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    st3.prefill(ids3)
+    b.record()
+    torch.cuda.synchronize(dev)
+    pre_ms = a.elapsed_time(b)
+    core_ms, step_ms = st3.profile_decode_step()
+    st3.prefill(ids3)
+    st3.capture()
+    st3.prefill(ids3)
+    a.record()
+    st3.decode(512)
+    b.record()
+    torch.cuda.synchronize(dev)
+    dec_ms = a.elapsed_time(b)
+    res["config3_stack_2b"] = {"prompt": 1024, "decode_steps": 512, "prefill_ms": pre_ms,
+                               "decode_tok_s": 512 / dec_ms * 1e3, "decode_ms_per_token": dec_ms / 512,
+                               "attention_core_share_eager": core_ms / step_ms, "gemv_mode": st3.gemv_mode,
+                               "weights_gb": st3.weight_bytes() / 1e9,
+                               "decode_weight_gbs": st3.weight_bytes() / (dec_ms / 512) / 1e6}
+    del st3
     return res
 
 

@@ -133,6 +133,17 @@ class HybridStack:
         self.gqa_ws = ops.GqaWorkspace(1, c.gqa_hq, c.gqa_hkv, self.cap, device=dev)
         self.argmax_ws = ops.ArgmaxWorkspace(dev)
 
+    def weight_bytes(self):
+        """Bytes of all weights (Q8F words + scales and the f32 tensors)."""
+        n = self.embed.words.numel() * 4 + self.embed.scales.numel() * 4 + self.final_norm.numel() * 4
+        for L in self.layers:
+            for k, v in L.items():
+                if isinstance(v, Q8F):
+                    n += v.words.numel() * 4 + v.scales.numel() * 4
+                elif torch.is_tensor(v) and k not in ("conv_state", "rec_state", "K", "V", "lens"):
+                    n += v.numel() * v.element_size()
+        return n
+
     def gemv(self, x, W: Q8F, y):
         return ops.q8_gemv(x, W.words, W.scales, y, mode=self.gemv_mode)
 
@@ -175,6 +186,32 @@ class HybridStack:
         ops.add_rmsnorm(b["mlp"], self.final_norm, b["x"], residual=b["h"], eps=c.eps)
         ops.q8_lm_head(b["x"], self.embed.words, self.embed.scales, b["logits"])
         ops.argmax(b["logits"], b["tok"], self.argmax_ws)
+
+    def profile_decode_step(self):
+        """One eager decode step with CUDA events around the attention cores
+        (q35_gdn_decode, q35_gqa_decode): returns (core ms, step ms)."""
+        evs = []
+        orig_gdn, orig_gqa = ops.gdn_decode, ops.gqa_decode
+
+        def timed(fn):
+            def run(*a, **k):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                r = fn(*a, **k)
+                e.record()
+                evs.append((s, e))
+                return r
+            return run
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ops.gdn_decode, ops.gqa_decode = timed(orig_gdn), timed(orig_gqa)
+        try:
+            t0.record()
+            self._decode_step()
+            t1.record()
+        finally:
+            ops.gdn_decode, ops.gqa_decode = orig_gdn, orig_gqa
+        torch.cuda.synchronize(self.dev)
+        return sum(s.elapsed_time(e) for s, e in evs), t0.elapsed_time(t1)
 
     def capture(self):
         """Capture one decode step in a CUDA graph (after a warm-up step)."""
