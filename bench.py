@@ -736,6 +736,10 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the config 0/1/2 side measurements")
     ap.add_argument("--prefill-tokens", type=int, default=0,
                     help="only run the config-2 GDN prefill at this prompt length (profiling aid)")
+    ap.add_argument("--gqa-prefill-tokens", type=int, default=0,
+                    help="only run the GQA prefill (8/2 heads, empty cache) at this prompt length (profiling aid)")
+    ap.add_argument("--gemv", type=str, default="",
+                    help="IN,OUT: only run the Q8F GEMV of that shape (profiling aid)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -743,7 +747,66 @@ def main():
         return run_reference(args)
     if args.prefill_tokens > 0:
         return run_prefill_only(args)
+    if args.gqa_prefill_tokens > 0 or args.gemv:
+        return run_kernel_only(args)
     return run_gpu(args)
+
+
+def run_kernel_only(args):
+    """--gqa-prefill-tokens T: the GQA prefill of a T-token prompt into an
+    empty cache (config-3 head shapes); --gemv IN,OUT: one Q8F GEMV (mode 0).
+    --warmup untimed calls, then --steps calls timed with CUDA events; one JSON
+    line.  A profiling aid, not the bench line."""
+    import torch
+
+    import q35attn
+    dev = torch.device("cuda:0")
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    if args.gemv:
+        ind, outd = (int(v) for v in args.gemv.split(","))
+        w = torch.randint(-2**31, 2**31 - 1, (ind, outd // 4), dtype=torch.int32, device=dev, generator=gen)
+        sc = torch.rand(ind, outd // 64, device=dev, generator=gen) * 0.01
+        x, y = torch.randn(ind, device=dev, generator=gen), torch.empty(outd, device=dev)
+
+        def call():
+            q35attn.q8_gemv(x, w, sc, y, mode=0)
+        case, size = "q8_gemv", {"in": ind, "out": outd}
+        alg = ind * outd + ind * (outd // 64) * 4 + 4 * (ind + outd)
+    else:
+        T = args.gqa_prefill_tokens
+        qg = torch.randn(1, T, HQ, 2 * D, device=dev, generator=gen)
+        kn, vn = torch.randn(1, T, HKV, D, device=dev, generator=gen), torch.randn(1, T, HKV, D, device=dev,
+                                                                                    generator=gen)
+        w0 = torch.zeros(D, device=dev)
+        inv = 1.0 / (THETA ** (torch.arange(0, ROT, 2, device=dev, dtype=torch.float32) / ROT))
+        ang = torch.arange(T, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
+        cos = torch.cat([ang.cos(), ang.cos()], -1)[None].contiguous()
+        sin = torch.cat([ang.sin(), ang.sin()], -1)[None].contiguous()
+        K, V = torch.zeros(1, HKV, T + 64, D, device=dev), torch.zeros(1, HKV, T + 64, D, device=dev)
+        lens, out = torch.zeros(1, dtype=torch.int32, device=dev), torch.empty(1, T, HQ * D, device=dev)
+        ws = q35attn.GqaPrefillWorkspace(1, HQ, HKV, T + 64, T)
+
+        def call():
+            lens.zero_()
+            q35attn.gqa_prefill(qg, kn, vn, w0, w0, cos, sin, K, V, lens, out, workspace=ws)
+        case, size = "gqa_prefill", {"tokens": T}
+        alg = None
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        call()
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / args.steps
+    line = {"case": case, **size, "steps": args.steps, "warmup": args.warmup, "ms_per_call": ms}
+    if alg:
+        line["achieved_gbs"] = alg / ms / 1e6
+    print(json.dumps(line))
+    return 0
 
 
 def run_prefill_only(args):
