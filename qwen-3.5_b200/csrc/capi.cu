@@ -2,6 +2,7 @@
 // include/q35attn.h): argument validation, error reporting, workspace
 // management and dispatch to the sm_100a kernels.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -56,6 +57,14 @@ int g_sm_major[64] = {0};
 }  // namespace
 
 void set_error(const std::string &msg) { g_last_error = msg; }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *v = std::getenv("Q35_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 int fail(int code, const std::string &msg) {
   set_error(msg);

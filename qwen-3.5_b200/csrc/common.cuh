@@ -21,6 +21,51 @@ void note_launch(int n = 1);
 int device_sm_count();
 int require_sm100();
 
+// Programmatic dependent launch on every library launch unless the
+// environment sets Q35_PDL=0.
+bool pdl_enabled();
+
+// cudaLaunchKernelEx with the PDL attribute (and a cluster shape when
+// cluster_x * cluster_y > 1).  launch_kernel_serial is the same launch in
+// plain stream order: the GQA flash-decode measured 8-10 % slower at batch 1
+// with its successor scheduled early, so it keeps the plain order.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel_impl(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t st, unsigned cluster_x, unsigned cluster_y, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  unsigned na = 0;
+  if (pdl && pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cluster_x * cluster_y > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster_x;
+    attr[na].val.clusterDim.y = cluster_y;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                          unsigned cluster_x, unsigned cluster_y, Args... args) {
+  return launch_kernel_impl(true, kernel, grid, block, smem, st, cluster_x, cluster_y, args...);
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel_serial(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 unsigned cluster_x, unsigned cluster_y, Args... args) {
+  return launch_kernel_impl(false, kernel, grid, block, smem, st, cluster_x, cluster_y, args...);
+}
+
 #define Q35_REQUIRE(cond, code, msg)          \
   do {                                        \
     if (!(cond)) return ::q35::fail(code, msg); \
@@ -185,6 +230,16 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Programmatic dependent launch.  Every kernel of the library starts with
+// pdl_entry(): wait until the previous grid in the stream has completed and
+// its memory is visible (a no-op when the launch had no PDL attribute), then
+// let the next grid be scheduled; so in a captured sequence of launches the
+// next kernel is launched and made resident while this one drains.
+__device__ __forceinline__ void pdl_entry() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {

@@ -76,6 +76,7 @@ __device__ __forceinline__ float conv_channel(const GdnDecodeParams &p, size_t x
 template <int SPLIT, int KC, bool SOLO>
 __global__ void __launch_bounds__(GdnDecodeCfg<SPLIT>::NT)
     gdn_decode_kernel(const GdnDecodeParams p) {
+  pdl_entry();
   using Cfg = GdnDecodeCfg<SPLIT>;
   constexpr int CS = Cfg::CS, QR = Cfg::QR, NT = Cfg::NT, RP = Cfg::RP, NP = Cfg::NP, NW = Cfg::NW;
   static_assert(!SOLO || SPLIT == 1, "SOLO implies one CTA per head");
@@ -255,6 +256,7 @@ struct StreamStage {
 
 template <int KC>
 __global__ void __launch_bounds__(kStreamThreads, 1) gdn_decode_stream_kernel(const GdnDecodeParams p) {
+  pdl_entry();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   StreamStage<KC> *stg = reinterpret_cast<StreamStage<KC> *>(smem_raw);
   __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
@@ -434,7 +436,7 @@ cudaError_t launch_stream(const GdnDecodeParams &p, int sms, cudaStream_t st) {
   const int items = p.B * p.Hk;
   const int grid = items < sms ? items : sms;
   note_launch();
-  gdn_decode_stream_kernel<KC><<<grid, kStreamThreads, smem, st>>>(p);
+  (void)launch_kernel(gdn_decode_stream_kernel<KC>, dim3(grid), dim3(kStreamThreads), smem, st, 1, 1, p);
   return cudaGetLastError();
 }
 
@@ -443,24 +445,13 @@ cudaError_t launch(const GdnDecodeParams &p, int ncl, cudaStream_t st) {
   if constexpr (SPLIT == 1) {
     if (ncl == 1) {
       note_launch();
-      gdn_decode_kernel<1, KC, true><<<dim3(1, p.Hk, p.B), GdnDecodeCfg<1>::NT, 0, st>>>(p);
+      (void)launch_kernel(gdn_decode_kernel<1, KC, true>, dim3(1, p.Hk, p.B), dim3(GdnDecodeCfg<1>::NT), 0, st, 1, 1, p);
       return cudaGetLastError();
     }
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(ncl, p.Hk, p.B);
-  cfg.blockDim = dim3(GdnDecodeCfg<SPLIT>::NT, 1, 1);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = ncl;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   note_launch();
-  return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<SPLIT, KC, false>, p);
+  return launch_kernel(gdn_decode_kernel<SPLIT, KC, false>, dim3(ncl, p.Hk, p.B), dim3(GdnDecodeCfg<SPLIT>::NT), 0,
+                       st, (unsigned)ncl, 1, p);
 }
 
 template <int KC>

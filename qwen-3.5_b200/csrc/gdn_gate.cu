@@ -19,6 +19,7 @@ __global__ void gate_decode_kernel(int in_dim, int H, const float *__restrict__ 
                                    const float *__restrict__ wa, const float *__restrict__ a_log,
                                    const float *__restrict__ dt_bias, float *__restrict__ beta,
                                    float *__restrict__ g) {
+  pdl_entry();
   extern __shared__ float partial[];  // [kSplits][2H]
   const int n = blockIdx.x;
   const int u = threadIdx.x;  // 0 .. 2*H*kSplits-1
@@ -57,6 +58,7 @@ __global__ void gate_prefill_kernel(int N, int in_dim, const float *__restrict__
                                     const float *__restrict__ wa, const float *__restrict__ a_log,
                                     const float *__restrict__ dt_bias, float *__restrict__ beta,
                                     float *__restrict__ g) {
+  pdl_entry();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= N) return;
@@ -94,6 +96,7 @@ __global__ void gate_prefill_any_kernel(int N, int in_dim, int H, const float *_
                                         const float *__restrict__ wb, const float *__restrict__ wa,
                                         const float *__restrict__ a_log, const float *__restrict__ dt_bias,
                                         float *__restrict__ beta, float *__restrict__ g) {
+  pdl_entry();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= N) return;
@@ -124,7 +127,7 @@ int gdn_gate_launch(int N, int in_dim, int H, const float *x, const float *wb, c
   if (mode == 0) {
     Q35_REQUIRE(2 * H * kSplits <= 1024, Q35_ERR_UNSUPPORTED, "gdn_gate: num_heads must be <= 64 for mode 0");
     note_launch();
-    gate_decode_kernel<<<N, 2 * H * kSplits, kSplits * 2 * H * sizeof(float), st>>>(in_dim, H, x, wb, wa, a_log,
+    (void)launch_kernel(gate_decode_kernel, dim3(N), dim3(2 * H * kSplits), kSplits * 2 * H * sizeof(float), st, 1, 1, in_dim, H, x, wb, wa, a_log,
                                                                                       dt_bias, beta, g);
     return check_cuda(cudaGetLastError(), "gdn_gate launch");
   }
@@ -132,12 +135,12 @@ int gdn_gate_launch(int N, int in_dim, int H, const float *x, const float *wb, c
   const int grid = (N + rows_per_cta - 1) / rows_per_cta;
   note_launch();
   switch (H) {
-    case 16: gate_prefill_kernel<16><<<grid, threads, 0, st>>>(N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
-    case 32: gate_prefill_kernel<32><<<grid, threads, 0, st>>>(N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
-    case 48: gate_prefill_kernel<48><<<grid, threads, 0, st>>>(N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
-    case 64: gate_prefill_kernel<64><<<grid, threads, 0, st>>>(N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
+    case 16: (void)launch_kernel(gate_prefill_kernel<16>, dim3(grid), dim3(threads), 0, st, 1, 1, N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
+    case 32: (void)launch_kernel(gate_prefill_kernel<32>, dim3(grid), dim3(threads), 0, st, 1, 1, N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
+    case 48: (void)launch_kernel(gate_prefill_kernel<48>, dim3(grid), dim3(threads), 0, st, 1, 1, N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
+    case 64: (void)launch_kernel(gate_prefill_kernel<64>, dim3(grid), dim3(threads), 0, st, 1, 1, N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
     default:
-      gate_prefill_any_kernel<<<grid, threads, 0, st>>>(N, in_dim, H, x, wb, wa, a_log, dt_bias, beta, g);
+      (void)launch_kernel(gate_prefill_any_kernel, dim3(grid), dim3(threads), 0, st, 1, 1, N, in_dim, H, x, wb, wa, a_log, dt_bias, beta, g);
       break;
   }
   return check_cuda(cudaGetLastError(), "gdn_gate launch");

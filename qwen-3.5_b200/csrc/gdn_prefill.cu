@@ -84,6 +84,7 @@ struct ChunkSmem {
 
 template <int KC>
 __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const PrefillParams p) {
+  pdl_entry();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   ChunkSmem &sm = *reinterpret_cast<ChunkSmem *>(smem_raw);
   float *kS = sm.r1[0], *qS = sm.r1[1], *kL = sm.r1[2], *qL = sm.r1[3];
@@ -553,6 +554,7 @@ __device__ __forceinline__ void stage_state(float (&st)[2][16 * 64], int r, int 
 
 template <int KC>
 __global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const PrefillParams p) {
+  pdl_entry();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   StateSmem &sm = *reinterpret_cast<StateSmem *>(smem_raw);
   const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -723,6 +725,7 @@ struct OutSmem {
 };
 
 __global__ void __launch_bounds__(kOutThreads, 1) gdn_prefill_output_kernel(const PrefillParams p) {
+  pdl_entry();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   OutSmem &sm = *reinterpret_cast<OutSmem *>(smem_raw);
   const int h = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
@@ -865,13 +868,13 @@ int launch_kc(const PrefillParams &p, cudaStream_t st) {
     e = cudaFuncSetAttribute(gdn_prefill_output_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s3);
   if (e != cudaSuccess) return check_cuda(e, "gdn_prefill attributes");
   note_launch();
-  gdn_prefill_chunk_kernel<KC><<<dim3(p.Hv, p.NC, p.B), kThreads, s1, st>>>(p);
+  (void)launch_kernel(gdn_prefill_chunk_kernel<KC>, dim3(p.Hv, p.NC, p.B), dim3(kThreads), s1, st, 1, 1, p);
   if ((e = cudaGetLastError()) != cudaSuccess) return check_cuda(e, "gdn_prefill chunk launch");
   note_launch();
-  gdn_prefill_state_kernel<KC><<<dim3(kSplit, p.Hv, p.B), kStateThreads, s2, st>>>(p);
+  (void)launch_kernel(gdn_prefill_state_kernel<KC>, dim3(kSplit, p.Hv, p.B), dim3(kStateThreads), s2, st, 1, 1, p);
   if ((e = cudaGetLastError()) != cudaSuccess) return check_cuda(e, "gdn_prefill state launch");
   note_launch();
-  gdn_prefill_output_kernel<<<dim3(p.Hv, p.NC, p.B), kOutThreads, s3, st>>>(p);
+  (void)launch_kernel(gdn_prefill_output_kernel, dim3(p.Hv, p.NC, p.B), dim3(kOutThreads), s3, st, 1, 1, p);
   return check_cuda(cudaGetLastError(), "gdn_prefill output launch");
 }
 

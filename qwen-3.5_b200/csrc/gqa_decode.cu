@@ -187,6 +187,7 @@ __device__ __forceinline__ void merge_partials(const GqaParams &p, const float *
 
 template <int G>
 __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(const GqaParams p) {
+  pdl_entry();
   constexpr int V = kKPW * G;  // (key, head) dots per warp per stage
   constexpr int LOGV = V == 1 ? 0 : V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : V == 16 ? 4 : 5;
   static_assert((1 << LOGV) == V && V <= 32, "V must be a power of two <= 32");
@@ -454,6 +455,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
 // M = max_r m_r, over n_parts partials [n][B][Hq][D+2] (one per context shard).
 __global__ void gqa_combine_kernel(int B, int Hq, int n_parts, const float *__restrict__ parts,
                                    const float *__restrict__ q_gate, float *__restrict__ out) {
+  pdl_entry();
   const int bh = blockIdx.x, d = threadIdx.x;
   const size_t stride = (size_t)B * Hq * (kD + 2);
   const float *base = parts + (size_t)bh * (kD + 2);
@@ -482,7 +484,7 @@ cudaError_t launch_g(const GqaParams &p, cudaStream_t st) {
   }
   dim3 grid(p.nsplit, p.Hkv, p.B);
   note_launch();
-  gqa_decode_kernel<G><<<grid, kThreads, smem, st>>>(p);
+  (void)launch_kernel_serial(gqa_decode_kernel<G>, dim3(grid), dim3(kThreads), smem, st, 1, 1, p);
   return cudaGetLastError();
 }
 
@@ -540,7 +542,7 @@ int gqa_combine_launch(int B, int Hq, int n_parts, const float *parts, const flo
                        cudaStream_t st) {
   if (B == 0) return Q35_OK;
   note_launch();
-  gqa_combine_kernel<<<B * Hq, kD, 0, st>>>(B, Hq, n_parts, parts, q_gate, out);
+  (void)launch_kernel_serial(gqa_combine_kernel, dim3(B * Hq), dim3(kD), 0, st, 1, 1, B, Hq, n_parts, parts, q_gate, out);
   return check_cuda(cudaGetLastError(), "gqa_combine launch");
 }
 

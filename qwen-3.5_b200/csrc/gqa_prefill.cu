@@ -80,6 +80,7 @@ __device__ __forceinline__ float4 lo4(float4 v) {
 
 // ---------------------------------------------------------------- (1) qkv
 __global__ void __launch_bounds__(1024) gqa_prefill_qkv_kernel(const PrefillParams p) {
+  pdl_entry();
   extern __shared__ __align__(16) float tmp_s[];  // [warps][256]
   const int t = blockIdx.x, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -125,6 +126,7 @@ __global__ void __launch_bounds__(1024) gqa_prefill_qkv_kernel(const PrefillPara
 
 // ---------------------------------------------------------------- (2) kv tiles
 __global__ void __launch_bounds__(kKvThreads) gqa_prefill_kv_kernel(const PrefillParams p) {
+  pdl_entry();
   extern __shared__ __align__(16) float kv_s[];  // K [64][kKvLd], V [64][kKvLd]
   float *Ks = kv_s, *Vs = kv_s + kBN * kKvLd;
   const int kt = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -176,6 +178,7 @@ struct AttnSmem {
 };
 
 __global__ void __launch_bounds__(kAttnThreads, 1) gqa_prefill_attn_kernel(const PrefillParams p) {
+  pdl_entry();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_raw);
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z / p.ns, ks = blockIdx.z % p.ns;
@@ -445,6 +448,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) gqa_prefill_attn_kernel(const
 // Query tiles with several key splits: merge the splits' (O, m, l) (base-2
 // exponents) and apply the gate.  Grid (T, B), one warp per q head.
 __global__ void gqa_prefill_combine_kernel(const PrefillParams p) {
+  pdl_entry();
   const int t = blockIdx.x, b = blockIdx.y;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (h >= p.Hq) return;
@@ -482,6 +486,7 @@ __global__ void gqa_prefill_combine_kernel(const PrefillParams p) {
 
 // ---------------------------------------------------------------- (4) lens
 __global__ void gqa_prefill_lens_kernel(const PrefillParams p) {
+  pdl_entry();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < p.B && !skip_seq(p, p.lens[b])) p.lens[b] += p.T;
 }
@@ -546,11 +551,11 @@ int gqa_prefill_launch(const q35_gqa_dims *d, int T, long long max_len, const fl
   const int nw = p.Hq + p.Hkv;
   Q35_REQUIRE((long long)p.B * p.ns <= 65535, Q35_ERR_UNSUPPORTED, "gqa_prefill: batch x key splits too large");
   note_launch(p.ns > 1 ? 5 : 4);
-  gqa_prefill_qkv_kernel<<<dim3(T, p.B), 32 * nw, nw * kD * sizeof(float), st>>>(p);
-  gqa_prefill_kv_kernel<<<dim3(p.nkt, p.Hkv, p.B), kKvThreads, 2 * kBN * kKvLd * sizeof(float), st>>>(p);
-  gqa_prefill_attn_kernel<<<dim3(p.ntq, p.Hq, p.B * p.ns), kAttnThreads, sizeof(AttnSmem), st>>>(p);
-  if (p.ns > 1) gqa_prefill_combine_kernel<<<dim3(T, p.B), 32 * p.Hq, 0, st>>>(p);
-  gqa_prefill_lens_kernel<<<(p.B + 127) / 128, 128, 0, st>>>(p);
+  (void)launch_kernel(gqa_prefill_qkv_kernel, dim3(T, p.B), dim3(32 * nw), nw * kD * sizeof(float), st, 1, 1, p);
+  (void)launch_kernel(gqa_prefill_kv_kernel, dim3(p.nkt, p.Hkv, p.B), dim3(kKvThreads), 2 * kBN * kKvLd * sizeof(float), st, 1, 1, p);
+  (void)launch_kernel(gqa_prefill_attn_kernel, dim3(p.ntq, p.Hq, p.B * p.ns), dim3(kAttnThreads), sizeof(AttnSmem), st, 1, 1, p);
+  if (p.ns > 1) (void)launch_kernel(gqa_prefill_combine_kernel, dim3(T, p.B), dim3(32 * p.Hq), 0, st, 1, 1, p);
+  (void)launch_kernel(gqa_prefill_lens_kernel, dim3((p.B + 127) / 128), dim3(128), 0, st, 1, 1, p);
   return check_cuda(cudaGetLastError(), "gqa_prefill launch");
 }
 

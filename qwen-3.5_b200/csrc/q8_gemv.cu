@@ -66,6 +66,7 @@ __device__ __forceinline__ int active_row(const GemvParams &p, int a) {
 // the row groups of a warp, then one shared-memory pass over the 8 warps.
 template <bool kCompat, int NQ>
 __global__ void __launch_bounds__(kGemvThreads, 2) q8_gemv_kernel(const GemvParams p) {
+  pdl_entry();
   constexpr int CW = 16 * NQ;        // columns per CTA
   constexpr int LPQ = 32 / NQ;       // lanes (row groups) per column quad in a warp
   constexpr int RG = kGemvThreads / NQ;
@@ -154,7 +155,7 @@ template <bool kCompat, int NQ>
 int launch_nq(const GemvParams &p, cudaStream_t st) {
   const int ctas = (p.out_dim + 16 * NQ - 1) / (16 * NQ);
   note_launch();
-  q8_gemv_kernel<kCompat, NQ><<<ctas, kGemvThreads, 0, st>>>(p);
+  (void)launch_kernel(q8_gemv_kernel<kCompat, NQ>, dim3(ctas), dim3(kGemvThreads), 0, st, 1, 1, p);
   return check_cuda(cudaGetLastError(), "q8_gemv launch");
 }
 

@@ -30,6 +30,7 @@ __device__ __forceinline__ float s8(uint32_t v, int j) { return (float)((int32_t
 // [0, vocab) give a zero row instead of an out-of-range read
 __global__ void q8_embedding_kernel(int n, int vocab, int dim, const int32_t *ids, const uint32_t *table,
                                     const float *scales, float *out) {
+  pdl_entry();
   const int i = blockIdx.y;
   const int w = blockIdx.x * blockDim.x + threadIdx.x;  // word index in the row
   if (i >= n || w >= dim / 4) return;
@@ -49,6 +50,7 @@ __global__ void q8_embedding_kernel(int n, int vocab, int dim, const int32_t *id
 // One CTA of 256 threads per row.
 __global__ void add_rmsnorm_kernel(int dim, const float *x, const float *residual, const float *w, float eps,
                                    float *out, float *sum_out) {
+  pdl_entry();
   __shared__ float red[8];
   const size_t row = blockIdx.x;
   const float *xr = x + row * dim;
@@ -82,6 +84,7 @@ __global__ void add_rmsnorm_kernel(int dim, const float *x, const float *residua
 
 // ------------------------------------------------------------- SwiGLU
 __global__ void silu_mul_kernel(size_t n, const float *gate, const float *up, float *out) {
+  pdl_entry();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] = up[i] * siluf_dev(gate[i]);
 }
@@ -93,6 +96,7 @@ constexpr int kHeadDim = 2048;
 constexpr int kHeadRows = 4;  // rows in flight per warp
 __global__ void __launch_bounds__(256) q8_lm_head_kernel(int vocab, const float *x, const uint4 *table,
                                                          const float *scales, float *logits) {
+  pdl_entry();
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nwarps = (gridDim.x * blockDim.x) >> 5;
   float xv[64];
@@ -168,6 +172,7 @@ __device__ __forceinline__ void block_argmax(float &m, int &i) {
   }
 }
 __global__ void argmax_stage1(int n, const float *x, float *pm, int *pi) {
+  pdl_entry();
   const int chunk = (n + gridDim.x - 1) / gridDim.x;
   const int a = blockIdx.x * chunk, e = min(n, a + chunk);
   float m = -INFINITY;
@@ -180,6 +185,7 @@ __global__ void argmax_stage1(int n, const float *x, float *pm, int *pi) {
   }
 }
 __global__ void argmax_stage2(int np, const float *pm, const int *pi, int32_t *out) {
+  pdl_entry();
   float m = -INFINITY;
   int idx = 0x7fffffff;
   for (int j = threadIdx.x; j < np; j += blockDim.x) better(m, idx, pm[j], pi[j]);
@@ -193,6 +199,7 @@ __global__ void argmax_stage2(int np, const float *pm, const int *pi, int32_t *o
 // past_len, model.rs:50-56); positions past the table give cos 1, sin 0.
 __global__ void rope_gather_kernel(int B, int rot, int max_pos, const int32_t *lens, const float *tc,
                                    const float *ts, float *oc, float *os) {
+  pdl_entry();
   const int b = blockIdx.x, i = threadIdx.x;
   if (b >= B || i >= rot) return;
   const int pos = lens[b];
@@ -204,6 +211,7 @@ __global__ void rope_gather_kernel(int B, int rot, int max_pos, const int32_t *l
 // ------------------------------------------------------------- dequant
 // out[r][c] = int8(w[r][c]) * scales[r][c / 64], f32 [rows, cols]
 __global__ void q8_dequant_kernel(int rows, int cols, const uint32_t *w, const float *scales, float *out) {
+  pdl_entry();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;  // word index
   const size_t nw = (size_t)rows * (cols / 4);
   if (i >= nw) return;
@@ -219,20 +227,20 @@ __global__ void q8_dequant_kernel(int rows, int cols, const uint32_t *w, const f
 int q8_embedding_launch(int n, int vocab, int dim, const int32_t *ids, const uint32_t *table, const float *scales,
                         float *out, cudaStream_t st) {
   note_launch();
-  q8_embedding_kernel<<<dim3((dim / 4 + 255) / 256, n), 256, 0, st>>>(n, vocab, dim, ids, table, scales, out);
+  (void)launch_kernel(q8_embedding_kernel, dim3((dim / 4 + 255) / 256, n), dim3(256), 0, st, 1, 1, n, vocab, dim, ids, table, scales, out);
   return check_cuda(cudaGetLastError(), "q8_embedding launch");
 }
 
 int add_rmsnorm_launch(int n, int dim, const float *x, const float *residual, const float *w, float eps, float *out,
                        float *sum_out, cudaStream_t st) {
   note_launch();
-  add_rmsnorm_kernel<<<n, 256, 0, st>>>(dim, x, residual, w, eps, out, sum_out);
+  (void)launch_kernel(add_rmsnorm_kernel, dim3(n), dim3(256), 0, st, 1, 1, dim, x, residual, w, eps, out, sum_out);
   return check_cuda(cudaGetLastError(), "add_rmsnorm launch");
 }
 
 int silu_mul_launch(size_t n, const float *gate, const float *up, float *out, cudaStream_t st) {
   note_launch();
-  silu_mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(n, gate, up, out);
+  (void)launch_kernel(silu_mul_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, 1, 1, n, gate, up, out);
   return check_cuda(cudaGetLastError(), "silu_mul launch");
 }
 
@@ -241,7 +249,7 @@ int q8_lm_head_launch(int vocab, int dim, const float *x, const uint32_t *table,
   Q35_REQUIRE(dim == kHeadDim, Q35_ERR_UNSUPPORTED, "q8_lm_head: hidden size 2048 is the compiled configuration");
   note_launch();
   const int blocks = 4 * device_sm_count();
-  q8_lm_head_kernel<<<blocks, 256, 0, st>>>(vocab, x, reinterpret_cast<const uint4 *>(table), scales, logits);
+  (void)launch_kernel(q8_lm_head_kernel, dim3(blocks), dim3(256), 0, st, 1, 1, vocab, x, reinterpret_cast<const uint4 *>(table), scales, logits);
   return check_cuda(cudaGetLastError(), "q8_lm_head launch");
 }
 
@@ -252,22 +260,22 @@ int argmax_launch(int n, const float *x, int32_t *out, void *ws, cudaStream_t st
   float *pm = static_cast<float *>(ws);
   int *pi = reinterpret_cast<int *>(pm + 1024);
   note_launch(2);
-  argmax_stage1<<<np, 256, 0, st>>>(n, x, pm, pi);
-  argmax_stage2<<<1, 1024, 0, st>>>(np, pm, pi, out);
+  (void)launch_kernel(argmax_stage1, dim3(np), dim3(256), 0, st, 1, 1, n, x, pm, pi);
+  (void)launch_kernel(argmax_stage2, dim3(1), dim3(1024), 0, st, 1, 1, np, pm, pi, out);
   return check_cuda(cudaGetLastError(), "argmax launch");
 }
 
 int rope_gather_launch(int B, int rot, int max_pos, const int32_t *lens, const float *tc, const float *ts, float *oc,
                        float *os, cudaStream_t st) {
   note_launch();
-  rope_gather_kernel<<<B, rot, 0, st>>>(B, rot, max_pos, lens, tc, ts, oc, os);
+  (void)launch_kernel(rope_gather_kernel, dim3(B), dim3(rot), 0, st, 1, 1, B, rot, max_pos, lens, tc, ts, oc, os);
   return check_cuda(cudaGetLastError(), "rope_gather launch");
 }
 
 int q8_dequant_launch(int rows, int cols, const uint32_t *w, const float *scales, float *out, cudaStream_t st) {
   const size_t nw = (size_t)rows * (cols / 4);
   note_launch();
-  q8_dequant_kernel<<<(unsigned)((nw + 255) / 256), 256, 0, st>>>(rows, cols, w, scales, out);
+  (void)launch_kernel(q8_dequant_kernel, dim3((unsigned)((nw + 255) / 256)), dim3(256), 0, st, 1, 1, rows, cols, w, scales, out);
   return check_cuda(cudaGetLastError(), "q8_dequant launch");
 }
 
