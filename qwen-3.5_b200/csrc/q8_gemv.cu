@@ -20,7 +20,10 @@
 // (kernels.rs:119-131) floors chunk = in/splits and then walks only
 // (chunk/8)*8 rows of each split, splits = clamp(25000/out, 1, max(in/80, 1))
 // (kernels.rs:504).  Mode 0 uses every row.
+#include <cuda.h>
+
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -159,6 +162,192 @@ int launch_nq(const GemvParams &p, cudaStream_t st) {
   return check_cuda(cudaGetLastError(), "q8_gemv launch");
 }
 
+// ---------------------------------------------------------------------------
+// TMA path (out_dim % 256 == 0, x 16-byte aligned): a CTA owns 64 output
+// columns (one scale per row) over every row.  A producer thread streams
+// 128-row boxes of the weights ([128 x 64] bytes) and of the scales ([128 x 4]
+// floats: the 16-byte TMA minimum, of which one column is used) from 2-D tensor
+// maps over the reference layout into a 6-stage ring -- one instruction per
+// box, so the stream is not capped by the SM's outstanding-load limit that
+// bounds the per-thread LDG kernel above.  Eight consumer warps take 8 rows x
+// 64 bytes per step (lane = row * 4 + 16-byte quarter) and reduce with warp
+// shuffles and one shared-memory pass.  When the column blocks alone give few
+// CTAs, the row boxes are split over a cluster of KS CTAs (grid.y) and rank 0
+// adds the ranks' 64 column sums through distributed shared memory in rank
+// order (deterministic).
+constexpr int kTC = 64;
+constexpr int kTR = 128;
+constexpr int kTNS = 6;
+constexpr int kTWarps = 8;
+constexpr int kTThreads = (kTWarps + 1) * 32;
+
+struct alignas(64) GemvTmaParams {
+  CUtensorMap wmap;  // uint8 [in][out], box {64, 128}
+  CUtensorMap smap;  // f32 [in][out / 64], box {4, 128}
+  const float *x;
+  float *y;
+  int in_dim, out_dim;
+  int chunk, per_split, ref_splits;  // mode 1 row set
+  int ks;                            // row-box split = cluster size
+};
+
+struct GemvTmaSmem {
+  unsigned char w[kTNS][kTR][kTC];
+  float sc[kTNS][kTR][4];
+  float red[kTWarps][kTC];
+  float mine[kTC];  // this CTA's column sums (read by rank 0 of the cluster)
+  uint64_t full[kTNS], empty[kTNS], xbar;
+  alignas(16) float x[4];  // in_dim floats (dynamic tail; 16-byte aligned for the bulk copy)
+};
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <bool kCompat>
+__global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_constant__ GemvTmaParams p) {
+  pdl_entry();
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  GemvTmaSmem &sm = *reinterpret_cast<GemvTmaSmem *>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c0 = blockIdx.x * kTC;
+  const int sb0 = (c0 / 64) & ~3, sj = (c0 / 64) & 3;  // scale box start (16-byte aligned) and our column in it
+  const int nst_all = (p.in_dim + kTR - 1) / kTR;
+  const int rk = blockIdx.y;  // row-box range of this CTA within the cluster
+  const int sbeg = (int)((long long)nst_all * rk / p.ks), send = (int)((long long)nst_all * (rk + 1) / p.ks);
+  const int nst = send - sbeg;
+  if (tid == 0) {
+    for (int i = 0; i < kTNS; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], kTWarps);
+    }
+    mbar_init(&sm.xbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  bool ok = true;
+  if (warp == kTWarps) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&sm.xbar, (uint32_t)p.in_dim * sizeof(float));
+      bulk_g2s_nohint(sm.x, p.x, (uint32_t)p.in_dim * sizeof(float), &sm.xbar);
+      for (int st = 0; st < nst && ok; ++st) {
+        const int slot = st % kTNS;
+        if (st >= kTNS && !mbar_wait(&sm.empty[slot], ((st / kTNS) - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&sm.full[slot], kTR * kTC + kTR * 4 * sizeof(float));
+        tma_load_2d(&sm.w[slot][0][0], &p.wmap, c0, (sbeg + st) * kTR, &sm.full[slot]);
+        tma_load_2d(&sm.sc[slot][0][0], &p.smap, sb0, (sbeg + st) * kTR, &sm.full[slot]);
+      }
+    }
+  } else {
+    float acc[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
+    if (!mbar_wait(&sm.xbar, 0)) ok = false;
+    const int q = lane & 3;
+    for (int st = 0; st < nst && ok; ++st) {
+      const int slot = st % kTNS;
+      if (!mbar_wait(&sm.full[slot], (st / kTNS) & 1)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int step = 0; step < kTR / (8 * kTWarps); ++step) {
+        const int rr = warp * (kTR / kTWarps) + step * 8 + (lane >> 2);
+        const int row = (sbeg + st) * kTR + rr;
+        bool live = row < p.in_dim;
+        if (kCompat && live) {
+          const int s = row / p.chunk;
+          live = s < p.ref_splits && row - s * p.chunk < p.per_split;
+        }
+        if (live) {
+          const uint4 w = *reinterpret_cast<const uint4 *>(&sm.w[slot][rr][16 * q]);
+          fma16(acc, w, sm.x[row] * sm.sc[slot][rr][sj]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty[slot]);
+    }
+    // reduce over the 8 rows of a step (lane bits 2-4): lane holds columns 16 q + 2 g, + 1 (g = lane / 4)
+#pragma unroll
+    for (int off = 16, n = 16; off >= 4; off >>= 1) {
+      const bool upper = (lane & off) != 0;
+      n >>= 1;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j < n) {
+          const float send = upper ? acc[j] : acc[j + n];
+          const float keep = upper ? acc[j + n] : acc[j];
+          acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+    }
+    sm.red[warp][16 * q + 2 * (lane >> 2)] = acc[0];
+    sm.red[warp][16 * q + 2 * (lane >> 2) + 1] = acc[1];
+  }
+  __syncthreads();
+  const float poison = __int_as_float(0x7fc00000);  // a bounded wait gave up
+  if (tid < kTC) {
+    float v = sm.red[0][tid];
+#pragma unroll
+    for (int w = 1; w < kTWarps; ++w) v += sm.red[w][tid];
+    if (!ok) v = poison;
+    if (p.ks == 1) p.y[c0 + tid] = v;
+    else sm.mine[tid] = v;
+  }
+  if (p.ks > 1) {
+    cluster_sync_all();
+    if (cluster_ctarank() == 0 && tid < kTC) {
+      float t = 0.0f;
+      for (int r = 0; r < p.ks; ++r) t += ld_dsmem_f32(&sm.mine[tid], (uint32_t)r);
+      p.y[c0 + tid] = t;
+    }
+    cluster_sync_all();  // no CTA leaves while rank 0 still reads its sums
+  }
+}
+
+bool gemv_tma_enabled() {
+  static const bool on = [] {
+    const char *v = std::getenv("Q35_GEMV_TMA");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// Encodes the two tensor maps; false when the driver rejects them.
+bool encode_gemv_maps(GemvTmaParams &p, const uint32_t *w, const float *scales, int in_dim, int out_dim) {
+  const cuuint64_t wd[2] = {(cuuint64_t)out_dim, (cuuint64_t)in_dim};
+  const cuuint64_t ws[1] = {(cuuint64_t)out_dim};
+  const cuuint32_t wb[2] = {kTC, kTR};
+  const cuuint64_t sd[2] = {(cuuint64_t)(out_dim / 64), (cuuint64_t)in_dim};
+  const cuuint64_t ss[1] = {(cuuint64_t)(out_dim / 64) * sizeof(float)};
+  const cuuint32_t sbx[2] = {4, kTR};
+  const cuuint32_t es[2] = {1, 1};
+  if (cuTensorMapEncodeTiled(&p.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint32_t *>(w), wd, ws, wb, es,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  return cuTensorMapEncodeTiled(&p.smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(scales), sd, ss, sbx,
+                                es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int launch_tma(const GemvTmaParams &p, bool compat, cudaStream_t st) {
+  const size_t smem = sizeof(GemvTmaSmem) + (size_t)p.in_dim * sizeof(float);  // x tail (over-sized by 16 B)
+  auto kern = compat ? q8_gemv_tma_kernel<true> : q8_gemv_tma_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return check_cuda(e, "q8_gemv attributes");
+  note_launch();
+  (void)launch_kernel(kern, dim3(p.out_dim / kTC, p.ks), dim3(kTThreads), smem, st, 1, (unsigned)p.ks, p);
+  return check_cuda(cudaGetLastError(), "q8_gemv launch");
+}
+
 }  // namespace
 
 int q8_gemv_launch(int in_dim, int out_dim, const float *x, const uint32_t *w, const float *scales, float *y,
@@ -174,6 +363,28 @@ int q8_gemv_launch(int in_dim, int out_dim, const float *x, const uint32_t *w, c
   p.rows = g.rows;
   p.chunk = g.chunk;
   p.per_split = std::max(g.per_split, 1);
+  if (gemv_tma_enabled() && out_dim % 256 == 0 && in_dim % 4 == 0 && in_dim <= 16384 &&
+      (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    GemvTmaParams t;
+    if (encode_gemv_maps(t, w, scales, in_dim, out_dim)) {
+      t.x = x;
+      t.y = y;
+      t.in_dim = in_dim;
+      t.out_dim = out_dim;
+      t.chunk = std::max(g.chunk, 1);
+      t.per_split = g.per_split;
+      t.ref_splits = g.per_split > 0 ? g.rows / g.per_split : 0;
+      // row-box split: the largest of 8 / 4 / 2 that keeps the grid within two CTAs per SM
+      const int ncb = out_dim / kTC, nst = (in_dim + kTR - 1) / kTR;
+      t.ks = 1;
+      for (int k : {8, 4, 2})
+        if (ncb * k <= 2 * device_sm_count() && k <= nst) {
+          t.ks = k;
+          break;
+        }
+      return launch_tma(t, mode == 1, st);
+    }
+  }
   if (mode == 1) return g.nq == 4 ? launch_nq<true, 4>(p, st) : launch_nq<true, 2>(p, st);
   return g.nq == 4 ? launch_nq<false, 4>(p, st) : launch_nq<false, 2>(p, st);
 }
