@@ -740,6 +740,8 @@ def main():
                     help="only run the GQA prefill (8/2 heads, empty cache) at this prompt length (profiling aid)")
     ap.add_argument("--gemv", type=str, default="",
                     help="IN,OUT: only run the Q8F GEMV of that shape (profiling aid)")
+    ap.add_argument("--config3-steps", type=int, default=0,
+                    help="only run config 3 (2B hybrid stack, 1024-token prompt) with this many graph decode steps")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -749,7 +751,42 @@ def main():
         return run_prefill_only(args)
     if args.gqa_prefill_tokens > 0 or args.gemv:
         return run_kernel_only(args)
+    if args.config3_steps > 0:
+        return run_config3_only(args)
     return run_gpu(args)
+
+
+def run_config3_only(args):
+    """Config 3 alone: the 2B hybrid stack (random Q8F weights), a 1024-token
+    random prompt, then --config3-steps greedy decode steps replayed from a CUDA
+    graph (--warmup prefills first).  One JSON line; a profiling aid."""
+    import torch
+
+    import q35attn.stack as qs
+    dev = torch.device("cuda:0")
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    st = qs.HybridStack(qs.QWEN35_2B, capacity=1024 + args.config3_steps + 16, seed=0, device=dev)
+    ids = torch.randint(0, qs.QWEN35_2B.vocab, (1024,), dtype=torch.int32, device=dev, generator=gen)
+    for _ in range(args.warmup):
+        st.prefill(ids)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    st.prefill(ids)
+    b.record()
+    torch.cuda.synchronize(dev)
+    pre = a.elapsed_time(b)
+    st.capture()
+    st.prefill(ids)
+    a.record()
+    toks = st.decode(args.config3_steps)
+    b.record()
+    torch.cuda.synchronize(dev)
+    dec = a.elapsed_time(b)
+    print(json.dumps({"case": "config3_stack_2b", "prompt": 1024, "decode_steps": args.config3_steps,
+                      "prefill_ms": pre, "decode_ms_per_token": dec / args.config3_steps,
+                      "decode_tok_s": args.config3_steps / dec * 1e3, "first_tokens": toks[:8].tolist()}))
+    return 0
 
 
 def run_kernel_only(args):
