@@ -147,6 +147,36 @@ int q35_q8_gemv(int32_t in_dim, int32_t out_dim, const float *x,
                 const uint32_t *w, const float *scales, float *y,
                 int32_t mode, void *stream);
 
+/* One Q8F projection of a fused GEMV launch (layout as for q35_q8_gemv). */
+typedef struct {
+  const uint32_t *w;     /* [in_dim, out_dim/4] u32, 16-byte aligned */
+  const float *scales;   /* [in_dim, out_dim/64] f32, 16-byte aligned */
+  float *y;              /* [out_dim] f32 */
+  int32_t out_dim;       /* multiple of 256 */
+} q35_q8_segment;
+
+/* Up to four Q8F GEMVs of the same input in one launch, with the decoder's
+ * RMSNorm optionally fused in front and the MLP's SwiGLU optionally behind.
+ * Replaces, per decoder layer (text_modules.rs:1053-1085), the input or
+ * post-attention RMSNorm (:800-809) followed by the projections that read its
+ * output: the GatedDeltaNet in_proj_qkvz pair (:498, :505), the attention
+ * q/k/v projections (:856, :877, :886) or the MLP up/gate pair (:1003-1005).
+ *   x         [in_dim] f32, 16-byte aligned
+ *   norm_w    NULL: the segments read x as it is.  Else [in_dim]: the input is
+ *             h / sqrt(mean(h^2) + eps) * (1 + norm_w), h = x (+ residual).
+ *   residual  NULL or [in_dim] (needs norm_w); sum_out, x_out: NULL or [in_dim]
+ *             receive h and the normalised input (need norm_w; must not
+ *             alias x or residual).
+ *   swiglu    1: exactly two segments (up, gate) of equal out_dim; segment
+ *             0's y receives up * silu(gate) and segment 1's y is unused.
+ *   mode      row coverage per segment, as for q35_q8_gemv.
+ * in_dim % 4 == 0 and at most 8192 with the norm (16384 without).
+ */
+int q35_q8_gemv_fused(int32_t in_dim, int32_t n_seg, const q35_q8_segment *segs,
+                      const float *x, const float *residual, const float *norm_w,
+                      float eps, float *sum_out, float *x_out, int32_t swiglu,
+                      int32_t mode, void *stream);
+
 /* --------------------------------------------------------------------------
  * Decoder-stack glue (outside the attention cores; used by the end-to-end
  * hybrid stack).  All tensors f32 unless stated, row-major, device pointers.

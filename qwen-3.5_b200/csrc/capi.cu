@@ -44,6 +44,9 @@ int gqa_combine_launch(int B, int Hq, int n_parts, const float *parts, const flo
 size_t gdn_prefill_workspace_bytes(const q35_gdn_dims *d, int T);
 int q8_gemv_launch(int in_dim, int out_dim, const float *x, const uint32_t *w, const float *scales, float *y,
                    int mode, cudaStream_t st);
+int q8_gemv_fused_launch(int in_dim, int n_seg, const q35_q8_segment *segs, const float *x, const float *residual,
+                         const float *norm_w, float eps, float *sum_out, float *x_out, int swiglu, int mode,
+                         cudaStream_t st);
 int gdn_prefill_launch(const q35_gdn_dims *d, int T, const float *mixed_qkv, const float *z, const float *beta,
                        const float *g, const float *conv_w, const float *norm_w, float *conv_state, int has_prev,
                        float *rec_state, int has_init, float *out, void *ws, size_t ws_bytes, cudaStream_t st);
@@ -208,6 +211,36 @@ int q35_q8_gemv(int32_t in_dim, int32_t out_dim, const float *x, const uint32_t 
   Q35_PTR(x); Q35_PTR16(w); Q35_PTR(scales); Q35_PTR(y);
   if (int rc = require_sm100()) return rc;
   return q8_gemv_launch(in_dim, out_dim, x, w, scales, y, mode, static_cast<cudaStream_t>(stream));
+}
+
+int q35_q8_gemv_fused(int32_t in_dim, int32_t n_seg, const q35_q8_segment *segs, const float *x,
+                      const float *residual, const float *norm_w, float eps, float *sum_out, float *x_out,
+                      int32_t swiglu, int32_t mode, void *stream) {
+  Q35_REQUIRE(in_dim > 0, Q35_ERR_INVALID_ARG, "q8_gemv_fused: in_dim must be > 0");
+  Q35_REQUIRE(mode == 0 || mode == 1, Q35_ERR_INVALID_ARG, "q8_gemv_fused: mode must be 0 or 1");
+  Q35_REQUIRE(swiglu == 0 || swiglu == 1, Q35_ERR_INVALID_ARG, "q8_gemv_fused: swiglu must be 0 or 1");
+  Q35_REQUIRE(n_seg >= 1 && n_seg <= 4, Q35_ERR_INVALID_ARG, "q8_gemv_fused: 1 to 4 segments");
+  Q35_PTR(segs); Q35_PTR16(x);
+  Q35_REQUIRE(!swiglu || (n_seg == 2 && segs[0].out_dim == segs[1].out_dim), Q35_ERR_INVALID_ARG,
+              "q8_gemv_fused: swiglu takes two segments (up, gate) of equal out_dim");
+  Q35_REQUIRE(in_dim % 4 == 0 && in_dim <= (norm_w ? 8192 : 16384), Q35_ERR_UNSUPPORTED,
+              "q8_gemv_fused: in_dim must be a multiple of 4, at most 8192 with the norm (16384 without)");
+  Q35_REQUIRE(norm_w != nullptr || (residual == nullptr && sum_out == nullptr && x_out == nullptr), Q35_ERR_INVALID_ARG,
+              "q8_gemv_fused: residual / sum_out / x_out need norm_w");
+  if (residual) Q35_PTR16(residual);
+  if (norm_w) Q35_PTR16(norm_w);
+  for (int k = 0; k < n_seg; ++k) {
+    Q35_REQUIRE(segs[k].out_dim > 0 && segs[k].out_dim % 256 == 0, Q35_ERR_UNSUPPORTED,
+                "q8_gemv_fused: every out_dim must be a positive multiple of 256");
+    Q35_PTR16(segs[k].w); Q35_PTR16(segs[k].scales); Q35_PTR(segs[k].y);
+  }
+  const void *outs[2] = {sum_out, x_out};
+  for (const void *o : outs)
+    Q35_REQUIRE(o == nullptr || (o != x && o != residual), Q35_ERR_INVALID_ARG,
+                "q8_gemv_fused: sum_out / x_out must not alias x or residual");
+  if (int rc = require_sm100()) return rc;
+  return q8_gemv_fused_launch(in_dim, n_seg, segs, x, residual, norm_w, eps, sum_out, x_out, swiglu, mode,
+                              static_cast<cudaStream_t>(stream));
 }
 
 size_t q35_gqa_prefill_workspace_size(const q35_gqa_dims *dims, int32_t seq_len, int64_t max_len) {

@@ -163,41 +163,56 @@ int launch_nq(const GemvParams &p, cudaStream_t st) {
 }
 
 // ---------------------------------------------------------------------------
-// TMA path (out_dim % 256 == 0, x 16-byte aligned): a CTA owns 64 output
-// columns (one scale per row) over every row.  A producer thread streams
-// 128-row boxes of the weights ([128 x 64] bytes) and of the scales ([128 x 4]
-// floats: the 16-byte TMA minimum, of which one column is used) from 2-D tensor
-// maps over the reference layout into a 6-stage ring -- one instruction per
-// box, so the stream is not capped by the SM's outstanding-load limit that
-// bounds the per-thread LDG kernel above.  Eight consumer warps take 8 rows x
-// 64 bytes per step (lane = row * 4 + 16-byte quarter) and reduce with warp
-// shuffles and one shared-memory pass.  When the column blocks alone give few
-// CTAs, the row boxes are split over a cluster of KS CTAs (grid.y) and rank 0
-// adds the ranks' 64 column sums through distributed shared memory in rank
-// order (deterministic).
+// TMA path (every out_dim % 256 == 0, x 16-byte aligned): a CTA owns 64
+// output columns (one scale per row) over every row.  A producer thread
+// streams 128-row boxes of the weights ([128 x 64] bytes) and of the scales
+// ([128 x 4] floats: the 16-byte TMA minimum, of which one column is used) from
+// 2-D tensor maps over the reference layout into a shared-memory ring -- one
+// instruction per box, so the stream is not capped by the SM's
+// outstanding-load limit that bounds the per-thread LDG kernel above.  Eight
+// consumer warps take 8 rows x 64 bytes per step (lane = row * 4 + 16-byte
+// quarter) and reduce with warp shuffles and one shared-memory pass.  When the
+// column blocks alone give few CTAs, the row boxes are split over a cluster of
+// KS CTAs (grid.y) and rank 0 adds the ranks' column sums through distributed
+// shared memory in rank order (deterministic).
+//
+// One launch serves up to 4 projections of the same input (segments, laid out
+// one after the other along grid.x), optionally with the decoder's input
+// RMSNorm fused in front (h = x + residual, the input is
+// h / sqrt(mean(h^2) + eps) * (1 + norm_w); text_modules.rs:800-809, residual of
+// :1053-1085) and optionally with the MLP's SwiGLU behind (two segments up and
+// gate streamed by the same CTA, y = up * silu(gate); :999-1011).
 constexpr int kTC = 64;
 constexpr int kTR = 128;
-constexpr int kTNS = 6;
 constexpr int kTWarps = 8;
 constexpr int kTThreads = (kTWarps + 1) * 32;
+constexpr int kMaxSeg = 4;
 
-struct alignas(64) GemvTmaParams {
+struct alignas(64) GemvSeg {
   CUtensorMap wmap;  // uint8 [in][out], box {64, 128}
   CUtensorMap smap;  // f32 [in][out / 64], box {4, 128}
-  const float *x;
   float *y;
-  int in_dim, out_dim;
-  int chunk, per_split, ref_splits;  // mode 1 row set
-  int ks;                            // row-box split = cluster size
+  int out_dim, ncb;                  // ncb = out_dim / 64 column blocks
+  int chunk, per_split, ref_splits;  // mode 1 row set of this projection
 };
 
+struct alignas(64) GemvTmaParams {
+  GemvSeg seg[kMaxSeg];
+  const float *x, *residual, *norm_w;
+  float *sum_out, *x_out;
+  float eps;
+  int in_dim, nseg, ks;
+};
+
+template <int NW, int NS>  // NW weight streams per CTA (2: SwiGLU), NS ring stages
 struct GemvTmaSmem {
-  unsigned char w[kTNS][kTR][kTC];
-  float sc[kTNS][kTR][4];
-  float red[kTWarps][kTC];
-  float mine[kTC];  // this CTA's column sums (read by rank 0 of the cluster)
-  uint64_t full[kTNS], empty[kTNS], xbar;
-  alignas(16) float x[4];  // in_dim floats (dynamic tail; 16-byte aligned for the bulk copy)
+  unsigned char w[NS][NW][kTR][kTC];
+  float sc[NS][NW][kTR][4];
+  float red[NW][kTWarps][kTC];
+  float mine[NW][kTC];  // this CTA's column sums (read by rank 0 of the cluster)
+  float part[kTWarps];
+  uint64_t full[NS], empty[NS], xbar;
+  alignas(16) float x[4];  // dynamic tail: x, then residual and norm_w when the norm is fused
 };
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
@@ -208,20 +223,32 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
-template <bool kCompat>
+template <bool kCompat, bool kNorm, int NW, int NS>
 __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_constant__ GemvTmaParams p) {
   pdl_entry();
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  GemvTmaSmem &sm = *reinterpret_cast<GemvTmaSmem *>(smem_raw);
+  using Smem = GemvTmaSmem<NW, NS>;
+  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int c0 = blockIdx.x * kTC;
+  // segment and column block of this CTA (SwiGLU: segments 0 and 1 together)
+  int sg = 0, cb = blockIdx.x;
+  if (NW == 1)
+    while (sg + 1 < p.nseg && cb >= p.seg[sg].ncb) {
+      cb -= p.seg[sg].ncb;
+      ++sg;
+    }
+  const GemvSeg *S[NW];
+#pragma unroll
+  for (int k = 0; k < NW; ++k) S[k] = &p.seg[sg + k];
+  const int c0 = cb * kTC;
   const int sb0 = (c0 / 64) & ~3, sj = (c0 / 64) & 3;  // scale box start (16-byte aligned) and our column in it
   const int nst_all = (p.in_dim + kTR - 1) / kTR;
   const int rk = blockIdx.y;  // row-box range of this CTA within the cluster
   const int sbeg = (int)((long long)nst_all * rk / p.ks), send = (int)((long long)nst_all * (rk + 1) / p.ks);
   const int nst = send - sbeg;
+  float *xs = sm.x, *rs = sm.x + p.in_dim, *ws = sm.x + 2 * p.in_dim;
   if (tid == 0) {
-    for (int i = 0; i < kTNS; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], kTWarps);
     }
@@ -232,28 +259,65 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
   bool ok = true;
   if (warp == kTWarps) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(&sm.xbar, (uint32_t)p.in_dim * sizeof(float));
-      bulk_g2s_nohint(sm.x, p.x, (uint32_t)p.in_dim * sizeof(float), &sm.xbar);
+      const uint32_t xb = (uint32_t)p.in_dim * sizeof(float);
+      const bool res = kNorm && p.residual != nullptr;
+      mbar_arrive_expect_tx(&sm.xbar, xb * (kNorm ? (res ? 3 : 2) : 1));
+      bulk_g2s_nohint(xs, p.x, xb, &sm.xbar);
+      if (kNorm) {
+        bulk_g2s_nohint(ws, p.norm_w, xb, &sm.xbar);
+        if (res) bulk_g2s_nohint(rs, p.residual, xb, &sm.xbar);
+      }
       for (int st = 0; st < nst && ok; ++st) {
-        const int slot = st % kTNS;
-        if (st >= kTNS && !mbar_wait(&sm.empty[slot], ((st / kTNS) - 1) & 1)) {
+        const int slot = st % NS;
+        if (st >= NS && !mbar_wait(&sm.empty[slot], ((st / NS) - 1) & 1)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&sm.full[slot], kTR * kTC + kTR * 4 * sizeof(float));
-        tma_load_2d(&sm.w[slot][0][0], &p.wmap, c0, (sbeg + st) * kTR, &sm.full[slot]);
-        tma_load_2d(&sm.sc[slot][0][0], &p.smap, sb0, (sbeg + st) * kTR, &sm.full[slot]);
+        mbar_arrive_expect_tx(&sm.full[slot], NW * (kTR * kTC + kTR * 4 * sizeof(float)));
+#pragma unroll
+        for (int k = 0; k < NW; ++k) {
+          tma_load_2d(&sm.w[slot][k][0][0], &S[k]->wmap, c0, (sbeg + st) * kTR, &sm.full[slot]);
+          tma_load_2d(&sm.sc[slot][k][0][0], &S[k]->smap, sb0, (sbeg + st) * kTR, &sm.full[slot]);
+        }
       }
     }
   } else {
-    float acc[16];
+    ok = __all_sync(0xffffffffu, mbar_wait(&sm.xbar, 0));
+    if (kNorm) {  // input RMSNorm over the whole row, by the 256 consumer threads
+      const bool res = p.residual != nullptr;
+      float ss = 0.0f;
+      for (int i = tid; i < p.in_dim; i += kTWarps * 32) {
+        float h = xs[i];
+        if (res) h = h + rs[i];
+        xs[i] = h;
+        ss = fmaf(h, h, ss);
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) sm.part[warp] = ss;
+      named_bar_sync(1, kTWarps * 32);
+      float tot = 0.0f;
 #pragma unroll
-    for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
-    if (!mbar_wait(&sm.xbar, 0)) ok = false;
+      for (int w = 0; w < kTWarps; ++w) tot += sm.part[w];
+      const float inv = 1.0f / sqrtf(tot / (float)p.in_dim + p.eps);
+      const bool first = blockIdx.x == 0 && blockIdx.y == 0;
+      for (int i = tid; i < p.in_dim; i += kTWarps * 32) {
+        const float h = xs[i];
+        const float v = (h * inv) * (1.0f + ws[i]);
+        if (first && p.sum_out) p.sum_out[i] = h;
+        if (first && p.x_out) p.x_out[i] = v;
+        xs[i] = v;
+      }
+      named_bar_sync(1, kTWarps * 32);
+    }
+    float acc[NW][16];
+#pragma unroll
+    for (int k = 0; k < NW; ++k)
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc[k][e] = 0.0f;
     const int q = lane & 3;
     for (int st = 0; st < nst && ok; ++st) {
-      const int slot = st % kTNS;
-      if (!mbar_wait(&sm.full[slot], (st / kTNS) & 1)) {
+      const int slot = st % NS;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.full[slot], (st / NS) & 1))) {
         ok = false;
         break;
       }
@@ -261,14 +325,17 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
       for (int step = 0; step < kTR / (8 * kTWarps); ++step) {
         const int rr = warp * (kTR / kTWarps) + step * 8 + (lane >> 2);
         const int row = (sbeg + st) * kTR + rr;
-        bool live = row < p.in_dim;
-        if (kCompat && live) {
-          const int s = row / p.chunk;
-          live = s < p.ref_splits && row - s * p.chunk < p.per_split;
-        }
-        if (live) {
-          const uint4 w = *reinterpret_cast<const uint4 *>(&sm.w[slot][rr][16 * q]);
-          fma16(acc, w, sm.x[row] * sm.sc[slot][rr][sj]);
+#pragma unroll
+        for (int k = 0; k < NW; ++k) {
+          bool live = row < p.in_dim;
+          if (kCompat && live) {
+            const int s = row / S[k]->chunk;
+            live = s < S[k]->ref_splits && row - s * S[k]->chunk < S[k]->per_split;
+          }
+          if (live) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(&sm.w[slot][k][rr][16 * q]);
+            fma16(acc[k], w, xs[row] * sm.sc[slot][k][rr][sj]);
+          }
         }
       }
       __syncwarp();
@@ -276,40 +343,57 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
     }
     // reduce over the 8 rows of a step (lane bits 2-4): lane holds columns 16 q + 2 g, + 1 (g = lane / 4)
 #pragma unroll
-    for (int off = 16, n = 16; off >= 4; off >>= 1) {
-      const bool upper = (lane & off) != 0;
-      n >>= 1;
+    for (int k = 0; k < NW; ++k) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (j < n) {
-          const float send = upper ? acc[j] : acc[j + n];
-          const float keep = upper ? acc[j + n] : acc[j];
-          acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      for (int off = 16, n = 16; off >= 4; off >>= 1) {
+        const bool upper = (lane & off) != 0;
+        n >>= 1;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (j < n) {
+            const float send = upper ? acc[k][j] : acc[k][j + n];
+            const float keep = upper ? acc[k][j + n] : acc[k][j];
+            acc[k][j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+          }
         }
       }
+      sm.red[k][warp][16 * q + 2 * (lane >> 2)] = acc[k][0];
+      sm.red[k][warp][16 * q + 2 * (lane >> 2) + 1] = acc[k][1];
     }
-    sm.red[warp][16 * q + 2 * (lane >> 2)] = acc[0];
-    sm.red[warp][16 * q + 2 * (lane >> 2) + 1] = acc[1];
   }
   __syncthreads();
   const float poison = __int_as_float(0x7fc00000);  // a bounded wait gave up
+  float v[NW];
   if (tid < kTC) {
-    float v = sm.red[0][tid];
 #pragma unroll
-    for (int w = 1; w < kTWarps; ++w) v += sm.red[w][tid];
-    if (!ok) v = poison;
-    if (p.ks == 1) p.y[c0 + tid] = v;
-    else sm.mine[tid] = v;
+    for (int k = 0; k < NW; ++k) {
+      float t = sm.red[k][0][tid];
+#pragma unroll
+      for (int w = 1; w < kTWarps; ++w) t += sm.red[k][w][tid];
+      v[k] = ok ? t : poison;
+      sm.mine[k][tid] = v[k];
+    }
   }
+  bool write = true;
   if (p.ks > 1) {
     cluster_sync_all();
-    if (cluster_ctarank() == 0 && tid < kTC) {
-      float t = 0.0f;
-      for (int r = 0; r < p.ks; ++r) t += ld_dsmem_f32(&sm.mine[tid], (uint32_t)r);
-      p.y[c0 + tid] = t;
+    write = cluster_ctarank() == 0;
+    if (write && tid < kTC) {
+#pragma unroll
+      for (int k = 0; k < NW; ++k) {
+        float t = 0.0f;
+        for (int r = 0; r < p.ks; ++r) t += ld_dsmem_f32(&sm.mine[k][tid], (uint32_t)r);
+        v[k] = t;
+      }
     }
-    cluster_sync_all();  // no CTA leaves while rank 0 still reads its sums
   }
+  if (write && tid < kTC) {
+    if (NW == 2)
+      S[0]->y[c0 + tid] = v[0] * siluf_dev(v[NW - 1]);  // up * silu(gate)
+    else
+      S[0]->y[c0 + tid] = v[0];
+  }
+  if (p.ks > 1) cluster_sync_all();  // no CTA leaves while rank 0 still reads its sums
 }
 
 bool gemv_tma_enabled() {
@@ -320,32 +404,87 @@ bool gemv_tma_enabled() {
   return on;
 }
 
-// Encodes the two tensor maps; false when the driver rejects them.
-bool encode_gemv_maps(GemvTmaParams &p, const uint32_t *w, const float *scales, int in_dim, int out_dim) {
+// cuTensorMapEncodeTiled, resolved through the runtime so that the library
+// does not link libcuda (it loads on machines without a driver, for the
+// symbol and argument checks).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled_fn() {
+  static const EncodeTiledFn fn = [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// Encodes the two tensor maps of one projection; false when the driver rejects them.
+bool encode_gemv_maps(GemvSeg &g, const uint32_t *w, const float *scales, int in_dim, int out_dim) {
+  const EncodeTiledFn cuTensorMapEncodeTiled = encode_tiled_fn();
+  if (!cuTensorMapEncodeTiled) return false;
   const cuuint64_t wd[2] = {(cuuint64_t)out_dim, (cuuint64_t)in_dim};
-  const cuuint64_t ws[1] = {(cuuint64_t)out_dim};
+  const cuuint64_t wstr[1] = {(cuuint64_t)out_dim};
   const cuuint32_t wb[2] = {kTC, kTR};
   const cuuint64_t sd[2] = {(cuuint64_t)(out_dim / 64), (cuuint64_t)in_dim};
-  const cuuint64_t ss[1] = {(cuuint64_t)(out_dim / 64) * sizeof(float)};
+  const cuuint64_t sstr[1] = {(cuuint64_t)(out_dim / 64) * sizeof(float)};
   const cuuint32_t sbx[2] = {4, kTR};
   const cuuint32_t es[2] = {1, 1};
-  if (cuTensorMapEncodeTiled(&p.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint32_t *>(w), wd, ws, wb, es,
+  if (cuTensorMapEncodeTiled(&g.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint32_t *>(w), wd, wstr, wb, es,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return false;
-  return cuTensorMapEncodeTiled(&p.smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(scales), sd, ss, sbx,
-                                es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+  return cuTensorMapEncodeTiled(&g.smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(scales), sd, sstr,
+                                sbx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int launch_tma(const GemvTmaParams &p, bool compat, cudaStream_t st) {
-  const size_t smem = sizeof(GemvTmaSmem) + (size_t)p.in_dim * sizeof(float);  // x tail (over-sized by 16 B)
-  auto kern = compat ? q8_gemv_tma_kernel<true> : q8_gemv_tma_kernel<false>;
+template <bool kCompat, bool kNorm, int NW, int NS>
+int launch_tma_t(const GemvTmaParams &p, int ctas, cudaStream_t st) {
+  const size_t smem = sizeof(GemvTmaSmem<NW, NS>) + (size_t)(kNorm ? 3 : 1) * p.in_dim * sizeof(float);
+  auto kern = q8_gemv_tma_kernel<kCompat, kNorm, NW, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "q8_gemv attributes");
   note_launch();
-  (void)launch_kernel(kern, dim3(p.out_dim / kTC, p.ks), dim3(kTThreads), smem, st, 1, (unsigned)p.ks, p);
+  (void)launch_kernel(kern, dim3(ctas, p.ks), dim3(kTThreads), smem, st, 1, (unsigned)p.ks, p);
   return check_cuda(cudaGetLastError(), "q8_gemv launch");
+}
+
+int launch_tma(GemvTmaParams &p, bool compat, bool norm, bool swiglu, cudaStream_t st) {
+  int ctas = 0;
+  for (int k = 0; k < p.nseg; ++k) ctas += p.seg[k].ncb;
+  if (swiglu) ctas = p.seg[0].ncb;
+  // row-box split: the largest of 8 / 4 / 2 that keeps the grid within two CTAs per SM
+  const int nst = (p.in_dim + kTR - 1) / kTR;
+  p.ks = 1;
+  for (int k : {8, 4, 2})
+    if (ctas * k <= 2 * device_sm_count() && k <= nst) {
+      p.ks = k;
+      break;
+    }
+  if (swiglu) {
+    if (compat) return norm ? launch_tma_t<true, true, 2, 4>(p, ctas, st) : launch_tma_t<true, false, 2, 4>(p, ctas, st);
+    return norm ? launch_tma_t<false, true, 2, 4>(p, ctas, st) : launch_tma_t<false, false, 2, 4>(p, ctas, st);
+  }
+  if (compat) return norm ? launch_tma_t<true, true, 1, 6>(p, ctas, st) : launch_tma_t<true, false, 1, 6>(p, ctas, st);
+  return norm ? launch_tma_t<false, true, 1, 6>(p, ctas, st) : launch_tma_t<false, false, 1, 6>(p, ctas, st);
+}
+
+// Fills segment k from (w, scales, y, out_dim) with the row plan of `mode`.
+bool fill_segment(GemvSeg &g, int in_dim, int out_dim, const uint32_t *w, const float *scales, float *y, int mode) {
+  if (!encode_gemv_maps(g, w, scales, in_dim, out_dim)) return false;
+  const GemvPlan pl = gemv_plan(in_dim, out_dim, mode, 148);
+  g.y = y;
+  g.out_dim = out_dim;
+  g.ncb = out_dim / kTC;
+  g.chunk = std::max(pl.chunk, 1);
+  g.per_split = pl.per_split;
+  g.ref_splits = pl.per_split > 0 ? pl.rows / pl.per_split : 0;
+  return true;
 }
 
 }  // namespace
@@ -365,28 +504,40 @@ int q8_gemv_launch(int in_dim, int out_dim, const float *x, const uint32_t *w, c
   p.per_split = std::max(g.per_split, 1);
   if (gemv_tma_enabled() && out_dim % 256 == 0 && in_dim % 4 == 0 && in_dim <= 16384 &&
       (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
-    GemvTmaParams t;
-    if (encode_gemv_maps(t, w, scales, in_dim, out_dim)) {
+    GemvTmaParams t = {};
+    if (fill_segment(t.seg[0], in_dim, out_dim, w, scales, y, mode)) {
       t.x = x;
-      t.y = y;
       t.in_dim = in_dim;
-      t.out_dim = out_dim;
-      t.chunk = std::max(g.chunk, 1);
-      t.per_split = g.per_split;
-      t.ref_splits = g.per_split > 0 ? g.rows / g.per_split : 0;
-      // row-box split: the largest of 8 / 4 / 2 that keeps the grid within two CTAs per SM
-      const int ncb = out_dim / kTC, nst = (in_dim + kTR - 1) / kTR;
-      t.ks = 1;
-      for (int k : {8, 4, 2})
-        if (ncb * k <= 2 * device_sm_count() && k <= nst) {
-          t.ks = k;
-          break;
-        }
-      return launch_tma(t, mode == 1, st);
+      t.nseg = 1;
+      return launch_tma(t, mode == 1, false, false, st);
     }
   }
   if (mode == 1) return g.nq == 4 ? launch_nq<true, 4>(p, st) : launch_nq<true, 2>(p, st);
   return g.nq == 4 ? launch_nq<false, 4>(p, st) : launch_nq<false, 2>(p, st);
+}
+
+}  // namespace q35
+
+namespace q35 {
+
+int q8_gemv_fused_launch(int in_dim, int n_seg, const q35_q8_segment *segs, const float *x, const float *residual,
+                         const float *norm_w, float eps, float *sum_out, float *x_out, int swiglu, int mode,
+                         cudaStream_t st) {
+  // shapes and pointers are validated at the C-ABI boundary
+  GemvTmaParams t = {};
+  for (int k = 0; k < n_seg; ++k) {
+    Q35_REQUIRE(fill_segment(t.seg[k], in_dim, segs[k].out_dim, segs[k].w, segs[k].scales, segs[k].y, mode),
+                Q35_ERR_INVALID_ARG, "q8_gemv_fused: tensor map rejected (alignment of w / scales)");
+  }
+  t.x = x;
+  t.residual = residual;
+  t.norm_w = norm_w;
+  t.sum_out = sum_out;
+  t.x_out = x_out;
+  t.eps = eps;
+  t.in_dim = in_dim;
+  t.nseg = n_seg;
+  return launch_tma(t, mode == 1, norm_w != nullptr, swiglu != 0, st);
 }
 
 }  // namespace q35

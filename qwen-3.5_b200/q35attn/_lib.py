@@ -38,6 +38,10 @@ class GqaDims(C.Structure):
                 ("capacity", C.c_int64), ("eps", C.c_float)]
 
 
+class Q8Segment(C.Structure):
+    _fields_ = [("w", C.c_void_p), ("scales", C.c_void_p), ("y", C.c_void_p), ("out_dim", C.c_int32)]
+
+
 _P = C.c_void_p
 _I32, _I64, _SZ = C.c_int32, C.c_int64, C.c_size_t
 
@@ -50,6 +54,8 @@ SIGNATURES = {
                                   _P]),
     "q35_gdn_gate": (C.c_int, [_I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _I32, _P]),
     "q35_q8_gemv": (C.c_int, [_I32, _I32, _P, _P, _P, _P, _I32, _P]),
+    "q35_q8_gemv_fused": (C.c_int, [_I32, _I32, C.POINTER(Q8Segment), _P, _P, _P, C.c_float, _P, _P, _I32, _I32,
+                                    _P]),
     "q35_q8_embedding": (C.c_int, [_I32, _I32, _I32, _P, _P, _P, _P, _P]),
     "q35_add_rmsnorm": (C.c_int, [_I32, _I32, _P, _P, _P, C.c_float, _P, _P, _P]),
     "q35_silu_mul": (C.c_int, [_I64, _P, _P, _P, _P]),

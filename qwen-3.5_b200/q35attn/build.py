@@ -82,7 +82,7 @@ def build(force: bool = False, verbose: bool = False, jobs: int = 8) -> str:
     if errs:
         raise RuntimeError("nvcc failed:\n" + "\n".join(errs))
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *GENCODE, "-shared", "-ccbin", "g++", "-o", tmp, *objs, "-lcuda"]
+    cmd = [nvcc(), *GENCODE, "-shared", "-ccbin", "g++", "-o", tmp, *objs]
     subprocess.run(cmd, check=True, env=env)
     os.replace(tmp, LIB)
     return LIB

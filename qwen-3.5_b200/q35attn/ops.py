@@ -10,10 +10,10 @@ import ctypes as C
 
 import torch
 
-from ._lib import GdnDims, GqaDims, Q35Error, check, load
+from ._lib import GdnDims, GqaDims, Q35Error, Q8Segment, check, load
 
 __all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_workspace", "gdn_gate", "GqaWorkspace", "gqa_decode", "GqaPrefillWorkspace", "gqa_prefill",
-           "q8_gemv", "launch_count", "Q35Error"]
+           "q8_gemv", "q8_gemv_fused", "launch_count", "Q35Error"]
 
 
 def _req(t: torch.Tensor, name: str, dtype=torch.float32) -> int:
@@ -112,6 +112,51 @@ def q8_gemv(x, w, scales, y=None, *, mode=0, stream=None):
     check(load().q35_q8_gemv(in_dim, out_dim, _req(x, "x"), w.data_ptr(), _req(scales, "scales"), _req(y, "y"),
                              int(mode), _stream(stream)))
     return y
+
+
+def _words(w, name="w") -> int:
+    if w.dtype not in (torch.int32, torch.uint32) or not w.is_contiguous() or w.device.type != "cuda":
+        raise TypeError(f"{name} must be a contiguous int32/uint32 CUDA tensor")
+    return w.data_ptr()
+
+
+class FusedGemv:
+    """A prepared q35_q8_gemv_fused call: the segment table is built once, so a
+    decode step (or a CUDA graph capture) pays no per-call Python packing."""
+
+    def __init__(self, x, weights, ys, *, residual=None, norm_w=None, eps=1e-6, sum_out=None, x_out=None,
+                 swiglu=False, mode=0):
+        if not 1 <= len(weights) <= 4 or len(ys) != len(weights):
+            raise ValueError("1 to 4 (w, scales) pairs, one y each")
+        self.in_dim = x.numel()
+        segs = (Q8Segment * len(weights))()
+        for k, ((w, sc), y) in enumerate(zip(weights, ys)):
+            segs[k].w = _words(w)
+            segs[k].scales = _req(sc, "scales")
+            segs[k].y = _req(y, "y")
+            segs[k].out_dim = w.shape[1] * 4
+        self.segs = segs
+        opt = lambda t, n: 0 if t is None else _req(t, n)
+        self.args = (self.in_dim, len(weights), segs, _req(x, "x"), opt(residual, "residual"), opt(norm_w, "norm_w"),
+                     float(eps), opt(sum_out, "sum_out"), opt(x_out, "x_out"), int(bool(swiglu)), int(mode))
+        self._keep = (x, weights, ys, residual, norm_w, sum_out, x_out)
+
+    def __call__(self, stream=None):
+        check(load().q35_q8_gemv_fused(*self.args, _stream(stream)))
+
+
+def q8_gemv_fused(x, weights, *, ys=None, residual=None, norm_w=None, eps=1e-6, sum_out=None, x_out=None,
+                  swiglu=False, mode=0, stream=None):
+    """Up to four Q8F GEMVs of one input in one launch (q35_q8_gemv_fused):
+    weights = [(w, scales), ...]; with norm_w the input is RMSNorm(x +
+    residual) * (1 + norm_w) and sum_out / x_out receive x + residual and the
+    normalised input; swiglu=True takes (up, gate) and returns up * silu(gate).
+    Returns the list of outputs (one tensor when swiglu)."""
+    if ys is None:
+        ys = [torch.empty(w.shape[1] * 4, device=x.device, dtype=torch.float32) for w, _ in weights]
+    FusedGemv(x, weights, ys, residual=residual, norm_w=norm_w, eps=eps, sum_out=sum_out, x_out=x_out,
+              swiglu=swiglu, mode=mode)(stream)
+    return ys[0] if swiglu else ys
 
 
 def gqa_dims(batch, num_q_heads, num_kv_heads, capacity, rotary_dim=64, eps=1e-6, head_dim=256) -> GqaDims:

@@ -68,8 +68,9 @@ class Q8F:
 
 class HybridStack:
     def __init__(self, cfg: StackConfig = QWEN35_2B, capacity: int = 2048, seed: int = 0, device="cuda",
-                 gemv_mode: int = 1, prefill_chunk: int = 2048):
+                 gemv_mode: int = 1, prefill_chunk: int = 2048, fused: bool = True):
         self.cfg, self.cap, self.dev, self.gemv_mode = cfg, capacity, torch.device(device), gemv_mode
+        self.fused, self._plan = fused, None
         g = torch.Generator(device=self.dev)
         g.manual_seed(seed)
         c, dev = cfg, self.dev
@@ -124,7 +125,7 @@ class HybridStack:
     def _decode_buffers(self):
         c, dev = self.cfg, self.dev
         e = lambda *s: torch.empty(*s, device=dev)
-        self.b = {"h": e(c.hidden), "x": e(c.hidden), "attn": e(c.hidden), "mlp": e(c.hidden),
+        self.b = {"h": e(c.hidden), "h2": e(c.hidden), "x": e(c.hidden), "attn": e(c.hidden), "mlp": e(c.hidden),
                   "mixed": e(1, c.conv_dim), "z": e(1, c.gdn_hv * 128), "beta": e(1, c.gdn_hv), "g": e(1, c.gdn_hv),
                   "core": e(1, max(c.gdn_hv * 128, c.gqa_hq * 256)), "qg": e(1, c.gqa_hq, 512),
                   "kk": e(1, c.gqa_hkv, 256), "vv": e(1, c.gqa_hkv, 256), "up": e(c.inter), "gt": e(c.inter),
@@ -150,6 +151,8 @@ class HybridStack:
     # ------------------------------------------------------------ decode
     def _decode_step(self):
         """One token: embedding of self.b['tok'] -> ... -> argmax into self.b['tok']."""
+        if self.fused:
+            return self._decode_step_fused()
         c, b = self.cfg, self.b
         ops.q8_embedding(b["tok"], self.embed.words, self.embed.scales, b["h"].view(1, -1))
         if self.gqa_layers:  # every GQA layer decodes at the same position
@@ -184,6 +187,64 @@ class HybridStack:
             self.gemv(b["act"], L["down"], b["mlp"])
             resid = True
         ops.add_rmsnorm(b["mlp"], self.final_norm, b["x"], residual=b["h"], eps=c.eps)
+        ops.q8_lm_head(b["x"], self.embed.words, self.embed.scales, b["logits"])
+        ops.argmax(b["logits"], b["tok"], self.argmax_ws)
+
+    def _fused_plan(self):
+        """Prepared q35_q8_gemv_fused calls of every layer.  The residual stream
+        alternates between two buffers (h, h2): each fused norm reads the
+        current one and writes h + x into the other, so no kernel reads a
+        buffer that the same launch writes."""
+        c, b, m = self.cfg, self.b, self.gemv_mode
+        W = lambda q: (q.words, q.scales)
+        hs = [b["h"], b["h2"]]
+        cur, plan = 0, []
+        for i, L in enumerate(self.layers):
+            first = i == 0
+            kw = dict(norm_w=L["in_norm"], eps=c.eps, mode=m,
+                      residual=None if first else hs[cur], sum_out=None if first else hs[1 - cur])
+            xin = hs[cur] if first else b["mlp"]
+            if not first:
+                cur = 1 - cur
+            if L["kind"] == "linear":  # in_proj_qkvz with the input norm; x_out feeds the gate projection
+                front = ops.FusedGemv(xin, [W(L["qkv"]), W(L["z"])], [b["mixed"].view(-1), b["z"].view(-1)],
+                                      x_out=b["x"], **kw)
+                out = ops.FusedGemv(b["core"][:, :c.gdn_hv * 128].view(-1), [W(L["out"])], [b["attn"]], mode=m)
+            else:
+                front = ops.FusedGemv(xin, [W(L["q"]), W(L["k"]), W(L["v"])],
+                                      [b["qg"].view(-1), b["kk"].view(-1), b["vv"].view(-1)], **kw)
+                out = ops.FusedGemv(b["core"][:, :c.gqa_hq * 256].view(-1), [W(L["o"])], [b["attn"]], mode=m)
+            mlp = ops.FusedGemv(b["attn"], [W(L["up"]), W(L["gate"])], [b["act"], b["gt"]], residual=hs[cur],
+                                norm_w=L["post_norm"], eps=c.eps, sum_out=hs[1 - cur], swiglu=True, mode=m)
+            cur = 1 - cur
+            down = ops.FusedGemv(b["act"], [W(L["down"])], [b["mlp"]], mode=m)
+            plan.append((L, front, out, mlp, down))
+        return plan, hs[cur]
+
+    def _decode_step_fused(self):
+        c, b = self.cfg, self.b
+        if self._plan is None:
+            self._plan = self._fused_plan()
+        plan, h_last = self._plan
+        ops.q8_embedding(b["tok"], self.embed.words, self.embed.scales, b["h"].view(1, -1))
+        if self.gqa_layers:
+            ops.rope_gather(self.gqa_layers[0]["lens"], self.rope_cos, self.rope_sin, b["cos"], b["sin"])
+        for L, front, out, mlp, down in plan:
+            front()
+            if L["kind"] == "linear":
+                ops.gdn_gate(b["x"].view(1, -1), L["w_b"], L["w_a"], L["a_log"], L["dt_bias"], mode=0,
+                             beta=b["beta"], g=b["g"])
+                ops.gdn_decode(b["mixed"], b["z"], b["beta"], b["g"], L["conv_w"], L["norm_w"], L["conv_state"],
+                               L["rec_state"], b["core"][:, :c.gdn_hv * 128], num_k_heads=c.gdn_hk,
+                               num_v_heads=c.gdn_hv, eps=c.eps)
+            else:
+                ops.gqa_decode(b["qg"], b["kk"], b["vv"], L["qn_w"], L["kn_w"], b["cos"], b["sin"], L["K"], L["V"],
+                               L["lens"], b["core"][:, :c.gqa_hq * 256], workspace=self.gqa_ws, max_len=self.cap,
+                               rotary_dim=c.rot, eps=c.eps)
+            out()
+            mlp()  # h += attn; act = up * silu(gate) of RMSNorm(h) * (1 + post_norm)
+            down()
+        ops.add_rmsnorm(b["mlp"], self.final_norm, b["x"], residual=h_last, eps=c.eps)
         ops.q8_lm_head(b["x"], self.embed.words, self.embed.scales, b["logits"])
         ops.argmax(b["logits"], b["tok"], self.argmax_ws)
 

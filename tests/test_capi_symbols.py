@@ -96,3 +96,24 @@ def test_python_wrappers_refuse_cpu_tensors():
         q35attn.gdn_decode(x, torch.zeros(1, 2048), torch.zeros(1, 16), torch.zeros(1, 16), torch.zeros(6144, 4),
                            torch.ones(128), torch.zeros(1, 6144, 3), torch.zeros(1, 16, 128, 128),
                            out=torch.zeros(1, 2048), num_k_heads=16, num_v_heads=16)
+
+
+def test_fused_gemv_validation_without_device():
+    lib = q35attn.load()
+    seg = (_lib.Q8Segment * 2)()
+    for k in range(2):
+        seg[k].w, seg[k].scales, seg[k].y, seg[k].out_dim = 4096, 8192, 12288, 256
+    call = lambda n, x=1 << 20, res=None, nw=None, so=None, xo=None, sw=0, mode=0, ind=256: lib.q35_q8_gemv_fused(
+        ind, n, seg, x, res, nw, 1e-6, so, xo, sw, mode, None)
+    assert call(0) == _lib.ERR_INVALID_ARG           # no segment
+    assert call(5) == _lib.ERR_INVALID_ARG           # more than four
+    assert call(2, x=(1 << 20) + 4) == _lib.ERR_INVALID_ARG  # x not 16-byte aligned
+    assert call(1, sw=1) == _lib.ERR_INVALID_ARG     # swiglu needs (up, gate)
+    assert call(2, res=1 << 21) == _lib.ERR_INVALID_ARG  # residual without norm_w
+    assert call(2, nw=1 << 21, so=1 << 20) == _lib.ERR_INVALID_ARG  # sum_out aliases x
+    assert call(2, ind=254) == _lib.ERR_UNSUPPORTED  # in_dim % 4
+    assert call(2, nw=1 << 21, ind=8196) == _lib.ERR_UNSUPPORTED  # too long for the norm's shared memory
+    seg[1].out_dim = 320
+    assert call(2) == _lib.ERR_UNSUPPORTED           # out_dim % 256
+    seg[1].out_dim = 256
+    assert call(2, mode=2) == _lib.ERR_INVALID_ARG

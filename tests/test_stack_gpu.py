@@ -5,7 +5,9 @@ built from the pinned oracle pieces.  A reduced configuration (4 layers, 2-head
 GDN, 2/1-head GQA, vocab 4096) keeps the CPU side fast; hidden stays 2048.
 Logits: max rel err <= 1e-3 per step; the reference is teacher-forced with the
 GPU's tokens, and every GPU token must equal the reference argmax unless the
-reference's top-2 gap is below 1e-4 of its max logit."""
+reference's top-2 gap is below 1e-4 of its max logit.  Decode runs both with
+the fused projections (q35_q8_gemv_fused: norm + GEMVs + SwiGLU per launch)
+and with one launch per projection."""
 import numpy as np
 import pytest
 import torch
@@ -25,9 +27,10 @@ def _check_token(tok, logits):
         assert tok == int(np.argmax(logits))
 
 
+@pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("gemv_mode", [1, 0])
-def test_small_stack_prefill_and_decode(gemv_mode):
-    st = qs.HybridStack(SMALL, capacity=128, seed=3, gemv_mode=gemv_mode)
+def test_small_stack_prefill_and_decode(gemv_mode, fused):
+    st = qs.HybridStack(SMALL, capacity=128, seed=3, gemv_mode=gemv_mode, fused=fused)
     ids = torch.from_numpy(np.random.RandomState(4).randint(0, SMALL.vocab, 45).astype(np.int32)).cuda()
     ref = StackRef(st)
     tok = int(st.prefill(ids).item())
