@@ -3,9 +3,16 @@
 // mode 0 restates kernels.rs:174-247 (gate_proj_kernel, used at decode,
 // text_modules.rs:569-576): 8 row splits summed sequentially in blocks of 8,
 // partial sums added in split order, softplus threshold tested on the
-// softplus value.  One CTA per input row; thread (split, which, head) owns one
-// partial exactly like the reference's unit layout, so the f32 summation order
-// is the reference's.
+// softplus value.  Each (split, which, head) partial is accumulated row by row
+// in the reference's order and the partials are added in split order, so the
+// f32 result is the reference's.  B200 layout: one 8-CTA cluster per input
+// row, CTA s = split s.  Its rows of w_b and w_a (contiguous, H floats per
+// row) are staged into shared memory with coalesced 16-byte loads before the
+// grid-dependency wait (the weights never depend on the previous kernel, so
+// the copy overlaps it); one warp-pair then runs the 2H sequential chains from
+// shared memory, and rank 0 adds the 8 partials through distributed shared
+// memory.  Shapes whose split does not fit shared memory use the one-CTA
+// kernel (one thread per partial, straight from global memory).
 // mode 1 restates the prefill branch text_modules.rs:578-595 (matmul, sigmoid,
 // softplus with the threshold on a + dt_bias): one warp per row.
 #include "common.cuh"
@@ -51,6 +58,70 @@ __global__ void gate_decode_kernel(int in_dim, int H, const float *__restrict__ 
       g[(size_t)n * H + h] = -expf(a_log[h]) * sp;
     }
   }
+}
+
+// Copies n floats global -> shared with all threads (16-byte loads when both
+// ends are 16-byte aligned and n % 4 == 0).
+__device__ __forceinline__ void stage_f32(float *dst, const float *src, int n) {
+  if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u) == 0 && (n & 3) == 0) {
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll 8
+    for (int i = threadIdx.x; i < n / 4; i += blockDim.x) d4[i] = __ldg(s4 + i);
+  } else {
+#pragma unroll 8
+    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldg(src + i);
+  }
+}
+
+constexpr int kGateThreads = 256;
+
+__global__ void __launch_bounds__(kGateThreads) gate_decode_cluster_kernel(
+    int in_dim, int H, const float *__restrict__ x, const float *__restrict__ wb, const float *__restrict__ wa,
+    const float *__restrict__ a_log, const float *__restrict__ dt_bias, float *__restrict__ beta,
+    float *__restrict__ g) {
+  extern __shared__ __align__(16) float gsm[];
+  const int n = blockIdx.y;
+  const int split = (int)cluster_ctarank();
+  const int chunk = in_dim / kSplits;
+  const int rows = (chunk / 8) * 8;  // rows the reference walks per split (kernels.rs:190-199)
+  const int row0 = split * chunk;
+  const int wrow = (rows * H + 3) & ~3;  // 16-byte aligned sub-buffers
+  float *wbs = gsm, *was = gsm + wrow, *xs = gsm + 2 * wrow, *part = xs + ((rows + 3) & ~3);
+  stage_f32(wbs, wb + (size_t)row0 * H, rows * H);
+  stage_f32(was, wa + (size_t)row0 * H, rows * H);
+  pdl_entry();  // x is the previous kernel's output
+  stage_f32(xs, x + (size_t)n * in_dim + row0, rows);
+  __syncthreads();
+  const int u = threadIdx.x;
+  if (u < 2 * H) {
+    const int h = u % H;
+    const float *w = u < H ? wbs : was;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int r = 0; r < rows; ++r) acc += xs[r] * w[r * H + h];
+    part[u] = acc;
+  }
+  cluster_sync_all();
+  if (split == 0 && u < 2 * H) {
+    float sum = 0.0f;
+    for (int i = 0; i < kSplits; ++i) sum += ld_dsmem_f32(&part[u], (uint32_t)i);
+    const int h = u % H;
+    if (u < H) {
+      beta[(size_t)n * H + h] = 1.0f / (1.0f + expf(-sum));
+    } else {
+      const float xg = sum + dt_bias[h];
+      const float pre = logf(expf(xg) + 1.0f);
+      const float sp = pre > 20.0f ? xg : pre;
+      g[(size_t)n * H + h] = -expf(a_log[h]) * sp;
+    }
+  }
+  cluster_sync_all();  // rank 0 reads the other ranks' partials until here
+}
+
+size_t gate_cluster_smem(int in_dim, int H) {
+  const int rows = (in_dim / kSplits / 8) * 8;
+  return ((size_t)2 * ((rows * H + 3) & ~3) + ((rows + 3) & ~3) + 2 * H) * sizeof(float);
 }
 
 template <int H>
@@ -126,6 +197,16 @@ int gdn_gate_launch(int N, int in_dim, int H, const float *x, const float *wb, c
   if (N == 0) return Q35_OK;
   if (mode == 0) {
     Q35_REQUIRE(2 * H * kSplits <= 1024, Q35_ERR_UNSUPPORTED, "gdn_gate: num_heads must be <= 64 for mode 0");
+    const size_t smem = gate_cluster_smem(in_dim, H);
+    if (N <= 65535 && smem <= 200 * 1024 && in_dim >= kSplits * 8) {
+      cudaError_t e = cudaFuncSetAttribute(gate_decode_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+      if (e != cudaSuccess) return check_cuda(e, "gdn_gate attributes");
+      note_launch();
+      (void)launch_kernel(gate_decode_cluster_kernel, dim3(kSplits, N), dim3(kGateThreads), smem, st, kSplits, 1,
+                          in_dim, H, x, wb, wa, a_log, dt_bias, beta, g);
+      return check_cuda(cudaGetLastError(), "gdn_gate launch");
+    }
     note_launch();
     (void)launch_kernel(gate_decode_kernel, dim3(N), dim3(2 * H * kSplits), kSplits * 2 * H * sizeof(float), st, 1, 1, in_dim, H, x, wb, wa, a_log,
                                                                                       dt_bias, beta, g);

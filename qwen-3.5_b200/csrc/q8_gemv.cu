@@ -225,7 +225,6 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 
 template <bool kCompat, bool kNorm, int NW, int NS>
 __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_constant__ GemvTmaParams p) {
-  pdl_entry();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   using Smem = GemvTmaSmem<NW, NS>;
   Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
@@ -247,15 +246,30 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
   const int sbeg = (int)((long long)nst_all * rk / p.ks), send = (int)((long long)nst_all * (rk + 1) / p.ks);
   const int nst = send - sbeg;
   float *xs = sm.x, *rs = sm.x + p.in_dim, *ws = sm.x + 2 * p.in_dim;
-  if (tid == 0) {
+  const bool producer = tid == kTWarps * 32;
+  auto issue = [&](int st) {  // one ring stage: NW weight boxes and their scale boxes
+    const int slot = st % NS;
+    mbar_arrive_expect_tx(&sm.full[slot], NW * (kTR * kTC + kTR * 4 * sizeof(float)));
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+      tma_load_2d(&sm.w[slot][k][0][0], &S[k]->wmap, c0, (sbeg + st) * kTR, &sm.full[slot]);
+      tma_load_2d(&sm.sc[slot][k][0][0], &S[k]->smap, sb0, (sbeg + st) * kTR, &sm.full[slot]);
+    }
+  };
+  if (producer) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], kTWarps);
     }
     mbar_init(&sm.xbar, 1);
     fence_mbar_init();
+    // The weights and scales are never written by an earlier kernel: fill the
+    // ring before the grid-dependency wait, so the first DRAM round trips
+    // overlap the previous kernel's tail.
+    for (int st = 0; st < NS && st < nst; ++st) issue(st);
   }
   __syncthreads();
+  pdl_entry();  // x, residual and the outputs belong to the kernel stream order from here
   bool ok = true;
   if (warp == kTWarps) {
     if (lane == 0) {
@@ -267,18 +281,12 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
         bulk_g2s_nohint(ws, p.norm_w, xb, &sm.xbar);
         if (res) bulk_g2s_nohint(rs, p.residual, xb, &sm.xbar);
       }
-      for (int st = 0; st < nst && ok; ++st) {
-        const int slot = st % NS;
-        if (st >= NS && !mbar_wait(&sm.empty[slot], ((st / NS) - 1) & 1)) {
+      for (int st = NS; st < nst && ok; ++st) {
+        if (!mbar_wait(&sm.empty[st % NS], ((st / NS) - 1) & 1)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&sm.full[slot], NW * (kTR * kTC + kTR * 4 * sizeof(float)));
-#pragma unroll
-        for (int k = 0; k < NW; ++k) {
-          tma_load_2d(&sm.w[slot][k][0][0], &S[k]->wmap, c0, (sbeg + st) * kTR, &sm.full[slot]);
-          tma_load_2d(&sm.sc[slot][k][0][0], &S[k]->smap, sb0, (sbeg + st) * kTR, &sm.full[slot]);
-        }
+        issue(st);
       }
     }
   } else {

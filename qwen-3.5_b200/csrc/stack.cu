@@ -48,6 +48,51 @@ __global__ void q8_embedding_kernel(int n, int vocab, int dim, const int32_t *id
 // ------------------------------------------------------------- add + RMSNorm
 // h = x (+ residual); sum_out = h (optional); out = h / sqrt(mean(h^2) + eps) * (1 + w)
 // One CTA of 256 threads per row.
+// dim <= 16 * 256: every element is loaded into a register before anything is
+// stored (one memory round trip, and in-place use -- sum_out == residual, out
+// == x -- is safe because each thread stores only the elements it loaded).
+constexpr int kNormRegs = 16;
+
+__global__ void __launch_bounds__(256) add_rmsnorm_reg_kernel(int dim, const float *x, const float *residual,
+                                                              const float *w, float eps, float *out,
+                                                              float *sum_out) {
+  __shared__ float red[8];
+  const size_t row = blockIdx.x;
+  const float *xr = x + row * dim;
+  const float *rr = residual ? residual + row * dim : nullptr;
+  float wv[kNormRegs];
+#pragma unroll
+  for (int j = 0; j < kNormRegs; ++j) {
+    const int c = threadIdx.x + j * 256;
+    wv[j] = c < dim ? __ldg(w + c) : 0.0f;  // the norm weight is not the previous kernel's output
+  }
+  pdl_entry();
+  float hv[kNormRegs];
+#pragma unroll
+  for (int j = 0; j < kNormRegs; ++j) {
+    const int c = threadIdx.x + j * 256;
+    hv[j] = c < dim ? xr[c] + (rr ? rr[c] : 0.0f) : 0.0f;
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kNormRegs; ++j) ss = fmaf(hv[j], hv[j], ss);
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float inv = 1.0f / sqrtf(tot / (float)dim + eps);
+#pragma unroll
+  for (int j = 0; j < kNormRegs; ++j) {
+    const int c = threadIdx.x + j * 256;
+    if (c < dim) {
+      if (sum_out) sum_out[row * dim + c] = hv[j];
+      out[row * dim + c] = (hv[j] * inv) * (1.0f + wv[j]);
+    }
+  }
+}
+
 __global__ void add_rmsnorm_kernel(int dim, const float *x, const float *residual, const float *w, float eps,
                                    float *out, float *sum_out) {
   pdl_entry();
@@ -234,7 +279,11 @@ int q8_embedding_launch(int n, int vocab, int dim, const int32_t *ids, const uin
 int add_rmsnorm_launch(int n, int dim, const float *x, const float *residual, const float *w, float eps, float *out,
                        float *sum_out, cudaStream_t st) {
   note_launch();
-  (void)launch_kernel(add_rmsnorm_kernel, dim3(n), dim3(256), 0, st, 1, 1, dim, x, residual, w, eps, out, sum_out);
+  if (dim <= kNormRegs * 256)
+    (void)launch_kernel(add_rmsnorm_reg_kernel, dim3(n), dim3(256), 0, st, 1, 1, dim, x, residual, w, eps, out,
+                        sum_out);
+  else
+    (void)launch_kernel(add_rmsnorm_kernel, dim3(n), dim3(256), 0, st, 1, 1, dim, x, residual, w, eps, out, sum_out);
   return check_cuda(cudaGetLastError(), "add_rmsnorm launch");
 }
 
