@@ -738,6 +738,8 @@ def main():
                     help="only run the config-2 GDN prefill at this prompt length (profiling aid)")
     ap.add_argument("--gqa-prefill-tokens", type=int, default=0,
                     help="only run the GQA prefill (8/2 heads, empty cache) at this prompt length (profiling aid)")
+    ap.add_argument("--gemv-fused", choices=["gdn_front", "gqa_front", "mlp"], default="",
+                    help="profiling aid: one fused decode projection launch of the 2B stack, timed alone")
     ap.add_argument("--gemv", type=str, default="",
                     help="IN,OUT: only run the Q8F GEMV of that shape (profiling aid)")
     ap.add_argument("--config3-steps", type=int, default=0,
@@ -749,7 +751,7 @@ def main():
         return run_reference(args)
     if args.prefill_tokens > 0:
         return run_prefill_only(args)
-    if args.gqa_prefill_tokens > 0 or args.gemv:
+    if args.gqa_prefill_tokens > 0 or args.gemv or args.gemv_fused:
         return run_kernel_only(args)
     if args.config3_steps > 0:
         return run_config3_only(args)
@@ -791,7 +793,8 @@ def run_config3_only(args):
 
 def run_kernel_only(args):
     """--gqa-prefill-tokens T: the GQA prefill of a T-token prompt into an
-    empty cache (config-3 head shapes); --gemv IN,OUT: one Q8F GEMV (mode 0).
+    empty cache (config-3 head shapes); --gemv IN,OUT: one Q8F GEMV (mode 0);
+    --gemv-fused SHAPE: one fused decode projection (norm in front, mode 1).
     --warmup untimed calls, then --steps calls timed with CUDA events; one JSON
     line.  A profiling aid, not the bench line."""
     import torch
@@ -810,6 +813,22 @@ def run_kernel_only(args):
             q35attn.q8_gemv(x, w, sc, y, mode=0)
         case, size = "q8_gemv", {"in": ind, "out": outd}
         alg = ind * outd + ind * (outd // 64) * 4 + 4 * (ind + outd)
+    elif args.gemv_fused:
+        # the fused decode projections of the 2B stack: RMSNorm(x + residual) in front, mode 1 rows
+        outs, swiglu = {"gdn_front": ([6144, 2048], False), "gqa_front": ([4096, 512, 512], False),
+                        "mlp": ([6144, 6144], True)}[args.gemv_fused]
+        ind = 2048
+        W = [(torch.randint(-2**31, 2**31 - 1, (ind, o // 4), dtype=torch.int32, device=dev, generator=gen),
+              torch.rand(ind, o // 64, device=dev, generator=gen) * 0.01) for o in outs]
+        x, res, nw = (torch.randn(ind, device=dev, generator=gen) for _ in range(3))
+        h = torch.empty(ind, device=dev)
+        fg = q35attn.ops.FusedGemv(x, W, [torch.empty(o, device=dev) for o in outs], residual=res, norm_w=nw,
+                                   sum_out=h, swiglu=swiglu, mode=1)
+
+        def call():
+            fg()
+        case, size = "q8_gemv_fused", {"shape": args.gemv_fused, "in": ind, "outs": outs}
+        alg = sum(ind * o + ind * (o // 64) * 4 for o in outs) + 4 * (4 * ind + sum(outs))
     else:
         T = args.gqa_prefill_tokens
         qg = torch.randn(1, T, HQ, 2 * D, device=dev, generator=gen)

@@ -171,10 +171,12 @@ int launch_nq(const GemvParams &p, cudaStream_t st) {
 // instruction per box, so the stream is not capped by the SM's
 // outstanding-load limit that bounds the per-thread LDG kernel above.  Eight
 // consumer warps take 8 rows x 64 bytes per step (lane = row * 4 + 16-byte
-// quarter) and reduce with warp shuffles and one shared-memory pass.  When the
-// column blocks alone give few CTAs, the row boxes are split over a cluster of
-// KS CTAs (grid.y) and rank 0 adds the ranks' column sums through distributed
-// shared memory in rank order (deterministic).
+// quarter) and reduce with warp shuffles and one shared-memory pass.  In mode 1
+// the rows the reference skips get x = 0 in the CTA's shared copy of x (adding
+// exact zeros leaves every f32 sum unchanged), so the inner loop has no row
+// test.  When the column blocks alone give few CTAs, the row boxes are split
+// over a cluster of KS CTAs (grid.y) and rank 0 adds the ranks' column sums
+// through distributed shared memory in rank order (deterministic).
 //
 // One launch serves up to 4 projections of the same input (segments, laid out
 // one after the other along grid.x), optionally with the decoder's input
@@ -211,6 +213,7 @@ struct GemvTmaSmem {
   float red[NW][kTWarps][kTC];
   float mine[NW][kTC];  // this CTA's column sums (read by rank 0 of the cluster)
   float part[kTWarps];
+  static_assert(kTR % (8 * kTWarps) == 0, "whole 8-row steps per consumer warp and box");
   uint64_t full[NS], empty[NS], xbar;
   alignas(16) float x[4];  // dynamic tail: x, then residual and norm_w when the norm is fused
 };
@@ -291,10 +294,11 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
     }
   } else {
     ok = __all_sync(0xffffffffu, mbar_wait(&sm.xbar, 0));
-    if (kNorm) {  // input RMSNorm over the whole row, by the 256 consumer threads
+    const int nthr = kTWarps * 32;
+    if (kNorm) {  // input RMSNorm over the whole row, by the consumer threads
       const bool res = p.residual != nullptr;
       float ss = 0.0f;
-      for (int i = tid; i < p.in_dim; i += kTWarps * 32) {
+      for (int i = tid; i < p.in_dim; i += nthr) {
         float h = xs[i];
         if (res) h = h + rs[i];
         xs[i] = h;
@@ -302,21 +306,28 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
       }
       ss = warp_sum(ss);
       if (lane == 0) sm.part[warp] = ss;
-      named_bar_sync(1, kTWarps * 32);
+      named_bar_sync(1, nthr);
       float tot = 0.0f;
 #pragma unroll
       for (int w = 0; w < kTWarps; ++w) tot += sm.part[w];
       const float inv = 1.0f / sqrtf(tot / (float)p.in_dim + p.eps);
       const bool first = blockIdx.x == 0 && blockIdx.y == 0;
-      for (int i = tid; i < p.in_dim; i += kTWarps * 32) {
+      for (int i = tid; i < p.in_dim; i += nthr) {
         const float h = xs[i];
         const float v = (h * inv) * (1.0f + ws[i]);
         if (first && p.sum_out) p.sum_out[i] = h;
         if (first && p.x_out) p.x_out[i] = v;
         xs[i] = v;
       }
-      named_bar_sync(1, kTWarps * 32);
     }
+    if (kCompat) {  // rows outside the reference's split coverage read x = 0 (one plan per CTA)
+      const int chunk = S[0]->chunk, per = S[0]->per_split, nsp = S[0]->ref_splits;
+      for (int i = tid; i < p.in_dim; i += nthr) {
+        const int sp = i / chunk;
+        if (sp >= nsp || i - sp * chunk >= per) xs[i] = 0.0f;
+      }
+    }
+    if (kNorm || kCompat) named_bar_sync(1, nthr);
     float acc[NW][16];
 #pragma unroll
     for (int k = 0; k < NW; ++k)
@@ -331,19 +342,13 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
       }
 #pragma unroll
       for (int step = 0; step < kTR / (8 * kTWarps); ++step) {
-        const int rr = warp * (kTR / kTWarps) + step * 8 + (lane >> 2);
+        const int rr = (step * kTWarps + warp) * 8 + (lane >> 2);  // this lane's row within the box
         const int row = (sbeg + st) * kTR + rr;
+        const float xv = row < p.in_dim ? xs[row] : 0.0f;  // rows past the end are TMA zero fill
 #pragma unroll
         for (int k = 0; k < NW; ++k) {
-          bool live = row < p.in_dim;
-          if (kCompat && live) {
-            const int s = row / S[k]->chunk;
-            live = s < S[k]->ref_splits && row - s * S[k]->chunk < S[k]->per_split;
-          }
-          if (live) {
-            const uint4 w = *reinterpret_cast<const uint4 *>(&sm.w[slot][k][rr][16 * q]);
-            fma16(acc[k], w, xs[row] * sm.sc[slot][k][rr][sj]);
-          }
+          const uint4 w = *reinterpret_cast<const uint4 *>(&sm.w[slot][k][rr][16 * q]);
+          fma16(acc[k], w, xv * sm.sc[slot][k][rr][sj]);
         }
       }
       __syncwarp();
@@ -466,7 +471,9 @@ int launch_tma(GemvTmaParams &p, bool compat, bool norm, bool swiglu, cudaStream
   int ctas = 0;
   for (int k = 0; k < p.nseg; ++k) ctas += p.seg[k].ncb;
   if (swiglu) ctas = p.seg[0].ncb;
-  // row-box split: the largest of 8 / 4 / 2 that keeps the grid within two CTAs per SM
+  // row-box split KS: the largest of 8 / 4 / 2 that keeps the grid within two
+  // CTAs per SM (measured on B200 against a split that evens out the CTAs per
+  // SM: the larger split with deeper rings was faster on every decode shape)
   const int nst = (p.in_dim + kTR - 1) / kTR;
   p.ks = 1;
   for (int k : {8, 4, 2})
