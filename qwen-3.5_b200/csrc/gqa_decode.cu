@@ -18,10 +18,16 @@
 //     (running max / sum per head, G x 8 output accumulators per lane) over
 //     KPW keys of every tile; a lane owns 8 of the 256 dims, q.k partial dots
 //     are finished with a butterfly reduce-scatter across the warp.
-// The CTA merges its warps in shared memory, writes an (m, l, o) partial to
-// the workspace, and the last CTA of each (sequence, kv head) to arrive
-// (atomic ticket, no spin-wait) merges the splits, applies sigmoid(gate) and
-// writes the output.  The last pair of each sequence increments lens[b].
+// The CTA merges its warps in shared memory and writes an (m, l, o) partial to
+// the workspace.  The splits are then merged in one of two ways:
+//   * many sequences (long splits, several waves of CTAs): the last CTA of each
+//     (sequence, kv head) to arrive (atomic ticket, no spin-wait) merges them
+//     in a two-level tree, applies sigmoid(gate) and writes the output, while
+//     other CTAs still stream; the last pair of a sequence increments lens[b];
+//   * few sequences (one wave): the tree's chain of fences, tickets and
+//     dependent L2 reads would sit after the stream (about 10 us on B200), so
+//     the kernel just ends and gqa_split_combine_kernel, launched behind it,
+//     merges every split in one pass and increments lens[b].
 #include "common.cuh"
 #include "gqa_common.cuh"
 
@@ -51,9 +57,11 @@ struct GqaParams {
   uint32_t *grp_cnt;   // [B * Hkv * ngroups]
   uint32_t *pair_cnt;  // [B * Hkv]
   uint32_t *seq_cnt;   // [B]
+  int32_t *lsnap;      // [B]: keys attended this step (-1: the step was refused), for the split combine
   uint32_t *status;
   long long cap;
   int B, Hq, Hkv, rot, nsplit, kps, ngroups;
+  int tree;  // 1: merge the splits in-kernel (ticket tree); 0: gqa_split_combine_kernel does
   float eps, qscale_log2;
 };
 
@@ -204,15 +212,14 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
 
   const int len = p.lens[b];
   const bool append = p.k_new != nullptr;  // false: attend the cached keys only (context-parallel shard)
-  if (append && len >= p.cap) {
-    if (s == 0 && kvh == 0 && tid == 0) atomicOr(p.status, Q35_STATUS_CACHE_FULL);
-    return;
-  }
   const int L = append ? len + 1 : len;
-  if (L > p.nsplit * p.kps) {
-    if (s == 0 && kvh == 0 && tid == 0) atomicOr(p.status, Q35_STATUS_LEN_HINT);
-    return;
+  const bool full = append && len >= p.cap, over = !full && L > p.nsplit * p.kps;
+  if (s == 0 && kvh == 0 && tid == 0) {
+    if (full) atomicOr(p.status, Q35_STATUS_CACHE_FULL);
+    if (over) atomicOr(p.status, Q35_STATUS_LEN_HINT);
+    if (!p.tree && p.nsplit > 1) p.lsnap[b] = (full || over) ? -1 : L;  // read by the split combine
   }
+  if (full || over) return;
   const int kbeg = s * p.kps;
   const int kend = min(kbeg + p.kps, L);
   const int nkeys = max(kend - kbeg, 0);
@@ -407,6 +414,8 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
     }
   }
 
+  if (!single && !p.tree) return;  // gqa_split_combine_kernel merges the splits
+
   // ---- cross-CTA combine: a two-level ticket tree (fan-in 8, no spin-wait).
   // The last split of each group of 8 to arrive merges the group; the last
   // group to finish merges the group partials into the output.
@@ -451,6 +460,70 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
   }
 }
 
+// Merge of the split partials of one decode step (the few-sequence regime):
+// CTA (pair, head g, 64-dim slice).  Pass 1: the threads stride over the live
+// splits' maxima (m in log2 units) and reduce M.  Pass 2: warp w takes splits
+// w, w + 8, ...; with M known the terms are independent, so a warp keeps 8
+// splits' loads in flight instead of one dependent L2 round trip per split.
+// The warps' sums meet in shared memory and go through write_final (gate, or
+// the context-parallel triple).  One CTA per sequence advances lens[b]; no CTA
+// of this kernel reads lens.
+constexpr int kCombSlice = 64;
+
+template <int G>
+__global__ void __launch_bounds__(256) gqa_split_combine_kernel(const GqaParams p) {
+  pdl_entry();
+  __shared__ float red[8][3][32][2];  // [warp][l, o0|o1][lane]
+  __shared__ float wmax[8];
+  const int pg = blockIdx.x, slice = blockIdx.y;
+  const size_t pair = (size_t)pg / G;
+  const int g = pg % G;
+  const int b = (int)(pair / p.Hkv), kvh = (int)(pair % p.Hkv);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int L = p.lsnap[b];
+  if (L < 0) return;  // the decode step was refused (cache full / length hint): no output, lens unchanged
+  const int nlive = min((L + p.kps - 1) / p.kps, p.nsplit);
+  const int d = slice * kCombSlice + 2 * lane;
+  const float *pml = p.part_ml + pair * p.nsplit * G * 2;
+  const float *po = p.part_o + pair * p.nsplit * G * kD;
+  float M = -INFINITY;
+  for (int j = tid; j < nlive; j += 256) M = fmaxf(M, __ldcg(pml + ((size_t)j * G + g) * 2));
+  M = warp_max(M);
+  if (lane == 0) wmax[warp] = M;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < 8; ++w) M = fmaxf(M, wmax[w]);
+  float l = 0.0f, o0 = 0.0f, o1 = 0.0f;
+  if (M != -INFINITY) {
+#pragma unroll 8
+    for (int j = warp; j < nlive; j += 8) {
+      const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pml + ((size_t)j * G + g) * 2));
+      const float2 oj = __ldcg(reinterpret_cast<const float2 *>(po + ((size_t)j * G + g) * kD + d));
+      const float wgt = ml.x == -INFINITY ? 0.0f : exp2f(ml.x - M);  // a split without keys adds nothing
+      l = fmaf(ml.y, wgt, l);
+      o0 = fmaf(oj.x, wgt, o0);
+      o1 = fmaf(oj.y, wgt, o1);
+    }
+  }
+  red[warp][0][lane][0] = l;
+  red[warp][1][lane][0] = o0;
+  red[warp][1][lane][1] = o1;
+  __syncthreads();
+  if (warp == 0) {
+    float Ls = 0.0f, O0 = 0.0f, O1 = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      Ls += red[w][0][lane][0];
+      O0 += red[w][1][lane][0];
+      O1 += red[w][1][lane][1];
+    }
+    const int h = kvh * G + g;
+    write_final(p, b, h, d, O0, M, Ls);
+    write_final(p, b, h, d + 1, O1, M, Ls);
+    if (lane == 0 && kvh == 0 && g == 0 && slice == 0 && p.k_new != nullptr) p.lens[b] = L;
+  }
+}
+
 // out[b, h, :] = (sum_r o_r 2^(m_r - M)) / (sum_r l_r 2^(m_r - M)) * sigmoid(gate),
 // M = max_r m_r, over n_parts partials [n][B][Hq][D+2] (one per context shard).
 __global__ void gqa_combine_kernel(int B, int Hq, int n_parts, const float *__restrict__ parts,
@@ -485,6 +558,13 @@ cudaError_t launch_g(const GqaParams &p, cudaStream_t st) {
   dim3 grid(p.nsplit, p.Hkv, p.B);
   note_launch();
   (void)launch_kernel_serial(gqa_decode_kernel<G>, dim3(grid), dim3(kThreads), smem, st, 1, 1, p);
+  if (p.nsplit > 1 && !p.tree) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    note_launch();
+    (void)launch_kernel(gqa_split_combine_kernel<G>, dim3(p.B * p.Hkv * G, kD / kCombSlice), dim3(256), 0, st, 1,
+                        1, p);
+  }
   return cudaGetLastError();
 }
 
@@ -493,10 +573,12 @@ cudaError_t launch_g(const GqaParams &p, cudaStream_t st) {
 // Keys per split.  Large problems (many tiles per SM) use long splits so the
 // combine traffic stays negligible; small ones are cut so that about one full
 // wave of CTAs (2 per SM) is resident.
+constexpr int kLongKps = 2048;  // split length of the many-sequence regime (in-kernel merge tree)
+
 int gqa_keys_per_split(int B, int Hkv, long long max_len, int sms) {
   const long long pairs = (long long)B * Hkv;
   const long long slots = 2LL * sms;
-  const long long long_kps = 2048;
+  const long long long_kps = kLongKps;
   if (pairs * ((max_len + long_kps - 1) / long_kps) >= 8 * slots) return (int)long_kps;
   long long per = (max_len * pairs + slots - 1) / slots;
   per = (per + kTK - 1) / kTK * kTK;
@@ -506,7 +588,7 @@ int gqa_keys_per_split(int B, int Hkv, long long max_len, int sms) {
 }
 
 struct GqaWsLayout {
-  size_t status, grp_cnt, pair_cnt, seq_cnt, part_o, part_ml, grp_o, grp_ml, total;
+  size_t status, grp_cnt, pair_cnt, seq_cnt, lsnap, part_o, part_ml, grp_o, grp_ml, total;
   int kps, nsplit, ngroups;
 };
 
@@ -521,7 +603,8 @@ GqaWsLayout gqa_ws_layout(int B, int Hq, int Hkv, long long max_len, int sms) {
   l.grp_cnt = 256;
   l.pair_cnt = l.grp_cnt + pairs * l.ngroups * sizeof(uint32_t);
   l.seq_cnt = l.pair_cnt + pairs * sizeof(uint32_t);
-  l.part_o = up(l.seq_cnt + (size_t)B * sizeof(uint32_t));
+  l.lsnap = l.seq_cnt + (size_t)B * sizeof(uint32_t);
+  l.part_o = up(l.lsnap + (size_t)B * sizeof(int32_t));
   l.part_ml = up(l.part_o + pairs * l.nsplit * G * kD * sizeof(float));
   l.grp_o = up(l.part_ml + pairs * l.nsplit * G * 2 * sizeof(float));
   l.grp_ml = up(l.grp_o + pairs * l.ngroups * G * kD * sizeof(float));
@@ -558,6 +641,7 @@ int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_g
   p.kps = lay.kps;
   p.nsplit = lay.nsplit;
   p.ngroups = lay.ngroups;
+  p.tree = lay.kps >= kLongKps;
   Q35_REQUIRE(ws != nullptr && ws_bytes >= lay.total && (reinterpret_cast<uintptr_t>(ws) & 255u) == 0,
               Q35_ERR_WORKSPACE,
               "gqa_decode: workspace missing, not 256-byte aligned or too small (need " +
@@ -571,6 +655,7 @@ int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_g
   p.grp_cnt = reinterpret_cast<uint32_t *>(base + lay.grp_cnt);
   p.pair_cnt = reinterpret_cast<uint32_t *>(base + lay.pair_cnt);
   p.seq_cnt = reinterpret_cast<uint32_t *>(base + lay.seq_cnt);
+  p.lsnap = reinterpret_cast<int32_t *>(base + lay.lsnap);
   p.part_o = reinterpret_cast<float *>(base + lay.part_o);
   p.part_ml = reinterpret_cast<float *>(base + lay.part_ml);
   p.grp_o = reinterpret_cast<float *>(base + lay.grp_o);

@@ -98,10 +98,11 @@ def test_empty_cache_returns_gated_value():
     assert int(lens.item()) == 1
 
 
-def test_full_cache_sets_status_and_skips():
+@pytest.mark.parametrize("cap", [16, 200])  # one split per pair (in-kernel output) / four splits (split combine)
+def test_full_cache_sets_status_and_skips(cap):
     """A sequence whose cache is full is skipped on the device (status bit,
     lens, cache and output untouched) while the others proceed."""
-    B, Hq, Hkv, D, cap = 2, 8, 2, 256, 16
+    B, Hq, Hkv, D = 2, 8, 2, 256
     dev = torch.device("cuda:0")
     rng = np.random.RandomState(11)
     qg = torch.from_numpy(rng.randn(B, Hq, 2 * D).astype(np.float32)).to(dev)
@@ -122,6 +123,37 @@ def test_full_cache_sets_status_and_skips():
     assert lens.cpu().tolist() == [cap, 6]
     assert torch.all(out[0] == 7.0) and not torch.all(out[1] == 7.0)
     assert torch.equal(Kc[0], K0[0])
+
+
+def test_length_hint_refuses_the_step():
+    """lens + 1 beyond the max_len the workspace was planned for: the step is
+    refused on the device (status bit), lens and the output stay as they were,
+    for both merge schedules."""
+    B, Hq, Hkv, D = 1, 8, 2, 256
+    dev = torch.device("cuda:0")
+    for l0, max_len in ((70, 64), (200, 130)):
+        cap = 256
+        rng = np.random.RandomState(l0)
+        qg = torch.from_numpy(rng.randn(B, Hq, 2 * D).astype(np.float32)).to(dev)
+        kn = torch.from_numpy(rng.randn(B, Hkv, D).astype(np.float32)).to(dev)
+        vn = torch.from_numpy(rng.randn(B, Hkv, D).astype(np.float32)).to(dev)
+        w = torch.zeros(D, device=dev)
+        cos, sin = rope([l0])
+        Kc, Vc = torch.randn(B, Hkv, cap, D, device=dev), torch.randn(B, Hkv, cap, D, device=dev)
+        lens = torch.tensor([l0], dtype=torch.int32, device=dev)
+        out = torch.full((B, Hq * D), 7.0, device=dev)
+        ws = q35attn.GqaWorkspace(B, Hq, Hkv, cap, max_len=max_len)
+        q35attn.gqa_decode(qg, kn, vn, w, w, torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev), Kc, Vc,
+                           lens, out, workspace=ws, max_len=max_len)
+        assert ws.status() & q35attn.STATUS_LEN_HINT
+        assert int(lens.item()) == l0 and torch.all(out == 7.0)
+
+
+def test_split_combine_schedule_matches_oracle_at_32k():
+    """One sequence at 32K context: the few-sequence schedule (short splits,
+    separate combine kernel) against the oracle, three steps."""
+    e_out, e_k, e_v = run_gqa(1, 8, 2, 3, [32768], 32768 + 4, seed=12, check_every=1)
+    assert e_out <= TOL and e_k <= TOL and e_v == 0.0
 
 
 def test_config4_shapes_long_splits():
