@@ -738,6 +738,9 @@ def main():
                     help="only run the config-2 GDN prefill at this prompt length (profiling aid)")
     ap.add_argument("--gqa-prefill-tokens", type=int, default=0,
                     help="only run the GQA prefill (8/2 heads, empty cache) at this prompt length (profiling aid)")
+    ap.add_argument("--gqa-decode-len", type=int, default=0,
+                    help="profiling aid: GQA decode of one sequence with this many cached tokens, 64 steps per "
+                         "CUDA-graph replay (config 1: 4096; single 32K sequence: 32768)")
     ap.add_argument("--gemv-fused", choices=["gdn_front", "gqa_front", "mlp"], default="",
                     help="profiling aid: one fused decode projection launch of the 2B stack, timed alone")
     ap.add_argument("--gemv", type=str, default="",
@@ -751,7 +754,7 @@ def main():
         return run_reference(args)
     if args.prefill_tokens > 0:
         return run_prefill_only(args)
-    if args.gqa_prefill_tokens > 0 or args.gemv or args.gemv_fused:
+    if args.gqa_prefill_tokens > 0 or args.gemv or args.gemv_fused or args.gqa_decode_len:
         return run_kernel_only(args)
     if args.config3_steps > 0:
         return run_config3_only(args)
@@ -794,7 +797,8 @@ def run_config3_only(args):
 def run_kernel_only(args):
     """--gqa-prefill-tokens T: the GQA prefill of a T-token prompt into an
     empty cache (config-3 head shapes); --gemv IN,OUT: one Q8F GEMV (mode 0);
-    --gemv-fused SHAPE: one fused decode projection (norm in front, mode 1).
+    --gemv-fused SHAPE: one fused decode projection (norm in front, mode 1);
+    --gqa-decode-len L: 64 GQA decode steps of one sequence per call (a graph).
     --warmup untimed calls, then --steps calls timed with CUDA events; one JSON
     line.  A profiling aid, not the bench line."""
     import torch
@@ -813,6 +817,40 @@ def run_kernel_only(args):
             q35attn.q8_gemv(x, w, sc, y, mode=0)
         case, size = "q8_gemv", {"in": ind, "out": outd}
         alg = ind * outd + ind * (outd // 64) * 4 + 4 * (ind + outd)
+    elif args.gqa_decode_len:
+        # one sequence, L cached tokens, 64 decode steps per graph replay (BASELINE config 1 at L=4096, the single
+        # 32K-context sequence at L=32768); --steps replays are timed
+        L0c, n1 = args.gqa_decode_len, 64
+        cap = L0c + n1 * (args.steps + args.warmup + 2) + 1
+        Kc, Vc = torch.empty(1, HKV, cap, D, device=dev), torch.empty(1, HKV, cap, D, device=dev)
+        Kc[:, :, :L0c].normal_(generator=gen)
+        Vc[:, :, :L0c].normal_(generator=gen)
+        lens = torch.full((1,), L0c, dtype=torch.int32, device=dev)
+        qg = torch.randn(n1, 1, HQ, 2 * D, device=dev, generator=gen)
+        kn, vn = torch.randn(n1, 1, HKV, D, device=dev, generator=gen), torch.randn(n1, 1, HKV, D, device=dev,
+                                                                                    generator=gen)
+        cs, sn = torch.randn(n1, 1, ROT, device=dev, generator=gen), torch.randn(n1, 1, ROT, device=dev, generator=gen)
+        w0, o1 = torch.zeros(D, device=dev), torch.empty(1, HQ * D, device=dev)
+        ws = q35attn.GqaWorkspace(1, HQ, HKV, cap, device=dev)
+
+        def steps64():
+            for i in range(n1):
+                q35attn.gqa_decode(qg[i], kn[i], vn[i], w0, w0, cs[i], sn[i], Kc, Vc, lens, o1, workspace=ws,
+                                   max_len=cap)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            steps64()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            steps64()
+
+        def call():
+            graph.replay()
+        case, size = "gqa_decode_b1", {"L0": L0c, "decode_steps_per_call": n1}
+        Lmid = L0c + n1 * (args.warmup + 1) + n1 * args.steps // 2
+        alg = n1 * (2 * HKV * (Lmid + 1) * D * 4 + 24576)
     elif args.gemv_fused:
         # the fused decode projections of the 2B stack: RMSNorm(x + residual) in front, mode 1 rows
         outs, swiglu = {"gdn_front": ([6144, 2048], False), "gqa_front": ([4096, 512, 512], False),
@@ -859,6 +897,8 @@ def run_kernel_only(args):
     torch.cuda.synchronize(dev)
     ms = a.elapsed_time(b) / args.steps
     line = {"case": case, **size, "steps": args.steps, "warmup": args.warmup, "ms_per_call": ms}
+    if args.gqa_decode_len:
+        line["us_per_step"] = ms * 1e3 / 64
     if alg:
         line["achieved_gbs"] = alg / ms / 1e6
     print(json.dumps(line))
