@@ -18,9 +18,9 @@
 //  (2) gdn_prefill_state_kernel, grid (8, Hv, B), walks the chunks in order.
 //      The value columns of the state are independent recurrences, so each
 //      CTA keeps 16 of them in shared memory, with no communication:
-//      v' = U - W S, S <- S e^(gamma_last) + k'^T v' as 4 x 4 register tiles
-//      with the contraction split across thread groups, the next chunk's
-//      operands prefetched meanwhile.  It publishes the state at every chunk
+//      v' = U - W S, S <- S e^(gamma_last) + k'^T v' as 8 x 8 register tiles
+//      (one shared-memory byte per FMA) with the contraction split across
+//      thread groups, the next chunk's operands prefetched meanwhile.  It publishes the state at every chunk
 //      start and v', and finally stores the state and the new conv state.
 //  (3) gdn_prefill_output_kernel, grid (Hv, chunks, B), fully parallel:
 //      o = q' S_c + Aqk v' on the tensor cores, then the gated RMS norm.
@@ -37,7 +37,7 @@ constexpr int kD = 128;     // head_k_dim == head_v_dim
 constexpr int kCS = 16;     // value columns per CTA in the state kernel
 constexpr int kSplit = kD / kCS;
 constexpr int kThreads = 512;  // 16 warps: the chunk phases are latency-bound
-constexpr int kStateThreads = 512;  // state pass: 16 warps hide the shared-memory latency
+constexpr int kStateThreads = 256;  // state pass: 4 compute warps (8 x 8 register tiles) + 4 for the merges
 // Workspace record per (b, h, chunk), offsets in floats.  Tiles that the
 // output kernel feeds to the tensor cores are stored in the 8x4-blocked
 // K-major layout of umma.cuh, split into 64-column slabs so that every
@@ -510,20 +510,12 @@ struct StateSmem {
   float U[2][kC][kCS];   // this CTA's 16 columns of U
   float dec[2][64];      // decay slot of the record
   float S[kD][kCS];      // the CTA's 16 state columns, [k][v]
-  float Pv[8][kC][kCS];  // k-split partials of W S; then ([4][128][16]) t-split partials of k'^T v'
+  float4 Pv[128 * 16];   // partial tiles: float4 q of compute thread i at 16 i + (q ^ (i % 16))
   float Vn[kC][kCS];     // v'
   float Sst[2][2][16 * 64];  // staging of S^T (2 slabs of blocked [16 v x 64 k]), by chunk parity
   float Vst[2][16 * 64];     // staging of v'^T (blocked [16 v x 64 t]), by chunk parity
   uint64_t barW[2];
 };
-
-// acc[r] += a[r] * s for a 4 x 4 register tile (rows in a, columns in s).
-__device__ __forceinline__ void tile4(float4 (&acc)[4], float4 a, float4 s) {
-  acc[0] = f4_fma(a.x, s, acc[0]);
-  acc[1] = f4_fma(a.y, s, acc[1]);
-  acc[2] = f4_fma(a.z, s, acc[2]);
-  acc[3] = f4_fma(a.w, s, acc[3]);
-}
 
 // W^T, k' and the decay of one chunk (bulk copies by thread 0) and this CTA's
 // U columns (one 16-byte cp.async per thread: 64 rows x 4) into buffer `buf`.
@@ -564,21 +556,31 @@ __global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const 
   float *rec0 = p.ws + ((size_t)b * p.Hv + h) * p.NC * kRec;
   uint64_t pol = 0;
 
-  // thread roles: (kq, iq, cq) for the 64 x 16 product with an 8-way split of
-  // the contraction; (h4, rq, cq) for the 128 x 16 update (4-way split);
-  // threads < 256 also own one (row, column quad) of the 64 x 16 reduction;
-  // (ur, uq) is the float4 of S this thread updates
-  const int kq = tid >> 6, iq = (tid & 63) >> 2, cq = tid & 3;
-  const int h4 = tid >> 7, rq = (tid & 127) >> 2;
-  const int ri = (tid & 255) >> 2;
-  const bool red = tid < kC * kCS / 4;
-  const int ur = tid >> 2, uq = tid & 3;
+  // thread roles.  Compute threads (tid < 128) hold an 8 x 8 register tile:
+  //   W S   : k-slice ks = tid / 16 (16 of the 128 k), rows 8 tr .. 8 tr + 7 of
+  //           the 64 tokens, columns 8 tc .. 8 tc + 7 of the 16;
+  //   k'^T v': token slice ts = tid / 32 (16 of the 64 t), rows 8 kr .. of the
+  //           128 k, columns 8 tc ...
+  // A tile's float4 q (= 2 * row-in-tile + half) goes to slot 16 i + (q ^ (i
+  // % 16)) of Pv: each store instruction of a warp spreads over all 32 banks,
+  // and the two tiles of one row block (tc = 0, 1) are 512 contiguous bytes.
+  // A merge warp takes one row block: lane l reads float4 l of that block in
+  // every slice (conflict-free), which is row 8 rb + q / 2, quad 2 (l / 16) +
+  // q % 2 with q = (l % 16) ^ ((2 rb + l / 16) % 16), so its writes of S, v'
+  // rows are again 512 contiguous bytes.
+  // (ur, uq0 .. uq0 + 1) are the two float4 of S this thread loads and stores.
+  const int lane = tid & 31, warp = tid >> 5;
+  const int ur = tid >> 1, uq0 = 2 * (tid & 1);
+  auto merge_q = [&](int rb) { return (lane & 15) ^ ((2 * rb + (lane >> 4)) & 15); };
 
   {  // initial state, also published as S_0 (staging parity 1 = "chunk -1")
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (p.has_init) a = *reinterpret_cast<const float4 *>(Sg + (size_t)ur * kD + col0 + 4 * uq);
-    *reinterpret_cast<float4 *>(&sm.S[ur][4 * uq]) = a;
-    stage_state(sm.Sst[1], ur, uq, a);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (p.has_init) a = *reinterpret_cast<const float4 *>(Sg + (size_t)ur * kD + col0 + 4 * (uq0 + e));
+      *reinterpret_cast<float4 *>(&sm.S[ur][4 * (uq0 + e)]) = a;
+      stage_state(sm.Sst[1], ur, uq0 + e, a);
+    }
   }
   if (tid == 0) {
     mbar_init(&sm.barW[0], 1);
@@ -610,63 +612,102 @@ __global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const 
     if (c + 1 < p.NC && ok) fetch_chunk(sm, rec + kRec, col0, buf ^ 1, pol, tid);
     cp_async_commit();
 
-    // v' = U - W S  (:315-324), contraction k split 8 ways
-    {
-      float4 acc[4] = {};
-#pragma unroll 8
+    // v' = U - W S  (:315-324): [64 t x 128 k] x [128 k x 16 v], k split 8 ways
+    if (tid < 128) {
+      const int ks = tid >> 4, tr = (tid >> 1) & 7, tc = tid & 1;
+      float acc[8][8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+#pragma unroll 4
       for (int kk = 0; kk < kD / 8; ++kk) {
-        const int k = (kD / 8) * kq + kk;
-        tile4(acc, *reinterpret_cast<const float4 *>(&sm.Wt[buf][k][4 * iq]),
-              *reinterpret_cast<const float4 *>(&sm.S[k][4 * cq]));
+        const int k = (kD / 8) * ks + kk;
+        const float4 w0 = *reinterpret_cast<const float4 *>(&sm.Wt[buf][k][8 * tr]);
+        const float4 w1 = *reinterpret_cast<const float4 *>(&sm.Wt[buf][k][8 * tr + 4]);
+        const float4 s0 = *reinterpret_cast<const float4 *>(&sm.S[k][8 * tc]);
+        const float4 s1 = *reinterpret_cast<const float4 *>(&sm.S[k][8 * tc + 4]);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(wv[i], sv[j], acc[i][j]);
       }
 #pragma unroll
-      for (int r = 0; r < 4; ++r) *reinterpret_cast<float4 *>(&sm.Pv[kq][4 * iq + r][4 * cq]) = acc[r];
+      for (int i = 0; i < 8; ++i) {
+        sm.Pv[16 * tid + ((2 * i) ^ (tid & 15))] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+        sm.Pv[16 * tid + ((2 * i + 1) ^ (tid & 15))] = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+      }
     }
     __syncthreads();
-    if (red) {
-      float4 v = *reinterpret_cast<const float4 *>(&sm.U[buf][ri][4 * cq]);
+    {  // merge the 8 k-slices: warp w takes token rows 8 w .. 8 w + 7
+      const int q = merge_q(warp);
+      const int mt = 8 * warp + (q >> 1), mvq = 2 * (lane >> 4) + (q & 1);
+      float4 v = *reinterpret_cast<const float4 *>(&sm.U[buf][mt][4 * mvq]);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 pv = *reinterpret_cast<const float4 *>(&sm.Pv[q][ri][4 * cq]);
+      for (int ks = 0; ks < 8; ++ks) {
+        const float4 pv = sm.Pv[16 * (16 * ks + 2 * warp) + lane];
         v = make_float4(v.x - pv.x, v.y - pv.y, v.z - pv.z, v.w - pv.w);
       }
-      *reinterpret_cast<float4 *>(&sm.Vn[ri][4 * cq]) = v;
+      *reinterpret_cast<float4 *>(&sm.Vn[mt][4 * mvq]) = v;
       using umma::blk_off;
-      sm.Vst[buf][blk_off(4 * cq + 0, ri, kC)] = v.x;
-      sm.Vst[buf][blk_off(4 * cq + 1, ri, kC)] = v.y;
-      sm.Vst[buf][blk_off(4 * cq + 2, ri, kC)] = v.z;
-      sm.Vst[buf][blk_off(4 * cq + 3, ri, kC)] = v.w;
+      sm.Vst[buf][blk_off(4 * mvq + 0, mt, kC)] = v.x;
+      sm.Vst[buf][blk_off(4 * mvq + 1, mt, kC)] = v.y;
+      sm.Vst[buf][blk_off(4 * mvq + 2, mt, kC)] = v.z;
+      sm.Vst[buf][blk_off(4 * mvq + 3, mt, kC)] = v.w;
     }
     __syncthreads();
 
-    // k'^T v'  (:342-349), contraction t split 4 ways
-    float(*Ps)[kD][kCS] = reinterpret_cast<float(*)[kD][kCS]>(&sm.Pv[0][0][0]);  // [4][128][16]
-    {
-      float4 acs[4] = {};
-#pragma unroll 8
+    // k'^T v'  (:342-349): [128 k x 64 t] x [64 t x 16 v], t split 4 ways
+    if (tid < 128) {
+      const int ts = tid >> 5, kr = lane >> 1, tc = lane & 1;
+      float acc[8][8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+#pragma unroll 4
       for (int tt = 0; tt < kC / 4; ++tt) {
-        const int t = (kC / 4) * h4 + tt;
-        tile4(acs, *reinterpret_cast<const float4 *>(&sm.Kp[buf][t][4 * rq]),
-              *reinterpret_cast<const float4 *>(&sm.Vn[t][4 * cq]));
+        const int t = (kC / 4) * ts + tt;
+        const float4 k0 = *reinterpret_cast<const float4 *>(&sm.Kp[buf][t][8 * kr]);
+        const float4 k1 = *reinterpret_cast<const float4 *>(&sm.Kp[buf][t][8 * kr + 4]);
+        const float4 v0 = *reinterpret_cast<const float4 *>(&sm.Vn[t][8 * tc]);
+        const float4 v1 = *reinterpret_cast<const float4 *>(&sm.Vn[t][8 * tc + 4]);
+        const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+        const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(kv[i], vv[j], acc[i][j]);
       }
 #pragma unroll
-      for (int r = 0; r < 4; ++r) *reinterpret_cast<float4 *>(&Ps[h4][4 * rq + r][4 * cq]) = acs[r];
+      for (int i = 0; i < 8; ++i) {
+        sm.Pv[16 * tid + ((2 * i) ^ (tid & 15))] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+        sm.Pv[16 * tid + ((2 * i + 1) ^ (tid & 15))] = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+      }
     }
     __syncthreads();
 
-    // S <- S e^(gamma_last) + k'^T v'  (:350); publish it as S_{c+1}
+    // S <- S e^(gamma_last) + k'^T v'  (:350); publish it as S_{c+1}.  Warp w
+    // merges the k row blocks rb = 2 w, 2 w + 1 over the 4 t-slices.
     {
       const float dec = sm.dec[buf][0];
-      float4 a = *reinterpret_cast<const float4 *>(&sm.S[ur][4 * uq]);
-      float4 ps = *reinterpret_cast<const float4 *>(&Ps[0][ur][4 * uq]);
 #pragma unroll
-      for (int q = 1; q < 4; ++q) {
-        const float4 pq = *reinterpret_cast<const float4 *>(&Ps[q][ur][4 * uq]);
-        ps = make_float4(ps.x + pq.x, ps.y + pq.y, ps.z + pq.z, ps.w + pq.w);
+      for (int it = 0; it < 2; ++it) {
+        const int rb = 2 * warp + it, q = merge_q(rb);
+        const int k = 8 * rb + (q >> 1), vq = 2 * (lane >> 4) + (q & 1);
+        float4 ps = sm.Pv[16 * (2 * rb) + lane];
+#pragma unroll
+        for (int t4 = 1; t4 < 4; ++t4) {
+          const float4 pq = sm.Pv[16 * (32 * t4 + 2 * rb) + lane];
+          ps = make_float4(ps.x + pq.x, ps.y + pq.y, ps.z + pq.z, ps.w + pq.w);
+        }
+        float4 a = *reinterpret_cast<const float4 *>(&sm.S[k][4 * vq]);
+        a = make_float4(a.x * dec + ps.x, a.y * dec + ps.y, a.z * dec + ps.z, a.w * dec + ps.w);
+        *reinterpret_cast<float4 *>(&sm.S[k][4 * vq]) = a;
+        if (c + 1 < p.NC) stage_state(sm.Sst[buf], k, vq, a);
       }
-      a = make_float4(a.x * dec + ps.x, a.y * dec + ps.y, a.z * dec + ps.z, a.w * dec + ps.w);
-      *reinterpret_cast<float4 *>(&sm.S[ur][4 * uq]) = a;
-      if (c + 1 < p.NC) stage_state(sm.Sst[buf], ur, uq, a);
     }
     fence_proxy_async_smem();
     __syncthreads();
@@ -680,8 +721,11 @@ __global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const 
     }
   }
   cp_async_wait<0>();
-  *reinterpret_cast<float4 *>(Sg + (size_t)ur * kD + col0 + 4 * uq) =
-      *reinterpret_cast<const float4 *>(&sm.S[ur][4 * uq]);
+  __syncthreads();  // the last update's rows were written by other threads
+#pragma unroll
+  for (int e = 0; e < 2; ++e)
+    *reinterpret_cast<float4 *>(Sg + (size_t)ur * kD + col0 + 4 * (uq0 + e)) =
+        *reinterpret_cast<const float4 *>(&sm.S[ur][4 * (uq0 + e)]);
   if (!ok && tid == 0) Sg[col0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison the state
 
   // new conv state = last K-1 inputs of [history, x] (:538-540): v channels of
