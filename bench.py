@@ -653,7 +653,9 @@ def run_single_seq_cp(dev, world, rank, steps=64, warmup=3):
     """BASELINE config 4's single 32K-context sequence decoded across all
     ranks: GDN heads-parallel, GQA KV length split, NCCL all-gather of the
     per-rank GQA softmax partials and GDN head outputs (q35attn.parallel).
-    Collective on every rank; returns the per-step time (max over ranks)."""
+    Collective on every rank; the timed steps replay as one CUDA graph that
+    holds the kernels and the all-gathers.  Returns the per-step time (max
+    over ranks)."""
     import torch
     import torch.distributed as dist
 
@@ -663,7 +665,8 @@ def run_single_seq_cp(dev, world, rank, steps=64, warmup=3):
     plan = ShardPlan(world, rank, HK, HV, L0)
     lo, hi = plan.kv_tokens
     n_loc = hi - lo
-    cap = n_loc + (steps + warmup + 2 if plan.holds_tail else 0) + 1
+    # the tail rank appends one key per step: the eager warm-up steps plus a warm and a timed graph replay
+    cap = n_loc + (warmup + 2 * steps + 2 if plan.holds_tail else 0) + 1
     gen = torch.Generator(device=dev)
     gen.manual_seed(777 + rank)
 
@@ -705,20 +708,32 @@ def run_single_seq_cp(dev, world, rank, steps=64, warmup=3):
         q35attn.gqa_combine_partials(parts, qg[i], out)
         dist.all_gather_into_tensor(gdn_all, out_l)
 
-    for i in range(warmup):
-        step(i)
-    dist.barrier(device_ids=[dev.index])
+    # eager warm-up on a side stream, then the timed steps captured once in a CUDA graph (kernels and the two
+    # NCCL all-gathers per step); every rank captures and replays the same sequence of collectives
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(warmup):
+            step(i)
     torch.cuda.synchronize(dev)
+    dist.barrier(device_ids=[dev.index])
+    gph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gph, stream=side):
+        for i in range(warmup, nst):
+            step(i)
+    gph.replay()
+    torch.cuda.synchronize(dev)
+    dist.barrier(device_ids=[dev.index])
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for i in range(warmup, nst):
-        step(i)
+    gph.replay()
     b.record()
     torch.cuda.synchronize(dev)
+    del gph  # a graph holding NCCL calls is released before the process group goes away
     t = torch.tensor([a.elapsed_time(b) / 1000.0 / steps], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     t = float(t.item())
-    by = gqa_bytes_per_seq(L0 + warmup + steps // 2) + GDN_BYTES_PER_SEQ + GDN_BYTES_SHARED
+    by = gqa_bytes_per_seq(L0 + warmup + steps + steps // 2) + GDN_BYTES_PER_SEQ + GDN_BYTES_SHARED
     return {"us_per_step": t * 1e6, "layer_steps_per_s": 2.0 / t, "alg_bytes_per_step_all_gpus": by,
             "achieved_gbs_all_gpus": by / t / 1e9, "collectives_per_step": 2,
             "partitioning": f"GDN heads {HV}/{world} per rank, GQA KV length {L0}/{world} per rank"}
