@@ -755,20 +755,22 @@ __global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const 
 // Kernel 3: per (chunk, head), fully parallel, on the tensor cores:
 //   o^T [128 v x 64 t] = S_c^T q'^T + v'^T Aqk^T   (:325-341)
 // in three K = 64 stages (S_c^T / q' slab 0, slab 1, then v'^T / Aqk), each a
-// bulk copy into one of two shared-memory buffers; the lo terms of the
-// 3xTF32 split are formed in place.  Epilogue: gated RMS norm over the 128
-// values of each token (:651-660, :85-117) and the output store.
+// bulk copy into one shared-memory buffer set; the lo terms of the 3xTF32
+// split are formed in place.  One buffer set (98 KB) lets two CTAs share an
+// SM, so one CTA's copies overlap the other's tensor-core work.  Epilogue:
+// gated RMS norm over the 128 values of each token (:651-660, :85-117) and the
+// output store.
 constexpr int kOutThreads = 256;
 struct OutSmem {
-  float A[2][2][kD * 64];  // [buffer][hi, lo], blocked [128 x 64]
-  float Bm[2][2][kC * 64]; // [buffer][hi, lo], blocked [64 x 64]
+  float A[2][kD * 64];  // [hi, lo], blocked [128 x 64]
+  float Bm[2][kC * 64]; // [hi, lo], blocked [64 x 64]
   float part[4][kC];
   float inv[kC];
   uint32_t tbase;
-  uint64_t barL[2], barM[2];
+  uint64_t barL, barM;
 };
 
-__global__ void __launch_bounds__(kOutThreads, 1) gdn_prefill_output_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(kOutThreads, 2) gdn_prefill_output_kernel(const PrefillParams p) {
   pdl_entry();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   OutSmem &sm = *reinterpret_cast<OutSmem *>(smem_raw);
@@ -777,23 +779,24 @@ __global__ void __launch_bounds__(kOutThreads, 1) gdn_prefill_output_kernel(cons
   const int t0 = c * kC;
   const float *rec = p.ws + (((size_t)b * p.Hv + h) * p.NC + c) * kRec;
   constexpr uint32_t kStageBytes = (kD * 64 + kC * 64) * sizeof(float);
+  // stage st: (A, B) = (S_c^T slab st, q' slab st) for st < 2, (v'^T, Aqk) for st = 2
+  auto load_stage = [&](int st, uint64_t pol) {
+    mbar_arrive_expect_tx(&sm.barL, kStageBytes);
+    const float *a = st < 2 ? rec + kOffSc + st * kD * 64 : rec + kOffVt;
+    const float *bm = st < 2 ? rec + kOffQs + st * kC * 64 : rec + kOffAq;
+    bulk_g2s(sm.A[0], a, kD * 64 * sizeof(float), &sm.barL, pol);
+    bulk_g2s(sm.Bm[0], bm, kC * 64 * sizeof(float), &sm.barL, pol);
+  };
 
   if (warp == 0) {
     umma::tmem_alloc(&sm.tbase, 64);
     umma::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.barL[i], 1);
-      mbar_init(&sm.barM[i], 1);
-    }
+    mbar_init(&sm.barL, 1);
+    mbar_init(&sm.barM, 1);
     fence_mbar_init();
-    const uint64_t pol = l2_policy_evict_first();
-    for (int sl = 0; sl < 2; ++sl) {
-      mbar_arrive_expect_tx(&sm.barL[sl], kStageBytes);
-      bulk_g2s(sm.A[sl][0], rec + kOffSc + sl * kD * 64, kD * 64 * sizeof(float), &sm.barL[sl], pol);
-      bulk_g2s(sm.Bm[sl][0], rec + kOffQs + sl * kC * 64, kC * 64 * sizeof(float), &sm.barL[sl], pol);
-    }
+    load_stage(0, l2_policy_evict_first());
   }
   umma::fence_before_sync();
   __syncthreads();
@@ -816,17 +819,16 @@ __global__ void __launch_bounds__(kOutThreads, 1) gdn_prefill_output_kernel(cons
 
 #pragma unroll 1
   for (int st = 0; st < 3; ++st) {
-    const int buf = st & 1;
-    if (ok && !mbar_wait(&sm.barL[buf], st >> 1)) ok = false;
+    if (ok && !mbar_wait(&sm.barL, st & 1)) ok = false;
     {  // lo terms
-      const float4 *ah = reinterpret_cast<const float4 *>(sm.A[buf][0]);
-      float4 *al = reinterpret_cast<float4 *>(sm.A[buf][1]);
+      const float4 *ah = reinterpret_cast<const float4 *>(sm.A[0]);
+      float4 *al = reinterpret_cast<float4 *>(sm.A[1]);
       for (int e = tid; e < kD * 64 / 4; e += kOutThreads) {
         const float4 v = ah[e];
         al[e] = make_float4(umma::tf32_lo(v.x), umma::tf32_lo(v.y), umma::tf32_lo(v.z), umma::tf32_lo(v.w));
       }
-      const float4 *bh = reinterpret_cast<const float4 *>(sm.Bm[buf][0]);
-      float4 *bl = reinterpret_cast<float4 *>(sm.Bm[buf][1]);
+      const float4 *bh = reinterpret_cast<const float4 *>(sm.Bm[0]);
+      float4 *bl = reinterpret_cast<float4 *>(sm.Bm[1]);
       for (int e = tid; e < kC * 64 / 4; e += kOutThreads) {
         const float4 v = bh[e];
         bl[e] = make_float4(umma::tf32_lo(v.x), umma::tf32_lo(v.y), umma::tf32_lo(v.z), umma::tf32_lo(v.w));
@@ -840,27 +842,25 @@ __global__ void __launch_bounds__(kOutThreads, 1) gdn_prefill_output_kernel(cons
       constexpr uint32_t sbo = (64 / 4) * 128;
 #pragma unroll 1
       for (int ks = 0; ks < 8; ++ks) {
-        const uint64_t ah = umma::smem_desc(sm.A[buf][0] + ks * 64, 128, sbo);
-        const uint64_t al = umma::smem_desc(sm.A[buf][1] + ks * 64, 128, sbo);
-        const uint64_t bh = umma::smem_desc(sm.Bm[buf][0] + ks * 64, 128, sbo);
-        const uint64_t bl = umma::smem_desc(sm.Bm[buf][1] + ks * 64, 128, sbo);
+        const uint64_t ah = umma::smem_desc(sm.A[0] + ks * 64, 128, sbo);
+        const uint64_t al = umma::smem_desc(sm.A[1] + ks * 64, 128, sbo);
+        const uint64_t bh = umma::smem_desc(sm.Bm[0] + ks * 64, 128, sbo);
+        const uint64_t bl = umma::smem_desc(sm.Bm[1] + ks * 64, 128, sbo);
         umma::mma_tf32(tb, ah, bh, id, (st > 0 || ks > 0) ? 1u : 0u);
         umma::mma_tf32(tb, ah, bl, id, 1);
         umma::mma_tf32(tb, al, bh, id, 1);
       }
-      umma::commit(&sm.barM[buf]);
-      if (st == 0) {  // buffer 0 takes v'^T / Aqk once stage 0's MMAs have read it
-        if (ok && !mbar_wait(&sm.barM[0], 0)) ok = false;
-        if (ok) {
-          const uint64_t pol = l2_policy_evict_first();
-          mbar_arrive_expect_tx(&sm.barL[0], kStageBytes);
-          bulk_g2s(sm.A[0][0], rec + kOffVt, kD * 64 * sizeof(float), &sm.barL[0], pol);
-          bulk_g2s(sm.Bm[0][0], rec + kOffAq, kC * 64 * sizeof(float), &sm.barL[0], pol);
-        }
+      umma::commit(&sm.barM);
+      // the buffers take the next stage once this stage's MMAs have read them
+      if (st < 2) {
+        if (ok && !mbar_wait(&sm.barM, st & 1)) ok = false;
+        if (ok) load_stage(st + 1, l2_policy_evict_first());
       }
     }
   }
-  if (ok && !mbar_wait(&sm.barM[0], 1)) ok = false;  // stage 2 (and so every MMA) complete
+  // stage 2 (and so every MMA) complete: the barrier's third phase (parity 0);
+  // every thread has passed stage 2's barrier, so phases 0 and 1 are done
+  if (ok && !mbar_wait(&sm.barM, 0)) ok = false;
   umma::fence_after_sync();
 
   // epilogue
