@@ -13,7 +13,9 @@ value   = layer-steps/s over all GPUs (256 seqs x 2 layers per step),
           inputs resident in HBM, CUDA events, max over ranks.
 e2e     = the same metric through the public C-ABI calls with the per-step
           inputs copied from pinned host memory and the outputs copied back
-          inside the timed region.
+          inside the timed region (pipelined as a serving loop would be: the
+          next step's inputs go up and the previous step's outputs come back
+          on two copy streams while the current step computes).
 roofline: the dominant kernel (GQA flash-decode) -- algorithmic bytes per
           launch over its CUDA-event duration, against MEASURED_PEAKS.json.
 cpu_baseline: the CPU oracle (restatement of the reference, which is Rust/Burn
@@ -369,24 +371,57 @@ def run_gpu(args):
     h_sin.copy_(sin_b[W + K:W + K + nE].cpu())
     h_out_gdn = torch.empty(nE, B, HV * DK, pin_memory=True)
     h_out_gqa = torch.empty(nE, B, HQ * D, pin_memory=True)
-    d_in = [torch.empty(B, CONV, device=dev), torch.empty(B, HV * DK, device=dev), torch.empty(B, HV, device=dev),
-            torch.empty(B, HV, device=dev), torch.empty(B, HQ, 2 * D, device=dev), torch.empty(B, HKV, D, device=dev),
-            torch.empty(B, HKV, D, device=dev), torch.empty(B, ROT, device=dev), torch.empty(B, ROT, device=dev)]
+    def dev_inputs():
+        return [torch.empty(B, CONV, device=dev), torch.empty(B, HV * DK, device=dev), torch.empty(B, HV, device=dev),
+                torch.empty(B, HV, device=dev), torch.empty(B, HQ, 2 * D, device=dev),
+                torch.empty(B, HKV, D, device=dev), torch.empty(B, HKV, D, device=dev),
+                torch.empty(B, ROT, device=dev), torch.empty(B, ROT, device=dev)]
+    # Pipelined like a serving loop: step i+1's inputs go up on `up` into the
+    # other input buffer while step i computes on `stream`, and step i's outputs
+    # come back on `down` from the other output buffer.  Events order every
+    # reuse of a buffer; all copies are inside the timed region.
+    d_in = [dev_inputs(), dev_inputs()]
+    d_out = [(torch.empty_like(out_gdn), torch.empty_like(out_gqa)) for _ in range(2)]
     h_bufs = [h_x, h_z, h_b, h_g, h_qg, h_kn, h_vn, h_cos, h_sin]
     h2d = sum(t[0].numel() * 4 for t in h_bufs)
     d2h = (h_out_gdn[0].numel() + h_out_gqa[0].numel()) * 4
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = lambda: torch.cuda.Event()
+    in_ready = [ev() for _ in range(nE)]   # step i's inputs are on the device
+    computed = [ev() for _ in range(nE)]   # step i's kernels are done (its inputs and outputs are free to reuse)
+    fetched = [ev() for _ in range(nE)]    # step i's outputs are on the host
+
+    def upload(i):
+        if i >= 2:
+            up.wait_event(computed[i - 2])  # step i-2 has finished reading this input buffer
+        with torch.cuda.stream(up):
+            for dbuf, hbuf in zip(d_in[i % 2], h_bufs):
+                dbuf.copy_(hbuf[i], non_blocking=True)
+        in_ready[i].record(up)
+
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    up.wait_event(e0)
+    upload(0)
     for i in range(nE):
-        for dbuf, hbuf in zip(d_in, h_bufs):
-            dbuf.copy_(hbuf[i], non_blocking=True)
-        q35attn.gdn_decode(d_in[0], d_in[1], d_in[2], d_in[3], conv_w, norm_w, cst, S, out_gdn, num_k_heads=HK,
+        if i + 1 < nE:
+            upload(i + 1)
+        di, (og, oq) = d_in[i % 2], d_out[i % 2]
+        stream.wait_event(in_ready[i])
+        if i >= 2:
+            stream.wait_event(fetched[i - 2])  # step i-2's outputs have left this output buffer
+        q35attn.gdn_decode(di[0], di[1], di[2], di[3], conv_w, norm_w, cst, S, og, num_k_heads=HK,
                            num_v_heads=HV, stream=stream)
-        q35attn.gqa_decode(d_in[4], d_in[5], d_in[6], qn_w, kn_w, d_in[7], d_in[8], Kc, Vc, lens, out_gqa,
+        q35attn.gqa_decode(di[4], di[5], di[6], qn_w, kn_w, di[7], di[8], Kc, Vc, lens, oq,
                            workspace=ws, max_len=cap, stream=stream)
-        h_out_gdn[i].copy_(out_gdn, non_blocking=True)
-        h_out_gqa[i].copy_(out_gqa, non_blocking=True)
+        computed[i].record(stream)
+        down.wait_event(computed[i])
+        with torch.cuda.stream(down):
+            h_out_gdn[i].copy_(og, non_blocking=True)
+            h_out_gqa[i].copy_(oq, non_blocking=True)
+        fetched[i].record(down)
+    stream.wait_event(fetched[nE - 1])
     e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_elapsed = max_over_ranks(e0.elapsed_time(e1) / 1000.0)
