@@ -467,13 +467,15 @@ cudaError_t launch_split(const GdnDecodeParams &p, int split, cudaStream_t st) {
 
 }  // namespace
 
-// Column split per head: enough CTAs to cover every SM twice, at most 8 CTAs
-// per cluster (portable cluster size).
+// Column split per head below the streaming threshold: none.  Measured on
+// B200 with the state L2-resident (256 dependent steps in a CUDA graph), one
+// CTA per head beat every cluster split (B=1: 4.52 us against 4.76-5.04 us for
+// splits 2-8; B=4: 4.57 against 5.0-6.6; B=16: 7.9 against 13-17): the two
+// cluster barriers of a split cost more than the wider state stream saves.
+// A split (q35_gdn_decode_split) stays available to callers.
 int gdn_decode_split(int B, int Hv, int rf, int sms) {
-  int split = 1;
-  while (split < 8 && (long long)B * Hv * split < 2LL * sms) split *= 2;
-  while (split > 1 && split * rf > 8) split /= 2;
-  return split;
+  (void)B, (void)Hv, (void)rf, (void)sms;
+  return 1;
 }
 
 int gdn_decode_launch(const q35_gdn_dims *d, const float *mixed_qkv, const float *z, const float *beta,
