@@ -265,6 +265,24 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Split cluster barrier: arrive (no memory ordering) early, wait (acquire) later.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Shared::cluster address of `local` in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t dsmem_addr(const void *local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  return remote;
+}
+// Asynchronous store of one float into another CTA's shared memory; its 4
+// bytes count against that CTA's mbarrier (complete_tx).
+__device__ __forceinline__ void st_async_f32(uint32_t remote_addr, float v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(remote_addr),
+               "f"(v), "r"(remote_bar)
+               : "memory");
+}
 // The float at the same shared-memory offset in CTA `rank` of the cluster.
 __device__ __forceinline__ float ld_dsmem_f32(const float *local, uint32_t rank) {
   uint32_t remote;

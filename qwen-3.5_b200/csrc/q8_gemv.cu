@@ -175,8 +175,11 @@ int launch_nq(const GemvParams &p, cudaStream_t st) {
 // the rows the reference skips get x = 0 in the CTA's shared copy of x (adding
 // exact zeros leaves every f32 sum unchanged), so the inner loop has no row
 // test.  When the column blocks alone give few CTAs, the row boxes are split
-// over a cluster of KS CTAs (grid.y) and rank 0 adds the ranks' column sums
-// through distributed shared memory in rank order (deterministic).
+// over a cluster of KS CTAs (grid.y): ranks 1 .. KS-1 push their column sums
+// into rank 0's shared memory with st.async (complete_tx on rank 0's
+// mbarrier) and exit; rank 0 adds them in rank order (deterministic).  One
+// split cluster barrier (arrive at entry, wait before the push) makes rank 0's
+// mbarrier initialisation visible; no barrier holds the ranks at the end.
 //
 // One launch serves up to 4 projections of the same input (segments, laid out
 // one after the other along grid.x), optionally with the decoder's input
@@ -211,11 +214,12 @@ struct GemvTmaSmem {
   unsigned char w[NS][NW][kTR][kTC];
   float sc[NS][NW][kTR][4];
   float red[NW][kTWarps][kTC];
-  float mine[NW][kTC];  // this CTA's column sums (read by rank 0 of the cluster)
   float part[kTWarps];
   static_assert(kTR % (8 * kTWarps) == 0, "whole 8-row steps per consumer warp and box");
-  uint64_t full[NS], empty[NS], xbar;
-  alignas(16) float x[4];  // dynamic tail: x, then residual and norm_w when the norm is fused
+  uint64_t full[NS], empty[NS], xbar, redbar;
+  // dynamic tail: x, then residual and norm_w when the norm is fused, then (on
+  // rank 0 of a cluster) the other ranks' column sums [KS - 1][NW][64]
+  alignas(16) float x[4];
 };
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
@@ -249,6 +253,7 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
   const int sbeg = (int)((long long)nst_all * rk / p.ks), send = (int)((long long)nst_all * (rk + 1) / p.ks);
   const int nst = send - sbeg;
   float *xs = sm.x, *rs = sm.x + p.in_dim, *ws = sm.x + 2 * p.in_dim;
+  float *recv = sm.x + (kNorm ? 3 : 1) * p.in_dim;  // [KS - 1][NW][kTC]
   const bool producer = tid == kTWarps * 32;
   auto issue = [&](int st) {  // one ring stage: NW weight boxes and their scale boxes
     const int slot = st % NS;
@@ -265,6 +270,10 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
       mbar_init(&sm.empty[i], kTWarps);
     }
     mbar_init(&sm.xbar, 1);
+    if (p.ks > 1) {  // rank 0 expects the other ranks' sums
+      mbar_init(&sm.redbar, 1);
+      if (blockIdx.y == 0) mbar_arrive_expect_tx(&sm.redbar, (uint32_t)((p.ks - 1) * NW * kTC * sizeof(float)));
+    }
     fence_mbar_init();
     // The weights and scales are never written by an earlier kernel: fill the
     // ring before the grid-dependency wait, so the first DRAM round trips
@@ -272,6 +281,7 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
     for (int st = 0; st < NS && st < nst; ++st) issue(st);
   }
   __syncthreads();
+  if (p.ks > 1) cluster_arrive_relaxed();  // this CTA's barriers are initialised (waited on before the push)
   pdl_entry();  // x, residual and the outputs belong to the kernel stream order from here
   bool ok = true;
   if (warp == kTWarps) {
@@ -384,29 +394,35 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
 #pragma unroll
       for (int w = 1; w < kTWarps; ++w) t += sm.red[k][w][tid];
       v[k] = ok ? t : poison;
-      sm.mine[k][tid] = v[k];
     }
   }
-  bool write = true;
   if (p.ks > 1) {
-    cluster_sync_all();
-    write = cluster_ctarank() == 0;
-    if (write && tid < kTC) {
+    cluster_wait();  // every CTA of the cluster has initialised its barriers
+    if (blockIdx.y != 0) {  // push this rank's sums to rank 0 and leave
+      if (tid < kTC) {
+        const uint32_t rbar = dsmem_addr(&sm.redbar, 0);
+#pragma unroll
+        for (int k = 0; k < NW; ++k)
+          st_async_f32(dsmem_addr(&recv[((blockIdx.y - 1) * NW + k) * kTC + tid], 0), v[k], rbar);
+      }
+      return;
+    }
+    if (tid < kTC) {  // rank 0: add the ranks' sums in rank order
+      const bool got = mbar_wait(&sm.redbar, 0);
 #pragma unroll
       for (int k = 0; k < NW; ++k) {
-        float t = 0.0f;
-        for (int r = 0; r < p.ks; ++r) t += ld_dsmem_f32(&sm.mine[k][tid], (uint32_t)r);
-        v[k] = t;
+        float t = v[k];
+        for (int r = 1; r < p.ks; ++r) t += recv[((r - 1) * NW + k) * kTC + tid];
+        v[k] = got ? t : poison;
       }
     }
   }
-  if (write && tid < kTC) {
+  if (tid < kTC) {
     if (NW == 2)
       S[0]->y[c0 + tid] = v[0] * siluf_dev(v[NW - 1]);  // up * silu(gate)
     else
       S[0]->y[c0 + tid] = v[0];
   }
-  if (p.ks > 1) cluster_sync_all();  // no CTA leaves while rank 0 still reads its sums
 }
 
 bool gemv_tma_enabled() {
@@ -458,7 +474,8 @@ bool encode_gemv_maps(GemvSeg &g, const uint32_t *w, const float *scales, int in
 
 template <bool kCompat, bool kNorm, int NW, int NS>
 int launch_tma_t(const GemvTmaParams &p, int ctas, cudaStream_t st) {
-  const size_t smem = sizeof(GemvTmaSmem<NW, NS>) + (size_t)(kNorm ? 3 : 1) * p.in_dim * sizeof(float);
+  const size_t smem = sizeof(GemvTmaSmem<NW, NS>) +
+                      ((size_t)(kNorm ? 3 : 1) * p.in_dim + (size_t)(p.ks - 1) * NW * kTC) * sizeof(float);
   auto kern = q8_gemv_tma_kernel<kCompat, kNorm, NW, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "q8_gemv attributes");
