@@ -10,8 +10,9 @@
 // row) are staged into shared memory with coalesced 16-byte loads before the
 // grid-dependency wait (the weights never depend on the previous kernel, so
 // the copy overlaps it); one warp-pair then runs the 2H sequential chains from
-// shared memory, and rank 0 adds the 8 partials through distributed shared
-// memory.  Shapes whose split does not fit shared memory use the one-CTA
+// shared memory, and ranks 1-7 push their partials into rank 0's shared
+// memory with st.async (complete_tx on rank 0's mbarrier) and exit; rank 0
+// adds the 8 partials in split order.  Shapes whose split does not fit shared memory use the one-CTA
 // kernel (one thread per partial, straight from global memory).
 // mode 1 restates the prefill branch text_modules.rs:578-595 (matmul, sigmoid,
 // softplus with the threshold on a + dt_bias): one warp per row.
@@ -87,25 +88,38 @@ __global__ void __launch_bounds__(kGateThreads) gate_decode_cluster_kernel(
   const int rows = (chunk / 8) * 8;  // rows the reference walks per split (kernels.rs:190-199)
   const int row0 = split * chunk;
   const int wrow = (rows * H + 3) & ~3;  // 16-byte aligned sub-buffers
-  float *wbs = gsm, *was = gsm + wrow, *xs = gsm + 2 * wrow, *part = xs + ((rows + 3) & ~3);
+  float *wbs = gsm, *was = gsm + wrow, *xs = gsm + 2 * wrow, *recv = xs + ((rows + 3) & ~3);  // recv [8][2H]
+  __shared__ uint64_t redbar;
+  if (split == 0 && threadIdx.x == 0) {  // rank 0 expects 7 ranks x 2H partials
+    mbar_init(&redbar, 1);
+    mbar_arrive_expect_tx(&redbar, (uint32_t)((kSplits - 1) * 2 * H * sizeof(float)));
+    fence_mbar_init();
+  }
+  cluster_arrive_relaxed();  // waited on before the push: rank 0's barrier is initialised
   stage_f32(wbs, wb + (size_t)row0 * H, rows * H);
   stage_f32(was, wa + (size_t)row0 * H, rows * H);
   pdl_entry();  // x is the previous kernel's output
   stage_f32(xs, x + (size_t)n * in_dim + row0, rows);
   __syncthreads();
   const int u = threadIdx.x;
+  float acc = 0.0f;
   if (u < 2 * H) {
     const int h = u % H;
     const float *w = u < H ? wbs : was;
-    float acc = 0.0f;
 #pragma unroll 8
     for (int r = 0; r < rows; ++r) acc += xs[r] * w[r * H + h];
-    part[u] = acc;
   }
-  cluster_sync_all();
-  if (split == 0 && u < 2 * H) {
-    float sum = 0.0f;
-    for (int i = 0; i < kSplits; ++i) sum += ld_dsmem_f32(&part[u], (uint32_t)i);
+  cluster_wait();
+  if (split != 0) {  // push this split's partials to rank 0 and leave
+    if (u < 2 * H)
+      st_async_f32(dsmem_addr(&recv[(split - 1) * 2 * H + u], 0), acc, dsmem_addr(&redbar, 0));
+    return;
+  }
+  if (u < 2 * H) {
+    const bool got = mbar_wait(&redbar, 0);
+    float sum = 0.0f + acc;  // split order: 0, 1, ..., 7
+    for (int i = 1; i < kSplits; ++i) sum += recv[(i - 1) * 2 * H + u];
+    if (!got) sum = __int_as_float(0x7fc00000);  // a bounded wait gave up
     const int h = u % H;
     if (u < H) {
       beta[(size_t)n * H + h] = 1.0f / (1.0f + expf(-sum));
@@ -116,12 +130,11 @@ __global__ void __launch_bounds__(kGateThreads) gate_decode_cluster_kernel(
       g[(size_t)n * H + h] = -expf(a_log[h]) * sp;
     }
   }
-  cluster_sync_all();  // rank 0 reads the other ranks' partials until here
 }
 
 size_t gate_cluster_smem(int in_dim, int H) {
   const int rows = (in_dim / kSplits / 8) * 8;
-  return ((size_t)2 * ((rows * H + 3) & ~3) + ((rows + 3) & ~3) + 2 * H) * sizeof(float);
+  return ((size_t)2 * ((rows * H + 3) & ~3) + ((rows + 3) & ~3) + (kSplits - 1) * 2 * H) * sizeof(float);
 }
 
 template <int H>
