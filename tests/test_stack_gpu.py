@@ -56,3 +56,52 @@ def test_generate_is_deterministic():
     st.capture()
     b = st.generate(ids, 8).cpu()
     assert torch.equal(a, b)
+
+
+def test_stack_from_safetensors_checkpoint(tmp_path):
+    """A stack loaded through q35attn.checkpoint (HF names, Linear [out, in],
+    Q8F quantisation) runs prefill and graph decode in agreement with the CPU
+    reference stack built from the same loaded tensors."""
+    from safetensors.torch import save_file
+
+    from q35attn import checkpoint as ck
+    cfg = qs.StackConfig(layer_types=("linear", "full"), gdn_hk=2, gdn_hv=2, gqa_hq=2, gqa_hkv=1, inter=512,
+                         vocab=1024)
+    g = torch.Generator().manual_seed(6)
+    r = lambda *s: torch.randn(*s, generator=g) * 0.02
+    H, conv = cfg.hidden, cfg.conv_dim
+    t = {"model.language_model.embed_tokens.weight": r(cfg.vocab, H), "model.language_model.norm.weight": r(H)}
+    for i, kind in enumerate(cfg.layer_types):
+        p = f"model.language_model.layers.{i}."
+        t.update({p + "input_layernorm.weight": r(H), p + "post_attention_layernorm.weight": r(H),
+                  p + "mlp.up_proj.weight": r(cfg.inter, H), p + "mlp.gate_proj.weight": r(cfg.inter, H),
+                  p + "mlp.down_proj.weight": r(H, cfg.inter)})
+        if kind == "linear":
+            a = p + "linear_attn."
+            t.update({a + "in_proj_qkv.weight": r(conv, H), a + "in_proj_z.weight": r(cfg.gdn_hv * 128, H),
+                      a + "in_proj_b.weight": r(cfg.gdn_hv, H), a + "in_proj_a.weight": r(cfg.gdn_hv, H),
+                      a + "A_log": torch.log(torch.rand(cfg.gdn_hv, generator=g) * 15 + 1),
+                      a + "dt_bias": torch.ones(cfg.gdn_hv), a + "conv1d.weight": r(conv, 1, 4) * 10,
+                      a + "norm.weight": torch.ones(128), a + "out_proj.weight": r(H, cfg.gdn_hv * 128)})
+        else:
+            a = p + "self_attn."
+            t.update({a + "q_proj.weight": r(cfg.gqa_hq * 512, H), a + "k_proj.weight": r(cfg.gqa_hkv * 256, H),
+                      a + "v_proj.weight": r(cfg.gqa_hkv * 256, H), a + "o_proj.weight": r(H, cfg.gqa_hq * 256),
+                      a + "q_norm.weight": r(256), a + "k_norm.weight": r(256)})
+    path = str(tmp_path / "model.safetensors")
+    save_file(t, path)
+    st = qs.HybridStack(cfg, capacity=64, seed=1)
+    ck.load_into(st, ck.read_safetensors(path))
+    assert torch.equal(st.layers[0]["w_b"].cpu(), t["model.language_model.layers.0.linear_attn.in_proj_b.weight"].t())
+    ref = StackRef(st)
+    ids = torch.arange(20, dtype=torch.int32, device="cuda") * 37 % cfg.vocab
+    tok = int(st.prefill(ids).item())
+    _, rlog = ref.prefill(ids.cpu().numpy())
+    assert max_rel_err(st.b["logits"].cpu().numpy(), rlog) <= 1e-3
+    st.capture()
+    for _ in range(3):
+        st.graph.replay()
+        torch.cuda.synchronize()
+        _, rlog = ref.decode(tok)
+        assert max_rel_err(st.b["logits"].cpu().numpy(), rlog) <= 1e-3
+        tok = int(st.b["tok"].item())
