@@ -190,3 +190,27 @@ def test_config4_shapes_long_splits():
     assert ws.status() == 0
     assert (lens.cpu().numpy() == L0 + steps).all()
     assert max_rel_err(Kc[sample][:, :, L0:L0 + steps].cpu().numpy(), oK[:, :, L0:L0 + steps]) <= TOL
+
+
+def test_known_answer_equal_scores():
+    """Hand-computed answer at the kernel's head size (d=256): q = ones (its
+    RMSNorm leaves it), cached key 16 e0 and new key 16 e1 (RMSNorm: mean square
+    1), identity RoPE tables; both scores are 16/sqrt(256) = 1, so the output is
+    the mean of the two values -- v0[i] = i and v_new[i] = 256 - i, mean 128 --
+    times sigmoid(0) = 1/2: 64 everywhere."""
+    D, dev = 256, torch.device("cuda:0")
+    qg = torch.zeros(1, 1, 2 * D, device=dev)
+    qg[0, 0, :D] = 1.0
+    kn = torch.zeros(1, 1, D, device=dev)
+    kn[0, 0, 1] = 16.0
+    vn = (256.0 - torch.arange(D, device=dev, dtype=torch.float32)).view(1, 1, D)
+    Kc, Vc = torch.zeros(1, 1, 4, D, device=dev), torch.zeros(1, 1, 4, D, device=dev)
+    Kc[0, 0, 0, 0] = 16.0
+    Vc[0, 0, 0] = torch.arange(D, device=dev, dtype=torch.float32)
+    lens = torch.ones(1, dtype=torch.int32, device=dev)
+    w = torch.zeros(D, device=dev)
+    cos, sin = torch.ones(1, 64, device=dev), torch.zeros(1, 64, device=dev)
+    ws = q35attn.GqaWorkspace(1, 1, 1, 4)
+    out = q35attn.gqa_decode(qg, kn, vn, w, w, cos, sin, Kc, Vc, lens, workspace=ws)
+    assert torch.allclose(out, torch.full_like(out, 64.0), atol=1e-3)
+    assert int(lens.item()) == 2 and float(Kc[0, 0, 1, 1]) == pytest.approx(16.0, rel=1e-5)
