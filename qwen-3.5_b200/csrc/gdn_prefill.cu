@@ -17,11 +17,11 @@
 //      tensor cores (3xTF32, TMEM accumulators).  Results go to the workspace.
 //  (2) gdn_prefill_state_kernel, grid (8, Hv, B), walks the chunks in order.
 //      The value columns of the state are independent recurrences, so each
-//      CTA keeps 16 of them in shared memory, with no communication:
-//      v' = U - W S, S <- S e^(gamma_last) + k'^T v' as 8 x 8 register tiles
-//      (one shared-memory byte per FMA) with the contraction split across
-//      thread groups, the next chunk's operands prefetched meanwhile.  It publishes the state at every chunk
-//      start and v', and finally stores the state and the new conv state.
+//      CTA owns 16 of them, with no communication: v' = U - W S and
+//      S <- S e^(gamma_last) + k'^T v' as two small tcgen05 MMAs per chunk
+//      (3xTF32), the state in registers, the next chunk's operands copied
+//      meanwhile.  It publishes the state at every chunk start and v', and
+//      finally stores the state and the new conv state.
 //  (3) gdn_prefill_output_kernel, grid (Hv, chunks, B), fully parallel:
 //      o = q' S_c + Aqk v' on the tensor cores, then the gated RMS norm.
 //  Only (2) is sequential, and it carries just the two contractions that the
@@ -37,14 +37,14 @@ constexpr int kD = 128;     // head_k_dim == head_v_dim
 constexpr int kCS = 16;     // value columns per CTA in the state kernel
 constexpr int kSplit = kD / kCS;
 constexpr int kThreads = 512;  // 16 warps: the chunk phases are latency-bound
-constexpr int kStateThreads = 256;  // state pass: 4 compute warps (8 x 8 register tiles) + 4 for the merges
+constexpr int kStateThreads = 256;  // state pass: 4 row warps, the MMA issuer warp, 3 warps for tf32 lo terms
 // Workspace record per (b, h, chunk), offsets in floats.  Tiles that the
 // output kernel feeds to the tensor cores are stored in the 8x4-blocked
 // K-major layout of umma.cuh, split into 64-column slabs so that every
 // pipeline stage is one contiguous bulk copy.
 constexpr int kOffU = 0;                  // U [64 t][128 v], row-major
-constexpr int kOffWt = kC * kD;           // W^T [128 k][64 t], row-major
-constexpr int kOffKp = 2 * kC * kD;       // k' [64 t][128 k], row-major
+constexpr int kOffWt = kC * kD;           // W [64 t][128 k]: 2 slabs of blocked [64][64]
+constexpr int kOffKp = 2 * kC * kD;       // k'^T [128 k][64 t], blocked
 constexpr int kOffQs = 3 * kC * kD;       // q' [64 t][128 k]: 2 slabs of blocked [64][64]
 constexpr int kOffAq = 4 * kC * kD;       // Aqk [64 i][64 j], blocked
 constexpr int kOffDec = kOffAq + kC * kC; // e^(gamma_last) of the chunk, slot of 64
@@ -343,13 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
       const float v = kS[blk_off(i, d, kD)];
       kT[blk_off(d, i, kC)] = v;
       kTL[blk_off(d, i, kC)] = umma::tf32_lo(v);
-    }
-    for (int it = warp - 2; it < (kC / 8) * (kD / 16); it += nw) {
-      const int r = lane & 7, c4 = lane >> 3;
-      const int i = 8 * (it / (kD / 16)) + r, d0 = 16 * (it % (kD / 16)) + 4 * c4;
-      const float4 v = *reinterpret_cast<const float4 *>(&kS[blk_off(i, d0, kD)]);
-      const float e = sm.ek[i];
-      *reinterpret_cast<float4 *>(Kp + (size_t)i * kD + d0) = make_float4(v.x * e, v.y * e, v.z * e, v.w * e);
+      Kp[blk_off(d, i, kC)] = v * sm.ek[i];  // k'^T, the A operand of the state pass
     }
   } else {  // level 0: block bb, column j
     const int bb = tid >> 4, j = tid & 15, o = 16 * bb;
@@ -469,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
   umma::fence_after_sync();
 
   // (8) epilogue: TMEM lane = d.  U[i][d] from U^T (warps with (w / 4) % 2 = 0),
-  // Wt[d][i] = W^T (the others); warps w >= 8 take column blocks 2 and 3.
+  // W[i][d] from W^T (the others); warps w >= 8 take column blocks 2 and 3.
   {
     const int quad = warp & 3, d = 32 * quad + lane;
     const bool isU = ((warp >> 2) & 1) == 0;
@@ -484,8 +478,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
         for (int e = 0; e < 16; ++e) U[(size_t)(16 * cb + e) * kD + d] = v[e];
       } else {
 #pragma unroll
-        for (int e = 0; e < 16; e += 4)
-          *reinterpret_cast<float4 *>(Wt + (size_t)d * kC + 16 * cb + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+        // W K-major, the A operand of the state pass: slab d / 64, blocked [64 t][64 k]
+#pragma unroll
+        for (int e = 0; e < 16; ++e) Wt[(d >> 6) * (kC * 64) + blk_off(16 * cb + e, d & 63, 64)] = v[e];
       }
     }
     if (!g2_ok && tid == 0) rec[kOffDec] = __int_as_float(0x7fc00000);
@@ -498,235 +493,271 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
 
 // ---------------------------------------------------------------------------
 // Kernel 2: the sequential pass over the chunks (:314-350 without the output
-// term).  The value columns of the state are independent recurrences, so a
-// CTA owns 16 of them ([128 k x 16 v] in shared memory) and needs no peer:
-//   v' = U - W S,   S <- S e^(gamma_last) + k'^T v'.
-// Per chunk it also publishes, as blocked tiles for the output kernel, the
-// state at the chunk start (S_c^T) and v'^T.  W^T, k' and the decay of the
-// next chunk are fetched by bulk copies (U by cp.async) during the current one.
+// term), on the tensor cores.  The value columns of the state are independent
+// recurrences, so a CTA owns 16 of them and needs no peer.  Per chunk:
+//   MMA1  D1[t x v] = W S_c          M = 64, K = 128
+//   v' = U - D1                      TMEM lanes 32 q + 0..15 = tokens 16 q + 0..15
+//   MMA2  D2[k x v] = k'^T v'        M = 128, K = 64
+//   S_{c+1} = e^(gamma_last) S_c + D2   TMEM lane = k
+// each as 3xTF32 with f32 accumulators in TMEM.  The hi and lo rows of the B
+// operand (S_c^T, v'^T) sit one above the other, so A_hi [B_hi; B_lo] is one
+// N = 32 MMA and A_lo B_hi one N = 16 MMA: two MMAs per K step, each A tile
+// read from shared memory twice instead of three times.  (With N this small
+// the MMAs are bound by those A reads.)  The state itself stays in registers:
+// thread k holds row k of the CTA's 16 columns.  Roles:
+//   warps 0-3  the state rows and (lanes 0-15) the v' rows; they write S_c^T
+//              and v'^T as hi / lo K-major operands (a per-lane rotation of the
+//              16 columns keeps the stores free of bank conflicts);
+//   thread 128 issues the MMAs, the bulk copies of the next chunk's W and k'^T,
+//              an L2 prefetch two chunks ahead, and the stores that publish
+//              S_c^T and v'^T for the output kernel;
+//   warps 5-7  form the tf32 lo terms of W and k'^T.
+// The roles hand over through mbarriers only (every wait bounded), so each
+// waits on its true dependency and nothing else.
 struct StateSmem {
-  float Wt[2][kD][kC];   // W^T of chunks c, c+1
-  float Kp[2][kC][kD];   // k' of chunks c, c+1
-  float U[2][kC][kCS];   // this CTA's 16 columns of U
-  float dec[2][64];      // decay slot of the record
-  float S[kD][kCS];      // the CTA's 16 state columns, [k][v]
-  float4 Pv[128 * 16];   // partial tiles: float4 q of compute thread i at 16 i + (q ^ (i % 16))
-  float Vn[kC][kCS];     // v'
-  float Sst[2][2][16 * 64];  // staging of S^T (2 slabs of blocked [16 v x 64 k]), by chunk parity
-  float Vst[2][16 * 64];     // staging of v'^T (blocked [16 v x 64 t]), by chunk parity
-  uint64_t barW[2];
+  float Wh[2][kC * kD];   // W of chunks c, c+1: [64 t][128 k] K-major, 2 slabs of blocked [64][64]
+  float Wl[kC * kD];      // tf32 lo term of the current W
+  float Kh[2][kD * kC];   // k'^T of chunks c, c+1: blocked [128 k][64 t]
+  float Kl[kD * kC];      // tf32 lo term of the current k'^T
+  float Sb[2][2][kCS * 64];  // S_c^T, per k slab [hi, lo] of blocked [16 v][64 k]
+  float Vb[2][kCS * kC];     // v'^T [hi, lo] of blocked [16 v][64 t]
+  uint64_t full[2], wlo, klo, sready, vready, m1, m2;
+  uint32_t tbase;
 };
+static_assert(sizeof(StateSmem) <= 227 * 1024, "state pass shared memory");
 
-// W^T, k' and the decay of one chunk (bulk copies by thread 0) and this CTA's
-// U columns (one 16-byte cp.async per thread: 64 rows x 4) into buffer `buf`.
-__device__ __forceinline__ void fetch_chunk(StateSmem &sm, const float *rec, int col0, int buf, uint64_t pol,
-                                            int tid) {
-  if (tid == 0) {
-    mbar_arrive_expect_tx(&sm.barW[buf], sizeof(sm.Wt[0]) + sizeof(sm.Kp[0]) + sizeof(sm.dec[0]));
-    bulk_g2s(&sm.Wt[buf][0][0], rec + kOffWt, sizeof(sm.Wt[0]), &sm.barW[buf], pol);
-    bulk_g2s(&sm.Kp[buf][0][0], rec + kOffKp, sizeof(sm.Kp[0]), &sm.barW[buf], pol);
-    bulk_g2s(&sm.dec[buf][0], rec + kOffDec, sizeof(sm.dec[0]), &sm.barW[buf], pol);
+constexpr int kStateRowThreads = 128;  // warps 0-3
+constexpr int kStateIssuer = 128;      // warp 4, lane 0
+constexpr int kStateLoThreads = 96;    // warps 5-7
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Row r (0..63) of a 16-column tile, written as column r of the K-major
+// blocked [16][64] operand (hi and tf32 lo).  Lane group g = (lane / 4) % 8
+// stores its columns rotated by g, so each store instruction of a warp covers
+// all 32 banks.
+__device__ __forceinline__ void store_operand_row(float *hi, float *lo, int r, const float (&v)[16], int lane) {
+  const int rot = (lane >> 2) & 7;
+  float a[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = v[i];
+#pragma unroll
+  for (int sh = 1; sh < 8; sh <<= 1) {
+    const bool on = (rot & sh) != 0;
+    float t[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) t[i] = a[(i & 8) | ((i + sh) & 7)];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a[i] = on ? t[i] : a[i];
   }
-  if (tid < kC * kCS / 4) {
-    const int r = tid >> 2, q4 = tid & 3;
-    cp_async16(&sm.U[buf][r][4 * q4], rec + kOffU + (size_t)r * kD + col0 + 4 * q4);
+  const int base = (r >> 2) * 32 + (r & 3);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int off = base + (i >> 3) * 512 + (((i + rot) & 7) << 2);
+    hi[off] = a[i];
+    lo[off] = umma::tf32_lo(a[i]);
   }
 }
 
-// Thread (r, q4) holds S[r][4 q4 .. 4 q4 + 3]; stage them as S^T rows 4 q4 + e.
-__device__ __forceinline__ void stage_state(float (&st)[2][16 * 64], int r, int q4, float4 a) {
-  using umma::blk_off;
-  float *d = st[r >> 6];
-  const int k = r & 63;
-  d[blk_off(4 * q4 + 0, k, 64)] = a.x;
-  d[blk_off(4 * q4 + 1, k, 64)] = a.y;
-  d[blk_off(4 * q4 + 2, k, 64)] = a.z;
-  d[blk_off(4 * q4 + 3, k, 64)] = a.w;
+__device__ __forceinline__ void lo_pass(const float *src, float *dst, int t) {
+  const float4 *s4 = reinterpret_cast<const float4 *>(src);
+  float4 *d4 = reinterpret_cast<float4 *>(dst);
+  for (int e = t; e < kC * kD / 4; e += kStateLoThreads) {
+    const float4 v = s4[e];
+    d4[e] = make_float4(umma::tf32_lo(v.x), umma::tf32_lo(v.y), umma::tf32_lo(v.z), umma::tf32_lo(v.w));
+  }
 }
 
 template <int KC>
-__global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(const PrefillParams p) {
   pdl_entry();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   StateSmem &sm = *reinterpret_cast<StateSmem *>(smem_raw);
   const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int col0 = s * kCS;
+  const int NC = p.NC;
   float *Sg = p.rec_state + ((size_t)b * p.Hv + h) * kD * kD;
-  float *rec0 = p.ws + ((size_t)b * p.Hv + h) * p.NC * kRec;
-  uint64_t pol = 0;
+  float *rec0 = p.ws + ((size_t)b * p.Hv + h) * NC * kRec;
 
-  // thread roles.  Compute threads (tid < 128) hold an 8 x 8 register tile:
-  //   W S   : k-slice ks = tid / 16 (16 of the 128 k), rows 8 tr .. 8 tr + 7 of
-  //           the 64 tokens, columns 8 tc .. 8 tc + 7 of the 16;
-  //   k'^T v': token slice ts = tid / 32 (16 of the 64 t), rows 8 kr .. of the
-  //           128 k, columns 8 tc ...
-  // A tile's float4 q (= 2 * row-in-tile + half) goes to slot 16 i + (q ^ (i
-  // % 16)) of Pv: each store instruction of a warp spreads over all 32 banks,
-  // and the two tiles of one row block (tc = 0, 1) are 512 contiguous bytes.
-  // A merge warp takes one row block: lane l reads float4 l of that block in
-  // every slice (conflict-free), which is row 8 rb + q / 2, quad 2 (l / 16) +
-  // q % 2 with q = (l % 16) ^ ((2 rb + l / 16) % 16), so its writes of S, v'
-  // rows are again 512 contiguous bytes.
-  // (ur, uq0 .. uq0 + 1) are the two float4 of S this thread loads and stores.
-  const int lane = tid & 31, warp = tid >> 5;
-  const int ur = tid >> 1, uq0 = 2 * (tid & 1);
-  auto merge_q = [&](int rb) { return (lane & 15) ^ ((2 * rb + (lane >> 4)) & 15); };
-
-  {  // initial state, also published as S_0 (staging parity 1 = "chunk -1")
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (p.has_init) a = *reinterpret_cast<const float4 *>(Sg + (size_t)ur * kD + col0 + 4 * (uq0 + e));
-      *reinterpret_cast<float4 *>(&sm.S[ur][4 * (uq0 + e)]) = a;
-      stage_state(sm.Sst[1], ur, uq0 + e, a);
-    }
+  if (warp == 4) {
+    umma::tmem_alloc(&sm.tbase, 128);  // D1: columns 0-47, D2: 64-111
+    umma::tmem_relinquish();
   }
-  if (tid == 0) {
-    mbar_init(&sm.barW[0], 1);
-    mbar_init(&sm.barW[1], 1);
+  if (tid == kStateIssuer) {
+    mbar_init(&sm.full[0], 1);
+    mbar_init(&sm.full[1], 1);
+    mbar_init(&sm.wlo, kStateLoThreads);
+    mbar_init(&sm.klo, kStateLoThreads);
+    mbar_init(&sm.sready, kStateRowThreads);
+    mbar_init(&sm.vready, kC);
+    mbar_init(&sm.m1, 1);
+    mbar_init(&sm.m2, 1);
     fence_mbar_init();
-    pol = l2_policy_evict_first();
   }
-  fence_proxy_async_smem();
+  umma::fence_before_sync();
   __syncthreads();
-  if (tid == 0) {
-    bulk_s2g(rec0 + kOffSc + 16 * 64 * s, sm.Sst[1][0], 16 * 64 * sizeof(float));
-    bulk_s2g(rec0 + kOffSc + kD * 64 + 16 * 64 * s, sm.Sst[1][1], 16 * 64 * sizeof(float));
-    bulk_commit();
-  }
-  fetch_chunk(sm, rec0, col0, 0, pol, tid);
-  cp_async_commit();
-
-  // A wait that gives up (ok = false) stops this thread waiting and issuing
-  // copies, but every barrier below is still executed; the final state is
-  // then poisoned.
+  umma::fence_after_sync();
+  const uint32_t tb = sm.tbase;
+  // A wait that gives up (ok = false) stops this thread waiting; the final
+  // state is then poisoned.
   bool ok = true;
-  for (int c = 0; c < p.NC; ++c) {
-    const int buf = c & 1;
-    float *rec = rec0 + (size_t)c * kRec;
-    if (ok && !mbar_wait(&sm.barW[buf], (c >> 1) & 1)) ok = false;  // W^T, k', decay of chunk c
-    cp_async_wait<0>();                                                 // U of chunk c
-    if (tid == 0) bulk_wait_read<1>();  // the stores of chunk c-2 have read staging buffer `buf`
-    __syncthreads();  // chunk c-1 is done with buffer buf ^ 1 and with Pv
-    if (c + 1 < p.NC && ok) fetch_chunk(sm, rec + kRec, col0, buf ^ 1, pol, tid);
-    cp_async_commit();
 
-    // v' = U - W S  (:315-324): [64 t x 128 k] x [128 k x 16 v], k split 8 ways
-    if (tid < 128) {
-      const int ks = tid >> 4, tr = (tid >> 1) & 7, tc = tid & 1;
-      float acc[8][8];
+  if (warp < 4) {
+    // ---- state rows (k = tid) and, for lanes 0-15, the v' rows (t = 16 warp + lane)
+    const int k = tid;
+    const bool vrow = lane < 16;
+    const int t = 16 * warp + lane;
+    float S[16];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-#pragma unroll 4
-      for (int kk = 0; kk < kD / 8; ++kk) {
-        const int k = (kD / 8) * ks + kk;
-        const float4 w0 = *reinterpret_cast<const float4 *>(&sm.Wt[buf][k][8 * tr]);
-        const float4 w1 = *reinterpret_cast<const float4 *>(&sm.Wt[buf][k][8 * tr + 4]);
-        const float4 s0 = *reinterpret_cast<const float4 *>(&sm.S[k][8 * tc]);
-        const float4 s1 = *reinterpret_cast<const float4 *>(&sm.S[k][8 * tc + 4]);
-        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(wv[i], sv[j], acc[i][j]);
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        sm.Pv[16 * tid + ((2 * i) ^ (tid & 15))] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-        sm.Pv[16 * tid + ((2 * i + 1) ^ (tid & 15))] = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
-      }
+    for (int q = 0; q < 4; ++q) {
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (p.has_init) a = *reinterpret_cast<const float4 *>(Sg + (size_t)k * kD + col0 + 4 * q);
+      S[4 * q] = a.x; S[4 * q + 1] = a.y; S[4 * q + 2] = a.z; S[4 * q + 3] = a.w;
     }
-    __syncthreads();
-    {  // merge the 8 k-slices: warp w takes token rows 8 w .. 8 w + 7
-      const int q = merge_q(warp);
-      const int mt = 8 * warp + (q >> 1), mvq = 2 * (lane >> 4) + (q & 1);
-      float4 v = *reinterpret_cast<const float4 *>(&sm.U[buf][mt][4 * mvq]);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const float4 pv = sm.Pv[16 * (16 * ks + 2 * warp) + lane];
-        v = make_float4(v.x - pv.x, v.y - pv.y, v.z - pv.z, v.w - pv.w);
-      }
-      *reinterpret_cast<float4 *>(&sm.Vn[mt][4 * mvq]) = v;
-      using umma::blk_off;
-      sm.Vst[buf][blk_off(4 * mvq + 0, mt, kC)] = v.x;
-      sm.Vst[buf][blk_off(4 * mvq + 1, mt, kC)] = v.y;
-      sm.Vst[buf][blk_off(4 * mvq + 2, mt, kC)] = v.z;
-      sm.Vst[buf][blk_off(4 * mvq + 3, mt, kC)] = v.w;
-    }
-    __syncthreads();
-
-    // k'^T v'  (:342-349): [128 k x 64 t] x [64 t x 16 v], t split 4 ways
-    if (tid < 128) {
-      const int ts = tid >> 5, kr = lane >> 1, tc = lane & 1;
-      float acc[8][8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-#pragma unroll 4
-      for (int tt = 0; tt < kC / 4; ++tt) {
-        const int t = (kC / 4) * ts + tt;
-        const float4 k0 = *reinterpret_cast<const float4 *>(&sm.Kp[buf][t][8 * kr]);
-        const float4 k1 = *reinterpret_cast<const float4 *>(&sm.Kp[buf][t][8 * kr + 4]);
-        const float4 v0 = *reinterpret_cast<const float4 *>(&sm.Vn[t][8 * tc]);
-        const float4 v1 = *reinterpret_cast<const float4 *>(&sm.Vn[t][8 * tc + 4]);
-        const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
-        const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(kv[i], vv[j], acc[i][j]);
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        sm.Pv[16 * tid + ((2 * i) ^ (tid & 15))] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-        sm.Pv[16 * tid + ((2 * i + 1) ^ (tid & 15))] = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
-      }
-    }
-    __syncthreads();
-
-    // S <- S e^(gamma_last) + k'^T v'  (:350); publish it as S_{c+1}.  Warp w
-    // merges the k row blocks rb = 2 w, 2 w + 1 over the 4 t-slices.
-    {
-      const float dec = sm.dec[buf][0];
-#pragma unroll
-      for (int it = 0; it < 2; ++it) {
-        const int rb = 2 * warp + it, q = merge_q(rb);
-        const int k = 8 * rb + (q >> 1), vq = 2 * (lane >> 4) + (q & 1);
-        float4 ps = sm.Pv[16 * (2 * rb) + lane];
-#pragma unroll
-        for (int t4 = 1; t4 < 4; ++t4) {
-          const float4 pq = sm.Pv[16 * (32 * t4 + 2 * rb) + lane];
-          ps = make_float4(ps.x + pq.x, ps.y + pq.y, ps.z + pq.z, ps.w + pq.w);
-        }
-        float4 a = *reinterpret_cast<const float4 *>(&sm.S[k][4 * vq]);
-        a = make_float4(a.x * dec + ps.x, a.y * dec + ps.y, a.z * dec + ps.z, a.w * dec + ps.w);
-        *reinterpret_cast<float4 *>(&sm.S[k][4 * vq]) = a;
-        if (c + 1 < p.NC) stage_state(sm.Sst[buf], k, vq, a);
-      }
-    }
+    store_operand_row(sm.Sb[k >> 6][0], sm.Sb[k >> 6][1], k & 63, S, lane);
     fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0) {
-      bulk_s2g(rec + kOffVt + 16 * kC * s, sm.Vst[buf], 16 * kC * sizeof(float));
-      if (c + 1 < p.NC) {
-        bulk_s2g(rec + kRec + kOffSc + 16 * 64 * s, sm.Sst[buf][0], 16 * 64 * sizeof(float));
-        bulk_s2g(rec + kRec + kOffSc + kD * 64 + 16 * 64 * s, sm.Sst[buf][1], 16 * 64 * sizeof(float));
+    mbar_arrive(&sm.sready);
+
+    float Un[16];
+    auto load_u = [&](const float *rec) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 a = __ldcg(reinterpret_cast<const float4 *>(rec + kOffU + (size_t)t * kD + col0 + 4 * q));
+        Un[4 * q] = a.x; Un[4 * q + 1] = a.y; Un[4 * q + 2] = a.z; Un[4 * q + 3] = a.w;
       }
+    };
+    if (vrow) load_u(rec0);
+    float decn = __ldcg(rec0 + kOffDec);
+    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    for (int c = 0; c < NC; ++c) {
+      const float *rec = rec0 + (size_t)c * kRec;
+      const float dec = decn;
+      float U[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) U[j] = Un[j];
+      if (c + 1 < NC) {
+        if (vrow) load_u(rec + kRec);
+        decn = __ldcg(rec + kRec + kOffDec);
+      }
+      {  // v' = U - W S_c  (:315-324).  The TMEM loads are warp-collective, so
+         // every lane issues them; lanes 16-31 (no token rows) drop the values.
+        if (ok && !mbar_wait(&sm.m1, c & 1)) ok = false;
+        __syncwarp();
+        umma::fence_after_sync();
+        float d[16], e[16], f[16];
+        umma::ld_32x32b_x16(tb + lane_base, d);
+        umma::ld_32x32b_x16(tb + lane_base + 16, e);
+        umma::ld_32x32b_x16(tb + lane_base + 32, f);
+        umma::wait_ld();
+        if (vrow) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) d[j] = U[j] - ((d[j] + e[j]) + f[j]);
+          store_operand_row(sm.Vb[0], sm.Vb[1], t, d, lane);
+          fence_proxy_async_smem();
+          umma::fence_before_sync();
+          mbar_arrive(&sm.vready);
+        }
+      }
+      // S <- S e^(gamma_last) + k'^T v'  (:342-350)
+      if (ok && !mbar_wait(&sm.m2, c & 1)) ok = false;
+      __syncwarp();
+      umma::fence_after_sync();
+      float d[16], e[16], f[16];
+      umma::ld_32x32b_x16(tb + lane_base + 64, d);
+      umma::ld_32x32b_x16(tb + lane_base + 80, e);
+      umma::ld_32x32b_x16(tb + lane_base + 96, f);
+      umma::wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) S[j] = S[j] * dec + ((d[j] + e[j]) + f[j]);
+      if (c + 1 < NC) {
+        store_operand_row(sm.Sb[k >> 6][0], sm.Sb[k >> 6][1], k & 63, S, lane);
+        fence_proxy_async_smem();
+        umma::fence_before_sync();
+        mbar_arrive(&sm.sready);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<float4 *>(Sg + (size_t)k * kD + col0 + 4 * q) =
+          make_float4(S[4 * q], S[4 * q + 1], S[4 * q + 2], S[4 * q + 3]);
+  } else if (tid == kStateIssuer) {
+    // ---- MMA issue, operand copies, publication stores
+    const uint64_t pol = l2_policy_evict_first();
+    constexpr uint32_t kOpBytes = (uint32_t)(2 * kC * kD * sizeof(float));
+    auto load_ops = [&](int c) {
+      const float *rec = rec0 + (size_t)c * kRec;
+      mbar_arrive_expect_tx(&sm.full[c & 1], kOpBytes);
+      bulk_g2s(sm.Wh[c & 1], rec + kOffWt, kC * kD * sizeof(float), &sm.full[c & 1], pol);
+      bulk_g2s(sm.Kh[c & 1], rec + kOffKp, kD * kC * sizeof(float), &sm.full[c & 1], pol);
+    };
+    load_ops(0);
+    if (NC > 1) prefetch_l2_bulk(rec0 + kRec + kOffU, (kOffKp + kD * kC - kOffU) * sizeof(float));
+    const uint32_t id1w = umma::idesc_tf32(64, 2 * kCS, 0, 0), id1 = umma::idesc_tf32(64, kCS, 0, 0);
+    const uint32_t id2w = umma::idesc_tf32(128, 2 * kCS, 0, 0), id2 = umma::idesc_tf32(128, kCS, 0, 0);
+    constexpr uint32_t sbo = (64 / 4) * 128;
+    for (int c = 0; c < NC; ++c) {
+      const int buf = c & 1;
+      float *rec = rec0 + (size_t)c * kRec;
+      // S_c is in Sb, and MMA2 of chunk c-1 is complete (so buffer buf ^ 1 is free)
+      if (ok && !mbar_wait(&sm.sready, c & 1)) ok = false;
+      if (c + 1 < NC && ok) load_ops(c + 1);
+      if (c + 2 < NC) {
+        prefetch_l2_bulk(rec + 2 * kRec + kOffU, (kOffKp + kD * kC - kOffU) * sizeof(float));
+        prefetch_l2_bulk(rec + 2 * kRec + kOffDec, 64 * sizeof(float));
+      }
+      bulk_s2g(rec + kOffSc + 16 * 64 * s, sm.Sb[0][0], 16 * 64 * sizeof(float));
+      bulk_s2g(rec + kOffSc + kD * 64 + 16 * 64 * s, sm.Sb[1][0], 16 * 64 * sizeof(float));
+      bulk_commit();
+      if (ok && !mbar_wait(&sm.full[buf], (c >> 1) & 1)) ok = false;
+      if (ok && !mbar_wait(&sm.wlo, c & 1)) ok = false;
+      bulk_wait_read<1>();  // the v'^T store of chunk c-1 has read Vb
+      umma::fence_after_sync();
+#pragma unroll 1
+      for (int ks = 0; ks < kD / 8; ++ks) {
+        const int ao = (ks >> 3) * (kC * 64) + (ks & 7) * 64;
+        const uint64_t ah = umma::smem_desc(sm.Wh[buf] + ao, 128, sbo), al = umma::smem_desc(sm.Wl + ao, 128, sbo);
+        const uint64_t bb = umma::smem_desc(sm.Sb[ks >> 3][0] + (ks & 7) * 64, 128, sbo);  // [hi; lo] rows
+        umma::mma_tf32(tb, ah, bb, id1w, ks > 0 ? 1u : 0u);
+        umma::mma_tf32(tb + 32, al, bb, id1, ks > 0 ? 1u : 0u);
+      }
+      umma::commit(&sm.m1);
+      if (ok && !mbar_wait(&sm.klo, c & 1)) ok = false;
+      if (ok && !mbar_wait(&sm.vready, c & 1)) ok = false;
+      bulk_wait_read<0>();  // the S_c^T stores have read Sb before S_{c+1} replaces it
+      umma::fence_after_sync();
+#pragma unroll 1
+      for (int ks = 0; ks < kC / 8; ++ks) {
+        const uint64_t ah = umma::smem_desc(sm.Kh[buf] + ks * 64, 128, sbo);
+        const uint64_t al = umma::smem_desc(sm.Kl + ks * 64, 128, sbo);
+        const uint64_t bb = umma::smem_desc(sm.Vb[0] + ks * 64, 128, sbo);  // [hi; lo] rows
+        umma::mma_tf32(tb + 64, ah, bb, id2w, ks > 0 ? 1u : 0u);
+        umma::mma_tf32(tb + 96, al, bb, id2, ks > 0 ? 1u : 0u);
+      }
+      umma::commit(&sm.m2);
+      bulk_s2g(rec + kOffVt + 16 * kC * s, sm.Vb[0], 16 * kC * sizeof(float));
       bulk_commit();
     }
+    bulk_wait<0>();  // every published tile is complete before the CTA retires
+  } else if (warp >= 5) {
+    // ---- tf32 lo terms of the chunk's W and k'^T, each once the MMA that
+    // read the previous chunk's is complete
+    const int t = tid - (kStateThreads - kStateLoThreads);
+    for (int c = 0; c < NC; ++c) {
+      const int buf = c & 1;
+      if (ok && !mbar_wait(&sm.full[buf], (c >> 1) & 1)) ok = false;
+      if (c > 0 && ok && !mbar_wait(&sm.m1, (c - 1) & 1)) ok = false;
+      lo_pass(sm.Wh[buf], sm.Wl, t);
+      fence_proxy_async_smem();
+      mbar_arrive(&sm.wlo);
+      if (c > 0 && ok && !mbar_wait(&sm.m2, (c - 1) & 1)) ok = false;
+      lo_pass(sm.Kh[buf], sm.Kl, t);
+      fence_proxy_async_smem();
+      mbar_arrive(&sm.klo);
+    }
   }
-  cp_async_wait<0>();
-  __syncthreads();  // the last update's rows were written by other threads
-#pragma unroll
-  for (int e = 0; e < 2; ++e)
-    *reinterpret_cast<float4 *>(Sg + (size_t)ur * kD + col0 + 4 * (uq0 + e)) =
-        *reinterpret_cast<const float4 *>(&sm.S[ur][4 * (uq0 + e)]);
-  if (!ok && tid == 0) Sg[col0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison the state
 
   // new conv state = last K-1 inputs of [history, x] (:538-540): v channels of
   // this CTA's columns, and (first value head of the key head) 32 of its 256
@@ -748,7 +779,11 @@ __global__ void __launch_bounds__(kStateThreads) gdn_prefill_state_kernel(const 
     const int li = s * (2 * kD / kSplit) + (tid - 32);
     write_conv(li < kD ? hk * kD + li : p.Hk * kD + hk * kD + (li - kD));
   }
-  if (tid == 0) bulk_wait<0>();  // every published tile is complete before the CTA retires
+
+  umma::fence_before_sync();
+  const int failed = __syncthreads_or(ok ? 0 : 1);
+  if (failed && tid == 0) Sg[col0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison the state
+  if (warp == 4) umma::tmem_dealloc(tb, 128);
 }
 
 // ---------------------------------------------------------------------------
