@@ -715,26 +715,29 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
       if (ok && !mbar_wait(&sm.wlo, c & 1)) ok = false;
       bulk_wait_read<1>();  // the v'^T store of chunk c-1 has read Vb
       umma::fence_after_sync();
-#pragma unroll 1
+      // Descriptors advance by adding the byte offset / 16 to the start
+      // address field (every operand lies below 228 KB, so it cannot carry).
+      const uint64_t dWh = umma::smem_desc(sm.Wh[buf], 128, sbo), dWl = umma::smem_desc(sm.Wl, 128, sbo);
+      const uint64_t dSb = umma::smem_desc(&sm.Sb[0][0][0], 128, sbo);  // [hi; lo] rows per k slab
+#pragma unroll
       for (int ks = 0; ks < kD / 8; ++ks) {
-        const int ao = (ks >> 3) * (kC * 64) + (ks & 7) * 64;
-        const uint64_t ah = umma::smem_desc(sm.Wh[buf] + ao, 128, sbo), al = umma::smem_desc(sm.Wl + ao, 128, sbo);
-        const uint64_t bb = umma::smem_desc(sm.Sb[ks >> 3][0] + (ks & 7) * 64, 128, sbo);  // [hi; lo] rows
-        umma::mma_tf32(tb, ah, bb, id1w, ks > 0 ? 1u : 0u);
-        umma::mma_tf32(tb + 32, al, bb, id1, ks > 0 ? 1u : 0u);
+        const uint64_t ao = (uint64_t)(((ks >> 3) * (kC * 64) + (ks & 7) * 64) * 4 / 16);
+        const uint64_t bo = (uint64_t)(((ks >> 3) * (2 * kCS * 64) + (ks & 7) * 64) * 4 / 16);
+        umma::mma_tf32(tb, dWh + ao, dSb + bo, id1w, ks > 0 ? 1u : 0u);
+        umma::mma_tf32(tb + 32, dWl + ao, dSb + bo, id1, ks > 0 ? 1u : 0u);
       }
       umma::commit(&sm.m1);
       if (ok && !mbar_wait(&sm.klo, c & 1)) ok = false;
       if (ok && !mbar_wait(&sm.vready, c & 1)) ok = false;
       bulk_wait_read<0>();  // the S_c^T stores have read Sb before S_{c+1} replaces it
       umma::fence_after_sync();
-#pragma unroll 1
+      const uint64_t dKh = umma::smem_desc(sm.Kh[buf], 128, sbo), dKl = umma::smem_desc(sm.Kl, 128, sbo);
+      const uint64_t dVb = umma::smem_desc(sm.Vb[0], 128, sbo);  // [hi; lo] rows
+#pragma unroll
       for (int ks = 0; ks < kC / 8; ++ks) {
-        const uint64_t ah = umma::smem_desc(sm.Kh[buf] + ks * 64, 128, sbo);
-        const uint64_t al = umma::smem_desc(sm.Kl + ks * 64, 128, sbo);
-        const uint64_t bb = umma::smem_desc(sm.Vb[0] + ks * 64, 128, sbo);  // [hi; lo] rows
-        umma::mma_tf32(tb + 64, ah, bb, id2w, ks > 0 ? 1u : 0u);
-        umma::mma_tf32(tb + 96, al, bb, id2, ks > 0 ? 1u : 0u);
+        const uint64_t o = (uint64_t)(ks * 64 * 4 / 16);
+        umma::mma_tf32(tb + 64, dKh + o, dVb + o, id2w, ks > 0 ? 1u : 0u);
+        umma::mma_tf32(tb + 96, dKl + o, dVb + o, id2, ks > 0 ? 1u : 0u);
       }
       umma::commit(&sm.m2);
       bulk_s2g(rec + kOffVt + 16 * kC * s, sm.Vb[0], 16 * kC * sizeof(float));
