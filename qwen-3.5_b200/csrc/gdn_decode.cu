@@ -105,6 +105,16 @@ __global__ void __launch_bounds__(GdnDecodeCfg<SPLIT>::NT)
 #pragma unroll
   for (int i = 0; i < NP; ++i)
     S[i] = __ldcs(reinterpret_cast<const float4 *>(Sp + (size_t)(r0 + i * RP) * kDV));
+  // The per-head gate inputs and the gated-norm operands are requested now as
+  // well, so that no global-memory round trip is left behind the barriers.
+  const float g_h = p.g[(size_t)b * p.Hv + h];
+  const float bt = p.beta[(size_t)b * p.Hv + h];
+  const size_t oidx = ((size_t)b * p.Hv + h) * kDV + col0 + tid;
+  float z_c = 0.0f, nw_c = 0.0f;
+  if (tid < CS) {
+    z_c = p.z[oidx];
+    nw_c = p.norm_w[col0 + tid];
+  }
 
   // (2) Causal conv update + SiLU.  q/k channels of key head hk are spread
   // over the cluster (channel i owned by rank i % ncl); v channels of the
@@ -152,8 +162,7 @@ __global__ void __launch_bounds__(GdnDecodeCfg<SPLIT>::NT)
   }
 
   // (4) Delta rule (text_modules.rs:412-430).
-  const float decay = expf(p.g[(size_t)b * p.Hv + h]);
-  const float bt = p.beta[(size_t)b * p.Hv + h];
+  const float decay = expf(g_h);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
@@ -224,9 +233,7 @@ __global__ void __launch_bounds__(GdnDecodeCfg<SPLIT>::NT)
 #pragma unroll
     for (int j = 0; j < SPLIT; ++j) tot += sq_parts[j];
     const float inv = 1.0f / sqrtf(tot / (float)kDV + p.eps);
-    const int col = col0 + tid;
-    const size_t oidx = ((size_t)b * p.Hv + h) * kDV + col;
-    p.out[oidx] = (p.norm_w[col] * (o_s[tid] * inv)) * siluf_dev(p.z[oidx]);
+    p.out[oidx] = (nw_c * (o_s[tid] * inv)) * siluf_dev(z_c);
   }
 }
 
