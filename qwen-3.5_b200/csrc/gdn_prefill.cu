@@ -43,7 +43,7 @@ constexpr int kStateThreads = 256;  // state pass: 4 row warps, the MMA issuer w
 // K-major layout of umma.cuh, split into 64-column slabs so that every
 // pipeline stage is one contiguous bulk copy.
 constexpr int kOffU = 0;                  // U [64 t][128 v], row-major
-constexpr int kOffWt = kC * kD;           // W [64 t][128 k]: 2 slabs of blocked [64][64]
+constexpr int kOffW = kC * kD;           // W [64 t][128 k]: 2 slabs of blocked [64][64]
 constexpr int kOffKp = 2 * kC * kD;       // k'^T [128 k][64 t], blocked
 constexpr int kOffQs = 3 * kC * kD;       // q' [64 t][128 k]: 2 slabs of blocked [64][64]
 constexpr int kOffAq = 4 * kC * kD;       // Aqk [64 i][64 j], blocked
@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
   __syncthreads();  // eg / ek ready
 
   float *rec = p.ws + (((size_t)b * p.Hv + h) * p.NC + c) * kRec;
-  float *U = rec + kOffU, *Wt = rec + kOffWt, *Kp = rec + kOffKp;
+  float *U = rec + kOffU, *Wk = rec + kOffW, *Kp = rec + kOffKp;
 
   if (tid == 0) rec[kOffDec] = expf(sm.gam[kC - 1]);
 
@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
 #pragma unroll
         // W K-major, the A operand of the state pass: slab d / 64, blocked [64 t][64 k]
 #pragma unroll
-        for (int e = 0; e < 16; ++e) Wt[(d >> 6) * (kC * 64) + blk_off(16 * cb + e, d & 63, 64)] = v[e];
+        for (int e = 0; e < 16; ++e) Wk[(d >> 6) * (kC * 64) + blk_off(16 * cb + e, d & 63, 64)] = v[e];
       }
     }
     if (!g2_ok && tid == 0) rec[kOffDec] = __int_as_float(0x7fc00000);
@@ -690,7 +690,7 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
     auto load_ops = [&](int c) {
       const float *rec = rec0 + (size_t)c * kRec;
       mbar_arrive_expect_tx(&sm.full[c & 1], kOpBytes);
-      bulk_g2s(sm.Wh[c & 1], rec + kOffWt, kC * kD * sizeof(float), &sm.full[c & 1], pol);
+      bulk_g2s(sm.Wh[c & 1], rec + kOffW, kC * kD * sizeof(float), &sm.full[c & 1], pol);
       bulk_g2s(sm.Kh[c & 1], rec + kOffKp, kD * kC * sizeof(float), &sm.full[c & 1], pol);
     };
     load_ops(0);
