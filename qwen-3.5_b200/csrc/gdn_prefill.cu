@@ -37,7 +37,7 @@ constexpr int kD = 128;     // head_k_dim == head_v_dim
 constexpr int kCS = 16;     // value columns per CTA in the state kernel
 constexpr int kSplit = kD / kCS;
 constexpr int kThreads = 512;  // 16 warps: the chunk phases are latency-bound
-constexpr int kStateThreads = 256;  // state pass: 4 row warps, the MMA issuer warp, 3 warps for tf32 lo terms
+constexpr int kStateThreads = 384;  // state pass: 4 row warps, the MMA issuer warp, 3 W-lo warps, 4 k'^T warps
 // Workspace record per (b, h, chunk), offsets in floats.  Tiles that the
 // output kernel feeds to the tensor cores are stored in the 8x4-blocked
 // K-major layout of umma.cuh, split into 64-column slabs so that every
@@ -495,43 +495,63 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
 // Kernel 2: the sequential pass over the chunks (:314-350 without the output
 // term), on the tensor cores.  The value columns of the state are independent
 // recurrences, so a CTA owns 16 of them and needs no peer.  Per chunk:
-//   MMA1  D1[t x v] = W S_c          M = 64, K = 128
-//   v' = U - D1                      TMEM lanes 32 q + 0..15 = tokens 16 q + 0..15
-//   MMA2  D2[k x v] = k'^T v'        M = 128, K = 64
-//   S_{c+1} = e^(gamma_last) S_c + D2   TMEM lane = k
-// each as 3xTF32 with f32 accumulators in TMEM.  The hi and lo rows of the B
-// operand (S_c^T, v'^T) sit one above the other, so A_hi [B_hi; B_lo] is one
-// N = 32 MMA and A_lo B_hi one N = 16 MMA: two MMAs per K step, each A tile
-// read from shared memory twice instead of three times.  (With N this small
-// the MMAs are bound by those A reads.)  The state itself stays in registers:
+//   MMA1  D1 = [W_hi; W_lo] [S_hi; S_lo]^T           M = 128, N = 32, K = 128
+//   v' = U - (W_hi S_hi + W_hi S_lo + W_lo S_hi + W_lo S_lo)
+//   MMA2  D2 = k'_hi [v'_hi; v'_lo]^T + k'_lo v'_hi^T   M = 128, K = 64
+//   S_{c+1} = e^(gamma_last) S_c + D2
+// with f32 accumulators in TMEM (3xTF32 or better).  A small tf32 MMA holds
+// the tensor pipe for about 45-50 cycles whatever its N, its layout or where
+// its A operand lives, so a chunk's time goes with its MMA count: W_lo is
+// stacked under W_hi as rows 64-127 of one A operand, and the hi and lo rows
+// of each B operand (S_c^T, v'^T) sit one above the other, for 16 + 16 MMAs.
+// W (hi and lo) is double-buffered in shared memory; k'^T (hi and lo) is the
+// A operand of MMA2 straight from TMEM.  The state itself stays in registers:
 // thread k holds row k of the CTA's 16 columns.  Roles:
-//   warps 0-3  the state rows and (lanes 0-15) the v' rows; they write S_c^T
-//              and v'^T as hi / lo K-major operands (a per-lane rotation of the
-//              16 columns keeps the stores free of bank conflicts);
-//   thread 128 issues the MMAs, the bulk copies of the next chunk's W and k'^T,
-//              an L2 prefetch two chunks ahead, and the stores that publish
-//              S_c^T and v'^T for the output kernel;
-//   warps 5-7  form the tf32 lo terms of W and k'^T.
+//   warps 0-3   the state rows; warps 2-3 hand the W_lo rows of D1 to warps
+//               0-1 through shared memory, and warps 0-1 form v'.  They write
+//               S_c^T and v'^T as hi / lo K-major operands (a per-lane
+//               rotation of the 16 columns keeps the stores free of bank
+//               conflicts);
+//   thread 128  issues the MMAs, the bulk copies of the next chunk's W, an L2
+//               prefetch two chunks ahead, and the stores that publish S_c^T
+//               and v'^T for the output kernel;
+//   warps 5-7   form the tf32 lo half of each W buffer;
+//   warps 8-11  (one per TMEM lane quadrant) load k'^T rows into registers
+//               ahead of time and store them, hi and lo, to TMEM once MMA2 of
+//               the previous chunk is complete.
 // The roles hand over through mbarriers only (every wait bounded), so each
 // waits on its true dependency and nothing else.
 struct StateSmem {
-  float Wh[2][kC * kD];   // W of chunks c, c+1: [64 t][128 k] K-major, 2 slabs of blocked [64][64]
-  float Wl[kC * kD];      // tf32 lo term of the current W
-  float Kh[2][kD * kC];   // k'^T of chunks c, c+1: blocked [128 k][64 t]
-  float Kl[kD * kC];      // tf32 lo term of the current k'^T
+  float Wb[2][2 * kC * kD];  // W of chunks c, c+1: per k slab [hi, lo], each blocked [64 t][64 k]
   float Sb[2][2][kCS * 64];  // S_c^T, per k slab [hi, lo] of blocked [16 v][64 k]
   float Vb[2][kCS * kC];     // v'^T [hi, lo] of blocked [16 v][64 t]
-  uint64_t full[2], wlo, klo, sready, vready, m1, m2;
+  float X[kC][kCS + 4];      // the W_lo rows of D1, warps 2-3 -> warps 0-1
+  uint64_t wfull[2], wlo, kready, sready, vready, m1, m2;
   uint32_t tbase;
 };
 static_assert(sizeof(StateSmem) <= 227 * 1024, "state pass shared memory");
 
-constexpr int kStateRowThreads = 128;  // warps 0-3
-constexpr int kStateIssuer = 128;      // warp 4, lane 0
-constexpr int kStateLoThreads = 96;    // warps 5-7
+constexpr int kStateRowThreads = 128;   // warps 0-3
+constexpr int kStateIssuer = 128;       // warp 4, lane 0
+constexpr int kStateLoThreads = 96;     // warps 5-7
+constexpr int kStateKWarp0 = 8;         // warps 8-11: k'^T into TMEM
+constexpr uint32_t kBarRows = 3;        // named barrier of the row warps
+// TMEM columns: D1 0-31, D2 64-111, k'^T hi 128-191 and lo 192-255
+constexpr uint32_t kTmemCols = 256, kColD2 = 64, kColKh = 128, kColKl = 192;
 
 __device__ __forceinline__ void prefetch_l2_bulk(const void *src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// tcgen05.mma with the A operand in tensor memory (columns = K, lane = row).
+__device__ __forceinline__ void mma_tf32_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 // Row r (0..63) of a 16-column tile, written as column r of the K-major
@@ -561,15 +581,6 @@ __device__ __forceinline__ void store_operand_row(float *hi, float *lo, int r, c
   }
 }
 
-__device__ __forceinline__ void lo_pass(const float *src, float *dst, int t) {
-  const float4 *s4 = reinterpret_cast<const float4 *>(src);
-  float4 *d4 = reinterpret_cast<float4 *>(dst);
-  for (int e = t; e < kC * kD / 4; e += kStateLoThreads) {
-    const float4 v = s4[e];
-    d4[e] = make_float4(umma::tf32_lo(v.x), umma::tf32_lo(v.y), umma::tf32_lo(v.z), umma::tf32_lo(v.w));
-  }
-}
-
 template <int KC>
 __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(const PrefillParams p) {
   pdl_entry();
@@ -583,14 +594,14 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
   float *rec0 = p.ws + ((size_t)b * p.Hv + h) * NC * kRec;
 
   if (warp == 4) {
-    umma::tmem_alloc(&sm.tbase, 128);  // D1: columns 0-47, D2: 64-111
+    umma::tmem_alloc(&sm.tbase, kTmemCols);
     umma::tmem_relinquish();
   }
   if (tid == kStateIssuer) {
-    mbar_init(&sm.full[0], 1);
-    mbar_init(&sm.full[1], 1);
+    mbar_init(&sm.wfull[0], 1);
+    mbar_init(&sm.wfull[1], 1);
     mbar_init(&sm.wlo, kStateLoThreads);
-    mbar_init(&sm.klo, kStateLoThreads);
+    mbar_init(&sm.kready, 128);
     mbar_init(&sm.sready, kStateRowThreads);
     mbar_init(&sm.vready, kC);
     mbar_init(&sm.m1, 1);
@@ -606,10 +617,9 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
   bool ok = true;
 
   if (warp < 4) {
-    // ---- state rows (k = tid) and, for lanes 0-15, the v' rows (t = 16 warp + lane)
+    // ---- state rows (k = tid); warps 0-1 are also the v' rows (t = tid)
     const int k = tid;
-    const bool vrow = lane < 16;
-    const int t = 16 * warp + lane;
+    const bool vrow = tid < kC;
     float S[16];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -625,7 +635,7 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
     auto load_u = [&](const float *rec) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const float4 a = __ldcg(reinterpret_cast<const float4 *>(rec + kOffU + (size_t)t * kD + col0 + 4 * q));
+        const float4 a = __ldcg(reinterpret_cast<const float4 *>(rec + kOffU + (size_t)tid * kD + col0 + 4 * q));
         Un[4 * q] = a.x; Un[4 * q + 1] = a.y; Un[4 * q + 2] = a.z; Un[4 * q + 3] = a.w;
       }
     };
@@ -642,20 +652,33 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
         if (vrow) load_u(rec + kRec);
         decn = __ldcg(rec + kRec + kOffDec);
       }
-      {  // v' = U - W S_c  (:315-324).  The TMEM loads are warp-collective, so
-         // every lane issues them; lanes 16-31 (no token rows) drop the values.
+      {  // v' = U - W S_c  (:315-324); TMEM lane = row of [W_hi; W_lo]
         if (ok && !mbar_wait(&sm.m1, c & 1)) ok = false;
         __syncwarp();
         umma::fence_after_sync();
-        float d[16], e[16], f[16];
+        float d[16], e[16];
         umma::ld_32x32b_x16(tb + lane_base, d);
         umma::ld_32x32b_x16(tb + lane_base + 16, e);
-        umma::ld_32x32b_x16(tb + lane_base + 32, f);
         umma::wait_ld();
-        if (vrow) {
+        if (!vrow) {  // W_lo rows: W_lo S_hi + W_lo S_lo of token tid - 64
+          float4 *x = reinterpret_cast<float4 *>(&sm.X[tid - kC][0]);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) d[j] = U[j] - ((d[j] + e[j]) + f[j]);
-          store_operand_row(sm.Vb[0], sm.Vb[1], t, d, lane);
+          for (int q = 0; q < 4; ++q)
+            x[q] = make_float4(d[4 * q] + e[4 * q], d[4 * q + 1] + e[4 * q + 1], d[4 * q + 2] + e[4 * q + 2],
+                               d[4 * q + 3] + e[4 * q + 3]);
+        }
+        named_bar_sync(kBarRows, kStateRowThreads);
+        if (vrow) {
+          const float4 *x = reinterpret_cast<const float4 *>(&sm.X[tid][0]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 xl = x[q];
+            d[4 * q] = U[4 * q] - ((d[4 * q] + e[4 * q]) + xl.x);
+            d[4 * q + 1] = U[4 * q + 1] - ((d[4 * q + 1] + e[4 * q + 1]) + xl.y);
+            d[4 * q + 2] = U[4 * q + 2] - ((d[4 * q + 2] + e[4 * q + 2]) + xl.z);
+            d[4 * q + 3] = U[4 * q + 3] - ((d[4 * q + 3] + e[4 * q + 3]) + xl.w);
+          }
+          store_operand_row(sm.Vb[0], sm.Vb[1], tid, d, lane);
           fence_proxy_async_smem();
           umma::fence_before_sync();
           mbar_arrive(&sm.vready);
@@ -666,9 +689,9 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
       __syncwarp();
       umma::fence_after_sync();
       float d[16], e[16], f[16];
-      umma::ld_32x32b_x16(tb + lane_base + 64, d);
-      umma::ld_32x32b_x16(tb + lane_base + 80, e);
-      umma::ld_32x32b_x16(tb + lane_base + 96, f);
+      umma::ld_32x32b_x16(tb + lane_base + kColD2, d);
+      umma::ld_32x32b_x16(tb + lane_base + kColD2 + 16, e);
+      umma::ld_32x32b_x16(tb + lane_base + kColD2 + 32, f);
       umma::wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) S[j] = S[j] * dec + ((d[j] + e[j]) + f[j]);
@@ -684,81 +707,113 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
       *reinterpret_cast<float4 *>(Sg + (size_t)k * kD + col0 + 4 * q) =
           make_float4(S[4 * q], S[4 * q + 1], S[4 * q + 2], S[4 * q + 3]);
   } else if (tid == kStateIssuer) {
-    // ---- MMA issue, operand copies, publication stores
+    // ---- MMA issue, W copies, publication stores
     const uint64_t pol = l2_policy_evict_first();
-    constexpr uint32_t kOpBytes = (uint32_t)(2 * kC * kD * sizeof(float));
-    auto load_ops = [&](int c) {
-      const float *rec = rec0 + (size_t)c * kRec;
-      mbar_arrive_expect_tx(&sm.full[c & 1], kOpBytes);
-      bulk_g2s(sm.Wh[c & 1], rec + kOffW, kC * kD * sizeof(float), &sm.full[c & 1], pol);
-      bulk_g2s(sm.Kh[c & 1], rec + kOffKp, kD * kC * sizeof(float), &sm.full[c & 1], pol);
+    constexpr uint32_t kSlabBytes = (uint32_t)(kC * 64 * sizeof(float));
+    auto load_w = [&](int c) {  // the hi half of each k slab
+      const float *src = rec0 + (size_t)c * kRec + kOffW;
+      mbar_arrive_expect_tx(&sm.wfull[c & 1], 2 * kSlabBytes);
+      bulk_g2s(sm.Wb[c & 1], src, kSlabBytes, &sm.wfull[c & 1], pol);
+      bulk_g2s(sm.Wb[c & 1] + 2 * kC * 64, src + kC * 64, kSlabBytes, &sm.wfull[c & 1], pol);
     };
-    load_ops(0);
-    if (NC > 1) prefetch_l2_bulk(rec0 + kRec + kOffU, (kOffKp + kD * kC - kOffU) * sizeof(float));
-    const uint32_t id1w = umma::idesc_tf32(64, 2 * kCS, 0, 0), id1 = umma::idesc_tf32(64, kCS, 0, 0);
-    const uint32_t id2w = umma::idesc_tf32(128, 2 * kCS, 0, 0), id2 = umma::idesc_tf32(128, kCS, 0, 0);
+    constexpr uint32_t kPrefetch = (kOffKp + kD * kC - kOffU) * sizeof(float);  // U, W, k'^T
+    load_w(0);
+    if (NC > 1) prefetch_l2_bulk(rec0 + kRec + kOffU, kPrefetch);
+    const uint32_t idw = umma::idesc_tf32(128, 2 * kCS, 0, 0), idn = umma::idesc_tf32(128, kCS, 0, 0);
     constexpr uint32_t sbo = (64 / 4) * 128;
     for (int c = 0; c < NC; ++c) {
       const int buf = c & 1;
       float *rec = rec0 + (size_t)c * kRec;
-      // S_c is in Sb, and MMA2 of chunk c-1 is complete (so buffer buf ^ 1 is free)
+      // S_c is in Sb, and MMA2 of chunk c-1 is complete: W buffer buf ^ 1 is free
       if (ok && !mbar_wait(&sm.sready, c & 1)) ok = false;
-      if (c + 1 < NC && ok) load_ops(c + 1);
+      if (c + 1 < NC && ok) load_w(c + 1);
       if (c + 2 < NC) {
-        prefetch_l2_bulk(rec + 2 * kRec + kOffU, (kOffKp + kD * kC - kOffU) * sizeof(float));
+        prefetch_l2_bulk(rec + 2 * kRec + kOffU, kPrefetch);
         prefetch_l2_bulk(rec + 2 * kRec + kOffDec, 64 * sizeof(float));
       }
       bulk_s2g(rec + kOffSc + 16 * 64 * s, sm.Sb[0][0], 16 * 64 * sizeof(float));
       bulk_s2g(rec + kOffSc + kD * 64 + 16 * 64 * s, sm.Sb[1][0], 16 * 64 * sizeof(float));
       bulk_commit();
-      if (ok && !mbar_wait(&sm.full[buf], (c >> 1) & 1)) ok = false;
+      if (ok && !mbar_wait(&sm.wfull[buf], (c >> 1) & 1)) ok = false;
       if (ok && !mbar_wait(&sm.wlo, c & 1)) ok = false;
       bulk_wait_read<1>();  // the v'^T store of chunk c-1 has read Vb
       umma::fence_after_sync();
       // Descriptors advance by adding the byte offset / 16 to the start
       // address field (every operand lies below 228 KB, so it cannot carry).
-      const uint64_t dWh = umma::smem_desc(sm.Wh[buf], 128, sbo), dWl = umma::smem_desc(sm.Wl, 128, sbo);
+      const uint64_t dW = umma::smem_desc(sm.Wb[buf], 128, sbo);       // rows 0-63 hi, 64-127 lo
       const uint64_t dSb = umma::smem_desc(&sm.Sb[0][0][0], 128, sbo);  // [hi; lo] rows per k slab
 #pragma unroll
       for (int ks = 0; ks < kD / 8; ++ks) {
-        const uint64_t ao = (uint64_t)(((ks >> 3) * (kC * 64) + (ks & 7) * 64) * 4 / 16);
+        const uint64_t ao = (uint64_t)(((ks >> 3) * (2 * kC * 64) + (ks & 7) * 64) * 4 / 16);
         const uint64_t bo = (uint64_t)(((ks >> 3) * (2 * kCS * 64) + (ks & 7) * 64) * 4 / 16);
-        umma::mma_tf32(tb, dWh + ao, dSb + bo, id1w, ks > 0 ? 1u : 0u);
-        umma::mma_tf32(tb + 32, dWl + ao, dSb + bo, id1, ks > 0 ? 1u : 0u);
+        umma::mma_tf32(tb, dW + ao, dSb + bo, idw, ks > 0 ? 1u : 0u);
       }
       umma::commit(&sm.m1);
-      if (ok && !mbar_wait(&sm.klo, c & 1)) ok = false;
+      if (ok && !mbar_wait(&sm.kready, c & 1)) ok = false;
       if (ok && !mbar_wait(&sm.vready, c & 1)) ok = false;
       bulk_wait_read<0>();  // the S_c^T stores have read Sb before S_{c+1} replaces it
       umma::fence_after_sync();
-      const uint64_t dKh = umma::smem_desc(sm.Kh[buf], 128, sbo), dKl = umma::smem_desc(sm.Kl, 128, sbo);
       const uint64_t dVb = umma::smem_desc(sm.Vb[0], 128, sbo);  // [hi; lo] rows
 #pragma unroll
       for (int ks = 0; ks < kC / 8; ++ks) {
         const uint64_t o = (uint64_t)(ks * 64 * 4 / 16);
-        umma::mma_tf32(tb + 64, dKh + o, dVb + o, id2w, ks > 0 ? 1u : 0u);
-        umma::mma_tf32(tb + 96, dKl + o, dVb + o, id2, ks > 0 ? 1u : 0u);
+        mma_tf32_tmem_a(tb + kColD2, tb + kColKh + 8 * ks, dVb + o, idw, ks > 0 ? 1u : 0u);
+        mma_tf32_tmem_a(tb + kColD2 + 32, tb + kColKl + 8 * ks, dVb + o, idn, ks > 0 ? 1u : 0u);
       }
       umma::commit(&sm.m2);
       bulk_s2g(rec + kOffVt + 16 * kC * s, sm.Vb[0], 16 * kC * sizeof(float));
       bulk_commit();
     }
     bulk_wait<0>();  // every published tile is complete before the CTA retires
-  } else if (warp >= 5) {
-    // ---- tf32 lo terms of the chunk's W and k'^T, each once the MMA that
-    // read the previous chunk's is complete
-    const int t = tid - (kStateThreads - kStateLoThreads);
+  } else if (warp >= 5 && warp < kStateKWarp0) {
+    // ---- tf32 lo half of each W buffer, once MMA1 of the previous chunk is
+    // complete (which keeps this role at most one chunk ahead)
+    const int t = tid - 5 * 32;
     for (int c = 0; c < NC; ++c) {
       const int buf = c & 1;
-      if (ok && !mbar_wait(&sm.full[buf], (c >> 1) & 1)) ok = false;
+      if (ok && !mbar_wait(&sm.wfull[buf], (c >> 1) & 1)) ok = false;
       if (c > 0 && ok && !mbar_wait(&sm.m1, (c - 1) & 1)) ok = false;
-      lo_pass(sm.Wh[buf], sm.Wl, t);
+      float4 *w4 = reinterpret_cast<float4 *>(sm.Wb[buf]);
+      for (int e = t; e < 2 * kC * 64 / 4; e += kStateLoThreads) {
+        const int i = (e >> 10) * (2 * kC * 64 / 4) + (e & 1023);  // float4 of k slab e / 1024
+        const float4 v = w4[i];
+        w4[i + kC * 64 / 4] =
+            make_float4(umma::tf32_lo(v.x), umma::tf32_lo(v.y), umma::tf32_lo(v.z), umma::tf32_lo(v.w));
+      }
       fence_proxy_async_smem();
       mbar_arrive(&sm.wlo);
-      if (c > 0 && ok && !mbar_wait(&sm.m2, (c - 1) & 1)) ok = false;
-      lo_pass(sm.Kh[buf], sm.Kl, t);
-      fence_proxy_async_smem();
-      mbar_arrive(&sm.klo);
+    }
+  } else if (warp >= kStateKWarp0) {
+    // ---- k'^T rows into TMEM: thread = TMEM lane = k (warp w % 4 owns lanes
+    // 32 (w % 4) ..), columns kColKh + t (hi) and kColKl + t (lo)
+    const int q = warp & 3, k = 32 * q + lane;
+    const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+    for (int c = 0; c < NC; ++c) {
+      // row k of the blocked [128 k][64 t] tile: 16 float4, t = 4 m .. 4 m + 3
+      const float4 *src = reinterpret_cast<const float4 *>(rec0 + (size_t)c * kRec + kOffKp);
+      float row[64];
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        const float4 v = __ldcg(src + ((k >> 3) * 16 + m) * 8 + (k & 7));
+        row[4 * m] = v.x; row[4 * m + 1] = v.y; row[4 * m + 2] = v.z; row[4 * m + 3] = v.w;
+      }
+      if (c > 0 && ok && !mbar_wait(&sm.m2, (c - 1) & 1)) ok = false;  // MMA2 of chunk c-1 has read k'^T
+      __syncwarp();
+      umma::fence_after_sync();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float hi[16], lo[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          hi[i] = row[16 * j + i];
+          lo[i] = umma::tf32_lo(row[16 * j + i]);
+        }
+        umma::st_32x32b_x16(tb + lane_base + kColKh + 16 * j, hi);
+        umma::st_32x32b_x16(tb + lane_base + kColKl + 16 * j, lo);
+      }
+      umma::wait_st();
+      umma::fence_before_sync();
+      mbar_arrive(&sm.kready);
     }
   }
 
@@ -786,7 +841,7 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
   umma::fence_before_sync();
   const int failed = __syncthreads_or(ok ? 0 : 1);
   if (failed && tid == 0) Sg[col0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison the state
-  if (warp == 4) umma::tmem_dealloc(tb, 128);
+  if (warp == 4) umma::tmem_dealloc(tb, kTmemCols);
 }
 
 // ---------------------------------------------------------------------------
