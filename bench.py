@@ -137,65 +137,113 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- CPU (oracle) leg
-class CpuWorkload:
-    """The CPU oracle (the reference's attention math restated in C) on one
-    config-4 sequence: a 32768-token KV cache that grows by one token per
-    decode step, plus one Gated DeltaNet layer state.  Every sampled
-    "sequence-step" is one GDN decode + one GQA decode, the same work each of
-    the 256 sequences does per step on the GPU."""
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
 
-    def __init__(self, threads, max_steps, seed=123):
+
+def host_mem_available():
+    """Bytes of host memory available to this process (MemAvailable), or None."""
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) * 1024
+    except (OSError, ValueError, IndexError):
+        pass
+    return None
+
+
+def cpu_cache_bytes(nseq, steps):
+    return nseq * 2 * HKV * (L0 + steps + 1) * D * 4
+
+
+def cpu_fit_seqs(want, steps, reserve=4 << 30):
+    """The largest sequence count <= want (halving) whose caches fit in the
+    host memory available now, with a margin."""
+    avail = host_mem_available()
+    n = want
+    if avail is None:
+        return n
+    while n > 1 and cpu_cache_bytes(n, steps) * 1.1 + reserve > avail:
+        n //= 2
+    return n
+
+
+class CpuBatch:
+    """The CPU oracle (the reference's attention math restated in C) on nseq
+    DISTINCT config-4 sequences: each has its own 32768-token KV cache, which
+    grows by one token per step, and its own Gated DeltaNet state.  One step()
+    is one config-4 step of those sequences: a GDN decode and a GQA decode of
+    the whole batch, the oracle threaded over sequences and heads."""
+
+    def __init__(self, nseq, threads, max_steps, seed=123):
+        import concurrent.futures as cf
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle  # test infrastructure: the checker / CPU baseline only
         self.oracle = oracle
         oracle.set_threads(threads)
-        self.threads = threads
-        rng = np.random.RandomState(seed)
+        self.nseq, self.threads = nseq, threads
         f = np.float32
         cap = L0 + max_steps + 1
-        self.K = np.zeros((1, HKV, cap, D), f)
-        self.V = np.zeros((1, HKV, cap, D), f)
-        fast = np.random.default_rng(seed)
-        self.K[:, :, :L0] = fast.standard_normal((1, HKV, L0, D), dtype=f)
-        self.V[:, :, :L0] = fast.standard_normal((1, HKV, L0, D), dtype=f)
-        self.S = (0.02 * rng.randn(1, HV, DK, DK)).astype(f)
+        self.K = np.empty((nseq, HKV, cap, D), f)
+        self.V = np.empty((nseq, HKV, cap, D), f)
+
+        def fill(i):  # sequence i's cache, from its own generator (threads release the GIL)
+            gen = np.random.default_rng([seed, i])
+            for h in range(HKV):
+                gen.standard_normal((L0, D), dtype=f, out=self.K[i, h, :L0])
+                gen.standard_normal((L0, D), dtype=f, out=self.V[i, h, :L0])
+
+        with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(fill, range(nseq)))
+        rng = np.random.RandomState(seed)
+        self.S = (0.02 * rng.randn(nseq, HV, DK, DK)).astype(f)
         self.conv_w = (0.5 * rng.randn(CONV, KCONV)).astype(f)
         self.norm_w = np.ones(DK, f)
-        self.cst = np.zeros((1, CONV, KCONV - 1), f)
+        self.cst = np.zeros((nseq, CONV, KCONV - 1), f)
         self.w0 = np.zeros(D, f)
-        self.lens = np.array([L0], np.int32)
+        self.lens = np.full(nseq, L0, np.int32)
         self.rng = rng
 
-    def run(self, n):
-        """n sequence-steps; returns the seconds spent inside the oracle calls."""
-        o, f, rng = self.oracle, np.float32, self.rng
-        elapsed = 0.0
-        for _ in range(n):
-            x = rng.randn(1, CONV).astype(f)
-            z = rng.randn(1, HV * DK).astype(f)
-            g = (-np.log1p(np.exp(rng.randn(1, HV)))).astype(f)
-            beta = (1 / (1 + np.exp(-rng.randn(1, HV)))).astype(f)
-            qg = rng.randn(1, HQ, 2 * D).astype(f)
-            kn = rng.randn(1, HKV, D).astype(f)
-            vn = rng.randn(1, HKV, D).astype(f)
-            cos, sin = o.rope_tables(self.lens.astype(np.int64), rot=ROT, theta=THETA)
-            t0 = time.perf_counter()
-            _, self.cst, self.S = o.gdn_decode(x, z, beta, g, self.conv_w, self.norm_w, self.cst, self.S, HK, HV)
-            _, self.K, self.V, self.lens = o.gqa_decode(qg, kn, vn, self.w0, self.w0, cos, sin, self.K, self.V,
-                                                        self.lens, rot=ROT, inplace=True)
-            elapsed += time.perf_counter() - t0
-        return elapsed
-
-    def describe(self, n, elapsed):
-        return (f"{n} sequence-steps of config 4 (each: 1 GDN decode + 1 GQA decode at L~32768), "
-                f"{self.threads} thread(s), {elapsed:.2f} s")
+    def step(self):
+        """One config-4 step over the batch; returns the seconds spent inside
+        the two oracle calls (input generation is outside)."""
+        o, f, rng, n = self.oracle, np.float32, self.rng, self.nseq
+        x = rng.randn(n, CONV).astype(f)
+        z = rng.randn(n, HV * DK).astype(f)
+        g = (-np.log1p(np.exp(rng.randn(n, HV)))).astype(f)
+        beta = (1 / (1 + np.exp(-rng.randn(n, HV)))).astype(f)
+        qg = rng.randn(n, HQ, 2 * D).astype(f)
+        kn = rng.randn(n, HKV, D).astype(f)
+        vn = rng.randn(n, HKV, D).astype(f)
+        cos, sin = o.rope_tables(self.lens.astype(np.int64), rot=ROT, theta=THETA)
+        t0 = time.perf_counter()
+        o.gdn_decode(x, z, beta, g, self.conv_w, self.norm_w, self.cst, self.S, HK, HV, inplace=True)
+        o.gqa_decode(qg, kn, vn, self.w0, self.w0, cos, sin, self.K, self.V, self.lens, rot=ROT, inplace=True)
+        return time.perf_counter() - t0
 
 
-def cpu_sample(threads, n=32):
-    w = CpuWorkload(threads, n + 1)
-    w.run(1)  # warm
-    el = w.run(n)
-    return 2 * n / el, w.describe(n, el)
+def cpu_sample(threads, nseq=32, min_s=10.0, max_steps=60):
+    """Bounded CPU baseline beside the GPU run: whole config-4 steps of nseq
+    distinct sequences, repeated until about min_s seconds of oracle time."""
+    nseq = cpu_fit_seqs(nseq, max_steps + 1)
+    w = CpuBatch(nseq, threads, max_steps + 1)
+    w.step()  # warm
+    el, n = 0.0, 0
+    while n < max_steps and el < min_s:
+        el += w.step()
+        n += 1
+    desc = (f"{n} config-4 steps of {nseq} distinct sequences (each step: 1 GDN decode + 1 GQA decode at "
+            f"L~32768 per sequence), {threads} thread(s), {el:.1f} s")
+    return 2 * nseq * n / el, desc, nseq
 
 
 def run_reference(args):
@@ -203,25 +251,33 @@ def run_reference(args):
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    w = CpuWorkload(threads, args.warmup + args.steps * args.ref_seqs + 1)
+    nsteps = args.warmup + args.steps
+    nseq = cpu_fit_seqs(args.ref_seqs_full, nsteps)
+    w = CpuBatch(nseq, threads, nsteps)
     for _ in range(args.warmup):
-        w.run(1)
-    vals, tot = [], 0.0
-    for i in range(args.steps):
-        el = w.run(args.ref_seqs)
-        tot += el
-        vals.append(2 * args.ref_seqs / el)
-    value = statistics.median(vals)
-    desc = w.describe(args.ref_seqs, tot / args.steps)
+        w.step()
+    tot = 0.0
+    for _ in range(args.steps):
+        tot += w.step()
+    value = 2 * nseq * args.steps / tot
+    desc = (f"{args.steps} timed config-4 steps of {nseq} distinct sequences, each with its own 32K KV cache "
+            f"and GDN state (1 GDN decode + 1 GQA decode per sequence per step), {threads} thread(s), "
+            f"{tot:.1f} s")
+    config = {"workload": "config4: %d seqs x (GDN decode + GQA decode @32K ctx) per step" % nseq,
+              "seqs": nseq, "kv_len_start": L0, "parallelism": "host cores",
+              "cpu": cpu_model()}
+    if nseq < args.ref_seqs_full:
+        config["note"] = (f"{args.ref_seqs_full} sequences need {cpu_cache_bytes(args.ref_seqs_full, nsteps) / 1e9:.1f}"
+                          f" GB of host memory, more than is available; {nseq} distinct sequences were timed instead")
+    elif nseq != NSEQ:
+        config["note"] = f"--ref-seqs-full {nseq}: a smaller batch than config 4's {NSEQ} sequences"
     line = {
         "impl": "reference", "metric": "attn layer-steps/s", "value": value, "unit": "layer-steps/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * 2 * NSEQ / value, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config4: 256 seqs x (GDN decode + GQA decode @32K), per-step bounded sample",
-                   "seqs": NSEQ, "kv_len": L0, "parallelism": "host cores"},
+        "ms_per_step": 1000.0 * tot / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
         "cpu_baseline": {"value": value, "unit": "layer-steps/s", "cores": threads, "kind": "port",
-                         "sample": desc + " (per timed step; median over steps)"},
+                         "cpu": cpu_model(), "sample": desc},
         "e2e": {"value": value, "unit": "layer-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference is Rust/Burn over wgpu; neither cargo nor a graphics stack exists here, so its "
                 "attention math runs as the C restatement in oracle/ on the host cores",
@@ -441,8 +497,9 @@ def run_gpu(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        v, desc = cpu_sample(threads, n=args.ref_seqs)
-        cpu = {"value": v, "unit": "layer-steps/s", "cores": threads, "kind": "port", "sample": desc}
+        v, desc, _ = cpu_sample(threads, nseq=args.ref_seqs)
+        cpu = {"value": v, "unit": "layer-steps/s", "cores": threads, "kind": "port", "cpu": cpu_model(),
+               "sample": desc}
 
     if rank == 0:
         traffic = None
@@ -780,7 +837,10 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--ref-seqs", type=int, default=32, help="sequence-steps in each CPU sample")
+    ap.add_argument("--ref-seqs", type=int, default=32,
+                    help="distinct sequences in the bounded CPU sample beside the GPU run")
+    ap.add_argument("--ref-seqs-full", type=int, default=NSEQ,
+                    help="distinct sequences timed by --impl reference (fewer only if host memory is short)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seqs", type=int, default=NSEQ, help="total sequences (256 = config 4; smaller for ncu)")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 0/1/2 side measurements")

@@ -102,7 +102,12 @@ int q35_gdn_decode(const q35_gdn_dims *dims, const float *mixed_qkv,
  *              :535-537), always overwritten with the last K-1 inputs.
  *   rec_state  [B, Hv, DK, DV]: initial state when has_init_state, else zero;
  *              overwritten with the final state.
- *   workspace  >= q35_gdn_prefill_workspace_size(dims, T) bytes.
+ *   workspace  >= q35_gdn_prefill_workspace_size(dims, T) bytes, 16-byte
+ *              aligned.  Its first 256 bytes hold the status word
+ *              (Q35_STATUS_WAIT_TIMEOUT when a bounded in-kernel wait gave
+ *              up; the state and outputs then hold NaN), read and cleared
+ *              with q35_workspace_status.  Zero them once with
+ *              q35_workspace_init(workspace, 256, stream) before first use.
  *   mixed_qkv, z, norm_w, rec_state and out must be 16-byte aligned.
  */
 size_t q35_gdn_prefill_workspace_size(const q35_gdn_dims *dims, int32_t seq_len);
@@ -310,7 +315,12 @@ int q35_gqa_combine_partials(int32_t batch, int32_t num_q_heads,
  * array, so calls that overlap on the GPU race; each call first clears the
  * array's counters with a memset on `stream`.  The first call on a device
  * looks up the array's device address and should come before any stream
- * capture.  Device-side skips (full cache) leave lens[b] unchanged. */
+ * capture.  Every argument check runs before anything is queued on
+ * `stream`.  The device-side status word (Q35_STATUS_* bits) lives in the
+ * private array and is cleared by the next call, so these callers cannot
+ * read it: a skipped sequence (full cache, length hint exceeded, a wait that
+ * gave up) shows only as lens[b] left unchanged.  Callers that need the bits
+ * use q35_gqa_decode with a workspace and q35_workspace_status. */
 int q35_gqa_decode_noalloc(const q35_gqa_dims *dims, int64_t max_len,
                            const float *q_gate, const float *k_new,
                            const float *v_new, const float *qn_w,
@@ -333,6 +343,16 @@ int q35_gdn_decode_split(const q35_gdn_dims *dims, int32_t split,
                          const float *conv_w, const float *norm_w,
                          float *conv_state, float *rec_state, float *out,
                          void *stream);
+
+/* Test hook: the next call that reaches the armed site withholds one of its
+ * asynchronous copies and bounds its waits at 2 ms, so that a wait runs out
+ * and the error path runs (status word set, outputs poisoned, every copy and
+ * tensor-core operation already started waited for) without a fault or a
+ * hang.  site 1: the q35_gdn_prefill state pass (chunk 1's W operand, needs
+ * seq_len > 64); site 2: the q35_gqa_decode producer (the first K tile of the
+ * first split); 0 disarms.  Arming is global to the process and consumed by
+ * one call. */
+int q35_test_arm_wait_fault(int32_t site);
 
 /* --------------------------------------------------------------------------
  * Library information. */

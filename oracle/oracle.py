@@ -132,10 +132,15 @@ def chunk_gdr(q, k, v, g, beta, S, chunk=64):
     return out, S
 
 
-def gdn_decode(mixed_qkv, z, beta, g, conv_w, norm_w, conv_state, S, Hk, Hv, DK=128, DV=128, eps=1e-6):
-    """Decode core of GatedDeltaNet::forward.  Returns (out, conv_state', S')."""
+def gdn_decode(mixed_qkv, z, beta, g, conv_w, norm_w, conv_state, S, Hk, Hv, DK=128, DV=128, eps=1e-6,
+               inplace=False):
+    """Decode core of GatedDeltaNet::forward.  Returns (out, conv_state', S');
+    with inplace=True the (contiguous float32) states are updated in place."""
     a = [_c(x) for x in (mixed_qkv, z, beta, g, conv_w, norm_w)]
-    st, S = _c(conv_state).copy(), _c(S).copy()
+    if inplace:
+        st, S = _c(conv_state), _c(S)
+    else:
+        st, S = _c(conv_state).copy(), _c(S).copy()
     B = a[0].shape[0]
     K = a[4].shape[1]
     out = np.empty((B, Hv * DV), np.float32)

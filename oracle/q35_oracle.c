@@ -420,9 +420,10 @@ static void gqa_core(int B, int T, int Hq, int Hkv, int D, int rot, int64_t cap,
                      int32_t *lens, float *out, float eps) {
   const int grp = Hq / Hkv;
   const float scale = 1.0f / sqrtf((float)D);
+  /* k_norm + RoPE, then cache append (:877-909), every sequence first */
+#pragma omp parallel for num_threads(g_threads) schedule(static)
   for (int b = 0; b < B; ++b) {
     const int64_t L0 = lens[b];
-    /* k_norm + RoPE, then cache append (:877-909) */
     for (int t = 0; t < T; ++t) {
       const int64_t tok = (int64_t)b * T + t;
       for (int kh = 0; kh < Hkv; ++kh) {
@@ -434,43 +435,47 @@ static void gqa_core(int B, int T, int Hq, int Hkv, int D, int rot, int64_t cap,
         q35o_apply_rope(D, rot, kd, cos + tok * rot, sin + tok * rot);
       }
     }
-#pragma omp parallel for num_threads(g_threads) schedule(dynamic, 1)
-    for (int64_t th = 0; th < (int64_t)T * Hq; ++th) {
-      const int t = (int)(th / Hq), h = (int)(th % Hq), kh = h / grp;
-      const int64_t tok = (int64_t)b * T + t;
-      const int64_t Lk = L0 + t + 1; /* causal: keys 0 .. L0+t */
-      float *qv = (float *)malloc(sizeof(float) * (D * 2 + (size_t)Lk));
-      float *o = qv + D, *sc = o + D;
-      const float *qg = q_gate + (tok * Hq + h) * 2 * D;
-      memcpy(qv, qg, sizeof(float) * D);
-      q35o_rmsnorm(1, D, qv, qn_w, eps);
-      q35o_apply_rope(D, rot, qv, cos + tok * rot, sin + tok * rot);
-      const float *Kc = k_cache + ((int64_t)b * Hkv + kh) * cap * D;
-      const float *Vc = v_cache + ((int64_t)b * Hkv + kh) * cap * D;
-      float mx = -INFINITY;
-      for (int64_t j = 0; j < Lk; ++j) {
-        float s = 0.0f;
-        for (int d = 0; d < D; ++d) s += qv[d] * Kc[j * D + d];
-        sc[j] = s * scale;
-        if (sc[j] > mx) mx = sc[j];
-      }
-      float den = 0.0f;
-      for (int64_t j = 0; j < Lk; ++j) {
-        sc[j] = expf(sc[j] - mx);
-        den += sc[j];
-      }
-      for (int d = 0; d < D; ++d) o[d] = 0.0f;
-      for (int64_t j = 0; j < Lk; ++j) {
-        const float p = sc[j] / den;
-        for (int d = 0; d < D; ++d) o[d] += p * Vc[j * D + d];
-      }
-      /* attn_output * sigmoid(gate) (:936) */
-      for (int d = 0; d < D; ++d)
-        out[(tok * Hq + h) * D + d] = o[d] * sigmoidf_(qg[D + d]);
-      free(qv);
-    }
-    lens[b] = (int32_t)(L0 + T);
   }
+  /* attention of every (sequence, token, query head), independently */
+#pragma omp parallel for num_threads(g_threads) schedule(dynamic, 1)
+  for (int64_t bth = 0; bth < (int64_t)B * T * Hq; ++bth) {
+    const int b = (int)(bth / ((int64_t)T * Hq));
+    const int64_t th = bth % ((int64_t)T * Hq);
+    const int t = (int)(th / Hq), h = (int)(th % Hq), kh = h / grp;
+    const int64_t L0 = lens[b];
+    const int64_t tok = (int64_t)b * T + t;
+    const int64_t Lk = L0 + t + 1; /* causal: keys 0 .. L0+t */
+    float *qv = (float *)malloc(sizeof(float) * (D * 2 + (size_t)Lk));
+    float *o = qv + D, *sc = o + D;
+    const float *qg = q_gate + (tok * Hq + h) * 2 * D;
+    memcpy(qv, qg, sizeof(float) * D);
+    q35o_rmsnorm(1, D, qv, qn_w, eps);
+    q35o_apply_rope(D, rot, qv, cos + tok * rot, sin + tok * rot);
+    const float *Kc = k_cache + ((int64_t)b * Hkv + kh) * cap * D;
+    const float *Vc = v_cache + ((int64_t)b * Hkv + kh) * cap * D;
+    float mx = -INFINITY;
+    for (int64_t j = 0; j < Lk; ++j) {
+      float s = 0.0f;
+      for (int d = 0; d < D; ++d) s += qv[d] * Kc[j * D + d];
+      sc[j] = s * scale;
+      if (sc[j] > mx) mx = sc[j];
+    }
+    float den = 0.0f;
+    for (int64_t j = 0; j < Lk; ++j) {
+      sc[j] = expf(sc[j] - mx);
+      den += sc[j];
+    }
+    for (int d = 0; d < D; ++d) o[d] = 0.0f;
+    for (int64_t j = 0; j < Lk; ++j) {
+      const float p = sc[j] / den;
+      for (int d = 0; d < D; ++d) o[d] += p * Vc[j * D + d];
+    }
+    /* attn_output * sigmoid(gate) (:936) */
+    for (int d = 0; d < D; ++d)
+      out[(tok * Hq + h) * D + d] = o[d] * sigmoidf_(qg[D + d]);
+    free(qv);
+  }
+  for (int b = 0; b < B; ++b) lens[b] = (int32_t)(lens[b] + T);
 }
 
 void q35o_gqa_decode(int B, int Hq, int Hkv, int D, int rot, int64_t cap,

@@ -42,6 +42,10 @@ int rope_gather_launch(int B, int rot, int max_pos, const int32_t *lens, const f
 int gqa_combine_launch(int B, int Hq, int n_parts, const float *parts, const float *q_gate, float *out,
                        cudaStream_t st);
 size_t gdn_prefill_workspace_bytes(const q35_gdn_dims *d, int T);
+int gqa_decode_check_args(const q35_gqa_dims *dims, int64_t max_len, const float *q_gate, const float *k_new,
+                          const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
+                          const float *sin, const float *k_cache, const float *v_cache, const int32_t *lens,
+                          const float *out);
 int q8_gemv_launch(int in_dim, int out_dim, const float *x, const uint32_t *w, const float *scales, float *y,
                    int mode, cudaStream_t st);
 int q8_gemv_fused_launch(int in_dim, int n_seg, const q35_q8_segment *segs, const float *x, const float *residual,
@@ -60,6 +64,15 @@ int g_sm_major[64] = {0};
 }  // namespace
 
 void set_error(const std::string &msg) { g_last_error = msg; }
+
+namespace {
+std::atomic<int> g_fault_site{kFaultNone};
+}  // namespace
+
+bool take_fault(int site) {
+  int s = site;
+  return site != kFaultNone && g_fault_site.compare_exchange_strong(s, kFaultNone);
+}
 
 bool pdl_enabled() {
   static const bool on = [] {
@@ -152,6 +165,26 @@ using namespace q35;
 #define Q35_PTR16(p) \
   Q35_REQUIRE((p) != nullptr && aligned16(p), Q35_ERR_INVALID_ARG, #p " must be a non-NULL 16-byte aligned pointer")
 
+// Every check q35_gqa_decode makes before it touches the device (shapes,
+// max_len against the capacity, pointer alignment, the device itself), so a
+// caller can validate a call before queueing anything on its stream.
+int q35::gqa_decode_check_args(const q35_gqa_dims *dims, int64_t max_len, const float *q_gate, const float *k_new,
+                          const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
+                          const float *sin, const float *k_cache, const float *v_cache, const int32_t *lens,
+                          const float *out) {
+  if (int rc = check_gqa_dims(dims)) return rc;
+  Q35_REQUIRE(max_len > 0, Q35_ERR_INVALID_ARG, "gqa_decode: max_len must be > 0");
+  Q35_REQUIRE(max_len <= dims->capacity, Q35_ERR_CAPACITY, "gqa_decode: max_len exceeds the cache capacity");
+  if (dims->batch == 0) return Q35_OK;
+  Q35_PTR16(q_gate); Q35_PTR16(k_new); Q35_PTR16(v_new); Q35_PTR16(qn_w); Q35_PTR16(kn_w);
+  if (dims->rotary_dim > 0) {
+    Q35_PTR(cos);
+    Q35_PTR(sin);
+  }
+  Q35_PTR16(k_cache); Q35_PTR16(v_cache); Q35_PTR(lens); Q35_PTR(out);
+  return require_sm100();
+}
+
 extern "C" {
 
 const char *q35_last_error(void) { return g_last_error.c_str(); }
@@ -160,6 +193,13 @@ const char *q35_version(void) { return "q35attn 0.1.0 (sm_100a)"; }
 
 uint64_t q35_launch_count(int32_t reset) {
   return reset ? g_launches.exchange(0) : g_launches.load();
+}
+
+int q35_test_arm_wait_fault(int32_t site) {
+  Q35_REQUIRE(site == kFaultNone || site == kFaultPrefillState || site == kFaultGqaDecode, Q35_ERR_INVALID_ARG,
+              "test_arm_wait_fault: unknown site");
+  g_fault_site.store(site);
+  return Q35_OK;
 }
 
 int q35_gdn_decode(const q35_gdn_dims *dims, const float *mixed_qkv, const float *z, const float *beta,
@@ -349,17 +389,10 @@ int q35_gqa_decode(const q35_gqa_dims *dims, int64_t max_len, const float *q_gat
                    const float *v_new, const float *qn_w, const float *kn_w, const float *cos, const float *sin,
                    float *k_cache, float *v_cache, int32_t *lens, float *out, void *workspace,
                    size_t workspace_bytes, void *stream) {
-  if (int rc = check_gqa_dims(dims)) return rc;
-  Q35_REQUIRE(max_len > 0, Q35_ERR_INVALID_ARG, "gqa_decode: max_len must be > 0");
-  Q35_REQUIRE(max_len <= dims->capacity, Q35_ERR_CAPACITY, "gqa_decode: max_len exceeds the cache capacity");
+  if (int rc = gqa_decode_check_args(dims, max_len, q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache,
+                                     lens, out))
+    return rc;
   if (dims->batch == 0) return Q35_OK;
-  Q35_PTR16(q_gate); Q35_PTR16(k_new); Q35_PTR16(v_new); Q35_PTR16(qn_w); Q35_PTR16(kn_w);
-  if (dims->rotary_dim > 0) {
-    Q35_PTR(cos);
-    Q35_PTR(sin);
-  }
-  Q35_PTR16(k_cache); Q35_PTR16(v_cache); Q35_PTR(lens); Q35_PTR(out);
-  if (int rc = require_sm100()) return rc;
   return gqa_decode_launch(dims, max_len, q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, lens, out,
                            workspace, workspace_bytes, static_cast<cudaStream_t>(stream), nullptr);
 }

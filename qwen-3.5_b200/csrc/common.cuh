@@ -125,16 +125,27 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 // Bounded wait on an mbarrier phase.  Returns false (and leaves the phase
-// incomplete) after kWaitLimitNs or kSpinLimit polls, whichever comes first.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// incomplete) after limit_ns or kSpinLimit polls, whichever comes first.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
   return false;
 }
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  return mbar_wait_ns(bar, parity, kWaitLimitNs);
+}
+
+// Test hook (q35_test_arm_wait_fault): the next launch of the armed site
+// withholds one asynchronous copy and waits with this short limit, so that a
+// bounded wait runs out and the error path is exercised without a fault.
+constexpr uint64_t kFaultWaitLimitNs = 2000000ull;  // 2 ms
+enum FaultSite : int { kFaultNone = 0, kFaultPrefillState = 1, kFaultGqaDecode = 2 };
+// Returns the armed site once (and disarms it) when it equals `site`.
+bool take_fault(int site);
 
 // Bulk (non-tensor) TMA copy global -> shared, completing `bytes` of
 // transaction count on `bar`.  src/dst 16-byte aligned, bytes % 16 == 0.

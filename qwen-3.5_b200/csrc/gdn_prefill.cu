@@ -56,9 +56,15 @@ static_assert((kOffSc * 4) % 16 == 0 && (kOffVt * 4) % 16 == 0 && (kRec * 4) % 1
 struct PrefillParams {
   const float *x, *z, *beta, *g, *conv_w, *norm_w;
   float *conv_state, *rec_state, *out, *ws;
+  uint32_t *status;   // word 0 of the workspace: Q35_STATUS_* bits
+  uint64_t wait_ns;   // limit of every bounded wait
   int B, T, NC, Hk, Hv, rf, C, has_prev, has_init;
+  int fault;          // test hook: the state pass withholds chunk 1's W copy
   float eps;
 };
+
+// Bytes in front of the per-(head, chunk) records: the status word.
+constexpr size_t kWsHeader = 256;
 
 // ---------------------------------------------------------------------------
 // Kernel 1 on the 5th-generation tensor cores.  The four intra-chunk
@@ -269,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
 
   if (tid == 0) rec[kOffDec] = expf(sm.gam[kC - 1]);
 
-  const bool g12_ok = mbar_wait(&sm.bar1, 0);
+  const bool g12_ok = mbar_wait_ns(&sm.bar1, 0, p.wait_ns);
   umma::fence_after_sync();
 
   // (4) epilogue of G12: TMEM lane = row of [k k^T ; q k^T]; the four warps
@@ -297,7 +303,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
         kL[blk_off(i, j, kC)] = j <= i ? v[jj] * expf(gi - sm.gam[j]) : 0.0f;
       }
     }
-    if (!g12_ok && tid == 0) rec[kOffDec] = __int_as_float(0x7fc00000);  // poisons state and outputs
+    if (!g12_ok && tid == 0) {
+      rec[kOffDec] = __int_as_float(0x7fc00000);  // poisons state and outputs
+      atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
+    }
   }
   // q' = q e^gamma (:303-307) in place, then q' (as two blocked [64 x 64]
   // slabs: each 8-row group of the [64 x 128] tile is two 2 KB halves) and
@@ -459,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
     }
     umma::commit(&sm.bar2);
   }
-  const bool g2_ok = mbar_wait(&sm.bar2, 0);
+  const bool g2_ok = mbar_wait_ns(&sm.bar2, 0, p.wait_ns);
   umma::fence_after_sync();
 
   // (8) epilogue: TMEM lane = d.  U[i][d] from U^T (warps with (w / 4) % 2 = 0),
@@ -483,7 +492,16 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_chunk_kernel(const Pr
         for (int e = 0; e < 16; ++e) Wk[(d >> 6) * (kC * 64) + blk_off(16 * cb + e, d & 63, 64)] = v[e];
       }
     }
-    if (!g2_ok && tid == 0) rec[kOffDec] = __int_as_float(0x7fc00000);
+    if (!g2_ok && tid == 0) {
+      rec[kOffDec] = __int_as_float(0x7fc00000);
+      atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
+    }
+  }
+  // Neither MMA group may still be writing TMEM when it is freed: after a
+  // wait that gave up, warp 0 waits (bounded) once more for both commits.
+  if (warp == 0 && !(g12_ok && g2_ok)) {
+    (void)mbar_wait_ns(&sm.bar1, 0, p.wait_ns);
+    (void)mbar_wait_ns(&sm.bar2, 0, p.wait_ns);
   }
   umma::fence_before_sync();
   __syncthreads();
@@ -612,9 +630,12 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tb = sm.tbase;
-  // A wait that gives up (ok = false) stops this thread waiting; the final
-  // state is then poisoned.
+  // A wait that gives up (ok = false) stops this thread waiting and writing
+  // operands (its loop still runs, so every named barrier is met); the
+  // issuer stops issuing and drains what it started; the final state is then
+  // poisoned and the status word flagged.
   bool ok = true;
+  const uint64_t wns = p.wait_ns;
 
   if (warp < 4) {
     // ---- state rows (k = tid); warps 0-1 are also the v' rows (t = tid)
@@ -653,14 +674,14 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
         decn = __ldcg(rec + kRec + kOffDec);
       }
       {  // v' = U - W S_c  (:315-324); TMEM lane = row of [W_hi; W_lo]
-        if (ok && !mbar_wait(&sm.m1, c & 1)) ok = false;
+        if (ok && !mbar_wait_ns(&sm.m1, c & 1, wns)) ok = false;
         __syncwarp();
         umma::fence_after_sync();
         float d[16], e[16];
         umma::ld_32x32b_x16(tb + lane_base, d);
         umma::ld_32x32b_x16(tb + lane_base + 16, e);
         umma::wait_ld();
-        if (!vrow) {  // W_lo rows: W_lo S_hi + W_lo S_lo of token tid - 64
+        if (!vrow && ok) {  // W_lo rows: W_lo S_hi + W_lo S_lo of token tid - 64
           float4 *x = reinterpret_cast<float4 *>(&sm.X[tid - kC][0]);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -668,7 +689,7 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
                                d[4 * q + 3] + e[4 * q + 3]);
         }
         named_bar_sync(kBarRows, kStateRowThreads);
-        if (vrow) {
+        if (vrow && ok) {
           const float4 *x = reinterpret_cast<const float4 *>(&sm.X[tid][0]);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -685,7 +706,7 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
         }
       }
       // S <- S e^(gamma_last) + k'^T v'  (:342-350)
-      if (ok && !mbar_wait(&sm.m2, c & 1)) ok = false;
+      if (ok && !mbar_wait_ns(&sm.m2, c & 1, wns)) ok = false;
       __syncwarp();
       umma::fence_after_sync();
       float d[16], e[16], f[16];
@@ -695,7 +716,7 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
       umma::wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) S[j] = S[j] * dec + ((d[j] + e[j]) + f[j]);
-      if (c + 1 < NC) {
+      if (c + 1 < NC && ok) {
         store_operand_row(sm.Sb[k >> 6][0], sm.Sb[k >> 6][1], k & 63, S, lane);
         fence_proxy_async_smem();
         umma::fence_before_sync();
@@ -717,6 +738,13 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
       bulk_g2s(sm.Wb[c & 1] + 2 * kC * 64, src + kC * 64, kSlabBytes, &sm.wfull[c & 1], pol);
     };
     constexpr uint32_t kPrefetch = (kOffKp + kD * kC - kOffU) * sizeof(float);  // U, W, k'^T
+    // Chunks [0, w_issued) have had their W copy issued, [0, w_seen) have
+    // been observed complete; m1_last / m2_last are the last chunks whose MMA
+    // groups were committed.  After a wait that gave up, nothing new is
+    // issued and every started copy and MMA is waited for (bounded) before
+    // the CTA frees its TMEM and shared memory.
+    int w_issued = 1, w_seen = 0, m1_last = -1, m2_last = -1;
+    const bool withhold = p.fault != 0;  // test hook: chunk 1's W copy is never issued
     load_w(0);
     if (NC > 1) prefetch_l2_bulk(rec0 + kRec + kOffU, kPrefetch);
     const uint32_t idw = umma::idesc_tf32(128, 2 * kCS, 0, 0), idn = umma::idesc_tf32(128, kCS, 0, 0);
@@ -725,8 +753,12 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
       const int buf = c & 1;
       float *rec = rec0 + (size_t)c * kRec;
       // S_c is in Sb, and MMA2 of chunk c-1 is complete: W buffer buf ^ 1 is free
-      if (ok && !mbar_wait(&sm.sready, c & 1)) ok = false;
-      if (c + 1 < NC && ok) load_w(c + 1);
+      if (ok && !mbar_wait_ns(&sm.sready, c & 1, wns)) ok = false;
+      if (!ok) break;
+      if (c + 1 < NC && !(withhold && c + 1 == 1)) {
+        load_w(c + 1);
+        w_issued = c + 2;
+      }
       if (c + 2 < NC) {
         prefetch_l2_bulk(rec + 2 * kRec + kOffU, kPrefetch);
         prefetch_l2_bulk(rec + 2 * kRec + kOffDec, 64 * sizeof(float));
@@ -734,8 +766,10 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
       bulk_s2g(rec + kOffSc + 16 * 64 * s, sm.Sb[0][0], 16 * 64 * sizeof(float));
       bulk_s2g(rec + kOffSc + kD * 64 + 16 * 64 * s, sm.Sb[1][0], 16 * 64 * sizeof(float));
       bulk_commit();
-      if (ok && !mbar_wait(&sm.wfull[buf], (c >> 1) & 1)) ok = false;
-      if (ok && !mbar_wait(&sm.wlo, c & 1)) ok = false;
+      if (ok && !mbar_wait_ns(&sm.wfull[buf], (c >> 1) & 1, wns)) ok = false;
+      if (ok) w_seen = c + 1;
+      if (ok && !mbar_wait_ns(&sm.wlo, c & 1, wns)) ok = false;
+      if (!ok) break;
       bulk_wait_read<1>();  // the v'^T store of chunk c-1 has read Vb
       umma::fence_after_sync();
       // Descriptors advance by adding the byte offset / 16 to the start
@@ -749,8 +783,10 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
         umma::mma_tf32(tb, dW + ao, dSb + bo, idw, ks > 0 ? 1u : 0u);
       }
       umma::commit(&sm.m1);
-      if (ok && !mbar_wait(&sm.kready, c & 1)) ok = false;
-      if (ok && !mbar_wait(&sm.vready, c & 1)) ok = false;
+      m1_last = c;
+      if (ok && !mbar_wait_ns(&sm.kready, c & 1, wns)) ok = false;
+      if (ok && !mbar_wait_ns(&sm.vready, c & 1, wns)) ok = false;
+      if (!ok) break;
       bulk_wait_read<0>();  // the S_c^T stores have read Sb before S_{c+1} replaces it
       umma::fence_after_sync();
       const uint64_t dVb = umma::smem_desc(sm.Vb[0], 128, sbo);  // [hi; lo] rows
@@ -761,9 +797,13 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
         mma_tf32_tmem_a(tb + kColD2 + 32, tb + kColKl + 8 * ks, dVb + o, idn, ks > 0 ? 1u : 0u);
       }
       umma::commit(&sm.m2);
+      m2_last = c;
       bulk_s2g(rec + kOffVt + 16 * kC * s, sm.Vb[0], 16 * kC * sizeof(float));
       bulk_commit();
     }
+    for (int j = w_seen; j < w_issued; ++j) (void)mbar_wait_ns(&sm.wfull[j & 1], (j >> 1) & 1, wns);
+    if (m1_last >= 0) (void)mbar_wait_ns(&sm.m1, m1_last & 1, wns);
+    if (m2_last >= 0) (void)mbar_wait_ns(&sm.m2, m2_last & 1, wns);
     bulk_wait<0>();  // every published tile is complete before the CTA retires
   } else if (warp >= 5 && warp < kStateKWarp0) {
     // ---- tf32 lo half of each W buffer, once MMA1 of the previous chunk is
@@ -771,10 +811,10 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
     const int t = tid - 5 * 32;
     for (int c = 0; c < NC; ++c) {
       const int buf = c & 1;
-      if (ok && !mbar_wait(&sm.wfull[buf], (c >> 1) & 1)) ok = false;
-      if (c > 0 && ok && !mbar_wait(&sm.m1, (c - 1) & 1)) ok = false;
+      if (ok && !mbar_wait_ns(&sm.wfull[buf], (c >> 1) & 1, wns)) ok = false;
+      if (c > 0 && ok && !mbar_wait_ns(&sm.m1, (c - 1) & 1, wns)) ok = false;
       float4 *w4 = reinterpret_cast<float4 *>(sm.Wb[buf]);
-      for (int e = t; e < 2 * kC * 64 / 4; e += kStateLoThreads) {
+      for (int e = t; ok && e < 2 * kC * 64 / 4; e += kStateLoThreads) {
         const int i = (e >> 10) * (2 * kC * 64 / 4) + (e & 1023);  // float4 of k slab e / 1024
         const float4 v = w4[i];
         w4[i + kC * 64 / 4] =
@@ -797,11 +837,12 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
         const float4 v = __ldcg(src + ((k >> 3) * 16 + m) * 8 + (k & 7));
         row[4 * m] = v.x; row[4 * m + 1] = v.y; row[4 * m + 2] = v.z; row[4 * m + 3] = v.w;
       }
-      if (c > 0 && ok && !mbar_wait(&sm.m2, (c - 1) & 1)) ok = false;  // MMA2 of chunk c-1 has read k'^T
-      __syncwarp();
+      if (c > 0 && ok && !mbar_wait_ns(&sm.m2, (c - 1) & 1, wns)) ok = false;  // MMA2 of chunk c-1 has read k'^T
+      // tcgen05.st is warp-collective: the whole warp stores or none of it
+      const bool wok = __all_sync(0xffffffffu, ok);
       umma::fence_after_sync();
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 4 && wok; ++j) {
         float hi[16], lo[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -840,7 +881,10 @@ __global__ void __launch_bounds__(kStateThreads, 1) gdn_prefill_state_kernel(con
 
   umma::fence_before_sync();
   const int failed = __syncthreads_or(ok ? 0 : 1);
-  if (failed && tid == 0) Sg[col0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison the state
+  if (failed && tid == 0) {  // a bounded wait gave up: poison the state, flag the status word
+    Sg[col0] = __int_as_float(0x7fc00000);
+    atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
+  }
   if (warp == 4) umma::tmem_dealloc(tb, kTmemCols);
 }
 
@@ -910,10 +954,16 @@ __global__ void __launch_bounds__(kOutThreads, 2) gdn_prefill_output_kernel(cons
 #pragma unroll
   for (int j = 0; j < 32; ++j) zv[j] = j < nt ? __ldg(zb + (size_t)j * rs) : 0.0f;
 
+  // Thread 0 issues the copies and MMAs: stages [0, l_issued) have been
+  // requested, [0, l_seen) seen complete, m_last is the last committed MMA
+  // group.  After a wait that gave up it issues nothing more and, before
+  // TMEM is freed, waits (bounded) for what it started.
+  int l_issued = 1, l_seen = 0, m_last = -1;
 #pragma unroll 1
   for (int st = 0; st < 3; ++st) {
-    if (ok && !mbar_wait(&sm.barL, st & 1)) ok = false;
-    {  // lo terms
+    if (ok && !mbar_wait_ns(&sm.barL, st & 1, p.wait_ns)) ok = false;
+    if (ok) l_seen = st + 1;
+    if (ok) {  // lo terms
       const float4 *ah = reinterpret_cast<const float4 *>(sm.A[0]);
       float4 *al = reinterpret_cast<float4 *>(sm.A[1]);
       for (int e = tid; e < kD * 64 / 4; e += kOutThreads) {
@@ -929,9 +979,11 @@ __global__ void __launch_bounds__(kOutThreads, 2) gdn_prefill_output_kernel(cons
     }
     fence_proxy_async_smem();
     umma::fence_before_sync();
-    __syncthreads();
+    // every thread's lo terms are written; a thread whose wait gave up votes the
+    // stage's MMAs off
+    const int all_ok = __syncthreads_and(ok ? 1 : 0);
     umma::fence_after_sync();
-    if (tid == 0) {
+    if (tid == 0 && all_ok) {
       constexpr uint32_t sbo = (64 / 4) * 128;
 #pragma unroll 1
       for (int ks = 0; ks < 8; ++ks) {
@@ -944,16 +996,25 @@ __global__ void __launch_bounds__(kOutThreads, 2) gdn_prefill_output_kernel(cons
         umma::mma_tf32(tb, al, bh, id, 1);
       }
       umma::commit(&sm.barM);
+      m_last = st;
       // the buffers take the next stage once this stage's MMAs have read them
       if (st < 2) {
-        if (ok && !mbar_wait(&sm.barM, st & 1)) ok = false;
-        if (ok) load_stage(st + 1, l2_policy_evict_first());
+        if (ok && !mbar_wait_ns(&sm.barM, st & 1, p.wait_ns)) ok = false;
+        if (ok) {
+          load_stage(st + 1, l2_policy_evict_first());
+          l_issued = st + 2;
+        }
       }
     }
+    if (!all_ok) ok = false;
   }
   // stage 2 (and so every MMA) complete: the barrier's third phase (parity 0);
   // every thread has passed stage 2's barrier, so phases 0 and 1 are done
-  if (ok && !mbar_wait(&sm.barM, 0)) ok = false;
+  if (ok && !mbar_wait_ns(&sm.barM, 0, p.wait_ns)) ok = false;
+  if (tid == 0) {
+    for (int j = l_seen; j < l_issued; ++j) (void)mbar_wait_ns(&sm.barL, j & 1, p.wait_ns);
+    if (m_last >= 0) (void)mbar_wait_ns(&sm.barM, m_last & 1, p.wait_ns);
+  }
   umma::fence_after_sync();
 
   // epilogue
@@ -988,9 +1049,12 @@ __global__ void __launch_bounds__(kOutThreads, 2) gdn_prefill_output_kernel(cons
 #pragma unroll
   for (int j = 0; j < 32; ++j)
     if (j < nt) ob[(size_t)j * rs] = (wv * (o[j] * sm.inv[32 * half + j])) * siluf_dev(zv[j]);
-  if (!ok && tid == 0 && nt > 0) ob[0] = __int_as_float(0x7fc00000);  // a bounded wait gave up: poison
   umma::fence_before_sync();
-  __syncthreads();
+  const int failed = __syncthreads_or(ok ? 0 : 1);
+  if (failed && nt > 0 && (tid & 127) == 0) {  // a bounded wait gave up: poison, flag the status word
+    ob[0] = __int_as_float(0x7fc00000);
+    atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
+  }
   if (warp == 0) umma::tmem_dealloc(tb, 64);
 }
 
@@ -1019,7 +1083,7 @@ int launch_kc(const PrefillParams &p, cudaStream_t st) {
 
 size_t gdn_prefill_workspace_bytes(const q35_gdn_dims *d, int T) {
   const size_t NC = (size_t)(T + kC - 1) / kC;
-  return (size_t)d->batch * d->num_v_heads * NC * kRec * sizeof(float);
+  return kWsHeader + (size_t)d->batch * d->num_v_heads * NC * kRec * sizeof(float);
 }
 
 int gdn_prefill_launch(const q35_gdn_dims *d, int T, const float *mixed_qkv, const float *z, const float *beta,
@@ -1030,7 +1094,11 @@ int gdn_prefill_launch(const q35_gdn_dims *d, int T, const float *mixed_qkv, con
               "gdn_prefill: workspace missing, unaligned or too small (need " + std::to_string(need) + " bytes)");
   PrefillParams p;
   p.x = mixed_qkv; p.z = z; p.beta = beta; p.g = g; p.conv_w = conv_w; p.norm_w = norm_w;
-  p.conv_state = conv_state; p.rec_state = rec_state; p.out = out; p.ws = static_cast<float *>(ws);
+  p.conv_state = conv_state; p.rec_state = rec_state; p.out = out;
+  p.status = static_cast<uint32_t *>(ws);
+  p.ws = reinterpret_cast<float *>(static_cast<unsigned char *>(ws) + kWsHeader);
+  p.fault = take_fault(kFaultPrefillState) ? 1 : 0;
+  p.wait_ns = p.fault ? kFaultWaitLimitNs : kWaitLimitNs;
   p.B = d->batch; p.T = T; p.NC = (T + kC - 1) / kC; p.Hk = d->num_k_heads; p.Hv = d->num_v_heads;
   p.rf = p.Hv / p.Hk; p.C = 2 * p.Hk * kD + p.Hv * kD; p.has_prev = has_prev; p.has_init = has_init;
   p.eps = d->eps;

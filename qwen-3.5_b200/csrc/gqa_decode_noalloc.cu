@@ -22,7 +22,13 @@
 //    before any stream capture;
 //  * the counters and status word must start at zero, so each call clears
 //    them with an asynchronous memset on `stream` before the launch (the array
-//    otherwise keeps the previous call's contents).
+//    otherwise keeps the previous call's contents);
+//  * the device-side status word (Q35_STATUS_* bits: a full cache, a length
+//    hint exceeded, a bounded wait that gave up) lives in the private array
+//    and is cleared by the next call, so it cannot be read by the caller.  A
+//    skipped sequence shows only as lens[b] left unchanged.  Callers that need
+//    the status bits use q35_gqa_decode with a workspace and
+//    q35_workspace_status.
 #include <mutex>
 
 #include "common.cuh"
@@ -30,6 +36,14 @@
 namespace q35 {
 
 size_t gqa_workspace_counter_bytes(int B, int Hq, int Hkv, long long max_len, int sms);
+int gqa_decode_check_args(const q35_gqa_dims *dims, int64_t max_len, const float *q_gate, const float *k_new,
+                          const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
+                          const float *sin, const float *k_cache, const float *v_cache, const int32_t *lens,
+                          const float *out);
+int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_gate, const float *k_new,
+                      const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
+                      const float *sin, float *k_cache, float *v_cache, int32_t *lens, float *out,
+                      void *ws, size_t ws_bytes, cudaStream_t st, float *part_out);
 
 namespace {
 
@@ -66,12 +80,15 @@ extern "C" int q35_gqa_decode_noalloc(const q35_gqa_dims *dims, int64_t max_len,
                                       const float *k_new, const float *v_new, const float *qn_w, const float *kn_w,
                                       const float *cos, const float *sin, float *k_cache, float *v_cache,
                                       int32_t *lens, float *out, void *stream) {
-  Q35_REQUIRE(dims != nullptr, Q35_ERR_INVALID_ARG, "dims is NULL");
-  Q35_REQUIRE(max_len > 0, Q35_ERR_INVALID_ARG, "gqa_decode_noalloc: max_len must be > 0");
+  // Every argument check runs before anything is queued on `stream`, so a
+  // rejected call leaves the stream (or a graph being captured) untouched and
+  // does not clear the counters of a call still running elsewhere.
+  if (int rc = gqa_decode_check_args(dims, max_len, q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache,
+                                     lens, out))
+    return rc;
   if (dims->batch == 0) return Q35_OK;
-  const size_t need = q35_gqa_decode_workspace_size(dims, max_len);  // 0 when dims are invalid
-  Q35_REQUIRE(need > 0, Q35_ERR_INVALID_ARG, "gqa_decode_noalloc: invalid dims");
-  if (int rc = require_sm100()) return rc;
+  const int sms = device_sm_count();
+  const size_t need = q35_gqa_decode_workspace_size(dims, max_len);
   Q35_REQUIRE(need <= kNoAllocScratchBytes, Q35_ERR_WORKSPACE,
               "gqa_decode_noalloc: this call needs " + std::to_string(need) +
                   " bytes of scratch, above the fixed " + std::to_string(kNoAllocScratchBytes) +
@@ -81,10 +98,9 @@ extern "C" int q35_gqa_decode_noalloc(const q35_gqa_dims *dims, int64_t max_len,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // status word + split / group / pair / sequence counters must start at zero
   const size_t counters = gqa_workspace_counter_bytes(dims->batch, dims->num_q_heads, dims->num_kv_heads, max_len,
-                                                      device_sm_count());
+                                                      sms);
   if (int rc = check_cuda(cudaMemsetAsync(scratch, 0, counters, st), "gqa_decode_noalloc: clear counters"))
     return rc;
-  // q35_gqa_decode's own argument checks and launch, on the fixed scratch
-  return q35_gqa_decode(dims, max_len, q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, lens, out,
-                        scratch, kNoAllocScratchBytes, stream);
+  return gqa_decode_launch(dims, max_len, q_gate, k_new, v_new, qn_w, kn_w, cos, sin, k_cache, v_cache, lens, out,
+                           scratch, kNoAllocScratchBytes, st, nullptr);
 }

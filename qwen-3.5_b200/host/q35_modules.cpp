@@ -154,7 +154,9 @@ void GatedDeltaNetCore::forward(const float *mixed_qkv, const float *z, const fl
     const int has_init = precomputed && cache->has_recurrent_state(layer_);
     const size_t need = q35_gdn_prefill_workspace_size(&d, seq_len);
     require(need > 0, Q35_ERR_INVALID_ARG, "GatedDeltaNet: invalid shape for the chunked path");
+    const size_t had = ws_.bytes();
     ws_.reserve(need);
+    if (ws_.bytes() != had) check(q35_workspace_init(ws_.data(), 256, stream));  // a fresh status word
     check(q35_gdn_prefill(&d, seq_len, mixed_qkv, z, beta, g, conv_w_, norm_w_, conv, precomputed ? 1 : 0, rec,
                           has_init, out, ws_.data(), ws_.bytes(), stream));
   }

@@ -78,6 +78,7 @@ SIGNATURES = {
     "q35_last_error": (C.c_char_p, []),
     "q35_version": (C.c_char_p, []),
     "q35_launch_count": (C.c_uint64, [_I32]),
+    "q35_test_arm_wait_fault": (C.c_int, [_I32]),
 }
 
 _lib = None

@@ -61,10 +61,20 @@ def gdn_decode(mixed_qkv, z, beta, g, conv_w, norm_w, conv_state, rec_state, out
     return out
 
 
-def gdn_prefill_workspace(B, T, num_k_heads, num_v_heads, conv_kernel=4, device="cuda"):
+def gdn_prefill_workspace(B, T, num_k_heads, num_v_heads, conv_kernel=4, device="cuda", stream=None):
+    """Workspace of q35_gdn_prefill; its leading status word is zeroed."""
     d = gdn_dims(B, num_k_heads, num_v_heads, conv_kernel)
     n = int(load().q35_gdn_prefill_workspace_size(C.byref(d), int(T)))
-    return torch.empty(max(n, 16), dtype=torch.uint8, device=device)
+    buf = torch.empty(max(n, 256), dtype=torch.uint8, device=device)
+    check(load().q35_workspace_init(buf.data_ptr(), 256, _stream(stream)))
+    return buf
+
+
+def workspace_status(workspace: torch.Tensor, clear=False, stream=None) -> int:
+    """Q35_STATUS_* bits of a workspace's leading status word (synchronizes)."""
+    v = C.c_uint32(0)
+    check(load().q35_workspace_status(workspace.data_ptr(), C.byref(v), int(clear), _stream(stream)))
+    return int(v.value)
 
 
 def gdn_prefill(mixed_qkv, z, beta, g, conv_w, norm_w, conv_state, rec_state, out=None, *, num_k_heads,

@@ -85,7 +85,7 @@ def test_workspace_sizes_are_positive_and_monotone():
     d = _lib.GdnDims(1, 16, 16, 128, 128, 4, 1e-6)
     # per (head, chunk): U, W^T, k', q' [64x128] + Aqk [64x64] + decay slot (64) + S_c^T [128x128] + v'^T [128x64]
     rec = 4 * 64 * 128 + 64 * 64 + 64 + 128 * 128 + 128 * 64
-    assert lib.q35_gdn_prefill_workspace_size(C.byref(d), 8192) == 16 * 128 * rec * 4
+    assert lib.q35_gdn_prefill_workspace_size(C.byref(d), 8192) == 256 + 16 * 128 * rec * 4  # status header
     assert lib.q35_gdn_prefill_workspace_size(C.byref(d), 0) == 0
 
 

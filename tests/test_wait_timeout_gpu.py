@@ -1,0 +1,66 @@
+"""Bounded in-kernel waits that run out.
+
+Every wait of the library's kernels on an mbarrier gives up after a time
+limit, sets Q35_STATUS_WAIT_TIMEOUT in a status word the caller can read, and
+the kernel returns with every copy and tensor-core operation it started
+waited for.  The test hook q35_test_arm_wait_fault makes the next call
+withhold one of its copies and wait only 2 ms, so the give-up path runs
+without faulting or hanging the GPU; afterwards the context is still usable
+and a normal call matches the oracle again.  (The reference panics on such
+errors instead, kernels.rs:442,472.)"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import q35attn
+from q35attn import _lib
+from conftest import max_rel_err
+from gdn_data import gdn_inputs
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+SITE_PREFILL_STATE, SITE_GQA_DECODE = 1, 2
+WAIT_TIMEOUT = 0x4
+
+
+def _arm(site):
+    _lib.check(q35attn.load().q35_test_arm_wait_fault(site))
+
+
+def _prefill_inputs(T, B=1, H=16, seed=5):
+    d = gdn_inputs(seed, B, H, H, T)
+    tr = lambda a: np.ascontiguousarray(a.transpose(1, 0, 2))
+    return d, tr(d["x"]), tr(d["z"]), tr(d["beta"]), tr(d["g"])
+
+
+def test_prefill_state_pass_wait_runs_out():
+    T, H = 200, 16  # 4 chunks: chunk 1's W copy is withheld
+    d, x, z, beta, g = _prefill_inputs(T)
+    Tt = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    ws = q35attn.gdn_prefill_workspace(1, T, H, H)
+    assert q35attn.ops.workspace_status(ws) == 0
+    S = Tt(d["S0"])
+    cst = Tt(d["conv0"])
+    _arm(SITE_PREFILL_STATE)
+    q35attn.gdn_prefill(Tt(x), Tt(z), Tt(beta), Tt(g), Tt(d["conv_w"]), Tt(d["norm_w"]), cst, S, num_k_heads=H,
+                        num_v_heads=H, has_prev_conv=True, has_init_state=True, workspace=ws)
+    torch.cuda.synchronize()  # the call returned: nothing is left waiting
+    assert q35attn.ops.workspace_status(ws, clear=True) & WAIT_TIMEOUT
+    assert torch.isnan(S).any(), "the final state of a failed pass is poisoned"
+    assert q35attn.ops.workspace_status(ws) == 0  # cleared
+
+    # the hook is consumed; the same call now runs normally and matches the oracle
+    S, cst = Tt(d["S0"]), Tt(d["conv0"])
+    out = q35attn.gdn_prefill(Tt(x), Tt(z), Tt(beta), Tt(g), Tt(d["conv_w"]), Tt(d["norm_w"]), cst, S,
+                              num_k_heads=H, num_v_heads=H, has_prev_conv=True, has_init_state=True, workspace=ws)
+    ref, _, rS = oracle.gdn_prefill(x, z, beta, g, d["conv_w"], d["norm_w"], d["conv0"], 1, d["S0"], 1, H, H)
+    torch.cuda.synchronize()
+    assert q35attn.ops.workspace_status(ws) == 0
+    assert max_rel_err(out.cpu().numpy(), ref) <= TOL
+    assert max_rel_err(S.cpu().numpy(), rS) <= TOL
+
+
+def test_arm_rejects_unknown_site():
+    assert q35attn.load().q35_test_arm_wait_fault(7) == _lib.ERR_INVALID_ARG
+    _arm(0)
