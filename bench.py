@@ -711,6 +711,25 @@ def run_extras(dev, reps=3):
         del ws_, ss_
     res["q8_gemv"] = gemv
 
+    # Q8F prefill GEMM (Linear::forward at seq_len > 1) at the config-3 prompt
+    # shapes, on the tensor cores; three bf16 products per output (hi/lo splits)
+    gemm = {}
+    for name, ind, outd in (("in_proj_qkv", 2048, 6144), ("o_proj", 2048, 2048), ("down_proj", 6144, 2048),
+                            ("up_proj", 2048, 6144)):
+        wq = torch.randint(-2**31, 2**31 - 1, (ind, outd // 4), dtype=torch.int32, device=dev)
+        sq = torch.rand(ind, outd // 64, device=dev) * 0.01
+        xq, yq = randn(1024, ind), torch.empty(1024, outd, device=dev)
+
+        def qcall():
+            for _ in range(8):
+                q35attn.q8_gemm(xq, wq, sq, yq)
+        tq = timed_graph(qcall, reps) / 8
+        fl = 2.0 * 1024 * ind * outd
+        gemm[name] = {"T": 1024, "in": ind, "out": outd, "us": tq * 1e6, "tflops": fl / tq / 1e12,
+                      "tensor_tflops_3_products": 3 * fl / tq / 1e12}
+        del wq, sq, xq, yq
+    res["q8_gemm_prefill"] = gemm
+
     # config 3: the 2B hybrid stack (24 layers, random Q8F weights), a
     # 1024-token random prompt, then 512 greedy decode steps (CUDA graph)
     import q35attn.stack as qs

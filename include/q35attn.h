@@ -152,6 +152,19 @@ int q35_q8_gemv(int32_t in_dim, int32_t out_dim, const float *x,
                 const uint32_t *w, const float *scales, float *y,
                 int32_t mode, void *stream);
 
+/* Q8F projection of a prompt: y[n_rows, out_dim] = x[n_rows, in_dim] W with
+ * W[k][n] = q[k][n] * scales[k][n/64] rounded to f32, the dense weight that
+ * Linear::forward multiplies with at seq_len > 1 (text_modules.rs:499-506,
+ * 663, 858-888, 941, 1007-1009).  Same weight layout as q35_q8_gemv; the
+ * int8 tiles are dequantised in shared memory (no dense copy of W), and the
+ * products run on the tensor cores as bf16 hi/lo splits with f32
+ * accumulation (relative error near 2^-16 per product).
+ * in_dim % 32 == 0, out_dim % 256 == 0, all pointers 16-byte aligned.  A
+ * bounded wait that gives up sets Q35_STATUS_WAIT_TIMEOUT in the device
+ * status word (q35_device_status). */
+int q35_q8_gemm(int32_t n_rows, int32_t in_dim, int32_t out_dim, const float *x,
+                const uint32_t *w, const float *scales, float *y, void *stream);
+
 /* One Q8F projection of a fused GEMV launch (layout as for q35_q8_gemv). */
 typedef struct {
   const uint32_t *w;     /* [in_dim, out_dim/4] u32, 16-byte aligned */
@@ -343,6 +356,11 @@ int q35_gdn_decode_split(const q35_gdn_dims *dims, int32_t split,
                          const float *conv_w, const float *norm_w,
                          float *conv_state, float *rec_state, float *out,
                          void *stream);
+
+/* Reads (and with clear != 0 resets) this device's status word, the
+ * Q35_STATUS_* bits of the kernels that take no workspace (q35_q8_gemm).
+ * Synchronizes `stream`.  status_out is a HOST pointer. */
+int q35_device_status(uint32_t *status_out, int32_t clear, void *stream);
 
 /* Test hook: the next call that reaches the armed site withholds one of its
  * asynchronous copies and bounds its waits at 2 ms, so that a wait runs out

@@ -44,6 +44,7 @@ class StackRef:
         c = stack.cfg
         self.cfg, self.cap, self.exact = c, stack.cap, stack.gemv_mode == 0
         self.emb_q, self.emb_s = _q8(stack.embed)
+        self._emb_dense = None
         self.final_norm = stack.final_norm.cpu().numpy()
         self.layers = []
         for L in stack.layers:
@@ -74,7 +75,9 @@ class StackRef:
         return self.emb_q[ids].astype(np.float32) * np.repeat(self.emb_s[ids], 64, axis=1)
 
     def _logits(self, x):
-        return (self.emb_q.astype(np.float32) * np.repeat(self.emb_s, 64, axis=1)) @ x
+        if self._emb_dense is None:  # the tied lm_head weight, dequantised once
+            self._emb_dense = self.emb_q.astype(np.float32) * np.repeat(self.emb_s, 64, axis=1)
+        return self._emb_dense @ x
 
     def prefill(self, ids):
         """Returns (first generated token, logits of the last prompt position)."""

@@ -46,6 +46,8 @@ int gqa_decode_check_args(const q35_gqa_dims *dims, int64_t max_len, const float
                           const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
                           const float *sin, const float *k_cache, const float *v_cache, const int32_t *lens,
                           const float *out);
+int q8_gemm_launch(int T, int K, int N, const float *x, const uint32_t *w, const float *scales, float *y,
+                   cudaStream_t st);
 int q8_gemv_launch(int in_dim, int out_dim, const float *x, const uint32_t *w, const float *scales, float *y,
                    int mode, cudaStream_t st);
 int q8_gemv_fused_launch(int in_dim, int n_seg, const q35_q8_segment *segs, const float *x, const float *residual,
@@ -68,6 +70,27 @@ void set_error(const std::string &msg) { g_last_error = msg; }
 namespace {
 std::atomic<int> g_fault_site{kFaultNone};
 }  // namespace
+
+// Status word of the kernels that take no workspace (Q35_STATUS_* bits), one
+// per device; kernels receive its device address as an argument.
+__device__ uint32_t g_device_status;
+
+namespace {
+std::mutex g_status_mu;
+uint32_t *g_status_ptr[64] = {nullptr};
+}  // namespace
+
+uint32_t *device_status_word() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if (g_status_ptr[dev] == nullptr) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+    g_status_ptr[dev] = static_cast<uint32_t *>(p);
+  }
+  return g_status_ptr[dev];
+}
 
 bool take_fault(int site) {
   int s = site;
@@ -193,6 +216,30 @@ const char *q35_version(void) { return "q35attn 0.1.0 (sm_100a)"; }
 
 uint64_t q35_launch_count(int32_t reset) {
   return reset ? g_launches.exchange(0) : g_launches.load();
+}
+
+int q35_q8_gemm(int32_t n_rows, int32_t in_dim, int32_t out_dim, const float *x, const uint32_t *w,
+                const float *scales, float *y, void *stream) {
+  Q35_REQUIRE(n_rows >= 0 && in_dim > 0 && out_dim > 0, Q35_ERR_INVALID_ARG, "q8_gemm: bad sizes");
+  if (n_rows == 0) return Q35_OK;
+  Q35_PTR16(x); Q35_PTR16(w); Q35_PTR16(scales); Q35_PTR16(y);
+  if (int rc = require_sm100()) return rc;
+  return q8_gemm_launch(n_rows, in_dim, out_dim, x, w, scales, y, static_cast<cudaStream_t>(stream));
+}
+
+int q35_device_status(uint32_t *status_out, int32_t clear, void *stream) {
+  Q35_PTR(status_out);
+  if (int rc = require_sm100()) return rc;
+  uint32_t *w = device_status_word();
+  Q35_REQUIRE(w != nullptr, Q35_ERR_CUDA, "device_status: status word unavailable");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  if (int rc = check_cuda(cudaMemcpyAsync(&v, w, sizeof(v), cudaMemcpyDeviceToHost, st), "device status read"))
+    return rc;
+  if (int rc = check_cuda(cudaStreamSynchronize(st), "device status sync")) return rc;
+  *status_out = v;
+  if (clear) return check_cuda(cudaMemsetAsync(w, 0, sizeof(uint32_t), st), "device status clear");
+  return Q35_OK;
 }
 
 int q35_test_arm_wait_fault(int32_t site) {

@@ -25,6 +25,10 @@ int require_sm100();
 // environment sets Q35_PDL=0.
 bool pdl_enabled();
 
+// Device address of this device's status word for kernels that take no
+// workspace (read with q35_device_status); nullptr when it cannot be resolved.
+uint32_t *device_status_word();
+
 // cudaLaunchKernelEx with the PDL attribute (and a cluster shape when
 // cluster_x * cluster_y > 1).  launch_kernel_serial is the same launch in
 // plain stream order: the GQA flash-decode measured 8-10 % slower at batch 1

@@ -26,6 +26,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace q35 {
 namespace {
@@ -222,13 +223,6 @@ struct GemvTmaSmem {
   alignas(16) float x[4];
 };
 
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
 
 template <bool kCompat, bool kNorm, int NW, int NS>
 __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_constant__ GemvTmaParams p) {
@@ -433,24 +427,6 @@ bool gemv_tma_enabled() {
   return on;
 }
 
-// cuTensorMapEncodeTiled, resolved through the runtime so that the library
-// does not link libcuda (it loads on machines without a driver, for the
-// symbol and argument checks).
-using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_tiled_fn() {
-  static const EncodeTiledFn fn = [] {
-    void *f = nullptr;
-    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      f = nullptr;
-    return reinterpret_cast<EncodeTiledFn>(f);
-  }();
-  return fn;
-}
 
 // Encodes the two tensor maps of one projection; false when the driver rejects them.
 bool encode_gemv_maps(GemvSeg &g, const uint32_t *w, const float *scales, int in_dim, int out_dim) {

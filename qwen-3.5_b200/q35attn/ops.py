@@ -13,7 +13,7 @@ import torch
 from ._lib import GdnDims, GqaDims, Q35Error, Q8Segment, check, load
 
 __all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_workspace", "gdn_gate", "GqaWorkspace", "gqa_decode", "GqaPrefillWorkspace", "gqa_prefill",
-           "q8_gemv", "q8_gemv_fused", "launch_count", "Q35Error"]
+           "q8_gemv", "q8_gemv_fused", "q8_gemm", "device_status", "launch_count", "Q35Error"]
 
 
 def _req(t: torch.Tensor, name: str, dtype=torch.float32) -> int:
@@ -122,6 +122,25 @@ def q8_gemv(x, w, scales, y=None, *, mode=0, stream=None):
     check(load().q35_q8_gemv(in_dim, out_dim, _req(x, "x"), w.data_ptr(), _req(scales, "scales"), _req(y, "y"),
                              int(mode), _stream(stream)))
     return y
+
+
+def q8_gemm(x, w, scales, y=None, *, stream=None):
+    """y [T, out] = x [T, in] @ W for a Q8F matrix (layout as for q8_gemv),
+    the prefill projection, on the tensor cores with W dequantised on load."""
+    T, in_dim = x.shape
+    out_dim = w.shape[1] * 4
+    if y is None:
+        y = torch.empty(T, out_dim, device=x.device, dtype=torch.float32)
+    check(load().q35_q8_gemm(int(T), int(in_dim), int(out_dim), _req(x, "x"), _words(w), _req(scales, "scales"),
+                             _req(y, "y"), _stream(stream)))
+    return y
+
+
+def device_status(clear=False, stream=None) -> int:
+    """Q35_STATUS_* bits of this device's status word (kernels without a workspace)."""
+    v = C.c_uint32(0)
+    check(load().q35_device_status(C.byref(v), int(clear), _stream(stream)))
+    return int(v.value)
 
 
 def _words(w, name="w") -> int:

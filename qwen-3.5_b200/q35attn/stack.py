@@ -6,7 +6,8 @@ with its two forward paths:
 
 * prefill (seq_len > 1): dense projections over the dequantised Q8F weights
   (``Linear::forward``, text_modules.rs:499-506, 578-595, 663, 858-888, 941,
-  1007-1009) as library GEMMs, the chunked GDN core (q35_gdn_prefill), the
+  1007-1009) as q35_q8_gemm tensor-core GEMMs that dequantise each weight tile
+  on load, the chunked GDN core (q35_gdn_prefill), the
   causal GQA core (q35_gqa_prefill), then the tied-embedding logits of the last
   position (model.rs:126-138) and argmax;
 * decode (seq_len == 1): Q8F GEMVs for every projection (kernels.rs:103-165;
@@ -306,12 +307,9 @@ class HybridStack:
         e = lambda *s: torch.empty(*s, device=dev)
         h = ops.q8_embedding(ids, self.embed.words, self.embed.scales)
         x, attn = e(T, c.hidden), e(T, c.hidden)
-        deq = e(max(c.hidden * max(c.conv_dim, c.inter, c.gqa_hq * 512), c.inter * c.hidden))
 
-        def mm(a, W: Q8F):
-            w = deq[:W.rows * W.cols].view(W.rows, W.cols)
-            ops.q8_dequant(W.words, W.scales, w)
-            return torch.matmul(a, w)
+        def mm(a, W: Q8F):  # Linear::forward of the dequantised weight, dequantised tile by tile on load
+            return ops.q8_gemm(a.contiguous(), W.words, W.scales)
 
         gdn_ws = ops.gdn_prefill_workspace(1, T, c.gdn_hk, c.gdn_hv, c.conv_k, dev)
         gqa_ws = ops.GqaPrefillWorkspace(1, c.gqa_hq, c.gqa_hkv, self.cap, T, device=dev)

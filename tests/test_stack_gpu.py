@@ -49,6 +49,36 @@ def test_small_stack_prefill_and_decode(gemv_mode, fused):
     assert int(st.gqa_layers[0]["lens"].item()) == 45 + 6
 
 
+def test_full_2b_stack_against_reference():
+    """BASELINE config 3 at its stated shape: 24 layers (18 GDN, 6 GQA), hidden
+    2048, 16-head GDN, 8/2-head GQA, intermediate 6144, vocab 248,320, random
+    Q8F weights, a 1024-token prompt.  Prefill logits (projections on
+    q35_q8_gemm) and 8 graph-replayed decode steps (fused Q8F GEMVs, the
+    reference's row coverage), teacher-forced, against the CPU reference stack
+    within 1e-3, with the greedy-token rule of the reduced test."""
+    T, steps = 1024, 8
+    st = qs.HybridStack(qs.QWEN35_2B, capacity=T + steps + 8, seed=11)
+    ids = torch.from_numpy(np.random.RandomState(12).randint(0, qs.QWEN35_2B.vocab, T).astype(np.int32)).cuda()
+    tok = int(st.prefill(ids).item())
+    ref = StackRef(st)
+    _, rlog = ref.prefill(ids.cpu().numpy())
+    e = max_rel_err(st.b["logits"].cpu().numpy(), rlog)
+    print(f"2B prefill logits max rel err {e:.2e}")
+    assert e <= 1e-3
+    _check_token(tok, rlog)
+    st.capture()
+    for step in range(steps):
+        st.graph.replay()
+        torch.cuda.synchronize()
+        _, rlog = ref.decode(tok)
+        e = max_rel_err(st.b["logits"].cpu().numpy(), rlog)
+        print(f"2B decode step {step} logits max rel err {e:.2e}")
+        assert e <= 1e-3, (step, e)
+        tok = int(st.b["tok"].item())
+        _check_token(tok, rlog)
+    assert int(st.gqa_layers[0]["lens"].item()) == T + steps
+
+
 def test_generate_is_deterministic():
     st = qs.HybridStack(SMALL, capacity=96, seed=5)
     ids = torch.arange(30, dtype=torch.int32, device="cuda") * 7
