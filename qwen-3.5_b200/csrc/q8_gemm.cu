@@ -154,7 +154,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
         mbar_arrive_expect_tx(&sm.raw_full[slot], kStageBytes);
         tma_load_2d(sm.rawX[slot], &p.xmap, s * kBK, t0, &sm.raw_full[slot]);
         tma_load_2d(sm.rawQ[slot], &p.qmap, n0 / 4, s * kBK, &sm.raw_full[slot]);
-        tma_load_2d(sm.rawS[slot], &p.smap, n0 / 64, s * kBK, &sm.raw_full[slot]);
+        // the scale box starts on a 4-block (16-byte) boundary; a 128-column
+        // tile uses 2 of its 4 blocks, from block (n0 / 64) % 4
+        tma_load_2d(sm.rawS[slot], &p.smap, (n0 / 256) * 4, s * kBK, &sm.raw_full[slot]);
         issued = s + 1;
       }
       // every copy this thread started has landed before the CTA retires
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
       // w: a task is 8 k rows x 32 words (128 columns); lane = word
       constexpr int kSegs = BN / 128, kTasks = 4 * kSegs;
       const uint32_t *rq = sm.rawQ[rs];
-      const float *rsc = sm.rawS[rs];
+      const float *rsc = sm.rawS[rs] + ((n0 / 64) & 3);
       for (int tk = cw; tk < kTasks; tk += kConvWarps) {
         const int kg = tk / kSegs, n4 = 32 * (tk % kSegs) + lane;
         uint32_t u[8];
