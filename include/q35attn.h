@@ -152,19 +152,6 @@ int q35_q8_gemv(int32_t in_dim, int32_t out_dim, const float *x,
                 const uint32_t *w, const float *scales, float *y,
                 int32_t mode, void *stream);
 
-/* Q8F projection of a prompt: y[n_rows, out_dim] = x[n_rows, in_dim] W with
- * W[k][n] = q[k][n] * scales[k][n/64] rounded to f32, the dense weight that
- * Linear::forward multiplies with at seq_len > 1 (text_modules.rs:499-506,
- * 663, 858-888, 941, 1007-1009).  Same weight layout as q35_q8_gemv; the
- * int8 tiles are dequantised in shared memory (no dense copy of W), and the
- * products run on the tensor cores as bf16 hi/lo splits with f32
- * accumulation (relative error near 2^-16 per product).
- * in_dim % 32 == 0, out_dim % 256 == 0, all pointers 16-byte aligned.  A
- * bounded wait that gives up sets Q35_STATUS_WAIT_TIMEOUT in the device
- * status word (q35_device_status). */
-int q35_q8_gemm(int32_t n_rows, int32_t in_dim, int32_t out_dim, const float *x,
-                const uint32_t *w, const float *scales, float *y, void *stream);
-
 /* One Q8F projection of a fused GEMV launch (layout as for q35_q8_gemv). */
 typedef struct {
   const uint32_t *w;     /* [in_dim, out_dim/4] u32, 16-byte aligned */
@@ -194,6 +181,33 @@ int q35_q8_gemv_fused(int32_t in_dim, int32_t n_seg, const q35_q8_segment *segs,
                       const float *x, const float *residual, const float *norm_w,
                       float eps, float *sum_out, float *x_out, int32_t swiglu,
                       int32_t mode, void *stream);
+
+/* --------------------------------------------------------------------------
+ * Q8F projections of a prompt: y[n_rows, out_dim] = x[n_rows, in_dim] W with
+ * W[k][n] = q[k][n] * scales[k][n/64] rounded to f32, the dense weight that
+ * Linear::forward multiplies with at seq_len > 1 (text_modules.rs:499-506,
+ * 663, 858-888, 941, 1007-1009).  Same weight layout as q35_q8_gemv; the
+ * int8 tiles are dequantised in shared memory (no dense copy of W) and the
+ * products run on the tensor cores as bf16 hi/lo splits with f32
+ * accumulation (relative error near 2^-16 per product).
+ *   workspace  >= q35_q8_gemm_workspace_size(n_rows, in_dim) bytes (x split
+ *              into its bf16 terms), 16-byte aligned; reused by every call.
+ * in_dim % 32 == 0, every out_dim % 256 == 0, x and every w / scales / y
+ * 16-byte aligned.  A bounded wait that gives up sets Q35_STATUS_WAIT_TIMEOUT
+ * in the device status word (q35_device_status). */
+size_t q35_q8_gemm_workspace_size(int32_t n_rows, int32_t in_dim);
+int q35_q8_gemm(int32_t n_rows, int32_t in_dim, int32_t out_dim, const float *x,
+                const uint32_t *w, const float *scales, float *y,
+                void *workspace, size_t workspace_bytes, void *stream);
+
+/* Up to four Q8F projections of the same prompt rows in one launch (the
+ * GatedDeltaNet in_proj_qkv / in_proj_z pair, :499-506; attention q / k / v,
+ * :858-888), or with swiglu = 1 exactly two (up, gate) of equal out_dim
+ * whose result up * silu(gate) goes to segs[0].y (the MLP, :1007-1009;
+ * segs[1].y is unused).  Layouts and limits as for q35_q8_gemm. */
+int q35_q8_gemm_fused(int32_t n_rows, int32_t in_dim, int32_t n_seg,
+                      const q35_q8_segment *segs, const float *x, int32_t swiglu,
+                      void *workspace, size_t workspace_bytes, void *stream);
 
 /* --------------------------------------------------------------------------
  * Decoder-stack glue (outside the attention cores; used by the end-to-end
@@ -358,7 +372,7 @@ int q35_gdn_decode_split(const q35_gdn_dims *dims, int32_t split,
                          void *stream);
 
 /* Reads (and with clear != 0 resets) this device's status word, the
- * Q35_STATUS_* bits of the kernels that take no workspace (q35_q8_gemm).
+ * Q35_STATUS_* bits of the kernels that report there (q35_q8_gemm).
  * Synchronizes `stream`.  status_out is a HOST pointer. */
 int q35_device_status(uint32_t *status_out, int32_t clear, void *stream);
 

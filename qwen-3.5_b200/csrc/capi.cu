@@ -46,8 +46,9 @@ int gqa_decode_check_args(const q35_gqa_dims *dims, int64_t max_len, const float
                           const float *v_new, const float *qn_w, const float *kn_w, const float *cos,
                           const float *sin, const float *k_cache, const float *v_cache, const int32_t *lens,
                           const float *out);
-int q8_gemm_launch(int T, int K, int N, const float *x, const uint32_t *w, const float *scales, float *y,
-                   cudaStream_t st);
+size_t q8_gemm_workspace_bytes(int T, int K);
+int q8_gemm_launch(int T, int K, int n_seg, const q35_q8_segment *segs, const float *x, int swiglu, void *ws,
+                   size_t ws_bytes, cudaStream_t st);
 int q8_gemv_launch(int in_dim, int out_dim, const float *x, const uint32_t *w, const float *scales, float *y,
                    int mode, cudaStream_t st);
 int q8_gemv_fused_launch(int in_dim, int n_seg, const q35_q8_segment *segs, const float *x, const float *residual,
@@ -218,13 +219,31 @@ uint64_t q35_launch_count(int32_t reset) {
   return reset ? g_launches.exchange(0) : g_launches.load();
 }
 
+size_t q35_q8_gemm_workspace_size(int32_t n_rows, int32_t in_dim) {
+  if (n_rows <= 0 || in_dim <= 0 || in_dim % 32 != 0) return 0;
+  return q8_gemm_workspace_bytes(n_rows, in_dim);
+}
+
 int q35_q8_gemm(int32_t n_rows, int32_t in_dim, int32_t out_dim, const float *x, const uint32_t *w,
-                const float *scales, float *y, void *stream) {
+                const float *scales, float *y, void *workspace, size_t workspace_bytes, void *stream) {
   Q35_REQUIRE(n_rows >= 0 && in_dim > 0 && out_dim > 0, Q35_ERR_INVALID_ARG, "q8_gemm: bad sizes");
   if (n_rows == 0) return Q35_OK;
   Q35_PTR16(x); Q35_PTR16(w); Q35_PTR16(scales); Q35_PTR16(y);
   if (int rc = require_sm100()) return rc;
-  return q8_gemm_launch(n_rows, in_dim, out_dim, x, w, scales, y, static_cast<cudaStream_t>(stream));
+  const q35_q8_segment seg = {w, scales, y, out_dim};
+  return q8_gemm_launch(n_rows, in_dim, 1, &seg, x, 0, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int q35_q8_gemm_fused(int32_t n_rows, int32_t in_dim, int32_t n_seg, const q35_q8_segment *segs, const float *x,
+                      int32_t swiglu, void *workspace, size_t workspace_bytes, void *stream) {
+  Q35_REQUIRE(n_rows >= 0 && in_dim > 0, Q35_ERR_INVALID_ARG, "q8_gemm_fused: bad sizes");
+  Q35_REQUIRE(swiglu == 0 || swiglu == 1, Q35_ERR_INVALID_ARG, "q8_gemm_fused: swiglu must be 0 or 1");
+  Q35_PTR(segs);
+  if (n_rows == 0) return Q35_OK;
+  Q35_PTR16(x);
+  if (int rc = require_sm100()) return rc;
+  return q8_gemm_launch(n_rows, in_dim, n_seg, segs, x, swiglu, workspace, workspace_bytes,
+                        static_cast<cudaStream_t>(stream));
 }
 
 int q35_device_status(uint32_t *status_out, int32_t clear, void *stream) {

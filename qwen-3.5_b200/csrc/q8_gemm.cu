@@ -7,30 +7,41 @@
 //   Y[T, N] = X[T, K] W[K, N],  W[k, n] = fl(q[k, n] * s[k, n / 64])
 // with q int8 stored 4 per u32 word (byte j of word c = column 4c + j) and f32
 // scales [K, N/64] -- the dense f32 weight the reference multiplies with.  No
-// dense copy of W is ever made: each CTA turns the int8 tile it streams into
-// bf16 operand tiles in shared memory.
+// dense copy of W is made: each CTA turns the int8 tile it streams into bf16
+// operand tiles in shared memory.
 //
-// Arithmetic: x = x_hi + x_lo and w = w_hi + w_lo, each term bf16 (round to
-// nearest); Y = x_hi w_hi + x_hi w_lo + x_lo w_hi on kind::f16 MMAs with f32
-// accumulation in TMEM.  The dropped x_lo w_lo term and the rounding of the lo
-// terms leave a relative error near 2^-16 per product, far inside the 1e-3
-// parity bar of the attention path.  q is converted exactly (int8 values are
+// Arithmetic: x = x_hi + x_lo and w = w_hi + w_lo with bf16 terms;
+// Y = x_hi w_hi + x_hi w_lo + x_lo w_hi on kind::f16 MMAs with f32
+// accumulation in TMEM (relative error near 2^-16 per product, far inside the
+// attention path's 1e-3 parity bar).  q is converted exactly (int8 values are
 // integers below 2^8) and w = q * s is rounded once to f32, as the reference's
 // dequantisation does.
 //
-// CTA tile: 128 tokens x BN (128 or 256) columns, K in stages of 32.
-//   warp 0 (one thread)  2-D TMA loads of the raw x tile (128-byte swizzle),
-//                        the int8 words and the scales into a 3-stage ring;
-//   warp 1 (one thread)  the MMAs: per stage 2 K-steps x 3 products, then a
-//                        commit that frees the operand buffers;
-//   warps 2-9            convert raw tiles into the bf16 hi/lo operands (two
-//                        operand buffers), then the epilogue (TMEM -> Y).
+// Two launches per call:
+//  (1) q8_gemm_split_x: x once into bf16 hi / lo (round to nearest), written
+//      as [128-row tile][32-k slab][term] blocks already in the MMA's K-major
+//      core-matrix layout, so the GEMM fetches each as one bulk copy;
+//  (2) q8_gemm_kernel: CTA tile = 128 tokens x NH halves of 128 output
+//      columns.  Each half is (segment, first column), so one launch serves up
+//      to four projections of the same input (a tile never straddles two), and
+//      in SwiGLU mode a tile pairs up-projection and gate-projection columns
+//      n0 .. n0+127 in one N=256 accumulator whose epilogue writes
+//      up * silu(gate).
+//        warp 0 (one thread)  bulk copy of the x blocks, 2-D TMA loads of the
+//                             int8 words and scales (3-stage ring);
+//        warp 1 (one thread)  per 32-k stage 2 K-steps x 3 products, N = 128 NH;
+//        warps 2-9            dequantise and split the weight tile into bf16
+//                             hi / lo (two operand buffers), then the epilogue.
+//      The weight split runs on the FMA pipe: the int8 -> float conversion is
+//      a byte permute into the mantissa of 2^23 and an exact subtraction, and
+//      hi is Veltkamp's split (c = w (2^16+1), hi = c - (c - w)), which rounds
+//      w to its leading 8 bits; lo = w - hi is exact and keeps its leading 8
+//      bits.  (bf16 conversion instructions issue on a quarter-rate pipe; a
+//      profile of that form showed them as the limit.)
 // The operands use the no-swizzle K-major layout (8 x 16-byte core matrices);
 // B's 8-row groups are 528 bytes apart instead of 512 so the converters'
 // 16-byte stores hit 32 distinct banks per quarter warp.
 #include <cuda.h>
-
-#include <algorithm>
 
 #include "common.cuh"
 #include "tma.cuh"
@@ -47,25 +58,31 @@ constexpr int kGemmThreads = 320;
 constexpr int kConvWarps = 8;
 constexpr uint32_t kSboA = 512;
 constexpr uint32_t kSboB = 528;
+constexpr uint32_t kTermBytes = kBM * kBK * 2;  // one bf16 term of a [128 x 32] x block
+constexpr int kMaxSeg = 4;
 
-template <int BN>
+template <int NH>
 struct GemmSmem {
-  float rawX[kRS][kBM * kBK];          // [128 t][32 k], 128-byte rows, swizzled (1024-byte aligned)
-  uint32_t rawQ[kRS][kBK * BN / 4];    // [32 k][BN/4 words]
-  float rawS[kRS][kBK * 4];            // [32 k][4 column blocks]
-  uint8_t opA[kOS][2][kBM / 8 * kSboA];  // x [hi, lo]
-  uint8_t opB[kOS][2][BN / 8 * kSboB];   // w [hi, lo]
+  uint8_t rawA[kRS][2][kTermBytes];      // x [hi, lo] in the MMA layout, from the split kernel
+  uint32_t rawQ[kRS][NH][kBK * 32];      // per half [32 k][32 words]
+  float rawS[kRS][NH][kBK * 4];          // per half [32 k][4 column blocks]
+  uint8_t opB[kOS][2][NH * 16 * kSboB];  // w [hi, lo], 128 NH rows
   uint64_t raw_full[kRS], raw_empty[kRS], op_full[kOS], op_empty[kOS], acc_full;
   uint32_t tbase;
 };
-static_assert(sizeof(GemmSmem<256>) + 1024 <= 227 * 1024, "GEMM shared memory");
+static_assert(sizeof(GemmSmem<2>) + 128 <= 227 * 1024, "GEMM shared memory");
+static_assert(2 * (sizeof(GemmSmem<1>) + 128) <= 227 * 1024, "two 128-column CTAs per SM");
 
 struct GemmParams {
-  CUtensorMap xmap, qmap, smap;
-  float *y;
+  CUtensorMap qmap[kMaxSeg], smap[kMaxSeg];
+  const uint8_t *xs;       // split x blocks
+  float *y[kMaxSeg];
+  int n_out[kMaxSeg];      // out_dim per segment
+  int tile_end[kMaxSeg];   // running count of tiles up to and including each segment (plain mode)
+  int n_seg, swiglu;
   uint32_t *status;
   uint64_t wait_ns;
-  int T, K, N;
+  int T, K;
 };
 
 // kind::f16 instruction descriptor: bf16 A and B (K-major), f32 accumulator.
@@ -83,40 +100,87 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo_elem, float hi_elem) {
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo_elem, float hi_elem) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi_elem), "f"(lo_elem));
   return r;
-}
-
-// Eight consecutive-k values -> one 16-byte core-matrix row of the hi term and
-// one of the lo term.
-__device__ __forceinline__ void split_store(const float (&v)[8], uint8_t *hi, uint8_t *lo) {
-  uint32_t h[4], l[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    h[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-    const float h0 = __uint_as_float(h[i] << 16), h1 = __uint_as_float(h[i] & 0xFFFF0000u);
-    l[i] = pack_bf16x2(v[2 * i] - h0, v[2 * i + 1] - h1);
-  }
-  *reinterpret_cast<uint4 *>(hi) = make_uint4(h[0], h[1], h[2], h[3]);
-  *reinterpret_cast<uint4 *>(lo) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
 
-template <int BN>
-__global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_constant__ GemmParams p) {
+// ---------------------------------------------------------------------------
+// (1) x [T, K] f32 -> blocks [ceil(T/128)][K/32][hi, lo] of [128 rows x 32 k]
+// bf16 in the K-major core-matrix layout (row r, k-group g at
+// (r / 8) * 512 + g * 128 + (r % 8) * 16 bytes).  Rows >= T are zero.
+// One thread = one (row, 8-k group); a block = one [128 x 32] tile.
+__global__ void __launch_bounds__(512) q8_gemm_split_x(const float *__restrict__ x, uint8_t *__restrict__ xs,
+                                                     int T, int K) {
+  pdl_entry();
+  const int ks = blockIdx.x, mt = blockIdx.y, nks = gridDim.x;
+  const int r = threadIdx.x >> 2, g = threadIdx.x & 3;
+  const int t = mt * kBM + r;
+  float v[8];
+  if (t < T) {
+    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * K + ks * kBK + 8 * g);
+    const float4 a = __ldg(src), b = __ldg(src + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+  }
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    h[i] = pack_bf16x2_rn(v[2 * i], v[2 * i + 1]);
+    const float h0 = __uint_as_float(h[i] << 16), h1 = __uint_as_float(h[i] & 0xFFFF0000u);
+    l[i] = pack_bf16x2_rn(v[2 * i] - h0, v[2 * i + 1] - h1);
+  }
+  uint8_t *blk = xs + ((size_t)mt * nks + ks) * 2 * kTermBytes;
+  const uint32_t off = (uint32_t)(r >> 3) * kSboA + g * 128 + (r & 7) * 16;
+  *reinterpret_cast<uint4 *>(blk + off) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4 *>(blk + kTermBytes + off) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Leading 8 bits of w (round to nearest, Veltkamp) and the exact remainder.
+__device__ __forceinline__ void split8(float w, float &hi, float &lo) {
+  const float c = __fmul_rn(w, 65537.0f);
+  hi = __fsub_rn(c, __fsub_rn(c, w));
+  lo = __fsub_rn(w, hi);
+}
+
+// ---------------------------------------------------------------------------
+// (2) the GEMM
+template <int NH>
+__global__ void __launch_bounds__(kGemmThreads, 3 - NH) q8_gemm_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ unsigned char smem_raw[];
-  GemmSmem<BN> &sm = *reinterpret_cast<GemmSmem<BN> *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                                      ~static_cast<uintptr_t>(1023));
+  GemmSmem<NH> &sm = *reinterpret_cast<GemmSmem<NH> *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                                      ~static_cast<uintptr_t>(127));
+  constexpr int BN = 128 * NH;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n0 = blockIdx.x * BN, t0 = blockIdx.y * kBM;
+  const int tile = blockIdx.x, mt = blockIdx.y, t0 = mt * kBM;
   const int nk = p.K / kBK;
   const uint64_t wns = p.wait_ns;
-  constexpr uint32_t kStageBytes = kBM * kBK * 4 + kBK * BN + kBK * 16;
+  // the halves of this tile: (segment, first column)
+  int hseg[NH], hcol[NH];
+  if (p.swiglu) {
+#pragma unroll
+    for (int h = 0; h < NH; ++h) {
+      hseg[h] = h;
+      hcol[h] = 128 * tile;
+    }
+  } else {
+    int s = 0;
+    while (s + 1 < p.n_seg && tile >= p.tile_end[s]) ++s;
+    const int first = s == 0 ? 0 : p.tile_end[s - 1];
+#pragma unroll
+    for (int h = 0; h < NH; ++h) {
+      hseg[h] = s;
+      hcol[h] = BN * (tile - first) + 128 * h;
+    }
+  }
+  constexpr uint32_t kStageBytes = 2 * kTermBytes + NH * (kBK * 128 + kBK * 16);
 
   if (warp == 1) {
     umma::tmem_alloc(&sm.tbase, BN);
@@ -125,7 +189,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
   if (tid == 0) {
     for (int i = 0; i < kRS; ++i) {
       mbar_init(&sm.raw_full[i], 1);
-      mbar_init(&sm.raw_empty[i], kConvWarps);
+      mbar_init(&sm.raw_empty[i], kConvWarps + 1);  // the converters (words, scales) and the MMA commit (x)
     }
     for (int i = 0; i < kOS; ++i) {
       mbar_init(&sm.op_full[i], kConvWarps);
@@ -133,30 +197,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
     }
     mbar_init(&sm.acc_full, 1);
     fence_mbar_init();
-    prefetch_tmap(&p.xmap);
-    prefetch_tmap(&p.qmap);
-    prefetch_tmap(&p.smap);
+#pragma unroll
+    for (int h = 0; h < NH; ++h) {
+      prefetch_tmap(&p.qmap[hseg[h]]);
+      prefetch_tmap(&p.smap[hseg[h]]);
+    }
   }
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tb = sm.tbase;
-  pdl_entry();  // x is the previous kernel's output
+  pdl_entry();  // the x blocks come from the split kernel
   bool ok = true;
 
   if (warp == 0) {
     if (lane == 0) {  // ---- producer
+      const uint8_t *xblk = p.xs + (size_t)mt * nk * 2 * kTermBytes;
       int issued = 0;
       for (int s = 0; s < nk; ++s) {
         const int slot = s % kRS;
         if (s >= kRS && !mbar_wait_ns(&sm.raw_empty[slot], ((s / kRS) - 1) & 1, wns)) ok = false;
         if (!ok) break;
         mbar_arrive_expect_tx(&sm.raw_full[slot], kStageBytes);
-        tma_load_2d(sm.rawX[slot], &p.xmap, s * kBK, t0, &sm.raw_full[slot]);
-        tma_load_2d(sm.rawQ[slot], &p.qmap, n0 / 4, s * kBK, &sm.raw_full[slot]);
-        // the scale box starts on a 4-block (16-byte) boundary; a 128-column
-        // tile uses 2 of its 4 blocks, from block (n0 / 64) % 4
-        tma_load_2d(sm.rawS[slot], &p.smap, (n0 / 256) * 4, s * kBK, &sm.raw_full[slot]);
+        bulk_g2s_nohint(sm.rawA[slot][0], xblk + (size_t)s * 2 * kTermBytes, 2 * kTermBytes, &sm.raw_full[slot]);
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          tma_load_2d(sm.rawQ[slot][h], &p.qmap[hseg[h]], hcol[h] / 4, s * kBK, &sm.raw_full[slot]);
+          // the scale box starts on a 4-block (16-byte) boundary; the half uses
+          // 2 of its 4 blocks, from block (col / 64) % 4
+          tma_load_2d(sm.rawS[slot][h], &p.smap[hseg[h]], (hcol[h] / 256) * 4, s * kBK, &sm.raw_full[slot]);
+        }
         issued = s + 1;
       }
       // every copy this thread started has landed before the CTA retires
@@ -167,14 +237,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
     if (lane == 0) {  // ---- MMA issue
       constexpr uint32_t id = idesc_bf16(kBM, BN);
       for (int s = 0; s < nk; ++s) {
-        const int os = s % kOS;
-        if (!mbar_wait_ns(&sm.op_full[os], (s / kOS) & 1, wns)) ok = false;
+        const int os = s % kOS, rs = s % kRS;
+        if (!mbar_wait_ns(&sm.raw_full[rs], (s / kRS) & 1, wns)) ok = false;  // x blocks
+        if (ok && !mbar_wait_ns(&sm.op_full[os], (s / kOS) & 1, wns)) ok = false;  // w operands
         if (!ok) break;
         umma::fence_after_sync();
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
-          const uint64_t ah = umma::smem_desc(sm.opA[os][0] + 256 * kk, 128, kSboA);
-          const uint64_t al = umma::smem_desc(sm.opA[os][1] + 256 * kk, 128, kSboA);
+          const uint64_t ah = umma::smem_desc(sm.rawA[rs][0] + 256 * kk, 128, kSboA);
+          const uint64_t al = umma::smem_desc(sm.rawA[rs][1] + 256 * kk, 128, kSboA);
           const uint64_t bh = umma::smem_desc(sm.opB[os][0] + 256 * kk, 128, kSboB);
           const uint64_t bl = umma::smem_desc(sm.opB[os][1] + 256 * kk, 128, kSboB);
           mma_bf16(tb, ah, bh, id, (s > 0 || kk > 0) ? 1u : 0u);
@@ -182,55 +253,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
           mma_bf16(tb, al, bh, id, 1u);
         }
         umma::commit(&sm.op_empty[os]);
+        umma::commit(&sm.raw_empty[rs]);
       }
       umma::commit(&sm.acc_full);  // arrives once every MMA issued above is complete
       if (!mbar_wait_ns(&sm.acc_full, 0, wns)) ok = false;
     }
   } else {
-    // ---- converters (warps 2-9), then the epilogue
+    // ---- converters (warps 2-9).  Lane = one word (4 columns) of a half.
+    // NH = 2: warp task = (half, 8-k group), 8 k rows -> 16-byte stores.
+    // NH = 1: warp task = (8-k group, k rows 0-3 or 4-7) -> 8-byte stores.
     const int cw = warp - 2;
+    const int h = NH == 2 ? cw >> 2 : 0, kg = NH == 2 ? cw & 3 : cw >> 1, j0 = NH == 2 ? 0 : 4 * (cw & 1);
+    constexpr int nj = NH == 2 ? 8 : 4;
     for (int s = 0; s < nk; ++s) {
       const int rs = s % kRS, os = s % kOS;
       if (ok && !mbar_wait_ns(&sm.raw_full[rs], (s / kRS) & 1, wns)) ok = false;
       if (ok && s >= kOS && !mbar_wait_ns(&sm.op_empty[os], ((s / kOS) - 1) & 1, wns)) ok = false;
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      // x: lane -> row 8 g + (lane & 7), k group lane >> 3 (8 values)
-      const float *rx = sm.rawX[rs];
+      const uint32_t *rq = sm.rawQ[rs][h];
+      const float *rsc = sm.rawS[rs][h] + ((hcol[h] / 64) & 3);
+      uint32_t u[nj];
+      float sc[nj];
 #pragma unroll
-      for (int gi = 0; gi < 2; ++gi) {
-        const int r = 8 * (cw + 8 * gi) + (lane & 7), kg = lane >> 3;
-        const float4 *row = reinterpret_cast<const float4 *>(rx + r * kBK);
-        const float4 a = row[(2 * kg) ^ (r & 7)], b = row[(2 * kg + 1) ^ (r & 7)];
-        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        const uint32_t off = (uint32_t)(r >> 3) * kSboA + kg * 128 + (r & 7) * 16;
-        split_store(v, sm.opA[os][0] + off, sm.opA[os][1] + off);
+      for (int j = 0; j < nj; ++j) {
+        const int k = 8 * kg + j0 + j;
+        u[j] = rq[k * 32 + lane] ^ 0x80808080u;  // bytes v + 128
+        sc[j] = rsc[k * 4 + (lane >> 4)];
       }
-      // w: a task is 8 k rows x 32 words (128 columns); lane = word
-      constexpr int kSegs = BN / 128, kTasks = 4 * kSegs;
-      const uint32_t *rq = sm.rawQ[rs];
-      const float *rsc = sm.rawS[rs] + ((n0 / 64) & 3);
-      for (int tk = cw; tk < kTasks; tk += kConvWarps) {
-        const int kg = tk / kSegs, n4 = 32 * (tk % kSegs) + lane;
-        uint32_t u[8];
-        float sc[8];
+      uint8_t *bh = sm.opB[os][0], *bl = sm.opB[os][1];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          u[j] = rq[(8 * kg + j) * (BN / 4) + n4] ^ 0x80808080u;  // bytes v + 128
-          sc[j] = rsc[(8 * kg + j) * 4 + (n4 >> 4)];
-        }
+      for (int c = 0; c < 4; ++c) {
+        uint32_t hw[nj / 2], lw[nj / 2];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float v[8];
+        for (int i = 0; i < nj / 2; ++i) {
+          float hv[2], lv[2];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            // 2^23 + (v + 128) as a float, then the exact integer v
+          for (int e = 0; e < 2; ++e) {
+            const int j = 2 * i + e;
+            // 2^23 + (v + 128) as a float, then the exact integer v, then fl(v s)
             const float m = __uint_as_float(__byte_perm(u[j], 0x4B000000u, 0x7540u | c));
-            v[j] = (m - 8388736.0f) * sc[j];
+            split8(__fmul_rn(__fsub_rn(m, 8388736.0f), sc[j]), hv[e], lv[e]);
           }
-          const int n = 4 * n4 + c;
-          const uint32_t off = (uint32_t)(n >> 3) * kSboB + kg * 128 + (n & 7) * 16;
-          split_store(v, sm.opB[os][0] + off, sm.opB[os][1] + off);
+          // bf16 = the upper 16 bits (hi has 8 significant bits; lo keeps its leading 8)
+          hw[i] = __byte_perm(__float_as_uint(hv[0]), __float_as_uint(hv[1]), 0x7632u);
+          lw[i] = __byte_perm(__float_as_uint(lv[0]), __float_as_uint(lv[1]), 0x7632u);
+        }
+        const int n = 128 * h + 4 * lane + c;
+        const uint32_t off = (uint32_t)(n >> 3) * kSboB + kg * 128 + (n & 7) * 16 + 2 * j0;
+        if constexpr (NH == 2) {
+          *reinterpret_cast<uint4 *>(bh + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4 *>(bl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        } else {
+          *reinterpret_cast<uint2 *>(bh + off) = make_uint2(hw[0], hw[1]);
+          *reinterpret_cast<uint2 *>(bl + off) = make_uint2(lw[0], lw[1]);
         }
       }
       fence_proxy_async_smem();
@@ -240,22 +316,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
         mbar_arrive(&sm.raw_empty[rs]);
       }
     }
-    // epilogue: TMEM lane = token row, column = output column
+    // ---- epilogue: TMEM lane = token row, column = output column of the tile
     if (ok && !mbar_wait_ns(&sm.acc_full, 0, wns)) ok = false;
     ok = __all_sync(0xffffffffu, ok);
     umma::fence_after_sync();
-    const int quad = warp & 3, half = cw >> 2;
+    const int quad = warp & 3, wh = cw >> 2;  // two warps per lane quadrant
     const int t = t0 + 32 * quad + lane;
-    float *yrow = p.y + (size_t)t * p.N + n0 + half * (BN / 2);
+    const uint32_t lrow = (uint32_t)(32 * quad) << 16;
+    if (NH == 2 && p.swiglu) {
+      // columns 0-127 up, 128-255 gate: y0 = up * silu(gate); warp half wh takes 64 of each
+      float *yr = p.y[0] + (size_t)t * p.n_out[0] + hcol[0] + 64 * wh;
 #pragma unroll 1
-    for (int cc = 0; cc < BN / 32; ++cc) {
-      float v[16];
-      umma::ld_32x32b_x16(tb + ((uint32_t)(32 * quad) << 16) + half * (BN / 2) + 16 * cc, v);
-      umma::wait_ld();
-      if (ok && t < p.T) {
-        float4 *dst = reinterpret_cast<float4 *>(yrow + 16 * cc);
+      for (int cc = 0; cc < 4; ++cc) {
+        float a[16], g[16];
+        umma::ld_32x32b_x16(tb + lrow + 64 * wh + 16 * cc, a);
+        umma::ld_32x32b_x16(tb + lrow + 128 + 64 * wh + 16 * cc, g);
+        umma::wait_ld();
+        if (ok && t < p.T) {
+          float4 *dst = reinterpret_cast<float4 *>(yr + 16 * cc);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_float4(a[4 * i] * siluf_dev(g[4 * i]), a[4 * i + 1] * siluf_dev(g[4 * i + 1]),
+                                 a[4 * i + 2] * siluf_dev(g[4 * i + 2]), a[4 * i + 3] * siluf_dev(g[4 * i + 3]));
+        }
+      }
+    } else {
+      // NH = 2: warp half wh takes half wh of the tile; NH = 1: 64 columns each
+      constexpr int kCols = BN / 2;
+      const int eh = NH == 2 ? wh : 0;
+      float *yr = p.y[hseg[eh]] + (size_t)t * p.n_out[hseg[eh]] + hcol[eh] + (NH == 2 ? 0 : 64 * wh);
+#pragma unroll 1
+      for (int cc = 0; cc < kCols / 16; ++cc) {
+        float v[16];
+        umma::ld_32x32b_x16(tb + lrow + kCols * wh + 16 * cc, v);
+        umma::wait_ld();
+        if (ok && t < p.T) {
+          float4 *dst = reinterpret_cast<float4 *>(yr + 16 * cc);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
       }
     }
   }
@@ -264,70 +363,102 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
   const int failed = __syncthreads_or(ok ? 0 : 1);
   if (failed && tid == 0) {  // a bounded wait gave up: flag it and poison the tile
     atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
-    if (t0 < p.T) p.y[(size_t)t0 * p.N + n0] = __int_as_float(0x7fc00000);
+    if (t0 < p.T) p.y[hseg[0]][(size_t)t0 * p.n_out[hseg[0]] + hcol[0]] = __int_as_float(0x7fc00000);
   }
   if (warp == 1) umma::tmem_dealloc(tb, BN);
 }
 
-template <int BN>
-int launch_bn(const GemmParams &p, cudaStream_t st) {
-  const size_t smem = sizeof(GemmSmem<BN>) + 1024;
-  auto kern = q8_gemm_kernel<BN>;
+template <int NH>
+int launch_nh(const GemmParams &p, int tiles, int mt, cudaStream_t st) {
+  const size_t smem = sizeof(GemmSmem<NH>) + 128;
+  auto kern = q8_gemm_kernel<NH>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "q8_gemm attributes");
   note_launch();
-  (void)launch_kernel(kern, dim3(p.N / BN, (p.T + kBM - 1) / kBM), dim3(kGemmThreads), smem, st, 1, 1, p);
+  (void)launch_kernel(kern, dim3(tiles, mt), dim3(kGemmThreads), smem, st, 1, 1, p);
   return check_cuda(cudaGetLastError(), "q8_gemm launch");
 }
 
 }  // namespace
 
-int q8_gemm_launch(int T, int K, int N, const float *x, const uint32_t *w, const float *scales, float *y,
-                   cudaStream_t st) {
-  Q35_REQUIRE(K % kBK == 0 && N % 256 == 0, Q35_ERR_UNSUPPORTED,
-              "q8_gemm: in_dim must be a multiple of 32 and out_dim a multiple of 256");
+size_t q8_gemm_workspace_bytes(int T, int K) {
+  const size_t mt = (size_t)(T + kBM - 1) / kBM;
+  return mt * (size_t)(K / kBK) * 2 * kTermBytes;
+}
+
+int q8_gemm_launch(int T, int K, int n_seg, const q35_q8_segment *segs, const float *x, int swiglu, void *ws,
+                   size_t ws_bytes, cudaStream_t st) {
+  Q35_REQUIRE(n_seg >= 1 && n_seg <= kMaxSeg, Q35_ERR_INVALID_ARG, "q8_gemm: 1 to 4 segments");
+  Q35_REQUIRE(K % kBK == 0, Q35_ERR_UNSUPPORTED, "q8_gemm: in_dim must be a multiple of 32");
+  Q35_REQUIRE(!swiglu || (n_seg == 2 && segs[0].out_dim == segs[1].out_dim), Q35_ERR_INVALID_ARG,
+              "q8_gemm: swiglu needs exactly two segments (up, gate) of equal out_dim");
+  for (int i = 0; i < n_seg; ++i)
+    Q35_REQUIRE(segs[i].out_dim > 0 && segs[i].out_dim % 256 == 0, Q35_ERR_UNSUPPORTED,
+                "q8_gemm: every out_dim must be a positive multiple of 256");
+  const size_t need = q8_gemm_workspace_bytes(T, K);
+  Q35_REQUIRE(ws != nullptr && ws_bytes >= need && (reinterpret_cast<uintptr_t>(ws) & 15u) == 0, Q35_ERR_WORKSPACE,
+              "q8_gemm: workspace missing, unaligned or too small (need " + std::to_string(need) + " bytes)");
   const EncodeTiledFn encode = encode_tiled_fn();
   Q35_REQUIRE(encode != nullptr, Q35_ERR_DEVICE, "q8_gemm: cuTensorMapEncodeTiled unavailable");
   uint32_t *status = device_status_word();
   Q35_REQUIRE(status != nullptr, Q35_ERR_CUDA, "q8_gemm: device status word unavailable");
-  GemmParams p;
-  p.y = y;
+
+  GemmParams p = {};
+  p.xs = static_cast<const uint8_t *>(ws);
+  p.n_seg = n_seg;
+  p.swiglu = swiglu ? 1 : 0;
   p.status = status;
   p.wait_ns = kWaitLimitNs;
-  p.T = T; p.K = K; p.N = N;
-  const cuuint32_t es[2] = {1, 1};
-  {
-    const cuuint64_t d[2] = {(cuuint64_t)K, (cuuint64_t)T};
-    const cuuint64_t str[1] = {(cuuint64_t)K * sizeof(float)};
-    const cuuint32_t box[2] = {kBK, kBM};
-    Q35_REQUIRE(encode(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(x), d, str, box, es,
-                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS,
-                Q35_ERR_INVALID_ARG, "q8_gemm: x tensor map rejected");
-  }
+  p.T = T;
+  p.K = K;
   const int sms = device_sm_count();
   const int mt = (T + kBM - 1) / kBM;
-  // 256-column tiles when they still give about a wave, else 128 (twice the CTAs)
-  const int BN = (long long)mt * (N / 256) * 4 >= 3LL * sms ? 256 : 128;
-  {
-    const cuuint64_t d[2] = {(cuuint64_t)(N / 4), (cuuint64_t)K};
-    const cuuint64_t str[1] = {(cuuint64_t)N};
-    const cuuint32_t box[2] = {(cuuint32_t)(BN / 4), kBK};
-    Q35_REQUIRE(encode(&p.qmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t *>(w), d, str, box, es,
-                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS,
+  int halves = 0;
+  for (int i = 0; i < n_seg; ++i) halves += segs[i].out_dim / 128;
+  // 256-column tiles (N = 256 MMAs, one CTA per SM) against 128-column tiles
+  // (up to two CTAs per SM sharing its tensor pipe): the waves each needs,
+  // weighted by the tile's work (1 per 128 columns) plus a fixed 0.25 per
+  // tile.  SwiGLU always pairs up and gate.
+  const long long ctas1 = (long long)mt * halves, ctas2 = ctas1 / 2;
+  const double cost1 = ctas1 <= sms ? 1.25 : (double)((ctas1 + 2 * sms - 1) / (2 * sms)) * 2.5;
+  const double cost2 = (double)((ctas2 + sms - 1) / sms) * 2.25;
+  const int NH = swiglu || cost2 <= cost1 ? 2 : 1;
+  int tiles = 0;
+  const cuuint32_t es[2] = {1, 1};
+  for (int i = 0; i < n_seg; ++i) {
+    const int N = segs[i].out_dim;
+    Q35_REQUIRE(segs[i].w != nullptr && segs[i].scales != nullptr && segs[i].y != nullptr &&
+                    (reinterpret_cast<uintptr_t>(segs[i].w) & 15u) == 0 &&
+                    (reinterpret_cast<uintptr_t>(segs[i].scales) & 15u) == 0 &&
+                    (reinterpret_cast<uintptr_t>(segs[i].y) & 15u) == 0,
+                Q35_ERR_INVALID_ARG, "q8_gemm: segment pointers must be non-NULL and 16-byte aligned");
+    p.y[i] = segs[i].y;
+    p.n_out[i] = N;
+    tiles += swiglu ? 0 : N / (128 * NH);
+    p.tile_end[i] = tiles;
+    const cuuint64_t qd[2] = {(cuuint64_t)(N / 4), (cuuint64_t)K};
+    const cuuint64_t qs[1] = {(cuuint64_t)N};
+    const cuuint32_t qb[2] = {32, kBK};
+    Q35_REQUIRE(encode(&p.qmap[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t *>(segs[i].w), qd, qs, qb,
+                       es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS,
                 Q35_ERR_INVALID_ARG, "q8_gemm: weight tensor map rejected");
-  }
-  {
-    const cuuint64_t d[2] = {(cuuint64_t)(N / 64), (cuuint64_t)K};
-    const cuuint64_t str[1] = {(cuuint64_t)(N / 64) * sizeof(float)};
-    const cuuint32_t box[2] = {4, kBK};
-    Q35_REQUIRE(encode(&p.smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(scales), d, str, box, es,
-                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS,
+    const cuuint64_t sd[2] = {(cuuint64_t)(N / 64), (cuuint64_t)K};
+    const cuuint64_t ss[1] = {(cuuint64_t)(N / 64) * sizeof(float)};
+    const cuuint32_t sb[2] = {4, kBK};
+    Q35_REQUIRE(encode(&p.smap[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(segs[i].scales), sd, ss,
+                       sb, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS,
                 Q35_ERR_INVALID_ARG, "q8_gemm: scale tensor map rejected");
   }
-  return BN == 256 ? launch_bn<256>(p, st) : launch_bn<128>(p, st);
+  if (swiglu) tiles = segs[0].out_dim / 128;
+  Q35_REQUIRE(tiles <= 65535 && mt <= 65535, Q35_ERR_UNSUPPORTED, "q8_gemm: problem too large for the grid");
+
+  note_launch();
+  (void)launch_kernel(q8_gemm_split_x, dim3(K / kBK, mt), dim3(512), 0, st, 1, 1, x, static_cast<uint8_t *>(ws), T,
+                      K);
+  if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return check_cuda(e, "q8_gemm split launch");
+  return NH == 2 ? launch_nh<2>(p, tiles, mt, st) : launch_nh<1>(p, tiles, mt, st);
 }
 
 }  // namespace q35

@@ -8,6 +8,7 @@ from ._lib import (GdnDims, GqaDims, LIB_PATH, Q35Error, STATUS_CACHE_FULL, STAT
                    STATUS_WAIT_TIMEOUT, load)
 from .ops import (GqaPrefillWorkspace, GqaWorkspace, gdn_decode, gdn_gate, gdn_prefill,  # noqa: F401
                   gdn_prefill_workspace, gqa_combine_partials, gqa_decode, gqa_decode_partial, gqa_prefill, launch_count,
-                  q8_gemm, q8_gemv, q8_gemv_fused, device_status, workspace_status)
+                  q8_gemm, q8_gemm_fused, q8_gemm_workspace, q8_gemv, q8_gemv_fused, device_status,
+                  workspace_status)
 
 __version__ = "0.1.0"

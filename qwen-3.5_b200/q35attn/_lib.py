@@ -80,7 +80,9 @@ SIGNATURES = {
     "q35_launch_count": (C.c_uint64, [_I32]),
     "q35_test_arm_wait_fault": (C.c_int, [_I32]),
     "q35_device_status": (C.c_int, [C.POINTER(C.c_uint32), _I32, _P]),
-    "q35_q8_gemm": (C.c_int, [_I32, _I32, _I32, _P, _P, _P, _P, _P]),
+    "q35_q8_gemm_workspace_size": (_SZ, [_I32, _I32]),
+    "q35_q8_gemm": (C.c_int, [_I32, _I32, _I32, _P, _P, _P, _P, _P, _SZ, _P]),
+    "q35_q8_gemm_fused": (C.c_int, [_I32, _I32, _I32, C.POINTER(Q8Segment), _P, _I32, _P, _SZ, _P]),
 }
 
 _lib = None

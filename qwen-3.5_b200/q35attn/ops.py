@@ -13,7 +13,7 @@ import torch
 from ._lib import GdnDims, GqaDims, Q35Error, Q8Segment, check, load
 
 __all__ = ["gdn_decode", "gdn_prefill", "gdn_prefill_workspace", "gdn_gate", "GqaWorkspace", "gqa_decode", "GqaPrefillWorkspace", "gqa_prefill",
-           "q8_gemv", "q8_gemv_fused", "q8_gemm", "device_status", "launch_count", "Q35Error"]
+           "q8_gemv", "q8_gemv_fused", "q8_gemm", "q8_gemm_fused", "q8_gemm_workspace", "device_status", "launch_count", "Q35Error"]
 
 
 def _req(t: torch.Tensor, name: str, dtype=torch.float32) -> int:
@@ -124,16 +124,46 @@ def q8_gemv(x, w, scales, y=None, *, mode=0, stream=None):
     return y
 
 
-def q8_gemm(x, w, scales, y=None, *, stream=None):
+def q8_gemm_workspace(n_rows, in_dim, device="cuda"):
+    """Workspace of q35_q8_gemm / q35_q8_gemm_fused (x split into bf16 terms)."""
+    n = int(load().q35_q8_gemm_workspace_size(int(n_rows), int(in_dim)))
+    if n == 0:
+        raise Q35Error(1, "invalid q8_gemm sizes for a workspace")
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def q8_gemm(x, w, scales, y=None, *, workspace=None, stream=None):
     """y [T, out] = x [T, in] @ W for a Q8F matrix (layout as for q8_gemv),
     the prefill projection, on the tensor cores with W dequantised on load."""
     T, in_dim = x.shape
     out_dim = w.shape[1] * 4
     if y is None:
         y = torch.empty(T, out_dim, device=x.device, dtype=torch.float32)
+    if workspace is None:
+        workspace = q8_gemm_workspace(T, in_dim, x.device)
     check(load().q35_q8_gemm(int(T), int(in_dim), int(out_dim), _req(x, "x"), _words(w), _req(scales, "scales"),
-                             _req(y, "y"), _stream(stream)))
+                             _req(y, "y"), _req(workspace, "workspace", torch.uint8), workspace.numel(),
+                             _stream(stream)))
     return y
+
+
+def q8_gemm_fused(x, weights, ys, *, swiglu=False, workspace=None, stream=None):
+    """Up to four Q8F projections of the same rows x [T, in] in one launch:
+    weights = [(words, scales), ...], ys = [y [T, out_i], ...].  With
+    swiglu=True, exactly (up, gate): ys[0] receives up * silu(gate)."""
+    T, in_dim = x.shape
+    n = len(weights)
+    segs = (Q8Segment * n)()
+    for i, ((w, sc), y) in enumerate(zip(weights, ys)):
+        segs[i].w = _words(w)
+        segs[i].scales = _req(sc, "scales")
+        segs[i].y = _req(y, "y")
+        segs[i].out_dim = int(w.shape[1] * 4)
+    if workspace is None:
+        workspace = q8_gemm_workspace(T, in_dim, x.device)
+    check(load().q35_q8_gemm_fused(int(T), int(in_dim), n, segs, _req(x, "x"), int(bool(swiglu)),
+                                   _req(workspace, "workspace", torch.uint8), workspace.numel(), _stream(stream)))
+    return ys[0]
 
 
 def device_status(clear=False, stream=None) -> int:

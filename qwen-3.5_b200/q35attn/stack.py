@@ -308,12 +308,20 @@ class HybridStack:
         h = ops.q8_embedding(ids, self.embed.words, self.embed.scales)
         x, attn = e(T, c.hidden), e(T, c.hidden)
 
-        def mm(a, W: Q8F):  # Linear::forward of the dequantised weight, dequantised tile by tile on load
-            return ops.q8_gemm(a.contiguous(), W.words, W.scales)
+        # Linear::forward of the dequantised weights: q35_q8_gemm(_fused) on the
+        # tensor cores, each weight tile dequantised on load; projections of the
+        # same input share one launch, and the MLP's up / gate pair writes
+        # up * silu(gate) from its epilogue
+        gws = ops.q8_gemm_workspace(T, max(c.hidden, c.inter, c.gdn_hv * 128, c.gqa_hq * 256), dev)
+        W = lambda q: (q.words, q.scales)
+
+        def mm(a, q):
+            return ops.q8_gemm(a, q.words, q.scales, workspace=gws)
 
         gdn_ws = ops.gdn_prefill_workspace(1, T, c.gdn_hk, c.gdn_hv, c.conv_k, dev)
         gqa_ws = ops.GqaPrefillWorkspace(1, c.gqa_hq, c.gqa_hkv, self.cap, T, device=dev)
         cos, sin = self.rope_cos[:T][None].contiguous(), self.rope_sin[:T][None].contiguous()
+        act = e(T, c.inter)
         mlp = None
         for L in self.layers:
             if mlp is None:
@@ -321,26 +329,23 @@ class HybridStack:
             else:
                 ops.add_rmsnorm(mlp, L["in_norm"], x, residual=h, sum_out=h, eps=c.eps)
             if L["kind"] == "linear":
-                mixed = mm(x, L["qkv"]).contiguous()
-                z = mm(x, L["z"]).contiguous()
+                mixed, z = e(T, c.conv_dim), e(T, c.gdn_hv * 128)
+                ops.q8_gemm_fused(x, [W(L["qkv"]), W(L["z"])], [mixed, z], workspace=gws)
                 beta, g = ops.gdn_gate(x, L["w_b"], L["w_a"], L["a_log"], L["dt_bias"], mode=1)
                 core = ops.gdn_prefill(mixed.view(1, T, -1), z.view(1, T, -1), beta.view(1, T, -1),
                                        g.view(1, T, -1), L["conv_w"], L["norm_w"], L["conv_state"], L["rec_state"],
                                        num_k_heads=c.gdn_hk, num_v_heads=c.gdn_hv, workspace=gdn_ws, eps=c.eps)
                 attn = mm(core.view(T, -1), L["out"])
             else:
-                qg = mm(x, L["q"]).contiguous().view(1, T, c.gqa_hq, 512)
-                kk = mm(x, L["k"]).contiguous().view(1, T, c.gqa_hkv, 256)
-                vv = mm(x, L["v"]).contiguous().view(1, T, c.gqa_hkv, 256)
+                qg, kk, vv = e(1, T, c.gqa_hq, 512), e(1, T, c.gqa_hkv, 256), e(1, T, c.gqa_hkv, 256)
+                ops.q8_gemm_fused(x, [W(L["q"]), W(L["k"]), W(L["v"])],
+                                  [qg.view(T, -1), kk.view(T, -1), vv.view(T, -1)], workspace=gws)
                 core = ops.gqa_prefill(qg, kk, vv, L["qn_w"], L["kn_w"], cos, sin, L["K"], L["V"], L["lens"],
                                        workspace=gqa_ws, max_len=self.cap, rotary_dim=c.rot, eps=c.eps)
                 attn = mm(core.view(T, -1), L["o"])
-            attn = attn.contiguous()
             ops.add_rmsnorm(attn, L["post_norm"], x, residual=h, sum_out=h, eps=c.eps)
-            up = mm(x, L["up"]).contiguous()
-            gt = mm(x, L["gate"]).contiguous()
-            act = ops.silu_mul(gt, up, torch.empty_like(up))
-            mlp = mm(act, L["down"]).contiguous()
+            ops.q8_gemm_fused(x, [W(L["up"]), W(L["gate"])], [act, act], swiglu=True, workspace=gws)
+            mlp = mm(act, L["down"])
         last = self.b["x"]
         ops.add_rmsnorm(mlp[T - 1:], self.final_norm, last.view(1, -1), residual=h[T - 1:], eps=c.eps)
         ops.q8_lm_head(last, self.embed.words, self.embed.scales, self.b["logits"])

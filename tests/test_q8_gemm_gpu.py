@@ -76,11 +76,43 @@ def test_known_answer_all_ones():
     np.testing.assert_array_equal(y, np.full((T, N), float(K), np.float32))
 
 
+def test_fused_segments_and_swiglu():
+    """Several projections of the same rows in one launch (q/k/v, qkv/z) and
+    the MLP's up/gate pair with up * silu(gate) written by the epilogue."""
+    dev = torch.device("cuda:0")
+    rng = np.random.RandomState(21)
+    T, K = 200, 2048
+    x = rng.randn(T, K).astype(np.float32)
+    xd = torch.from_numpy(x).to(dev)
+    ws = q35attn.q8_gemm_workspace(T, K)
+    mats = [q8f(rng, K, N) for N in (4096, 512, 512)]
+    dev_w = [(torch.from_numpy(np.ascontiguousarray(q).view(np.int32)).to(dev), torch.from_numpy(s).to(dev))
+             for q, s in mats]
+    ys = [torch.empty(T, q.shape[1], device=dev) for q, _ in mats]
+    q35attn.q8_gemm_fused(xd, dev_w, ys, workspace=ws)
+    torch.cuda.synchronize()
+    for (q, s), y in zip(mats, ys):
+        assert max_rel_err(y.cpu().numpy(), x.astype(np.float64) @ dense(q, s).astype(np.float64)) <= TOL
+    # SwiGLU
+    up, gate = q8f(rng, K, 1024), q8f(rng, K, 1024)
+    dev_w = [(torch.from_numpy(np.ascontiguousarray(q).view(np.int32)).to(dev), torch.from_numpy(s).to(dev))
+             for q, s in (up, gate)]
+    act = torch.empty(T, 1024, device=dev)
+    q35attn.q8_gemm_fused(xd, dev_w, [act, act], swiglu=True, workspace=ws)
+    torch.cuda.synchronize()
+    u = x.astype(np.float64) @ dense(*up).astype(np.float64)
+    g = x.astype(np.float64) @ dense(*gate).astype(np.float64)
+    assert max_rel_err(act.cpu().numpy(), u * (g / (1.0 + np.exp(-g)))) <= TOL
+    assert q35attn.device_status() == 0
+
+
 def test_rejects_unsupported_shapes():
     lib = q35attn.load()
     buf = torch.zeros(1 << 16, device="cuda:0")
     p = buf.data_ptr()
-    assert lib.q35_q8_gemm(4, 48, 256, p, p, p, p, None) == _lib.ERR_UNSUPPORTED   # in_dim % 32
-    assert lib.q35_q8_gemm(4, 64, 320, p, p, p, p, None) == _lib.ERR_UNSUPPORTED   # out_dim % 256
-    assert lib.q35_q8_gemm(4, 64, 256, p + 4, p, p, p, None) == _lib.ERR_INVALID_ARG  # unaligned x
-    assert lib.q35_q8_gemm(0, 64, 256, None, None, None, None, None) == _lib.OK
+    n = buf.numel() * 4
+    assert lib.q35_q8_gemm(4, 48, 256, p, p, p, p, p, n, None) == _lib.ERR_UNSUPPORTED   # in_dim % 32
+    assert lib.q35_q8_gemm(4, 64, 320, p, p, p, p, p, n, None) == _lib.ERR_UNSUPPORTED   # out_dim % 256
+    assert lib.q35_q8_gemm(4, 64, 256, p + 4, p, p, p, p, n, None) == _lib.ERR_INVALID_ARG  # unaligned x
+    assert lib.q35_q8_gemm(4, 64, 256, p, p, p, p, p, 16, None) == _lib.ERR_WORKSPACE  # workspace too small
+    assert lib.q35_q8_gemm(0, 64, 256, None, None, None, None, None, 0, None) == _lib.OK
