@@ -27,10 +27,12 @@
 //      in SwiGLU mode a tile pairs up-projection and gate-projection columns
 //      n0 .. n0+127 in one N=256 accumulator whose epilogue writes
 //      up * silu(gate).
-//        warp 0 (one thread)  bulk copy of the x blocks, 2-D TMA loads of the
-//                             int8 words and scales (3-stage ring);
+//        warp 0 (one thread)  2-D TMA loads of the int8 words and scales
+//                             (6-stage ring, freed by the converters);
+//        warp 2 (one thread)  bulk copies of the x blocks (4-stage ring, freed
+//                             by the MMA commit);
 //        warp 1 (one thread)  per 32-k stage 2 K-steps x 3 products, N = 128 NH;
-//        warps 2-9            dequantise and split the weight tile into bf16
+//        warps 3-18           dequantise and split the weight tile into bf16
 //                             hi / lo (two operand buffers), then the epilogue.
 //      The weight split runs on the FMA pipe: the int8 -> float conversion is
 //      a byte permute into the mantissa of 2^23 and an exact subtraction, and
@@ -52,10 +54,12 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 32;
-constexpr int kRS = 3;
-constexpr int kOS = 2;
-constexpr int kGemmThreads = 320;
-constexpr int kConvWarps = 8;
+constexpr int kAS = 4;             // x-block stages (released by the MMA commit)
+constexpr int kQS = 6;             // weight-tile stages (released by the converters)
+constexpr int kOS = 2;             // converted operand stages
+constexpr int kConvWarps = 16;
+constexpr int kConvWarp0 = 3;      // warps 0 (weight loads), 1 (MMA), 2 (x loads), then the converters
+constexpr int kGemmThreads = 32 * (kConvWarp0 + kConvWarps);
 constexpr uint32_t kSboA = 512;
 constexpr uint32_t kSboB = 528;
 constexpr uint32_t kTermBytes = kBM * kBK * 2;  // one bf16 term of a [128 x 32] x block
@@ -63,15 +67,14 @@ constexpr int kMaxSeg = 4;
 
 template <int NH>
 struct GemmSmem {
-  uint8_t rawA[kRS][2][kTermBytes];      // x [hi, lo] in the MMA layout, from the split kernel
-  uint32_t rawQ[kRS][NH][kBK * 32];      // per half [32 k][32 words]
-  float rawS[kRS][NH][kBK * 4];          // per half [32 k][4 column blocks]
+  uint8_t rawA[kAS][2][kTermBytes];      // x [hi, lo] in the MMA layout, from the split kernel
+  uint32_t rawQ[kQS][NH][kBK * 32];      // per half [32 k][32 words]
+  float rawS[kQS][NH][kBK * 4];          // per half [32 k][4 column blocks]
   uint8_t opB[kOS][2][NH * 16 * kSboB];  // w [hi, lo], 128 NH rows
-  uint64_t raw_full[kRS], raw_empty[kRS], op_full[kOS], op_empty[kOS], acc_full;
+  uint64_t a_full[kAS], a_empty[kAS], q_full[kQS], q_empty[kQS], op_full[kOS], op_empty[kOS], acc_full;
   uint32_t tbase;
 };
 static_assert(sizeof(GemmSmem<2>) + 128 <= 227 * 1024, "GEMM shared memory");
-static_assert(2 * (sizeof(GemmSmem<1>) + 128) <= 227 * 1024, "two 128-column CTAs per SM");
 
 struct GemmParams {
   CUtensorMap qmap[kMaxSeg], smap[kMaxSeg];
@@ -153,7 +156,7 @@ __device__ __forceinline__ void split8(float w, float &hi, float &lo) {
 // ---------------------------------------------------------------------------
 // (2) the GEMM
 template <int NH>
-__global__ void __launch_bounds__(kGemmThreads, 3 - NH) q8_gemm_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ unsigned char smem_raw[];
   GemmSmem<NH> &sm = *reinterpret_cast<GemmSmem<NH> *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
                                                       ~static_cast<uintptr_t>(127));
@@ -162,34 +165,31 @@ __global__ void __launch_bounds__(kGemmThreads, 3 - NH) q8_gemm_kernel(const __g
   const int tile = blockIdx.x, mt = blockIdx.y, t0 = mt * kBM;
   const int nk = p.K / kBK;
   const uint64_t wns = p.wait_ns;
-  // the halves of this tile: (segment, first column)
-  int hseg[NH], hcol[NH];
+  // the tile's halves: (seg0, col0) and, when NH = 2, (seg1, col0 + dcol)
+  int seg0, seg1, col0, dcol;
   if (p.swiglu) {
-#pragma unroll
-    for (int h = 0; h < NH; ++h) {
-      hseg[h] = h;
-      hcol[h] = 128 * tile;
-    }
+    seg0 = 0; seg1 = 1; col0 = 128 * tile; dcol = 0;
   } else {
     int s = 0;
     while (s + 1 < p.n_seg && tile >= p.tile_end[s]) ++s;
-    const int first = s == 0 ? 0 : p.tile_end[s - 1];
-#pragma unroll
-    for (int h = 0; h < NH; ++h) {
-      hseg[h] = s;
-      hcol[h] = BN * (tile - first) + 128 * h;
-    }
+    seg0 = seg1 = s;
+    col0 = BN * (tile - (s == 0 ? 0 : p.tile_end[s - 1]));
+    dcol = 128;
   }
-  constexpr uint32_t kStageBytes = 2 * kTermBytes + NH * (kBK * 128 + kBK * 16);
+  constexpr uint32_t kQBytes = NH * (kBK * 128 + kBK * 16);
 
   if (warp == 1) {
     umma::tmem_alloc(&sm.tbase, BN);
     umma::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < kRS; ++i) {
-      mbar_init(&sm.raw_full[i], 1);
-      mbar_init(&sm.raw_empty[i], kConvWarps + 1);  // the converters (words, scales) and the MMA commit (x)
+    for (int i = 0; i < kAS; ++i) {
+      mbar_init(&sm.a_full[i], 1);
+      mbar_init(&sm.a_empty[i], 1);
+    }
+    for (int i = 0; i < kQS; ++i) {
+      mbar_init(&sm.q_full[i], 1);
+      mbar_init(&sm.q_empty[i], kConvWarps);
     }
     for (int i = 0; i < kOS; ++i) {
       mbar_init(&sm.op_full[i], kConvWarps);
@@ -197,55 +197,69 @@ __global__ void __launch_bounds__(kGemmThreads, 3 - NH) q8_gemm_kernel(const __g
     }
     mbar_init(&sm.acc_full, 1);
     fence_mbar_init();
-#pragma unroll
-    for (int h = 0; h < NH; ++h) {
-      prefetch_tmap(&p.qmap[hseg[h]]);
-      prefetch_tmap(&p.smap[hseg[h]]);
+    prefetch_tmap(&p.qmap[seg0]);
+    prefetch_tmap(&p.smap[seg0]);
+    if (NH == 2) {
+      prefetch_tmap(&p.qmap[seg1]);
+      prefetch_tmap(&p.smap[seg1]);
     }
   }
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tb = sm.tbase;
-  pdl_entry();  // the x blocks come from the split kernel
   bool ok = true;
 
   if (warp == 0) {
-    if (lane == 0) {  // ---- producer
-      const uint8_t *xblk = p.xs + (size_t)mt * nk * 2 * kTermBytes;
+    if (lane == 0) {  // ---- weight tiles: 2-D TMA of the int8 words and the scales
       int issued = 0;
       for (int s = 0; s < nk; ++s) {
-        const int slot = s % kRS;
-        if (s >= kRS && !mbar_wait_ns(&sm.raw_empty[slot], ((s / kRS) - 1) & 1, wns)) ok = false;
+        const int slot = s % kQS;
+        if (s >= kQS && !mbar_wait_ns(&sm.q_empty[slot], ((s / kQS) - 1) & 1, wns)) ok = false;
         if (!ok) break;
-        mbar_arrive_expect_tx(&sm.raw_full[slot], kStageBytes);
-        bulk_g2s_nohint(sm.rawA[slot][0], xblk + (size_t)s * 2 * kTermBytes, 2 * kTermBytes, &sm.raw_full[slot]);
+        mbar_arrive_expect_tx(&sm.q_full[slot], kQBytes);
 #pragma unroll
         for (int h = 0; h < NH; ++h) {
-          tma_load_2d(sm.rawQ[slot][h], &p.qmap[hseg[h]], hcol[h] / 4, s * kBK, &sm.raw_full[slot]);
+          const int sg = h == 0 ? seg0 : seg1, cl = col0 + h * dcol;
+          tma_load_2d(sm.rawQ[slot][h], &p.qmap[sg], cl / 4, s * kBK, &sm.q_full[slot]);
           // the scale box starts on a 4-block (16-byte) boundary; the half uses
           // 2 of its 4 blocks, from block (col / 64) % 4
-          tma_load_2d(sm.rawS[slot][h], &p.smap[hseg[h]], (hcol[h] / 256) * 4, s * kBK, &sm.raw_full[slot]);
+          tma_load_2d(sm.rawS[slot][h], &p.smap[sg], (cl / 256) * 4, s * kBK, &sm.q_full[slot]);
         }
         issued = s + 1;
       }
-      // every copy this thread started has landed before the CTA retires
-      for (int s = max(0, issued - kRS); s < issued; ++s)
-        (void)mbar_wait_ns(&sm.raw_full[s % kRS], (s / kRS) & 1, wns);
+      for (int s = max(0, issued - kQS); s < issued; ++s)  // nothing of ours is in flight at exit
+        (void)mbar_wait_ns(&sm.q_full[s % kQS], (s / kQS) & 1, wns);
+    }
+  } else if (warp == 2) {
+    if (lane == 0) {  // ---- x blocks (written by the split kernel: wait for it here only)
+      pdl_entry();
+      const uint8_t *xblk = p.xs + (size_t)mt * nk * 2 * kTermBytes;
+      int issued = 0;
+      for (int s = 0; s < nk; ++s) {
+        const int slot = s % kAS;
+        if (s >= kAS && !mbar_wait_ns(&sm.a_empty[slot], ((s / kAS) - 1) & 1, wns)) ok = false;
+        if (!ok) break;
+        mbar_arrive_expect_tx(&sm.a_full[slot], 2 * kTermBytes);
+        bulk_g2s_nohint(sm.rawA[slot][0], xblk + (size_t)s * 2 * kTermBytes, 2 * kTermBytes, &sm.a_full[slot]);
+        issued = s + 1;
+      }
+      for (int s = max(0, issued - kAS); s < issued; ++s)
+        (void)mbar_wait_ns(&sm.a_full[s % kAS], (s / kAS) & 1, wns);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---- MMA issue
       constexpr uint32_t id = idesc_bf16(kBM, BN);
       for (int s = 0; s < nk; ++s) {
-        const int os = s % kOS, rs = s % kRS;
-        if (!mbar_wait_ns(&sm.raw_full[rs], (s / kRS) & 1, wns)) ok = false;  // x blocks
-        if (ok && !mbar_wait_ns(&sm.op_full[os], (s / kOS) & 1, wns)) ok = false;  // w operands
+        const int os = s % kOS, as = s % kAS;
+        if (!mbar_wait_ns(&sm.a_full[as], (s / kAS) & 1, wns)) ok = false;
+        if (ok && !mbar_wait_ns(&sm.op_full[os], (s / kOS) & 1, wns)) ok = false;
         if (!ok) break;
         umma::fence_after_sync();
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
-          const uint64_t ah = umma::smem_desc(sm.rawA[rs][0] + 256 * kk, 128, kSboA);
-          const uint64_t al = umma::smem_desc(sm.rawA[rs][1] + 256 * kk, 128, kSboA);
+          const uint64_t ah = umma::smem_desc(sm.rawA[as][0] + 256 * kk, 128, kSboA);
+          const uint64_t al = umma::smem_desc(sm.rawA[as][1] + 256 * kk, 128, kSboA);
           const uint64_t bh = umma::smem_desc(sm.opB[os][0] + 256 * kk, 128, kSboB);
           const uint64_t bl = umma::smem_desc(sm.opB[os][1] + 256 * kk, 128, kSboB);
           mma_bf16(tb, ah, bh, id, (s > 0 || kk > 0) ? 1u : 0u);
@@ -253,30 +267,34 @@ __global__ void __launch_bounds__(kGemmThreads, 3 - NH) q8_gemm_kernel(const __g
           mma_bf16(tb, al, bh, id, 1u);
         }
         umma::commit(&sm.op_empty[os]);
-        umma::commit(&sm.raw_empty[rs]);
+        umma::commit(&sm.a_empty[as]);
       }
       umma::commit(&sm.acc_full);  // arrives once every MMA issued above is complete
       if (!mbar_wait_ns(&sm.acc_full, 0, wns)) ok = false;
     }
   } else {
-    // ---- converters (warps 2-9).  Lane = one word (4 columns) of a half.
-    // NH = 2: warp task = (half, 8-k group), 8 k rows -> 16-byte stores.
-    // NH = 1: warp task = (8-k group, k rows 0-3 or 4-7) -> 8-byte stores.
-    const int cw = warp - 2;
-    const int h = NH == 2 ? cw >> 2 : 0, kg = NH == 2 ? cw & 3 : cw >> 1, j0 = NH == 2 ? 0 : 4 * (cw & 1);
-    constexpr int nj = NH == 2 ? 8 : 4;
+    // ---- converters (16 warps).  Lane = one word (4 columns) of a half; a
+    // warp takes JN consecutive k rows of one 8-row group:
+    //   NH = 2: (half, k group, rows 0-3 / 4-7) -> 8-byte stores;
+    //   NH = 1: (k group, rows 0-1 / 2-3 / 4-5 / 6-7) -> 4-byte stores.
+    const int cw = warp - kConvWarp0;
+    constexpr int JN = NH == 2 ? 4 : 2;
+    const int h = NH == 2 ? cw >> 3 : 0;
+    const int kg = NH == 2 ? (cw >> 1) & 3 : cw >> 2;
+    const int j0 = NH == 2 ? 4 * (cw & 1) : 2 * (cw & 3);
+    const int hc = col0 + h * dcol;  // first column of this warp's half
     for (int s = 0; s < nk; ++s) {
-      const int rs = s % kRS, os = s % kOS;
-      if (ok && !mbar_wait_ns(&sm.raw_full[rs], (s / kRS) & 1, wns)) ok = false;
+      const int qs = s % kQS, os = s % kOS;
+      if (ok && !mbar_wait_ns(&sm.q_full[qs], (s / kQS) & 1, wns)) ok = false;
       if (ok && s >= kOS && !mbar_wait_ns(&sm.op_empty[os], ((s / kOS) - 1) & 1, wns)) ok = false;
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      const uint32_t *rq = sm.rawQ[rs][h];
-      const float *rsc = sm.rawS[rs][h] + ((hcol[h] / 64) & 3);
-      uint32_t u[nj];
-      float sc[nj];
+      const uint32_t *rq = sm.rawQ[qs][h];
+      const float *rsc = sm.rawS[qs][h] + ((hc / 64) & 3);
+      uint32_t u[JN];
+      float sc[JN];
 #pragma unroll
-      for (int j = 0; j < nj; ++j) {
+      for (int j = 0; j < JN; ++j) {
         const int k = 8 * kg + j0 + j;
         u[j] = rq[k * 32 + lane] ^ 0x80808080u;  // bytes v + 128
         sc[j] = rsc[k * 4 + (lane >> 4)];
@@ -284,9 +302,9 @@ __global__ void __launch_bounds__(kGemmThreads, 3 - NH) q8_gemm_kernel(const __g
       uint8_t *bh = sm.opB[os][0], *bl = sm.opB[os][1];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t hw[nj / 2], lw[nj / 2];
+        uint32_t hw[JN / 2], lw[JN / 2];
 #pragma unroll
-        for (int i = 0; i < nj / 2; ++i) {
+        for (int i = 0; i < JN / 2; ++i) {
           float hv[2], lv[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
@@ -302,35 +320,36 @@ __global__ void __launch_bounds__(kGemmThreads, 3 - NH) q8_gemm_kernel(const __g
         const int n = 128 * h + 4 * lane + c;
         const uint32_t off = (uint32_t)(n >> 3) * kSboB + kg * 128 + (n & 7) * 16 + 2 * j0;
         if constexpr (NH == 2) {
-          *reinterpret_cast<uint4 *>(bh + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          *reinterpret_cast<uint4 *>(bl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        } else {
           *reinterpret_cast<uint2 *>(bh + off) = make_uint2(hw[0], hw[1]);
           *reinterpret_cast<uint2 *>(bl + off) = make_uint2(lw[0], lw[1]);
+        } else {
+          *reinterpret_cast<uint32_t *>(bh + off) = hw[0];
+          *reinterpret_cast<uint32_t *>(bl + off) = lw[0];
         }
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&sm.op_full[os]);
-        mbar_arrive(&sm.raw_empty[rs]);
+        mbar_arrive(&sm.q_empty[qs]);
       }
     }
-    // ---- epilogue: TMEM lane = token row, column = output column of the tile
+    // ---- epilogue: TMEM lane = token row, column = output column of the tile;
+    // four warps per lane quadrant, each BN / 4 columns
     if (ok && !mbar_wait_ns(&sm.acc_full, 0, wns)) ok = false;
     ok = __all_sync(0xffffffffu, ok);
     umma::fence_after_sync();
-    const int quad = warp & 3, wh = cw >> 2;  // two warps per lane quadrant
+    const int quad = warp & 3, wq = cw >> 2;
     const int t = t0 + 32 * quad + lane;
     const uint32_t lrow = (uint32_t)(32 * quad) << 16;
     if (NH == 2 && p.swiglu) {
-      // columns 0-127 up, 128-255 gate: y0 = up * silu(gate); warp half wh takes 64 of each
-      float *yr = p.y[0] + (size_t)t * p.n_out[0] + hcol[0] + 64 * wh;
+      // columns 0-127 up, 128-255 gate: y0 = up * silu(gate); warp wq takes 32 of each
+      float *yr = p.y[0] + (size_t)t * p.n_out[0] + col0 + 32 * wq;
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
+      for (int cc = 0; cc < 2; ++cc) {
         float a[16], g[16];
-        umma::ld_32x32b_x16(tb + lrow + 64 * wh + 16 * cc, a);
-        umma::ld_32x32b_x16(tb + lrow + 128 + 64 * wh + 16 * cc, g);
+        umma::ld_32x32b_x16(tb + lrow + 32 * wq + 16 * cc, a);
+        umma::ld_32x32b_x16(tb + lrow + 128 + 32 * wq + 16 * cc, g);
         umma::wait_ld();
         if (ok && t < p.T) {
           float4 *dst = reinterpret_cast<float4 *>(yr + 16 * cc);
@@ -341,14 +360,13 @@ __global__ void __launch_bounds__(kGemmThreads, 3 - NH) q8_gemm_kernel(const __g
         }
       }
     } else {
-      // NH = 2: warp half wh takes half wh of the tile; NH = 1: 64 columns each
-      constexpr int kCols = BN / 2;
-      const int eh = NH == 2 ? wh : 0;
-      float *yr = p.y[hseg[eh]] + (size_t)t * p.n_out[hseg[eh]] + hcol[eh] + (NH == 2 ? 0 : 64 * wh);
+      // plain: the tile's columns are col0 .. col0 + BN - 1 of segment seg0
+      constexpr int kCols = BN / 4;
+      float *yr = p.y[seg0] + (size_t)t * p.n_out[seg0] + col0 + kCols * wq;
 #pragma unroll 1
       for (int cc = 0; cc < kCols / 16; ++cc) {
         float v[16];
-        umma::ld_32x32b_x16(tb + lrow + kCols * wh + 16 * cc, v);
+        umma::ld_32x32b_x16(tb + lrow + kCols * wq + 16 * cc, v);
         umma::wait_ld();
         if (ok && t < p.T) {
           float4 *dst = reinterpret_cast<float4 *>(yr + 16 * cc);
@@ -363,7 +381,7 @@ __global__ void __launch_bounds__(kGemmThreads, 3 - NH) q8_gemm_kernel(const __g
   const int failed = __syncthreads_or(ok ? 0 : 1);
   if (failed && tid == 0) {  // a bounded wait gave up: flag it and poison the tile
     atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
-    if (t0 < p.T) p.y[hseg[0]][(size_t)t0 * p.n_out[hseg[0]] + hcol[0]] = __int_as_float(0x7fc00000);
+    if (t0 < p.T) p.y[seg0][(size_t)t0 * p.n_out[seg0] + col0] = __int_as_float(0x7fc00000);
   }
   if (warp == 1) umma::tmem_dealloc(tb, BN);
 }
@@ -415,13 +433,12 @@ int q8_gemm_launch(int T, int K, int n_seg, const q35_q8_segment *segs, const fl
   const int mt = (T + kBM - 1) / kBM;
   int halves = 0;
   for (int i = 0; i < n_seg; ++i) halves += segs[i].out_dim / 128;
-  // 256-column tiles (N = 256 MMAs, one CTA per SM) against 128-column tiles
-  // (up to two CTAs per SM sharing its tensor pipe): the waves each needs,
-  // weighted by the tile's work (1 per 128 columns) plus a fixed 0.25 per
-  // tile.  SwiGLU always pairs up and gate.
+  // 256-column tiles (N = 256 MMAs) against 128-column tiles (twice the CTAs):
+  // the waves each needs, weighted by the tile's work (1 per 128 columns)
+  // plus a fixed 0.5 per tile.  SwiGLU always pairs up and gate.
   const long long ctas1 = (long long)mt * halves, ctas2 = ctas1 / 2;
-  const double cost1 = ctas1 <= sms ? 1.25 : (double)((ctas1 + 2 * sms - 1) / (2 * sms)) * 2.5;
-  const double cost2 = (double)((ctas2 + sms - 1) / sms) * 2.25;
+  const double cost1 = (double)((ctas1 + sms - 1) / sms) * 1.5;
+  const double cost2 = (double)((ctas2 + sms - 1) / sms) * 2.5;
   const int NH = swiglu || cost2 <= cost1 ? 2 : 1;
   int tiles = 0;
   const cuuint32_t es[2] = {1, 1};
