@@ -28,12 +28,14 @@
 //      n0 .. n0+127 in one N=256 accumulator whose epilogue writes
 //      up * silu(gate).
 //        warp 0 (one thread)  2-D TMA loads of the int8 words and scales
-//                             (6-stage ring, freed by the converters);
-//        warp 2 (one thread)  bulk copies of the x blocks (4-stage ring, freed
+//                             (4-stage ring, freed by the converters);
+//        warp 2 (one thread)  bulk copies of the x blocks (3-stage ring, freed
 //                             by the MMA commit);
 //        warp 1 (one thread)  per 32-k stage 2 K-steps x 3 products, N = 128 NH;
-//        warps 3-18           dequantise and split the weight tile into bf16
-//                             hi / lo (two operand buffers), then the epilogue.
+//        warps 3-18           four groups of four warps: group g dequantises
+//                             and splits the weight tiles of stages g, g+4, ...
+//                             into bf16 hi / lo in operand buffer g; then all
+//                             sixteen run the epilogue.
 //      The weight split runs on the FMA pipe: the int8 -> float conversion is
 //      a byte permute into the mantissa of 2^23 and an exact subtraction, and
 //      hi is Veltkamp's split (c = w (2^16+1), hi = c - (c - w)), which rounds
@@ -54,10 +56,12 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 32;
-constexpr int kAS = 4;             // x-block stages (released by the MMA commit)
-constexpr int kQS = 6;             // weight-tile stages (released by the converters)
-constexpr int kOS = 2;             // converted operand stages
-constexpr int kConvWarps = 16;
+constexpr int kAS = 3;             // x-block stages (released by the MMA commit)
+constexpr int kGroups = 4;         // converter groups; stage s is converted by group s % kGroups
+constexpr int kQS = kGroups;       // weight-tile stages: one per group
+constexpr int kOS = kGroups;       // converted operand stages: one per group
+constexpr int kGroupWarps = 4;
+constexpr int kConvWarps = kGroups * kGroupWarps;
 constexpr int kConvWarp0 = 3;      // warps 0 (weight loads), 1 (MMA), 2 (x loads), then the converters
 constexpr int kGemmThreads = 32 * (kConvWarp0 + kConvWarps);
 constexpr uint32_t kSboA = 512;
@@ -189,10 +193,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
     }
     for (int i = 0; i < kQS; ++i) {
       mbar_init(&sm.q_full[i], 1);
-      mbar_init(&sm.q_empty[i], kConvWarps);
+      mbar_init(&sm.q_empty[i], kGroupWarps);
     }
     for (int i = 0; i < kOS; ++i) {
-      mbar_init(&sm.op_full[i], kConvWarps);
+      mbar_init(&sm.op_full[i], kGroupWarps);
       mbar_init(&sm.op_empty[i], 1);
     }
     mbar_init(&sm.acc_full, 1);
@@ -273,65 +277,65 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
       if (!mbar_wait_ns(&sm.acc_full, 0, wns)) ok = false;
     }
   } else {
-    // ---- converters (16 warps).  Lane = one word (4 columns) of a half; a
-    // warp takes JN consecutive k rows of one 8-row group:
-    //   NH = 2: (half, k group, rows 0-3 / 4-7) -> 8-byte stores;
-    //   NH = 1: (k group, rows 0-1 / 2-3 / 4-5 / 6-7) -> 4-byte stores.
-    const int cw = warp - kConvWarp0;
-    constexpr int JN = NH == 2 ? 4 : 2;
-    const int h = NH == 2 ? cw >> 3 : 0;
-    const int kg = NH == 2 ? (cw >> 1) & 3 : cw >> 2;
-    const int j0 = NH == 2 ? 4 * (cw & 1) : 2 * (cw & 3);
-    const int hc = col0 + h * dcol;  // first column of this warp's half
-    for (int s = 0; s < nk; ++s) {
-      const int qs = s % kQS, os = s % kOS;
-      if (ok && !mbar_wait_ns(&sm.q_full[qs], (s / kQS) & 1, wns)) ok = false;
-      if (ok && s >= kOS && !mbar_wait_ns(&sm.op_empty[os], ((s / kOS) - 1) & 1, wns)) ok = false;
+    // ---- converters: four groups of four warps; group g converts stages
+    // g, g + 4, ... into operand buffer g, so four stages are in conversion at
+    // once and the fixed latency of each (waits, proxy fence, arrivals)
+    // overlaps.  A warp task is one 8-row k group of one 128-column half:
+    // lane = one word (4 columns) -> four 16-byte core-matrix rows per term.
+    // NH = 2: warp i of a group takes (half i / 2, k groups 2 (i % 2), +1);
+    // NH = 1: warp i takes k group i.
+    const int cw = warp - kConvWarp0, grp = cw / kGroupWarps, wi = cw % kGroupWarps;
+    constexpr int kTasks = NH == 2 ? 2 : 1;
+    for (int s = grp; s < nk; s += kGroups) {
+      const int slot = grp;  // = s % kQS = s % kOS
+      const uint32_t ph = (uint32_t)(s / kGroups) & 1u;
+      if (ok && !mbar_wait_ns(&sm.q_full[slot], ph, wns)) ok = false;
+      if (ok && s >= kGroups && !mbar_wait_ns(&sm.op_empty[slot], ph ^ 1u, wns)) ok = false;
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      const uint32_t *rq = sm.rawQ[qs][h];
-      const float *rsc = sm.rawS[qs][h] + ((hc / 64) & 3);
-      uint32_t u[JN];
-      float sc[JN];
+      uint8_t *bh = sm.opB[slot][0], *bl = sm.opB[slot][1];
+#pragma unroll 1
+      for (int task = 0; task < kTasks; ++task) {
+        const int h = NH == 2 ? wi >> 1 : 0;
+        const int kg = NH == 2 ? 2 * (wi & 1) + task : wi;
+        const int hc = col0 + h * dcol;  // first column of this half
+        const uint32_t *rq = sm.rawQ[slot][h];
+        const float *rsc = sm.rawS[slot][h] + ((hc / 64) & 3);
+        uint32_t u[8];
+        float sc[8];
 #pragma unroll
-      for (int j = 0; j < JN; ++j) {
-        const int k = 8 * kg + j0 + j;
-        u[j] = rq[k * 32 + lane] ^ 0x80808080u;  // bytes v + 128
-        sc[j] = rsc[k * 4 + (lane >> 4)];
-      }
-      uint8_t *bh = sm.opB[os][0], *bl = sm.opB[os][1];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t hw[JN / 2], lw[JN / 2];
-#pragma unroll
-        for (int i = 0; i < JN / 2; ++i) {
-          float hv[2], lv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int j = 2 * i + e;
-            // 2^23 + (v + 128) as a float, then the exact integer v, then fl(v s)
-            const float m = __uint_as_float(__byte_perm(u[j], 0x4B000000u, 0x7540u | c));
-            split8(__fmul_rn(__fsub_rn(m, 8388736.0f), sc[j]), hv[e], lv[e]);
-          }
-          // bf16 = the upper 16 bits (hi has 8 significant bits; lo keeps its leading 8)
-          hw[i] = __byte_perm(__float_as_uint(hv[0]), __float_as_uint(hv[1]), 0x7632u);
-          lw[i] = __byte_perm(__float_as_uint(lv[0]), __float_as_uint(lv[1]), 0x7632u);
+        for (int j = 0; j < 8; ++j) {
+          u[j] = rq[(8 * kg + j) * 32 + lane] ^ 0x80808080u;  // bytes v + 128
+          sc[j] = rsc[(8 * kg + j) * 4 + (lane >> 4)];
         }
-        const int n = 128 * h + 4 * lane + c;
-        const uint32_t off = (uint32_t)(n >> 3) * kSboB + kg * 128 + (n & 7) * 16 + 2 * j0;
-        if constexpr (NH == 2) {
-          *reinterpret_cast<uint2 *>(bh + off) = make_uint2(hw[0], hw[1]);
-          *reinterpret_cast<uint2 *>(bl + off) = make_uint2(lw[0], lw[1]);
-        } else {
-          *reinterpret_cast<uint32_t *>(bh + off) = hw[0];
-          *reinterpret_cast<uint32_t *>(bl + off) = lw[0];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float hv[2], lv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int j = 2 * i + e;
+              // 2^23 + (v + 128) as a float, then the exact integer v, then fl(v s)
+              const float m = __uint_as_float(__byte_perm(u[j], 0x4B000000u, 0x7540u | c));
+              split8(__fmul_rn(__fsub_rn(m, 8388736.0f), sc[j]), hv[e], lv[e]);
+            }
+            // bf16 = the upper 16 bits (hi has 8 significant bits; lo keeps its leading 8)
+            hw[i] = __byte_perm(__float_as_uint(hv[0]), __float_as_uint(hv[1]), 0x7632u);
+            lw[i] = __byte_perm(__float_as_uint(lv[0]), __float_as_uint(lv[1]), 0x7632u);
+          }
+          const int n = 128 * h + 4 * lane + c;
+          const uint32_t off = (uint32_t)(n >> 3) * kSboB + kg * 128 + (n & 7) * 16;
+          *reinterpret_cast<uint4 *>(bh + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4 *>(bl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&sm.op_full[os]);
-        mbar_arrive(&sm.q_empty[qs]);
+        mbar_arrive(&sm.op_full[slot]);
+        mbar_arrive(&sm.q_empty[slot]);
       }
     }
     // ---- epilogue: TMEM lane = token row, column = output column of the tile;
