@@ -36,15 +36,15 @@
 //                             and splits the weight tiles of stages g, g+4, ...
 //                             into bf16 hi / lo in operand buffer g; then all
 //                             sixteen run the epilogue.
-//      The weight split runs on the FMA pipe: the int8 -> float conversion is
-//      a byte permute into the mantissa of 2^23 and an exact subtraction, and
-//      hi is Veltkamp's split (c = w (2^16+1), hi = c - (c - w)), which rounds
-//      w to its leading 8 bits; lo = w - hi is exact and keeps its leading 8
-//      bits.  (bf16 conversion instructions issue on a quarter-rate pipe; a
-//      profile of that form showed them as the limit.)
-// The operands use the no-swizzle K-major layout (8 x 16-byte core matrices);
-// B's 8-row groups are 528 bytes apart instead of 512 so the converters'
-// 16-byte stores hit 32 distinct banks per quarter warp.
+//      The weight split runs on the FMA pipe with packed f32x2 operations:
+//      the int8 -> float conversion is a byte permute into the mantissa of
+//      2^23 and an exact subtraction, and hi is Veltkamp's split
+//      (c = w (2^16+1), hi = c - (c - w)), which rounds w to its leading 8
+//      bits; lo = w - hi is exact and keeps its leading 8 bits.  (bf16
+//      conversion instructions issue on a quarter-rate pipe; a profile of that
+//      form showed them as the limit.)
+// The operands use the no-swizzle K-major layout (8 x 16-byte core matrices,
+// 128-byte aligned, 8-row groups 512 bytes apart).
 #include <cuda.h>
 
 #include "common.cuh"
@@ -65,7 +65,7 @@ constexpr int kConvWarps = kGroups * kGroupWarps;
 constexpr int kConvWarp0 = 3;      // warps 0 (weight loads), 1 (MMA), 2 (x loads), then the converters
 constexpr int kGemmThreads = 32 * (kConvWarp0 + kConvWarps);
 constexpr uint32_t kSboA = 512;
-constexpr uint32_t kSboB = 528;
+constexpr uint32_t kSboB = 512;
 constexpr uint32_t kTermBytes = kBM * kBK * 2;  // one bf16 term of a [128 x 32] x block
 constexpr int kMaxSeg = 4;
 
@@ -150,12 +150,24 @@ __global__ void __launch_bounds__(512) q8_gemm_split_x(const float *__restrict__
   *reinterpret_cast<uint4 *>(blk + kTermBytes + off) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// Leading 8 bits of w (round to nearest, Veltkamp) and the exact remainder.
-__device__ __forceinline__ void split8(float w, float &hi, float &lo) {
-  const float c = __fmul_rn(w, 65537.0f);
-  hi = __fsub_rn(c, __fsub_rn(c, w));
-  lo = __fsub_rn(w, hi);
+// Packed pairs of f32 (low word = first element) and the sm_100 f32x2 ops,
+// round to nearest, no contraction.
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
 }
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 
 // ---------------------------------------------------------------------------
 // (2) the GEMM
@@ -280,12 +292,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
     // ---- converters: four groups of four warps; group g converts stages
     // g, g + 4, ... into operand buffer g, so four stages are in conversion at
     // once and the fixed latency of each (waits, proxy fence, arrivals)
-    // overlaps.  A warp task is one 8-row k group of one 128-column half:
-    // lane = one word (4 columns) -> four 16-byte core-matrix rows per term.
-    // NH = 2: warp i of a group takes (half i / 2, k groups 2 (i % 2), +1);
-    // NH = 1: warp i takes k group i.
-    const int cw = warp - kConvWarp0, grp = cw / kGroupWarps, wi = cw % kGroupWarps;
-    constexpr int kTasks = NH == 2 ? 2 : 1;
+    // overlaps.  Warp i of a group takes k group i (8 k rows) of the stage, in
+    // passes of 32 columns: lane = one column n, its 8 int8 weights are byte
+    // n % 4 of word n / 4 in 8 rows (four lanes share each word load), and its
+    // hi / lo terms are one 16-byte core-matrix row each.  A quarter warp
+    // stores 8 consecutive columns, i.e. 8 distinct 16-byte slots of one
+    // 128-byte core matrix: no bank conflicts.
+    const int cw = warp - kConvWarp0, grp = cw / kGroupWarps, kg = cw % kGroupWarps;
+    const uint64_t kMagic2 = pack2(8388736.0f, 8388736.0f), kSplit2 = pack2(65537.0f, 65537.0f);
+    const uint32_t sel = 0x7540u | (uint32_t)(lane & 3);  // byte n % 4 into the mantissa of 2^23
     for (int s = grp; s < nk; s += kGroups) {
       const int slot = grp;  // = s % kQS = s % kOS
       const uint32_t ph = (uint32_t)(s / kGroups) & 1u;
@@ -295,41 +310,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
       if (!ok) break;
       uint8_t *bh = sm.opB[slot][0], *bl = sm.opB[slot][1];
 #pragma unroll 1
-      for (int task = 0; task < kTasks; ++task) {
-        const int h = NH == 2 ? wi >> 1 : 0;
-        const int kg = NH == 2 ? 2 * (wi & 1) + task : wi;
-        const int hc = col0 + h * dcol;  // first column of this half
-        const uint32_t *rq = sm.rawQ[slot][h];
-        const float *rsc = sm.rawS[slot][h] + ((hc / 64) & 3);
-        uint32_t u[8];
-        float sc[8];
+      for (int pass = 0; pass < 4 * NH; ++pass) {
+        const int h = pass >> 2, nl = 32 * (pass & 3) + lane;  // half, column within the half
+        const int hc = col0 + h * dcol;
+        const uint32_t *rq = sm.rawQ[slot][h] + (8 * kg) * 32 + (nl >> 2);
+        const float *rsc = sm.rawS[slot][h] + (8 * kg) * 4 + ((hc / 64) & 3) + (nl >> 6);
+        uint32_t hw[4], lw[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          u[j] = rq[(8 * kg + j) * 32 + lane] ^ 0x80808080u;  // bytes v + 128
-          sc[j] = rsc[(8 * kg + j) * 4 + (lane >> 4)];
+        for (int i = 0; i < 4; ++i) {
+          // rows 2i, 2i+1: 2^23 + (v + 128) as floats, then the exact v, then fl(v s)
+          const float m0 = __uint_as_float(__byte_perm(rq[(2 * i) * 32] ^ 0x80808080u, 0x4B000000u, sel));
+          const float m1 = __uint_as_float(__byte_perm(rq[(2 * i + 1) * 32] ^ 0x80808080u, 0x4B000000u, sel));
+          const uint64_t w2 = mul2(sub2(pack2(m0, m1), kMagic2), pack2(rsc[(2 * i) * 4], rsc[(2 * i + 1) * 4]));
+          // Veltkamp: hi = leading 8 bits of w (round to nearest), lo = w - hi exactly
+          const uint64_t c2 = mul2(w2, kSplit2);
+          const uint64_t hi2 = sub2(c2, sub2(c2, w2));
+          const uint64_t lo2 = sub2(w2, hi2);
+          // bf16 = the upper 16 bits (hi has 8 significant bits; lo keeps its leading 8)
+          hw[i] = __byte_perm((uint32_t)hi2, (uint32_t)(hi2 >> 32), 0x7632u);
+          lw[i] = __byte_perm((uint32_t)lo2, (uint32_t)(lo2 >> 32), 0x7632u);
         }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t hw[4], lw[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float hv[2], lv[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int j = 2 * i + e;
-              // 2^23 + (v + 128) as a float, then the exact integer v, then fl(v s)
-              const float m = __uint_as_float(__byte_perm(u[j], 0x4B000000u, 0x7540u | c));
-              split8(__fmul_rn(__fsub_rn(m, 8388736.0f), sc[j]), hv[e], lv[e]);
-            }
-            // bf16 = the upper 16 bits (hi has 8 significant bits; lo keeps its leading 8)
-            hw[i] = __byte_perm(__float_as_uint(hv[0]), __float_as_uint(hv[1]), 0x7632u);
-            lw[i] = __byte_perm(__float_as_uint(lv[0]), __float_as_uint(lv[1]), 0x7632u);
-          }
-          const int n = 128 * h + 4 * lane + c;
-          const uint32_t off = (uint32_t)(n >> 3) * kSboB + kg * 128 + (n & 7) * 16;
-          *reinterpret_cast<uint4 *>(bh + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          *reinterpret_cast<uint4 *>(bl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        }
+        const int n = 128 * h + nl;
+        const uint32_t off = (uint32_t)(n >> 3) * kSboB + kg * 128 + (n & 7) * 16;
+        *reinterpret_cast<uint4 *>(bh + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4 *>(bl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
