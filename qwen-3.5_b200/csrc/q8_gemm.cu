@@ -36,13 +36,12 @@
 //                             and splits the weight tiles of stages g, g+4, ...
 //                             into bf16 hi / lo in operand buffer g; then all
 //                             sixteen run the epilogue.
-//      The weight split runs on the FMA pipe with packed f32x2 operations:
+//      The weight split avoids the bf16 conversion instructions (they issue on
+//      a quarter-rate pipe; a profile of that form showed them as the limit):
 //      the int8 -> float conversion is a byte permute into the mantissa of
-//      2^23 and an exact subtraction, and hi is Veltkamp's split
-//      (c = w (2^16+1), hi = c - (c - w)), which rounds w to its leading 8
-//      bits; lo = w - hi is exact and keeps its leading 8 bits.  (bf16
-//      conversion instructions issue on a quarter-rate pipe; a profile of that
-//      form showed them as the limit.)
+//      2^23 and an exact subtraction (packed f32x2), hi is w rounded to its
+//      leading 8 bits by an integer add of half an ulp and a mask, and
+//      lo = w - hi is exact and keeps its leading 8 bits.
 // The operands use the no-swizzle K-major layout (8 x 16-byte core matrices,
 // 128-byte aligned, 8-row groups 512 bytes apart).
 #include <cuda.h>
@@ -299,7 +298,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
     // stores 8 consecutive columns, i.e. 8 distinct 16-byte slots of one
     // 128-byte core matrix: no bank conflicts.
     const int cw = warp - kConvWarp0, grp = cw / kGroupWarps, kg = cw % kGroupWarps;
-    const uint64_t kMagic2 = pack2(8388736.0f, 8388736.0f), kSplit2 = pack2(65537.0f, 65537.0f);
+    const uint64_t kMagic2 = pack2(8388736.0f, 8388736.0f);
     const uint32_t sel = 0x7540u | (uint32_t)(lane & 3);  // byte n % 4 into the mantissa of 2^23
     for (int s = grp; s < nk; s += kGroups) {
       const int slot = grp;  // = s % kQS = s % kOS
@@ -322,12 +321,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
           const float m0 = __uint_as_float(__byte_perm(rq[(2 * i) * 32] ^ 0x80808080u, 0x4B000000u, sel));
           const float m1 = __uint_as_float(__byte_perm(rq[(2 * i + 1) * 32] ^ 0x80808080u, 0x4B000000u, sel));
           const uint64_t w2 = mul2(sub2(pack2(m0, m1), kMagic2), pack2(rsc[(2 * i) * 4], rsc[(2 * i + 1) * 4]));
-          // Veltkamp: hi = leading 8 bits of w (round to nearest), lo = w - hi exactly
-          const uint64_t c2 = mul2(w2, kSplit2);
-          const uint64_t hi2 = sub2(c2, sub2(c2, w2));
-          const uint64_t lo2 = sub2(w2, hi2);
+          // hi = w rounded to its leading 8 bits (add half an ulp of bit 16, cut
+          // the low 16 bits), lo = w - hi exactly
+          const uint32_t w0 = (uint32_t)w2, w1 = (uint32_t)(w2 >> 32);
+          const uint32_t r0 = w0 + 0x8000u, r1 = w1 + 0x8000u;
+          const uint64_t lo2 = sub2(w2, pack2(__uint_as_float(r0 & 0xFFFF0000u), __uint_as_float(r1 & 0xFFFF0000u)));
           // bf16 = the upper 16 bits (hi has 8 significant bits; lo keeps its leading 8)
-          hw[i] = __byte_perm((uint32_t)hi2, (uint32_t)(hi2 >> 32), 0x7632u);
+          hw[i] = __byte_perm(r0, r1, 0x7632u);
           lw[i] = __byte_perm((uint32_t)lo2, (uint32_t)(lo2 >> 32), 0x7632u);
         }
         const int n = 128 * h + nl;
