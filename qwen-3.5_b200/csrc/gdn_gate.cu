@@ -137,41 +137,51 @@ size_t gate_cluster_smem(int in_dim, int H) {
   return ((size_t)2 * ((rows * H + 3) & ~3) + ((rows + 3) & ~3) + (kSplits - 1) * 2 * H) * sizeof(float);
 }
 
+// Prefill (mode 1), 2H in {32, 64, 128}: a CTA of 256 threads takes R = 256 / (2H)
+// rows; thread (r, o) accumulates output o (o < H: the b head o, else the a head
+// o - H) of row r.  The in_dim axis is walked in chunks of KC whose [w_b | w_a]
+// rows and x values are staged in shared memory once for all R rows, so the
+// weights are read once per CTA instead of once per row.  Lanes read
+// consecutive weight columns (conflict-free) and one broadcast x value.
 template <int H>
-__global__ void gate_prefill_kernel(int N, int in_dim, const float *__restrict__ x, const float *__restrict__ wb,
-                                    const float *__restrict__ wa, const float *__restrict__ a_log,
-                                    const float *__restrict__ dt_bias, float *__restrict__ beta,
-                                    float *__restrict__ g) {
+__global__ void __launch_bounds__(256) gate_prefill_kernel(int N, int in_dim, const float *__restrict__ x,
+                                                           const float *__restrict__ wb,
+                                                           const float *__restrict__ wa,
+                                                           const float *__restrict__ a_log,
+                                                           const float *__restrict__ dt_bias,
+                                                           float *__restrict__ beta, float *__restrict__ g) {
+  constexpr int O = 2 * H, R = 256 / O, KC = H == 64 ? 64 : 128;
+  __shared__ float ws[KC][O];
+  __shared__ float xs[R][KC];
   pdl_entry();
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= N) return;
-  const float *xr = x + (size_t)warp * in_dim;
-  float ab[H], aa[H];
-#pragma unroll
-  for (int h = 0; h < H; ++h) ab[h] = aa[h] = 0.0f;
-  for (int row = lane; row < in_dim; row += 32) {
-    const float xv = xr[row];
-#pragma unroll
-    for (int h = 0; h < H; ++h) {
-      ab[h] = fmaf(xv, wb[(size_t)row * H + h], ab[h]);
-      aa[h] = fmaf(xv, wa[(size_t)row * H + h], aa[h]);
+  const int tid = threadIdx.x, r = tid / O, o = tid % O;
+  const int row0 = blockIdx.x * R;
+  float acc = 0.0f;
+  for (int k0 = 0; k0 < in_dim; k0 += KC) {
+    const int kn = min(KC, in_dim - k0);
+    for (int e = tid; e < kn * O; e += 256) {
+      const int k = e / O, c = e % O;
+      ws[k][c] = c < H ? wb[(size_t)(k0 + k) * H + c] : wa[(size_t)(k0 + k) * H + (c - H)];
     }
+    for (int e = tid; e < R * kn; e += 256) {
+      const int rr = e / kn, k = e % kn;
+      xs[rr][k] = row0 + rr < N ? x[(size_t)(row0 + rr) * in_dim + k0 + k] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < kn; ++k) acc = fmaf(xs[r][k], ws[k][o], acc);
+    __syncthreads();
   }
-#pragma unroll
-  for (int h = 0; h < H; ++h) {
-    ab[h] = warp_sum(ab[h]);
-    aa[h] = warp_sum(aa[h]);
-  }
-  if (lane < H) {
-    float bsum = 0.f, asum = 0.f;
-#pragma unroll
-    for (int h = 0; h < H; ++h)
-      if (h == lane) { bsum = ab[h]; asum = aa[h]; }
-    const float xg = asum + dt_bias[lane];
-    const float sp = xg > 20.0f ? xg : logf(expf(xg) + 1.0f);
-    beta[(size_t)warp * H + lane] = sigmoidf_dev(bsum);
-    g[(size_t)warp * H + lane] = -expf(a_log[lane]) * sp;
+  const int row = row0 + r;
+  if (row < N) {
+    if (o < H) {
+      beta[(size_t)row * H + o] = sigmoidf_dev(acc);
+    } else {
+      const int h = o - H;
+      const float xg = acc + dt_bias[h];
+      const float sp = xg > 20.0f ? xg : logf(expf(xg) + 1.0f);
+      g[(size_t)row * H + h] = -expf(a_log[h]) * sp;
+    }
   }
 }
 
@@ -225,17 +235,17 @@ int gdn_gate_launch(int N, int in_dim, int H, const float *x, const float *wb, c
                                                                                       dt_bias, beta, g);
     return check_cuda(cudaGetLastError(), "gdn_gate launch");
   }
-  const int threads = 256, rows_per_cta = threads / 32;
-  const int grid = (N + rows_per_cta - 1) / rows_per_cta;
   note_launch();
   switch (H) {
-    case 16: (void)launch_kernel(gate_prefill_kernel<16>, dim3(grid), dim3(threads), 0, st, 1, 1, N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
-    case 32: (void)launch_kernel(gate_prefill_kernel<32>, dim3(grid), dim3(threads), 0, st, 1, 1, N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
-    case 48: (void)launch_kernel(gate_prefill_kernel<48>, dim3(grid), dim3(threads), 0, st, 1, 1, N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
-    case 64: (void)launch_kernel(gate_prefill_kernel<64>, dim3(grid), dim3(threads), 0, st, 1, 1, N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
-    default:
+    case 16: (void)launch_kernel(gate_prefill_kernel<16>, dim3((N + 7) / 8), dim3(256), 0, st, 1, 1, N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
+    case 32: (void)launch_kernel(gate_prefill_kernel<32>, dim3((N + 3) / 4), dim3(256), 0, st, 1, 1, N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
+    case 64: (void)launch_kernel(gate_prefill_kernel<64>, dim3((N + 1) / 2), dim3(256), 0, st, 1, 1, N, in_dim, x, wb, wa, a_log, dt_bias, beta, g); break;
+    default: {
+      const int threads = 256, rows_per_cta = threads / 32;
+      const int grid = (N + rows_per_cta - 1) / rows_per_cta;
       (void)launch_kernel(gate_prefill_any_kernel, dim3(grid), dim3(threads), 0, st, 1, 1, N, in_dim, H, x, wb, wa, a_log, dt_bias, beta, g);
       break;
+    }
   }
   return check_cuda(cudaGetLastError(), "gdn_gate launch");
 }

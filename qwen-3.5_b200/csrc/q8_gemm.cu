@@ -46,6 +46,8 @@
 // 128-byte aligned, 8-row groups 512 bytes apart).
 #include <cuda.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "tma.cuh"
 #include "umma.cuh"
@@ -56,11 +58,7 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 32;
 constexpr int kAS = 3;             // x-block stages (released by the MMA commit)
-constexpr int kGroups = 4;         // converter groups; stage s is converted by group s % kGroups
-constexpr int kQS = kGroups;       // weight-tile stages: one per group
-constexpr int kOS = kGroups;       // converted operand stages: one per group
-constexpr int kGroupWarps = 4;
-constexpr int kConvWarps = kGroups * kGroupWarps;
+constexpr int kConvWarps = 16;
 constexpr int kConvWarp0 = 3;      // warps 0 (weight loads), 1 (MMA), 2 (x loads), then the converters
 constexpr int kGemmThreads = 32 * (kConvWarp0 + kConvWarps);
 constexpr uint32_t kSboA = 512;
@@ -68,16 +66,22 @@ constexpr uint32_t kSboB = 512;
 constexpr uint32_t kTermBytes = kBM * kBK * 2;  // one bf16 term of a [128 x 32] x block
 constexpr int kMaxSeg = 4;
 
-template <int NH>
+// A CTA tile is MS row blocks of 128 tokens x NH halves of 128 columns.
+// Stage s is converted by converter group s % G (16 / G warps each), into the
+// group's own weight-tile and operand buffers.
+template <int NH, int MS>
 struct GemmSmem {
-  uint8_t rawA[kAS][2][kTermBytes];      // x [hi, lo] in the MMA layout, from the split kernel
-  uint32_t rawQ[kQS][NH][kBK * 32];      // per half [32 k][32 words]
-  float rawS[kQS][NH][kBK * 4];          // per half [32 k][4 column blocks]
-  uint8_t opB[kOS][2][NH * 16 * kSboB];  // w [hi, lo], 128 NH rows
-  uint64_t a_full[kAS], a_empty[kAS], q_full[kQS], q_empty[kQS], op_full[kOS], op_empty[kOS], acc_full;
+  static constexpr int G = (NH == 2 && MS == 2) ? 2 : 4;
+  uint8_t rawA[kAS][MS][2][kTermBytes];  // x [hi, lo] per row block, MMA layout, from the split kernel
+  uint32_t rawQ[G][NH][kBK * 32];        // per half [32 k][32 words]
+  float rawS[G][NH][kBK * 4];            // per half [32 k][4 column blocks]
+  uint8_t opB[G][2][NH * 16 * kSboB];    // w [hi, lo], 128 NH rows
+  uint64_t a_full[kAS], a_empty[kAS], q_full[G], q_empty[G], op_full[G], op_empty[G], acc_full;
   uint32_t tbase;
 };
-static_assert(sizeof(GemmSmem<2>) + 128 <= 227 * 1024, "GEMM shared memory");
+static_assert(sizeof(GemmSmem<2, 1>) + 128 <= 227 * 1024, "GEMM shared memory");
+static_assert(sizeof(GemmSmem<2, 2>) + 128 <= 227 * 1024, "GEMM shared memory");
+static_assert(sizeof(GemmSmem<1, 2>) + 128 <= 227 * 1024, "GEMM shared memory");
 
 struct GemmParams {
   CUtensorMap qmap[kMaxSeg], smap[kMaxSeg];
@@ -170,14 +174,15 @@ __device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
 
 // ---------------------------------------------------------------------------
 // (2) the GEMM
-template <int NH>
+template <int NH, int MS>
 __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_constant__ GemmParams p) {
+  using Smem = GemmSmem<NH, MS>;
+  constexpr int G = Smem::G, GW = kConvWarps / G;  // groups, warps per group
   extern __shared__ unsigned char smem_raw[];
-  GemmSmem<NH> &sm = *reinterpret_cast<GemmSmem<NH> *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
-                                                      ~static_cast<uintptr_t>(127));
+  Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
   constexpr int BN = 128 * NH;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int tile = blockIdx.x, mt = blockIdx.y, t0 = mt * kBM;
+  const int tile = blockIdx.x, mb = blockIdx.y * MS, t0 = mb * kBM;  // first row block, first row
   const int nk = p.K / kBK;
   const uint64_t wns = p.wait_ns;
   // the tile's halves: (seg0, col0) and, when NH = 2, (seg1, col0 + dcol)
@@ -194,7 +199,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
   constexpr uint32_t kQBytes = NH * (kBK * 128 + kBK * 16);
 
   if (warp == 1) {
-    umma::tmem_alloc(&sm.tbase, BN);
+    umma::tmem_alloc(&sm.tbase, MS * BN);
     umma::tmem_relinquish();
   }
   if (tid == 0) {
@@ -202,12 +207,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
       mbar_init(&sm.a_full[i], 1);
       mbar_init(&sm.a_empty[i], 1);
     }
-    for (int i = 0; i < kQS; ++i) {
+    for (int i = 0; i < G; ++i) {
       mbar_init(&sm.q_full[i], 1);
-      mbar_init(&sm.q_empty[i], kGroupWarps);
-    }
-    for (int i = 0; i < kOS; ++i) {
-      mbar_init(&sm.op_full[i], kGroupWarps);
+      mbar_init(&sm.q_empty[i], GW);
+      mbar_init(&sm.op_full[i], GW);
       mbar_init(&sm.op_empty[i], 1);
     }
     mbar_init(&sm.acc_full, 1);
@@ -229,8 +232,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
     if (lane == 0) {  // ---- weight tiles: 2-D TMA of the int8 words and the scales
       int issued = 0;
       for (int s = 0; s < nk; ++s) {
-        const int slot = s % kQS;
-        if (s >= kQS && !mbar_wait_ns(&sm.q_empty[slot], ((s / kQS) - 1) & 1, wns)) ok = false;
+        const int slot = s % G;
+        if (s >= G && !mbar_wait_ns(&sm.q_empty[slot], ((s / G) - 1) & 1, wns)) ok = false;
         if (!ok) break;
         mbar_arrive_expect_tx(&sm.q_full[slot], kQBytes);
 #pragma unroll
@@ -243,43 +246,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
         }
         issued = s + 1;
       }
-      for (int s = max(0, issued - kQS); s < issued; ++s)  // nothing of ours is in flight at exit
-        (void)mbar_wait_ns(&sm.q_full[s % kQS], (s / kQS) & 1, wns);
+      for (int s = max(0, issued - G); s < issued; ++s)  // nothing of ours is in flight at exit
+        (void)mbar_wait_ns(&sm.q_full[s % G], (s / G) & 1, wns);
     }
   } else if (warp == 2) {
     if (lane == 0) {  // ---- x blocks (written by the split kernel: wait for it here only)
       pdl_entry();
-      const uint8_t *xblk = p.xs + (size_t)mt * nk * 2 * kTermBytes;
       int issued = 0;
       for (int s = 0; s < nk; ++s) {
         const int slot = s % kAS;
         if (s >= kAS && !mbar_wait_ns(&sm.a_empty[slot], ((s / kAS) - 1) & 1, wns)) ok = false;
         if (!ok) break;
-        mbar_arrive_expect_tx(&sm.a_full[slot], 2 * kTermBytes);
-        bulk_g2s_nohint(sm.rawA[slot][0], xblk + (size_t)s * 2 * kTermBytes, 2 * kTermBytes, &sm.a_full[slot]);
+        mbar_arrive_expect_tx(&sm.a_full[slot], MS * 2 * kTermBytes);
+#pragma unroll
+        for (int ms = 0; ms < MS; ++ms)
+          bulk_g2s_nohint(sm.rawA[slot][ms][0], p.xs + ((size_t)(mb + ms) * nk + s) * 2 * kTermBytes,
+                          2 * kTermBytes, &sm.a_full[slot]);
         issued = s + 1;
       }
       for (int s = max(0, issued - kAS); s < issued; ++s)
         (void)mbar_wait_ns(&sm.a_full[s % kAS], (s / kAS) & 1, wns);
     }
   } else if (warp == 1) {
-    if (lane == 0) {  // ---- MMA issue
+    if (lane == 0) {  // ---- MMA issue: per stage and row block 2 K-steps x 3 products
       constexpr uint32_t id = idesc_bf16(kBM, BN);
       for (int s = 0; s < nk; ++s) {
-        const int os = s % kOS, as = s % kAS;
+        const int os = s % G, as = s % kAS;
         if (!mbar_wait_ns(&sm.a_full[as], (s / kAS) & 1, wns)) ok = false;
-        if (ok && !mbar_wait_ns(&sm.op_full[os], (s / kOS) & 1, wns)) ok = false;
+        if (ok && !mbar_wait_ns(&sm.op_full[os], (s / G) & 1, wns)) ok = false;
         if (!ok) break;
         umma::fence_after_sync();
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
-          const uint64_t ah = umma::smem_desc(sm.rawA[as][0] + 256 * kk, 128, kSboA);
-          const uint64_t al = umma::smem_desc(sm.rawA[as][1] + 256 * kk, 128, kSboA);
           const uint64_t bh = umma::smem_desc(sm.opB[os][0] + 256 * kk, 128, kSboB);
           const uint64_t bl = umma::smem_desc(sm.opB[os][1] + 256 * kk, 128, kSboB);
-          mma_bf16(tb, ah, bh, id, (s > 0 || kk > 0) ? 1u : 0u);
-          mma_bf16(tb, ah, bl, id, 1u);
-          mma_bf16(tb, al, bh, id, 1u);
+#pragma unroll
+          for (int ms = 0; ms < MS; ++ms) {
+            const uint64_t ah = umma::smem_desc(sm.rawA[as][ms][0] + 256 * kk, 128, kSboA);
+            const uint64_t al = umma::smem_desc(sm.rawA[as][ms][1] + 256 * kk, 128, kSboA);
+            const uint32_t d = tb + ms * BN;
+            mma_bf16(d, ah, bh, id, (s > 0 || kk > 0) ? 1u : 0u);
+            mma_bf16(d, ah, bl, id, 1u);
+            mma_bf16(d, al, bh, id, 1u);
+          }
         }
         umma::commit(&sm.op_empty[os]);
         umma::commit(&sm.a_empty[as]);
@@ -288,29 +297,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
       if (!mbar_wait_ns(&sm.acc_full, 0, wns)) ok = false;
     }
   } else {
-    // ---- converters: four groups of four warps; group g converts stages
-    // g, g + 4, ... into operand buffer g, so four stages are in conversion at
-    // once and the fixed latency of each (waits, proxy fence, arrivals)
-    // overlaps.  Warp i of a group takes k group i (8 k rows) of the stage, in
-    // passes of 32 columns: lane = one column n, its 8 int8 weights are byte
-    // n % 4 of word n / 4 in 8 rows (four lanes share each word load), and its
-    // hi / lo terms are one 16-byte core-matrix row each.  A quarter warp
-    // stores 8 consecutive columns, i.e. 8 distinct 16-byte slots of one
-    // 128-byte core matrix: no bank conflicts.
-    const int cw = warp - kConvWarp0, grp = cw / kGroupWarps, kg = cw % kGroupWarps;
+    // ---- converters: G groups; group g converts stages g, g + G, ... into its
+    // own operand buffer, so G stages are in conversion at once and the fixed
+    // latency of each (waits, proxy fence, arrivals) overlaps.  A warp takes
+    // one k group (8 k rows) of the stage for PW passes of 32 columns: lane =
+    // one column n, its 8 int8 weights are byte n % 4 of word n / 4 in 8 rows
+    // (four lanes share each word load), and its hi / lo terms are one 16-byte
+    // core-matrix row each.  A quarter warp stores 8 consecutive columns, i.e.
+    // 8 distinct 16-byte slots of one 128-byte core matrix: no bank conflicts.
+    const int cw = warp - kConvWarp0, grp = cw / GW, wi = cw % GW;
+    const int kg = wi & 3;
+    constexpr int PW = 16 * NH / GW;  // passes per warp
+    const int gp0 = (wi >> 2) * PW;   // first global pass (h = pass / 4, 32-column chunk = pass % 4)
     const uint64_t kMagic2 = pack2(8388736.0f, 8388736.0f);
     const uint32_t sel = 0x7540u | (uint32_t)(lane & 3);  // byte n % 4 into the mantissa of 2^23
-    for (int s = grp; s < nk; s += kGroups) {
-      const int slot = grp;  // = s % kQS = s % kOS
-      const uint32_t ph = (uint32_t)(s / kGroups) & 1u;
+    for (int s = grp; s < nk; s += G) {
+      const int slot = grp;  // = s % G
+      const uint32_t ph = (uint32_t)(s / G) & 1u;
       if (ok && !mbar_wait_ns(&sm.q_full[slot], ph, wns)) ok = false;
-      if (ok && s >= kGroups && !mbar_wait_ns(&sm.op_empty[slot], ph ^ 1u, wns)) ok = false;
+      if (ok && s >= G && !mbar_wait_ns(&sm.op_empty[slot], ph ^ 1u, wns)) ok = false;
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       uint8_t *bh = sm.opB[slot][0], *bl = sm.opB[slot][1];
 #pragma unroll 1
-      for (int pass = 0; pass < 4 * NH; ++pass) {
-        const int h = pass >> 2, nl = 32 * (pass & 3) + lane;  // half, column within the half
+      for (int pp = 0; pp < PW; ++pp) {
+        const int gp = gp0 + pp;
+        const int h = gp >> 2, nl = 32 * (gp & 3) + lane;  // half, column within the half
         const int hc = col0 + h * dcol;
         const uint32_t *rq = sm.rawQ[slot][h] + (8 * kg) * 32 + (nl >> 2);
         const float *rsc = sm.rawS[slot][h] + (8 * kg) * 4 + ((hc / 64) & 3) + (nl >> 6);
@@ -342,22 +354,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
         mbar_arrive(&sm.q_empty[slot]);
       }
     }
-    // ---- epilogue: TMEM lane = token row, column = output column of the tile;
-    // four warps per lane quadrant, each BN / 4 columns
+    // ---- epilogue: TMEM lane = token row of a row block, column = ms * BN +
+    // output column; four warps per lane quadrant split MS * BN columns
     if (ok && !mbar_wait_ns(&sm.acc_full, 0, wns)) ok = false;
     ok = __all_sync(0xffffffffu, ok);
     umma::fence_after_sync();
     const int quad = warp & 3, wq = cw >> 2;
-    const int t = t0 + 32 * quad + lane;
-    const uint32_t lrow = (uint32_t)(32 * quad) << 16;
+    const int ms = MS == 2 ? wq >> 1 : 0, part = MS == 2 ? wq & 1 : wq;  // row block, column part
+    constexpr int kParts = 4 / MS;
+    const int t = t0 + 128 * ms + 32 * quad + lane;
+    const uint32_t lrow = ((uint32_t)(32 * quad) << 16) + ms * BN;
     if (NH == 2 && p.swiglu) {
-      // columns 0-127 up, 128-255 gate: y0 = up * silu(gate); warp wq takes 32 of each
-      float *yr = p.y[0] + (size_t)t * p.n_out[0] + col0 + 32 * wq;
+      // columns 0-127 up, 128-255 gate: y0 = up * silu(gate)
+      constexpr int kCols = 128 / kParts;
+      float *yr = p.y[0] + (size_t)t * p.n_out[0] + col0 + kCols * part;
 #pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
+      for (int cc = 0; cc < kCols / 16; ++cc) {
         float a[16], g[16];
-        umma::ld_32x32b_x16(tb + lrow + 32 * wq + 16 * cc, a);
-        umma::ld_32x32b_x16(tb + lrow + 128 + 32 * wq + 16 * cc, g);
+        umma::ld_32x32b_x16(tb + lrow + kCols * part + 16 * cc, a);
+        umma::ld_32x32b_x16(tb + lrow + 128 + kCols * part + 16 * cc, g);
         umma::wait_ld();
         if (ok && t < p.T) {
           float4 *dst = reinterpret_cast<float4 *>(yr + 16 * cc);
@@ -369,12 +384,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
       }
     } else {
       // plain: the tile's columns are col0 .. col0 + BN - 1 of segment seg0
-      constexpr int kCols = BN / 4;
-      float *yr = p.y[seg0] + (size_t)t * p.n_out[seg0] + col0 + kCols * wq;
+      constexpr int kCols = BN / kParts;
+      float *yr = p.y[seg0] + (size_t)t * p.n_out[seg0] + col0 + kCols * part;
 #pragma unroll 1
       for (int cc = 0; cc < kCols / 16; ++cc) {
         float v[16];
-        umma::ld_32x32b_x16(tb + lrow + kCols * wq + 16 * cc, v);
+        umma::ld_32x32b_x16(tb + lrow + kCols * part + 16 * cc, v);
         umma::wait_ld();
         if (ok && t < p.T) {
           float4 *dst = reinterpret_cast<float4 *>(yr + 16 * cc);
@@ -391,25 +406,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q8_gemm_kernel(const __grid_c
     atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
     if (t0 < p.T) p.y[seg0][(size_t)t0 * p.n_out[seg0] + col0] = __int_as_float(0x7fc00000);
   }
-  if (warp == 1) umma::tmem_dealloc(tb, BN);
+  if (warp == 1) umma::tmem_dealloc(tb, MS * BN);
 }
 
-template <int NH>
-int launch_nh(const GemmParams &p, int tiles, int mt, cudaStream_t st) {
-  const size_t smem = sizeof(GemmSmem<NH>) + 128;
-  auto kern = q8_gemm_kernel<NH>;
+template <int NH, int MS>
+int launch_cfg(const GemmParams &p, int tiles, int mt, cudaStream_t st) {
+  const size_t smem = sizeof(GemmSmem<NH, MS>) + 128;
+  auto kern = q8_gemm_kernel<NH, MS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "q8_gemm attributes");
   note_launch();
-  (void)launch_kernel(kern, dim3(tiles, mt), dim3(kGemmThreads), smem, st, 1, 1, p);
+  (void)launch_kernel(kern, dim3(tiles, (mt + MS - 1) / MS), dim3(kGemmThreads), smem, st, 1, 1, p);
   return check_cuda(cudaGetLastError(), "q8_gemm launch");
 }
 
 }  // namespace
 
+// Row blocks of the split x, padded to an even count (a two-block CTA reads a
+// zero block past the last one).
+static int padded_row_blocks(int T) { return ((T + kBM - 1) / kBM + 1) & ~1; }
+
 size_t q8_gemm_workspace_bytes(int T, int K) {
-  const size_t mt = (size_t)(T + kBM - 1) / kBM;
-  return mt * (size_t)(K / kBK) * 2 * kTermBytes;
+  return (size_t)padded_row_blocks(T) * (size_t)(K / kBK) * 2 * kTermBytes;
 }
 
 int q8_gemm_launch(int T, int K, int n_seg, const q35_q8_segment *segs, const float *x, int swiglu, void *ws,
@@ -441,13 +459,24 @@ int q8_gemm_launch(int T, int K, int n_seg, const q35_q8_segment *segs, const fl
   const int mt = (T + kBM - 1) / kBM;
   int halves = 0;
   for (int i = 0; i < n_seg; ++i) halves += segs[i].out_dim / 128;
-  // 256-column tiles (N = 256 MMAs) against 128-column tiles (twice the CTAs):
-  // the waves each needs, weighted by the tile's work (1 per 128 columns)
-  // plus a fixed 0.5 per tile.  SwiGLU always pairs up and gate.
-  const long long ctas1 = (long long)mt * halves, ctas2 = ctas1 / 2;
-  const double cost1 = (double)((ctas1 + sms - 1) / sms) * 1.5;
-  const double cost2 = (double)((ctas2 + sms - 1) / sms) * 2.5;
-  const int NH = swiglu || cost2 <= cost1 ? 2 : 1;
+  // Tile shape (NH halves of 128 columns, MS row blocks of 128): the waves
+  // each needs times the tile's time, modelled as MMA work MS * NH (units of a
+  // 128 x 128 tile stage) against weight conversion 1.2 NH (independent of MS,
+  // the two overlap) plus 0.3 fixed.  SwiGLU needs NH = 2.
+  auto cost = [&](int nh, int msub) {
+    const long long ctas = (long long)((mt + msub - 1) / msub) * (halves / nh);
+    const double per = std::max((double)(msub * nh), 1.2 * nh);
+    return (double)((ctas + sms - 1) / sms) * (per + 0.3);
+  };
+  int NH = 2, MS = 1;
+  double best = 1e30;
+  for (int nh = swiglu ? 2 : 1; nh <= 2; ++nh)
+    for (int msub = 1; msub <= 2; ++msub)
+      if (cost(nh, msub) < best - 1e-9) {
+        best = cost(nh, msub);
+        NH = nh;
+        MS = msub;
+      }
   int tiles = 0;
   const cuuint32_t es[2] = {1, 1};
   for (int i = 0; i < n_seg; ++i) {
@@ -480,10 +509,11 @@ int q8_gemm_launch(int T, int K, int n_seg, const q35_q8_segment *segs, const fl
   Q35_REQUIRE(tiles <= 65535 && mt <= 65535, Q35_ERR_UNSUPPORTED, "q8_gemm: problem too large for the grid");
 
   note_launch();
-  (void)launch_kernel(q8_gemm_split_x, dim3(K / kBK, mt), dim3(512), 0, st, 1, 1, x, static_cast<uint8_t *>(ws), T,
-                      K);
+  (void)launch_kernel(q8_gemm_split_x, dim3(K / kBK, padded_row_blocks(T)), dim3(512), 0, st, 1, 1, x,
+                      static_cast<uint8_t *>(ws), T, K);
   if (cudaError_t e = cudaGetLastError(); e != cudaSuccess) return check_cuda(e, "q8_gemm split launch");
-  return NH == 2 ? launch_nh<2>(p, tiles, mt, st) : launch_nh<1>(p, tiles, mt, st);
+  if (NH == 2) return MS == 2 ? launch_cfg<2, 2>(p, tiles, mt, st) : launch_cfg<2, 1>(p, tiles, mt, st);
+  return MS == 2 ? launch_cfg<1, 2>(p, tiles, mt, st) : launch_cfg<1, 1>(p, tiles, mt, st);
 }
 
 }  // namespace q35
