@@ -372,7 +372,9 @@ int q35_gdn_decode_split(const q35_gdn_dims *dims, int32_t split,
                          void *stream);
 
 /* Reads (and with clear != 0 resets) this device's status word, the
- * Q35_STATUS_* bits of the kernels that report there (q35_q8_gemm).
+ * Q35_STATUS_* bits of the kernels that take no workspace and report there
+ * (q35_q8_gemm(_fused), q35_q8_gemv(_fused), q35_gdn_gate mode 0 and the
+ * streaming schedule of q35_gdn_decode).
  * Synchronizes `stream`.  status_out is a HOST pointer. */
 int q35_device_status(uint32_t *status_out, int32_t clear, void *stream);
 

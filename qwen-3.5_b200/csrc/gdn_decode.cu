@@ -36,9 +36,25 @@ constexpr int kDV = 128;
 struct GdnDecodeParams {
   const float *mixed_qkv, *z, *beta, *g, *conv_w, *norm_w;
   float *conv_state, *rec_state, *out;
+  uint32_t *status;  // device status word (streaming kernel): Q35_STATUS_WAIT_TIMEOUT
   int B, Hk, Hv, rf, C;
   float eps;
 };
+
+// bar.sync over `nthreads` that also returns whether every participating
+// thread passed pred != 0.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
 
 template <int SPLIT>
 struct GdnDecodeCfg {
@@ -293,9 +309,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gdn_decode_stream_kernel(co
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
+      int issued = 0;
       for (int t = 0; t < ntiles; ++t) {
         const int sidx = t % kStages;
-        if (t >= kStages && !mbar_wait(&empty_bar[sidx], ((t / kStages) - 1) & 1)) break;
+        if (t >= kStages && !mbar_wait(&empty_bar[sidx], ((t / kStages) - 1) & 1)) {
+          atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
+          break;
+        }
+        issued = t + 1;
         const int item = blockIdx.x + (t / p.rf) * gridDim.x;
         const int r = t % p.rf;
         const int b = item / p.Hk, hk = item % p.Hk, h = hk * p.rf + r;
@@ -316,6 +337,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gdn_decode_stream_kernel(co
         bulk_g2s(sg.cv, p.conv_state + (xrow + cv0) * (KC - 1), kStBytes, &full_bar[sidx], pol);
         bulk_g2s(sg.z, p.z + ((size_t)b * p.Hv + h) * kDV, kDV * sizeof(float), &full_bar[sidx], pol);
       }
+      // every copy this thread started has landed before the CTA retires
+      for (int t = max(0, issued - kStages); t < issued; ++t)
+        (void)mbar_wait(&full_bar[t % kStages], (t / kStages) & 1);
     }
     return;
   }
@@ -331,7 +355,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gdn_decode_stream_kernel(co
     const float decay = expf(__ldg(p.g + (size_t)b * p.Hv + h));
     const float bt = __ldg(p.beta + (size_t)b * p.Hv + h);
     StreamStage<KC> &sg = stg[sidx];
-    if (!mbar_wait(&full_bar[sidx], (t / kStages) & 1)) break;
+    const bool got = mbar_wait(&full_bar[sidx], (t / kStages) & 1);
 
     // causal conv update + SiLU (text_modules.rs:145-161) from the staged inputs
     auto conv = [&](const float *win_state, float xin, int c, float &y) {
@@ -360,7 +384,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gdn_decode_stream_kernel(co
       conv(sg.cv + tid * (KC - 1), sg.xv[tid], 2 * p.Hk * kDK + h * kDV + tid, y);
       v_loc[tid] = y;
     }
-    named_bar_sync(1, kCons);
+    // every consumer thread saw the tile land, or all stop together (a wait
+    // gave up: the status word says so, the state of this tile is not valid)
+    if (!named_bar_and(1, kCons, got)) {
+      if (tid == 0) atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
+      break;
+    }
     if (r == 0) {
       if (warp < 2) {  // l2norm of q and k (text_modules.rs:184-187)
         float ss = 0.0f;
@@ -494,6 +523,7 @@ int gdn_decode_launch(const q35_gdn_dims *d, const float *mixed_qkv, const float
   p.B = d->batch; p.Hk = d->num_k_heads; p.Hv = d->num_v_heads; p.rf = p.Hv / p.Hk;
   p.C = 2 * p.Hk * kDK + p.Hv * kDV;
   p.eps = d->eps;
+  p.status = device_status_word();
   const int sms = device_sm_count();
   // Large batches stream persistent tiles through shared memory; small ones
   // split each head's columns over a cluster to occupy every SM.

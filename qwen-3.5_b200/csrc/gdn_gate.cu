@@ -80,7 +80,7 @@ constexpr int kGateThreads = 256;
 __global__ void __launch_bounds__(kGateThreads) gate_decode_cluster_kernel(
     int in_dim, int H, const float *__restrict__ x, const float *__restrict__ wb, const float *__restrict__ wa,
     const float *__restrict__ a_log, const float *__restrict__ dt_bias, float *__restrict__ beta,
-    float *__restrict__ g) {
+    float *__restrict__ g, uint32_t *status) {
   extern __shared__ __align__(16) float gsm[];
   const int n = blockIdx.y;
   const int split = (int)cluster_ctarank();
@@ -119,7 +119,10 @@ __global__ void __launch_bounds__(kGateThreads) gate_decode_cluster_kernel(
     const bool got = mbar_wait(&redbar, 0);
     float sum = 0.0f + acc;  // split order: 0, 1, ..., 7
     for (int i = 1; i < kSplits; ++i) sum += recv[(i - 1) * 2 * H + u];
-    if (!got) sum = __int_as_float(0x7fc00000);  // a bounded wait gave up
+    if (!got) {  // a bounded wait gave up: poison, flag the device status word
+      sum = __int_as_float(0x7fc00000);
+      if (status != nullptr) atomicOr(status, Q35_STATUS_WAIT_TIMEOUT);
+    }
     const int h = u % H;
     if (u < H) {
       beta[(size_t)n * H + h] = 1.0f / (1.0f + expf(-sum));
@@ -227,7 +230,7 @@ int gdn_gate_launch(int N, int in_dim, int H, const float *x, const float *wb, c
       if (e != cudaSuccess) return check_cuda(e, "gdn_gate attributes");
       note_launch();
       (void)launch_kernel(gate_decode_cluster_kernel, dim3(kSplits, N), dim3(kGateThreads), smem, st, kSplits, 1,
-                          in_dim, H, x, wb, wa, a_log, dt_bias, beta, g);
+                          in_dim, H, x, wb, wa, a_log, dt_bias, beta, g, device_status_word());
       return check_cuda(cudaGetLastError(), "gdn_gate launch");
     }
     note_launch();

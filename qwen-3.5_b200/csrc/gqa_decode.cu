@@ -62,6 +62,8 @@ struct GqaParams {
   long long cap;
   int B, Hq, Hkv, rot, nsplit, kps, ngroups;
   int tree;  // 1: merge the splits in-kernel (ticket tree); 0: gqa_split_combine_kernel does
+  int fault;  // test hook: CTA (0, 0, 0) issues none of its copies, so its waits run out
+  uint64_t wait_ns;  // limit of every bounded wait
   float eps, qscale_log2;
 };
 
@@ -258,9 +260,11 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
     }
     if (lane == 0 && ntiles > 0) {
       const uint64_t pol = l2_policy_evict_first();
-      for (int t = 0; t < ntiles; ++t) {
+      const bool withhold = p.fault && s == 0 && kvh == 0 && b == 0;
+      int issued = 0;
+      for (int t = 0; t < ntiles && !withhold; ++t) {
         const int st = t % kNS;
-        if (t >= kNS && !mbar_wait(&empty_bar[st], ((t / kNS) - 1) & 1)) {
+        if (t >= kNS && !mbar_wait_ns(&empty_bar[st], ((t / kNS) - 1) & 1, p.wait_ns)) {
           atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
           break;
         }
@@ -270,8 +274,14 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
         mbar_arrive_expect_tx(&full_bar[st], 2 * bytes);
         bulk_g2s(&sm.k[st][0][0], Kc + (size_t)k0 * kD, bytes, &full_bar[st], pol);
         bulk_g2s(&sm.v[st][0][0], Vc + (size_t)k0 * kD, bytes, &full_bar[st], pol);
+        issued = t + 1;
       }
+      // every copy this thread started has landed before the ring is reused
+      for (int t = max(0, issued - kNS); t < issued; ++t)
+        (void)mbar_wait_ns(&full_bar[t % kNS], (t / kNS) & 1, p.wait_ns);
     }
+    __syncwarp();
+    named_bar_arrive(2, (kNW + 1) * 32);  // the consumers may now reuse the ring
     return;
   }
 
@@ -306,7 +316,9 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
   bool ok = true;
   for (int t = 0; t < ntiles && ok; ++t) {
     const int st = t % kNS;
-    if (!mbar_wait(&full_bar[st], (t / kNS) & 1)) {
+    // warp-uniform: every lane of a warp leaves together (the shuffles below
+    // need the full warp)
+    if (!__all_sync(0xffffffffu, mbar_wait_ns(&full_bar[st], (t / kNS) & 1, p.wait_ns))) {
       if (lane == 0) atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
       ok = false;
       break;
@@ -372,8 +384,18 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
     if (lane == 0) mbar_arrive(&empty_bar[st]);
   }
 
-  // ---- merge the NW warps of this CTA (stage buffers are drained: reuse)
-  named_bar_sync(1, kNW * 32);
+  // ---- merge the NW warps of this CTA.  The producer has seen all its copies
+  // land (barrier 2), so the ring is free for reuse.  A warp whose wait gave up
+  // contributes nothing (m = -inf); the status word already says so.
+  if (!ok) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      m_run[g] = -INFINITY;
+      l_run[g] = 0.0f;
+      a0[g] = a1[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  named_bar_sync(2, (kNW + 1) * 32);
   float *wacc = &sm.k[0][0][0];            // [NW][G][D]
   float *wml = wacc + kNW * G * kD;        // [NW][G][2]
 #pragma unroll
@@ -461,69 +483,73 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
 }
 
 // Merge of the split partials of one decode step (the few-sequence regime):
-// CTA (pair, head g, 64-dim slice).  Pass 1: the threads stride over every
-// split's maximum (m in log2 units; each decode CTA writes its partial every
-// step, -inf when it held no keys) and reduce M, while the step's key count
-// arrives.  Pass 2: warp w takes the live splits w, w + 8, ...; with M known
-// the terms are independent, so a warp keeps 8 splits' loads in flight instead
-// of one dependent L2 round trip per split.  The CTA's 3 KB of shared memory
-// and 8K registers fit beside two decode CTAs (G <= 4), so under programmatic
-// dependent launch it is resident before the decode grid ends.
-// The warps' sums meet in shared memory and go through write_final (gate, or
-// the context-parallel triple).  One CTA per sequence advances lens[b]; no CTA
-// of this kernel reads lens.
-constexpr int kCombSlice = 64;
+// CTA (pair, head g, 32-dim slice), lane = one output dim.  Warp w takes the
+// live splits w, w + 8, ... and merges them online (running maximum, rescaled
+// sums), so no load waits for another: each warp issues all its splits' loads
+// (up to kCombBatch) in one round, which is the whole critical path after the
+// decode grid ends.  The warps' (m, l, o) meet in shared memory and go through
+// write_final (gate, or the context-parallel triple).  One CTA per sequence
+// advances lens[b]; no CTA of this kernel reads lens.
+constexpr int kCombSlice = 32;
+constexpr int kCombBatch = 20;
+
+__device__ __forceinline__ void merge_online(float &m, float &l, float &o, float mj, float lj, float oj) {
+  if (mj == -INFINITY) return;  // a split without keys adds nothing
+  if (mj > m) {
+    const float sc = exp2f(m - mj);  // exp2(-inf) = 0 while m is still -inf
+    l = fmaf(l, sc, lj);
+    o = fmaf(o, sc, oj);
+    m = mj;
+  } else {
+    const float w = exp2f(mj - m);
+    l = fmaf(lj, w, l);
+    o = fmaf(oj, w, o);
+  }
+}
 
 template <int G>
 __global__ void __launch_bounds__(256) gqa_split_combine_kernel(const GqaParams p) {
   pdl_entry();
-  __shared__ float red[8][32][3];  // [warp][lane][l, o0, o1]
-  __shared__ float wmax[8];
+  __shared__ float red[8][32][3];  // [warp][lane][m, l, o]
   const int pg = blockIdx.x, slice = blockIdx.y;
   const size_t pair = (size_t)pg / G;
   const int g = pg % G;
   const int b = (int)(pair / p.Hkv), kvh = (int)(pair % p.Hkv);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = __ldcg(p.lsnap + b);
-  const int d = slice * kCombSlice + 2 * lane;
-  const float *pml = p.part_ml + pair * p.nsplit * G * 2;
-  const float *po = p.part_o + pair * p.nsplit * G * kD;
-  float M = -INFINITY;
-  for (int j = tid; j < p.nsplit; j += 256) M = fmaxf(M, __ldcg(pml + ((size_t)j * G + g) * 2));
-  M = warp_max(M);
-  if (lane == 0) wmax[warp] = M;
-  __syncthreads();
   if (L < 0) return;  // the decode step was refused (cache full / length hint): no output, lens unchanged
+  const int d = slice * kCombSlice + lane;
+  const float *pml = p.part_ml + pair * p.nsplit * G * 2 + g * 2;
+  const float *po = p.part_o + pair * p.nsplit * G * kD + g * kD + d;
   const int nlive = min((L + p.kps - 1) / p.kps, p.nsplit);
+  float m = -INFINITY, l = 0.0f, o = 0.0f;
+  for (int j0 = warp; j0 < nlive; j0 += 8 * kCombBatch) {
+    float mj[kCombBatch], lj[kCombBatch], oj[kCombBatch];
 #pragma unroll
-  for (int w = 0; w < 8; ++w) M = fmaxf(M, wmax[w]);
-  float l = 0.0f, o0 = 0.0f, o1 = 0.0f;
-  if (M != -INFINITY) {
-#pragma unroll 8
-    for (int j = warp; j < nlive; j += 8) {
-      const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pml + ((size_t)j * G + g) * 2));
-      const float2 oj = __ldcg(reinterpret_cast<const float2 *>(po + ((size_t)j * G + g) * kD + d));
-      const float wgt = ml.x == -INFINITY ? 0.0f : exp2f(ml.x - M);  // a split without keys adds nothing
-      l = fmaf(ml.y, wgt, l);
-      o0 = fmaf(oj.x, wgt, o0);
-      o1 = fmaf(oj.y, wgt, o1);
+    for (int c = 0; c < kCombBatch; ++c) {
+      const int j = j0 + 8 * c;
+      if (j < nlive) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pml + (size_t)j * G * 2));
+        mj[c] = ml.x;
+        lj[c] = ml.y;
+        oj[c] = __ldcg(po + (size_t)j * G * kD);
+      } else {
+        mj[c] = -INFINITY;
+        lj[c] = oj[c] = 0.0f;
+      }
     }
+#pragma unroll
+    for (int c = 0; c < kCombBatch; ++c) merge_online(m, l, o, mj[c], lj[c], oj[c]);
   }
-  red[warp][lane][0] = l;
-  red[warp][lane][1] = o0;
-  red[warp][lane][2] = o1;
+  red[warp][lane][0] = m;
+  red[warp][lane][1] = l;
+  red[warp][lane][2] = o;
   __syncthreads();
   if (warp == 0) {
-    float Ls = 0.0f, O0 = 0.0f, O1 = 0.0f;
+    float M = -INFINITY, Ls = 0.0f, O = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      Ls += red[w][lane][0];
-      O0 += red[w][lane][1];
-      O1 += red[w][lane][2];
-    }
-    const int h = kvh * G + g;
-    write_final(p, b, h, d, O0, M, Ls);
-    write_final(p, b, h, d + 1, O1, M, Ls);
+    for (int w = 0; w < 8; ++w) merge_online(M, Ls, O, red[w][lane][0], red[w][lane][1], red[w][lane][2]);
+    write_final(p, b, kvh * G + g, d, O, M, Ls);
     if (lane == 0 && kvh == 0 && g == 0 && slice == 0 && p.k_new != nullptr) p.lens[b] = L;
   }
 }
@@ -660,6 +686,8 @@ int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_g
   p.q_gate = q_gate; p.k_new = k_new; p.v_new = v_new; p.qn_w = qn_w; p.kn_w = kn_w; p.cos = cos; p.sin = sin;
   p.k_cache = k_cache; p.v_cache = v_cache; p.lens = lens; p.out = out; p.part_out = part_out;
   p.qscale_log2 = (1.0f / sqrtf((float)kD)) * kLog2e;
+  p.fault = take_fault(kFaultGqaDecode) ? 1 : 0;
+  p.wait_ns = p.fault ? kFaultWaitLimitNs : kWaitLimitNs;
   unsigned char *base = static_cast<unsigned char *>(ws);
   p.status = reinterpret_cast<uint32_t *>(base + lay.status);
   p.grp_cnt = reinterpret_cast<uint32_t *>(base + lay.grp_cnt);

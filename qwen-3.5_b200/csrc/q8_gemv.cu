@@ -206,6 +206,7 @@ struct alignas(64) GemvTmaParams {
   GemvSeg seg[kMaxSeg];
   const float *x, *residual, *norm_w;
   float *sum_out, *x_out;
+  uint32_t *status;  // device status word: Q35_STATUS_WAIT_TIMEOUT when a bounded wait gave up
   float eps;
   int in_dim, nseg, ks;
 };
@@ -288,13 +289,17 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
         bulk_g2s_nohint(ws, p.norm_w, xb, &sm.xbar);
         if (res) bulk_g2s_nohint(rs, p.residual, xb, &sm.xbar);
       }
+      int issued = min(NS, nst);
       for (int st = NS; st < nst && ok; ++st) {
         if (!mbar_wait(&sm.empty[st % NS], ((st / NS) - 1) & 1)) {
           ok = false;
           break;
         }
         issue(st);
+        issued = st + 1;
       }
+      // every box this thread requested has landed before the CTA retires
+      for (int st = max(0, issued - NS); st < issued; ++st) (void)mbar_wait(&sm.full[st % NS], (st / NS) & 1);
     }
   } else {
     ok = __all_sync(0xffffffffu, mbar_wait(&sm.xbar, 0));
@@ -378,8 +383,9 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
       sm.red[k][warp][16 * q + 2 * (lane >> 2) + 1] = acc[k][1];
     }
   }
-  __syncthreads();
+  const int failed = __syncthreads_or(ok ? 0 : 1);
   const float poison = __int_as_float(0x7fc00000);  // a bounded wait gave up
+  if (failed && tid == 0 && p.status != nullptr) atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
   float v[NW];
   if (tid < kTC) {
 #pragma unroll
@@ -387,7 +393,7 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
       float t = sm.red[k][0][tid];
 #pragma unroll
       for (int w = 1; w < kTWarps; ++w) t += sm.red[k][w][tid];
-      v[k] = ok ? t : poison;
+      v[k] = failed ? poison : t;
     }
   }
   if (p.ks > 1) {
@@ -403,6 +409,7 @@ __global__ void __launch_bounds__(kTThreads) q8_gemv_tma_kernel(const __grid_con
     }
     if (tid < kTC) {  // rank 0: add the ranks' sums in rank order
       const bool got = mbar_wait(&sm.redbar, 0);
+      if (!got && p.status != nullptr) atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
 #pragma unroll
       for (int k = 0; k < NW; ++k) {
         float t = v[k];
@@ -461,6 +468,7 @@ int launch_tma_t(const GemvTmaParams &p, int ctas, cudaStream_t st) {
 }
 
 int launch_tma(GemvTmaParams &p, bool compat, bool norm, bool swiglu, cudaStream_t st) {
+  p.status = device_status_word();
   int ctas = 0;
   for (int k = 0; k < p.nseg; ++k) ctas += p.seg[k].ncb;
   if (swiglu) ctas = p.seg[0].ncb;

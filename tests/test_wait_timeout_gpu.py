@@ -61,6 +61,47 @@ def test_prefill_state_pass_wait_runs_out():
     assert max_rel_err(S.cpu().numpy(), rS) <= TOL
 
 
+def test_gqa_decode_wait_runs_out():
+    """Split 0 of (sequence 0, kv head 0) withholds its K/V copies: its
+    consumers give up after 2 ms, the split contributes nothing, the status
+    word says so, and every counter is left consistent -- the next step is
+    exact again."""
+    B, Hq, Hkv, D, cap = 2, 8, 2, 256, 700
+    rng = np.random.RandomState(9)
+    dev = torch.device("cuda:0")
+    Tt = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    K = Tt(rng.randn(B, Hkv, cap, D).astype(np.float32))
+    V = Tt(rng.randn(B, Hkv, cap, D).astype(np.float32))
+    lens = torch.tensor([500, 37], dtype=torch.int32, device=dev)
+    w0 = torch.zeros(D, device=dev)
+    ws = q35attn.GqaWorkspace(B, Hq, Hkv, cap, device=dev)
+
+    def inputs():
+        qg = rng.randn(B, Hq, 2 * D).astype(np.float32)
+        kn = rng.randn(B, Hkv, D).astype(np.float32)
+        vn = rng.randn(B, Hkv, D).astype(np.float32)
+        cos, sin = oracle.rope_tables(lens.cpu().numpy().astype(np.int64), rot=64, theta=1e7)
+        return qg, kn, vn, cos, sin
+
+    qg, kn, vn, cos, sin = inputs()
+    _arm(SITE_GQA_DECODE)
+    q35attn.gqa_decode(Tt(qg), Tt(kn), Tt(vn), w0, w0, Tt(cos), Tt(sin), K, V, lens, workspace=ws)
+    torch.cuda.synchronize()  # the call returned: nothing is left waiting
+    assert ws.status(clear=True) & WAIT_TIMEOUT
+    assert lens.cpu().tolist() == [501, 38]
+
+    # the next step runs normally and matches the oracle on the state the GPU holds
+    qg, kn, vn, cos, sin = inputs()
+    Kh, Vh, lh = K.cpu().numpy(), V.cpu().numpy(), lens.cpu().numpy()
+    out = q35attn.gqa_decode(Tt(qg), Tt(kn), Tt(vn), w0, w0, Tt(cos), Tt(sin), K, V, lens, workspace=ws)
+    ref, _, _, lr = oracle.gqa_decode(qg, kn, vn, np.zeros(D, np.float32), np.zeros(D, np.float32), cos, sin, Kh,
+                                      Vh, lh)
+    torch.cuda.synchronize()
+    assert ws.status() == 0
+    assert max_rel_err(out.cpu().numpy(), ref) <= TOL
+    assert lens.cpu().tolist() == lr.tolist()
+
+
 def test_arm_rejects_unknown_site():
     assert q35attn.load().q35_test_arm_wait_fault(7) == _lib.ERR_INVALID_ARG
     _arm(0)
