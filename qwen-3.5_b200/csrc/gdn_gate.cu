@@ -154,27 +154,41 @@ __global__ void __launch_bounds__(256) gate_prefill_kernel(int N, int in_dim, co
                                                            const float *__restrict__ dt_bias,
                                                            float *__restrict__ beta, float *__restrict__ g) {
   constexpr int O = 2 * H, R = 256 / O, KC = H == 64 ? 64 : 128;
+  constexpr int WP = KC * O / 256, XP = (R * KC + 255) / 256;  // weight / x elements per thread per chunk
   __shared__ float ws[KC][O];
   __shared__ float xs[R][KC];
   pdl_entry();
   const int tid = threadIdx.x, r = tid / O, o = tid % O;
   const int row0 = blockIdx.x * R;
+  // chunk loads go to registers first, all in flight at once, and the next
+  // chunk's are requested before this chunk's products
+  float wr[WP], xr[XP];
+#define Q35_GATE_LOAD(K0)                                                                                          \
+  do {                                                                                                              \
+    _Pragma("unroll") for (int i = 0; i < WP; ++i) {                                                                \
+      const int e = tid + 256 * i, k = (K0) + e / O, c = e % O;                                                     \
+      wr[i] = k < in_dim ? (c < H ? __ldg(wb + (size_t)k * H + c) : __ldg(wa + (size_t)k * H + (c - H))) : 0.0f;    \
+    }                                                                                                               \
+    _Pragma("unroll") for (int i = 0; i < XP; ++i) {                                                                \
+      const int e = tid + 256 * i, rr = e / KC, k = (K0) + e % KC;                                                  \
+      xr[i] = (e < R * KC && row0 + rr < N && k < in_dim) ? __ldg(x + (size_t)(row0 + rr) * in_dim + k) : 0.0f;    \
+    }                                                                                                               \
+  } while (0)
   float acc = 0.0f;
+  Q35_GATE_LOAD(0);
   for (int k0 = 0; k0 < in_dim; k0 += KC) {
-    const int kn = min(KC, in_dim - k0);
-    for (int e = tid; e < kn * O; e += 256) {
-      const int k = e / O, c = e % O;
-      ws[k][c] = c < H ? wb[(size_t)(k0 + k) * H + c] : wa[(size_t)(k0 + k) * H + (c - H)];
-    }
-    for (int e = tid; e < R * kn; e += 256) {
-      const int rr = e / kn, k = e % kn;
-      xs[rr][k] = row0 + rr < N ? x[(size_t)(row0 + rr) * in_dim + k0 + k] : 0.0f;
-    }
+#pragma unroll
+    for (int i = 0; i < WP; ++i) (&ws[0][0])[tid + 256 * i] = wr[i];
+#pragma unroll
+    for (int i = 0; i < XP; ++i)
+      if (tid + 256 * i < R * KC) (&xs[0][0])[tid + 256 * i] = xr[i];
     __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < kn; ++k) acc = fmaf(xs[r][k], ws[k][o], acc);
+    if (k0 + KC < in_dim) Q35_GATE_LOAD(k0 + KC);
+#pragma unroll 16
+    for (int k = 0; k < KC; ++k) acc = fmaf(xs[r][k], ws[k][o], acc);
     __syncthreads();
   }
+#undef Q35_GATE_LOAD
   const int row = row0 + r;
   if (row < N) {
     if (o < H) {
