@@ -762,16 +762,16 @@ def run_extras(dev, reps=3):
 
 def run_single_seq_cp(dev, world, rank, steps=64, warmup=3):
     """BASELINE config 4's single 32K-context sequence decoded across all
-    ranks: GDN heads-parallel, GQA KV length split, NCCL all-gather of the
-    per-rank GQA softmax partials and GDN head outputs (q35attn.parallel).
-    Collective on every rank; the timed steps replay as one CUDA graph that
-    holds the kernels and the all-gathers.  Returns the per-step time (max
-    over ranks)."""
+    ranks: GDN heads-parallel, GQA KV length split; each rank stores its GDN
+    head outputs and GQA softmax partials into every peer's receive buffer
+    and merges what it received (q35attn.PeerExchange, one kernel, bounded
+    flag waits, no collective in the step).  The timed steps replay as one
+    CUDA graph.  Returns the per-step time (max over ranks)."""
     import torch
     import torch.distributed as dist
 
     import q35attn
-    from q35attn.parallel import ShardPlan
+    from q35attn.parallel import PeerExchange, ShardPlan
 
     plan = ShardPlan(world, rank, HK, HV, L0)
     lo, hi = plan.kv_tokens
@@ -804,23 +804,27 @@ def run_single_seq_cp(dev, world, rank, steps=64, warmup=3):
     qg, kn, vn = randn(nst, 1, HQ, 2 * D), randn(nst, 1, HKV, D), randn(nst, 1, HKV, D)
     cs, sn = randn(nst, 1, ROT), randn(nst, 1, ROT)
     part = torch.empty(1, HQ, D + 2, device=dev)
-    parts = torch.empty(world, 1, HQ, D + 2, device=dev)
     out_l = torch.empty(1, hv_l * DK, device=dev)
-    gdn_all = torch.empty(world, 1, hv_l * DK, device=dev)
+    gdn_all = torch.empty(1, world * hv_l * DK, device=dev)
     out = torch.empty(1, HQ * D, device=dev)
     tail = plan.holds_tail
+    # the exchange over peer memory: receive buffers mapped by CUDA IPC (handles gathered once over the group)
+
+    def gather_handles(h):
+        lst = [None] * world
+        dist.all_gather_object(lst, h)
+        return lst
+    xchg = PeerExchange(world, rank, 1, hv_l * DK, HQ, gather_handles)
 
     def step(i):
         q35attn.gdn_decode(x[i], z[i], beta[i], g[i], conv_w, norm_w, cst, S, out_l, num_k_heads=hk_l,
                            num_v_heads=hv_l)
         q35attn.gqa_decode_partial(qg[i], kn[i] if tail else None, vn[i] if tail else None, w0, w0, cs[i], sn[i],
                                    Kc, Vc, lens, part, workspace=ws, max_len=cap)
-        dist.all_gather_into_tensor(parts, part)
-        q35attn.gqa_combine_partials(parts, qg[i], out)
-        dist.all_gather_into_tensor(gdn_all, out_l)
+        xchg(out_l, part, qg[i], gdn_all, out)
 
-    # eager warm-up on a side stream, then the timed steps captured once in a CUDA graph (kernels and the two
-    # NCCL all-gathers per step); every rank captures and replays the same sequence of collectives
+    # eager warm-up on a side stream, then the timed steps captured once in a CUDA graph (three kernels per step:
+    # GDN heads, GQA partial, peer exchange + merge); every rank replays the same number of exchanges
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
@@ -840,13 +844,18 @@ def run_single_seq_cp(dev, world, rank, steps=64, warmup=3):
     gph.replay()
     b.record()
     torch.cuda.synchronize(dev)
-    del gph  # a graph holding NCCL calls is released before the process group goes away
+    del gph
+    status = xchg.status()
     t = torch.tensor([a.elapsed_time(b) / 1000.0 / steps], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     t = float(t.item())
+    xchg.close(barrier=lambda: dist.barrier(device_ids=[dev.index]))
+    if status:
+        raise SystemExit(f"single-sequence exchange reported device status {status}")
     by = gqa_bytes_per_seq(L0 + warmup + steps + steps // 2) + GDN_BYTES_PER_SEQ + GDN_BYTES_SHARED
     return {"us_per_step": t * 1e6, "layer_steps_per_s": 2.0 / t, "alg_bytes_per_step_all_gpus": by,
-            "achieved_gbs_all_gpus": by / t / 1e9, "collectives_per_step": 2,
+            "achieved_gbs_all_gpus": by / t / 1e9, "collectives_per_step": 0,
+            "exchange": "peer-memory stores over NVLink + epoch flags, one kernel per step (q35_cp_exchange)",
             "partitioning": f"GDN heads {HV}/{world} per rank, GQA KV length {L0}/{world} per rank"}
 
 

@@ -333,6 +333,41 @@ int q35_gqa_combine_partials(int32_t batch, int32_t num_q_heads,
                              const float *parts, const float *q_gate,
                              float *out, void *stream);
 
+/* --------------------------------------------------------------------------
+ * Exchange step of one sequence decoded across the GPUs of a node over peer
+ * memory (the single-sequence variant of BASELINE config 4; the reference
+ * runs one device and has no counterpart).  Each rank holds a shard:
+ * GatedDeltaNet value heads (its outputs, n_gdn floats per sequence, are one
+ * slice of out_proj's input, text_modules.rs:651-662) and a length range of
+ * the KV cache (its softmax partials [B, Hq, D+2] from
+ * q35_gqa_decode_partial, text_modules.rs:899-928).  q35_cp_exchange stores
+ * this rank's payload into every peer's receive buffer over NVLink, publishes
+ * a per-step epoch flag, waits (bounded, 1 s) for every peer's flag, and
+ * writes on every rank
+ *   gdn_full [B, world * n_gdn]  the GDN outputs in rank order, and
+ *   gqa_out  [B, Hq * D]         the merged attention output * sigmoid(gate)
+ *                                (gate from q_gate [B, Hq, 2 * D]).
+ * Set-up (not on the hot path): q35_cp_create allocates this rank's receive
+ * buffer and returns its 64-byte CUDA IPC handle; the caller exchanges the
+ * handles (e.g. over its process group) and passes all of them, in rank
+ * order, to q35_cp_connect.  Every rank calls q35_cp_exchange the same number
+ * of times, in the same order; each call is one kernel and allocates nothing,
+ * so the steps can be captured in a CUDA graph.  A wait that gives up sets
+ * Q35_STATUS_WAIT_TIMEOUT (q35_cp_status) and poisons the outputs with NaN. */
+int q35_cp_create(int32_t world, int32_t rank, int32_t batch, int32_t n_gdn,
+                  int32_t num_q_heads, int32_t head_dim, void **ctx_out,
+                  void *ipc_handle_out);
+int q35_cp_connect(void *ctx, const void *ipc_handles);
+int q35_cp_exchange(void *ctx, const float *gdn_local, const float *gqa_part,
+                    const float *q_gate, float *gdn_full, float *gqa_out,
+                    void *stream);
+int q35_cp_status(void *ctx, uint32_t *status_out, int32_t clear, void *stream);
+/* Tear-down: every rank calls q35_cp_disconnect (unmaps the peers' buffers)
+ * with no exchange in flight, the ranks meet at a barrier, then each calls
+ * q35_cp_destroy (frees its own buffer). */
+int q35_cp_disconnect(void *ctx);
+int q35_cp_destroy(void *ctx);
+
 /* q35_gqa_decode for callers that cannot allocate device memory (no entry
  * in the reference: its Burn host always allocates).  Same arguments and
  * semantics minus the workspace: the split-K scratch lives in a fixed 16 MiB
@@ -384,8 +419,9 @@ int q35_device_status(uint32_t *status_out, int32_t clear, void *stream);
  * tensor-core operation already started waited for) without a fault or a
  * hang.  site 1: the q35_gdn_prefill state pass (chunk 1's W operand, needs
  * seq_len > 64); site 2: the q35_gqa_decode producer (the first K tile of the
- * first split); 0 disarms.  Arming is global to the process and consumed by
- * one call. */
+ * first split); site 3: q35_cp_exchange (this rank's arrival flags are not
+ * published, so its own wait runs out); 0 disarms.  Arming is global to the
+ * process and consumed by one call. */
 int q35_test_arm_wait_fault(int32_t site);
 
 /* --------------------------------------------------------------------------

@@ -262,7 +262,7 @@ int q35_device_status(uint32_t *status_out, int32_t clear, void *stream) {
 }
 
 int q35_test_arm_wait_fault(int32_t site) {
-  Q35_REQUIRE(site == kFaultNone || site == kFaultPrefillState || site == kFaultGqaDecode, Q35_ERR_INVALID_ARG,
+  Q35_REQUIRE(site >= kFaultNone && site <= kFaultCpExchange, Q35_ERR_INVALID_ARG,
               "test_arm_wait_fault: unknown site");
   g_fault_site.store(site);
   return Q35_OK;

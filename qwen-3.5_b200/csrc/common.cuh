@@ -147,7 +147,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
 // withholds one asynchronous copy and waits with this short limit, so that a
 // bounded wait runs out and the error path is exercised without a fault.
 constexpr uint64_t kFaultWaitLimitNs = 2000000ull;  // 2 ms
-enum FaultSite : int { kFaultNone = 0, kFaultPrefillState = 1, kFaultGqaDecode = 2 };
+enum FaultSite : int { kFaultNone = 0, kFaultPrefillState = 1, kFaultGqaDecode = 2, kFaultCpExchange = 3 };
 // Returns the armed site once (and disarms it) when it equals `site`.
 bool take_fault(int site);
 

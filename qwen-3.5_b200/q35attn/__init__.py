@@ -10,5 +10,6 @@ from .ops import (GqaPrefillWorkspace, GqaWorkspace, gdn_decode, gdn_gate, gdn_p
                   gdn_prefill_workspace, gqa_combine_partials, gqa_decode, gqa_decode_partial, gqa_prefill, launch_count,
                   q8_gemm, q8_gemm_fused, q8_gemm_workspace, q8_gemv, q8_gemv_fused, device_status,
                   workspace_status)
+from .parallel import PeerExchange  # noqa: F401
 
 __version__ = "0.1.0"

@@ -79,6 +79,12 @@ SIGNATURES = {
     "q35_version": (C.c_char_p, []),
     "q35_launch_count": (C.c_uint64, [_I32]),
     "q35_test_arm_wait_fault": (C.c_int, [_I32]),
+    "q35_cp_create": (C.c_int, [_I32, _I32, _I32, _I32, _I32, _I32, C.POINTER(C.c_void_p), _P]),
+    "q35_cp_connect": (C.c_int, [_P, _P]),
+    "q35_cp_exchange": (C.c_int, [_P, _P, _P, _P, _P, _P, _P]),
+    "q35_cp_status": (C.c_int, [_P, C.POINTER(C.c_uint32), _I32, _P]),
+    "q35_cp_disconnect": (C.c_int, [_P]),
+    "q35_cp_destroy": (C.c_int, [_P]),
     "q35_device_status": (C.c_int, [C.POINTER(C.c_uint32), _I32, _P]),
     "q35_q8_gemm_workspace_size": (_SZ, [_I32, _I32]),
     "q35_q8_gemm": (C.c_int, [_I32, _I32, _I32, _P, _P, _P, _P, _P, _SZ, _P]),

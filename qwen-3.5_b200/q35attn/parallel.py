@@ -14,7 +14,10 @@ single-sequence variant).
 
 The compute and the collective are injected, so the same orchestration runs
 with the CUDA kernels over NCCL and, in the CPU tests, with a numpy stand-in
-over gloo.
+over gloo.  On the GPUs the two gathers and the merge are one kernel,
+q35_cp_exchange (PeerExchange below): each rank stores its GDN outputs and
+partials straight into every peer's receive buffer over NVLink, publishes an
+epoch flag, waits (bounded) for every rank's flag and merges locally.
 """
 from __future__ import annotations
 
@@ -84,3 +87,70 @@ def decode_step(plan: ShardPlan, gdn_local, gqa_partial, all_gather, combine):
     g_all = all_gather(g_local)
     p_all = all_gather(p_local)
     return g_all, combine(p_all)
+
+
+class PeerExchange:
+    """The exchange step over peer memory (q35_cp_exchange): this rank's GDN
+    head outputs and GQA softmax partials go straight into every peer's
+    receive buffer over NVLink, and every rank merges them locally -- one
+    kernel per step, no collective.  Set-up exchanges the buffers' CUDA IPC
+    handles through `gather_handles` (a callable mapping this rank's 64-byte
+    handle to the list of every rank's, in rank order)."""
+
+    def __init__(self, world, rank, batch, n_gdn, num_q_heads, gather_handles, head_dim=256):
+        import ctypes as C
+
+        from . import _lib
+        self._lib = _lib.load()
+        self._C = C
+        ctx = C.c_void_p()
+        handle = (C.c_ubyte * 64)()
+        _lib.check(self._lib.q35_cp_create(world, rank, batch, n_gdn, num_q_heads, head_dim, C.byref(ctx), handle))
+        self.ctx = ctx
+        self.world, self.batch, self.n_gdn, self.hq = world, batch, n_gdn, num_q_heads
+        handles = gather_handles(bytes(handle))
+        if len(handles) != world or any(len(h) != 64 for h in handles):
+            raise ValueError("gather_handles must return one 64-byte handle per rank")
+        buf = (C.c_ubyte * (64 * world)).from_buffer_copy(b"".join(handles))
+        _lib.check(self._lib.q35_cp_connect(self.ctx, buf))
+
+    def __call__(self, gdn_local, gqa_part, q_gate, gdn_full, gqa_out, stream=None):
+        import torch
+
+        from . import _lib
+        st = torch.cuda.current_stream().cuda_stream if stream is None else int(stream)
+        B, G, H = self.batch, self.n_gdn, self.hq
+        for t, n, name in ((gdn_local, B * G, "gdn_local"), (gdn_full, B * G * self.world, "gdn_full"),
+                           (gqa_part, B * H * 258, "gqa_part"), (q_gate, B * H * 512, "q_gate"),
+                           (gqa_out, B * H * 256, "gqa_out")):
+            if t is None:
+                if G == 0 and name.startswith("gdn"):
+                    continue
+                raise ValueError(f"{name} is None")
+            if t.dtype != torch.float32 or not t.is_contiguous() or t.numel() != n or not t.is_cuda:
+                raise ValueError(f"{name}: contiguous float32 CUDA tensor of {n} elements expected")
+        ptr = lambda t: None if t is None else t.data_ptr()
+        _lib.check(self._lib.q35_cp_exchange(self.ctx, ptr(gdn_local), ptr(gqa_part), ptr(q_gate), ptr(gdn_full),
+                                             ptr(gqa_out), st))
+        return gdn_full, gqa_out
+
+    def status(self, clear=False):
+        import torch
+
+        from . import _lib
+        v = self._C.c_uint32(0)
+        _lib.check(self._lib.q35_cp_status(self.ctx, self._C.byref(v), int(clear),
+                                           torch.cuda.current_stream().cuda_stream))
+        return int(v.value)
+
+    def close(self, barrier=None):
+        """Unmap the peers' buffers, meet the other ranks at `barrier` (none
+        may still use ours), then free this rank's buffer."""
+        if self.ctx is not None:
+            import torch
+            torch.cuda.synchronize()  # no exchange of this rank is still in flight
+            self._lib.q35_cp_disconnect(self.ctx)
+            if barrier is not None:
+                barrier()
+            self._lib.q35_cp_destroy(self.ctx)
+            self.ctx = None
