@@ -46,6 +46,7 @@ CONV = 2 * HK * DK + HV * DK  # 6144
 KCONV = 4
 HQ, HKV, D, ROT = 8, 2, 256, 64
 L0 = 32768
+L2_BYTES = 126 << 20  # B200 L2
 THETA = 1e7
 
 GDN_BYTES_PER_SEQ = (2 * HV * DK * DK * 4          # state read + write
@@ -493,6 +494,7 @@ def run_gpu(args):
     if rank == 0 and world == 1 and not args.no_extras:
         del x, z, g, beta, qg, kn, vn
         extras = run_extras(dev)
+        extras["single_seq_context_parallel"] = run_single_seq_cp(dev, 1, 0)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -761,12 +763,18 @@ def run_extras(dev, reps=3):
 
 
 def run_single_seq_cp(dev, world, rank, steps=64, warmup=3):
-    """BASELINE config 4's single 32K-context sequence decoded across all
-    ranks: GDN heads-parallel, GQA KV length split; each rank stores its GDN
-    head outputs and GQA softmax partials into every peer's receive buffer
-    and merges what it received (q35attn.PeerExchange, one kernel, bounded
-    flag waits, no collective in the step).  The timed steps replay as one
-    CUDA graph.  Returns the per-step time (max over ranks)."""
+    """BASELINE config 4's single 32K-context sequence, one decode step of a
+    GDN layer and a GQA layer, across all ranks: GDN heads-parallel, GQA KV
+    length split; each rank stores its GDN head outputs and GQA softmax
+    partials into every peer's receive buffer and merges what it received
+    (q35attn.PeerExchange, one kernel, bounded waits, no collective in the
+    step).  With one rank the same step is the single-GPU path (all heads,
+    q35_gqa_decode over the whole cache, no exchange) -- the figure the
+    multi-GPU ones are compared with.  Consecutive steps rotate over several
+    independent sequences, each a full 32K context sharded the same way, so
+    that what one step reads was last read more than an L2 (126 MB) ago.  The
+    timed steps replay as one CUDA graph.  Returns the per-step time (max over
+    ranks)."""
     import torch
     import torch.distributed as dist
 
@@ -776,8 +784,11 @@ def run_single_seq_cp(dev, world, rank, steps=64, warmup=3):
     plan = ShardPlan(world, rank, HK, HV, L0)
     lo, hi = plan.kv_tokens
     n_loc = hi - lo
-    # the tail rank appends one key per step: the eager warm-up steps plus a warm and a timed graph replay
-    cap = n_loc + (warmup + 2 * steps + 2 if plan.holds_tail else 0) + 1
+    tail = plan.holds_tail
+    shard_bytes = 2 * HKV * n_loc * D * 4
+    nring = max(1, -(-(2 * L2_BYTES) // shard_bytes))
+    # the tail rank appends one key per step of a sequence: the eager warm-up steps plus a warm and a timed replay
+    cap = n_loc + (-(-(warmup + 2 * steps) // nring) + 2 if tail else 0) + 1
     gen = torch.Generator(device=dev)
     gen.manual_seed(777 + rank)
 
@@ -786,14 +797,14 @@ def run_single_seq_cp(dev, world, rank, steps=64, warmup=3):
         t.normal_(0.0, scale, generator=gen)
         return t
 
-    Kc, Vc = randn(1, HKV, cap, D), randn(1, HKV, cap, D)
-    lens = torch.full((1,), n_loc, dtype=torch.int32, device=dev)
-    ws = q35attn.GqaWorkspace(1, HQ, HKV, cap, device=dev)
-    hk_l = HK // world
-    hv_l = HV // world
+    hk_l, hv_l = HK // world, HV // world
     c_loc = 2 * hk_l * DK + hv_l * DK
-    S = randn(1, hv_l, DK, DK, scale=0.02)
-    cst = randn(1, c_loc, KCONV - 1, scale=0.5)
+    seqs = []
+    for _ in range(nring):
+        seqs.append(dict(K=randn(1, HKV, cap, D), V=randn(1, HKV, cap, D),
+                         lens=torch.full((1,), n_loc, dtype=torch.int32, device=dev),
+                         S=randn(1, hv_l, DK, DK, scale=0.02), cst=randn(1, c_loc, KCONV - 1, scale=0.5)))
+    ws = q35attn.GqaWorkspace(1, HQ, HKV, cap, device=dev)
     conv_w = randn(c_loc, KCONV, scale=0.5)
     norm_w = torch.ones(DK, device=dev)
     w0 = torch.zeros(D, device=dev)
@@ -807,56 +818,75 @@ def run_single_seq_cp(dev, world, rank, steps=64, warmup=3):
     out_l = torch.empty(1, hv_l * DK, device=dev)
     gdn_all = torch.empty(1, world * hv_l * DK, device=dev)
     out = torch.empty(1, HQ * D, device=dev)
-    tail = plan.holds_tail
-    # the exchange over peer memory: receive buffers mapped by CUDA IPC (handles gathered once over the group)
-
-    def gather_handles(h):
-        lst = [None] * world
-        dist.all_gather_object(lst, h)
-        return lst
-    xchg = PeerExchange(world, rank, 1, hv_l * DK, HQ, gather_handles)
+    xchg = None
+    if world > 1:
+        # receive buffers mapped by CUDA IPC (handles gathered once over the group)
+        def gather_handles(h):
+            lst = [None] * world
+            dist.all_gather_object(lst, h)
+            return lst
+        xchg = PeerExchange(world, rank, 1, hv_l * DK, HQ, gather_handles)
 
     def step(i):
-        q35attn.gdn_decode(x[i], z[i], beta[i], g[i], conv_w, norm_w, cst, S, out_l, num_k_heads=hk_l,
+        sq = seqs[i % nring]
+        q35attn.gdn_decode(x[i], z[i], beta[i], g[i], conv_w, norm_w, sq["cst"], sq["S"], out_l, num_k_heads=hk_l,
                            num_v_heads=hv_l)
+        if xchg is None:
+            q35attn.gqa_decode(qg[i], kn[i], vn[i], w0, w0, cs[i], sn[i], sq["K"], sq["V"], sq["lens"], out,
+                               workspace=ws, max_len=cap)
+            return
         q35attn.gqa_decode_partial(qg[i], kn[i] if tail else None, vn[i] if tail else None, w0, w0, cs[i], sn[i],
-                                   Kc, Vc, lens, part, workspace=ws, max_len=cap)
+                                   sq["K"], sq["V"], sq["lens"], part, workspace=ws, max_len=cap)
         xchg(out_l, part, qg[i], gdn_all, out)
 
-    # eager warm-up on a side stream, then the timed steps captured once in a CUDA graph (three kernels per step:
-    # GDN heads, GQA partial, peer exchange + merge); every rank replays the same number of exchanges
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+
+    # eager warm-up on a side stream, then the timed steps captured once in a CUDA graph (with an exchange: GDN
+    # heads, GQA partial and its split combine, peer exchange + merge); every rank replays the same exchanges
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
         for i in range(warmup):
             step(i)
     torch.cuda.synchronize(dev)
-    dist.barrier(device_ids=[dev.index])
+    barrier()
     gph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gph, stream=side):
         for i in range(warmup, nst):
             step(i)
     gph.replay()
     torch.cuda.synchronize(dev)
-    dist.barrier(device_ids=[dev.index])
+    barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     gph.replay()
     b.record()
     torch.cuda.synchronize(dev)
     del gph
-    status = xchg.status()
-    t = torch.tensor([a.elapsed_time(b) / 1000.0 / steps], device=dev, dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    t = float(t.item())
-    xchg.close(barrier=lambda: dist.barrier(device_ids=[dev.index]))
+    status = (xchg.status() if xchg is not None else 0) | ws.status()
+    t = a.elapsed_time(b) / 1000.0 / steps
+    if world > 1:
+        tt = torch.tensor([t], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+        xchg.close(barrier=barrier)
     if status:
-        raise SystemExit(f"single-sequence exchange reported device status {status}")
-    by = gqa_bytes_per_seq(L0 + warmup + steps + steps // 2) + GDN_BYTES_PER_SEQ + GDN_BYTES_SHARED
-    return {"us_per_step": t * 1e6, "layer_steps_per_s": 2.0 / t, "alg_bytes_per_step_all_gpus": by,
-            "achieved_gbs_all_gpus": by / t / 1e9, "collectives_per_step": 0,
-            "exchange": "peer-memory stores over NVLink + epoch flags, one kernel per step (q35_cp_exchange)",
-            "partitioning": f"GDN heads {HV}/{world} per rank, GQA KV length {L0}/{world} per rank"}
+        raise SystemExit(f"single-sequence step reported device status {status}")
+    if not (torch.isfinite(out).all() and torch.isfinite(gdn_all if world > 1 else out_l).all()):
+        raise SystemExit("single-sequence step: non-finite outputs")
+    by = gqa_bytes_per_seq(L0 + (warmup + steps + steps // 2) // nring) + GDN_BYTES_PER_SEQ + GDN_BYTES_SHARED
+    res = {"us_per_step": t * 1e6, "layer_steps_per_s": 2.0 / t, "alg_bytes_per_step_all_gpus": by,
+           "achieved_gbs_all_gpus": by / t / 1e9, "sequences_rotated": nring,
+           "l2": f"{nring} sequences of {shard_bytes / 1e6:.1f} MB KV per GPU rotated (> 2 x 126 MB L2)"}
+    if world > 1:
+        res.update({"collectives_per_step": 0,
+                    "exchange": "epoch-tagged peer-memory stores over NVLink, one kernel per step (q35_cp_exchange)",
+                    "partitioning": f"GDN heads {HV}/{world} per rank, GQA KV length {L0}/{world} per rank"})
+    else:
+        res["path"] = "one GPU: GDN decode (all heads) + q35_gqa_decode over the whole cache"
+    return res
 
 
 def main():

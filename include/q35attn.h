@@ -341,8 +341,9 @@ int q35_gqa_combine_partials(int32_t batch, int32_t num_q_heads,
  * slice of out_proj's input, text_modules.rs:651-662) and a length range of
  * the KV cache (its softmax partials [B, Hq, D+2] from
  * q35_gqa_decode_partial, text_modules.rs:899-928).  q35_cp_exchange stores
- * this rank's payload into every peer's receive buffer over NVLink, publishes
- * a per-step epoch flag, waits (bounded, 1 s) for every peer's flag, and
+ * this rank's payload into every peer's receive buffer over NVLink, each
+ * value in an 8-byte word tagged with the step's epoch, polls (bounded, 1 s)
+ * its own buffer until every rank's words of the step are there, and
  * writes on every rank
  *   gdn_full [B, world * n_gdn]  the GDN outputs in rank order, and
  *   gqa_out  [B, Hq * D]         the merged attention output * sigmoid(gate)
@@ -352,7 +353,8 @@ int q35_gqa_combine_partials(int32_t batch, int32_t num_q_heads,
  * handles (e.g. over its process group) and passes all of them, in rank
  * order, to q35_cp_connect.  Every rank calls q35_cp_exchange the same number
  * of times, in the same order; each call is one kernel and allocates nothing,
- * so the steps can be captured in a CUDA graph.  A wait that gives up sets
+ * so the steps can be captured in a CUDA graph.  n_gdn must be even and
+ * every buffer 8-byte aligned.  A wait that gives up sets
  * Q35_STATUS_WAIT_TIMEOUT (q35_cp_status) and poisons the outputs with NaN. */
 int q35_cp_create(int32_t world, int32_t rank, int32_t batch, int32_t n_gdn,
                   int32_t num_q_heads, int32_t head_dim, void **ctx_out,
@@ -419,8 +421,8 @@ int q35_device_status(uint32_t *status_out, int32_t clear, void *stream);
  * tensor-core operation already started waited for) without a fault or a
  * hang.  site 1: the q35_gdn_prefill state pass (chunk 1's W operand, needs
  * seq_len > 64); site 2: the q35_gqa_decode producer (the first K tile of the
- * first split); site 3: q35_cp_exchange (this rank's arrival flags are not
- * published, so its own wait runs out); 0 disarms.  Arming is global to the
+ * first split); site 3: q35_cp_exchange (this rank stores none of its
+ * words, so its own waits run out); 0 disarms.  Arming is global to the
  * process and consumed by one call. */
 int q35_test_arm_wait_fault(int32_t site);
 
