@@ -271,6 +271,12 @@ __device__ __forceinline__ void pdl_entry() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// L2 prefetch of `bytes` (a multiple of 16) from a 16-byte aligned global
+// address; no completion to wait for.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Thread-block cluster helpers (DSMEM).
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -197,7 +197,6 @@ __device__ __forceinline__ void merge_partials(const GqaParams &p, const float *
 
 template <int G>
 __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(const GqaParams p) {
-  pdl_entry();
   constexpr int V = kKPW * G;  // (key, head) dots per warp per stage
   constexpr int LOGV = V == 1 ? 0 : V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : V == 16 ? 4 : 5;
   static_assert((1 << LOGV) == V && V <= 32, "V must be a power of two <= 32");
@@ -211,6 +210,33 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
 
   const int s = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const size_t pair = (size_t)b * p.Hkv + kvh;
+  float *Kc = p.k_cache + pair * (size_t)p.cap * kD;
+  float *Vc = p.v_cache + pair * (size_t)p.cap * kD;
+
+  // Before the grid-dependency wait, only what no earlier kernel writes: the
+  // ring barriers, and (few-sequence schedule, where this grid is launched
+  // while the previous kernel drains) an L2 prefetch of the first ring's worth
+  // of this split's cached keys and values.  Positions at or beyond lens[b]
+  // may be fetched too (lens is not read yet); they stay inside the cache.
+  if (tid == 0) {
+    for (int i = 0; i < kNS; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], kNW);
+    }
+    fence_mbar_init();
+  }
+  if (!p.tree && warp == kNW && lane == 0) {
+    const long long k0 = (long long)s * p.kps;
+    const long long k1 = min(min(k0 + kNS * kTK, k0 + p.kps), p.cap);
+    if (k1 > k0) {
+      const uint32_t bytes = (uint32_t)(k1 - k0) * kD * sizeof(float);
+      bulk_prefetch_l2(Kc + k0 * kD, bytes);
+      bulk_prefetch_l2(Vc + k0 * kD, bytes);
+    }
+  }
+  __syncthreads();
+  pdl_entry();
 
   const int len = p.lens[b];
   const bool append = p.k_new != nullptr;  // false: attend the cached keys only (context-parallel shard)
@@ -226,18 +252,6 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_kernel(
   const int kend = min(kbeg + p.kps, L);
   const int nkeys = max(kend - kbeg, 0);
   const int ntiles = (nkeys + kTK - 1) / kTK;
-  const size_t pair = (size_t)b * p.Hkv + kvh;
-  float *Kc = p.k_cache + pair * (size_t)p.cap * kD;
-  float *Vc = p.v_cache + pair * (size_t)p.cap * kD;
-
-  if (tid == 0) {
-    for (int i = 0; i < kNS; ++i) {
-      mbar_init(&full_bar[i], 1);
-      mbar_init(&empty_bar[i], kNW);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
 
   if (warp == kNW) {
     // ---------------------------------------------------------- producer
