@@ -214,3 +214,72 @@ def test_known_answer_equal_scores():
     out = q35attn.gqa_decode(qg, kn, vn, w, w, cos, sin, Kc, Vc, lens, workspace=ws)
     assert torch.allclose(out, torch.full_like(out, 64.0), atol=1e-3)
     assert int(lens.item()) == 2 and float(Kc[0, 0, 1, 1]) == pytest.approx(16.0, rel=1e-5)
+
+
+def _ragged_many(B, Hq, Hkv, cap, lens0, sample, steps, seed, arm_first=False):
+    """Many sequences of ragged length on the even-range schedule; the sampled
+    sequences are followed by the oracle, every sequence's lens is checked."""
+    D = 256
+    dev = torch.device("cuda:0")
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    Kc = torch.empty(B, Hkv, cap, D, device=dev)
+    Vc = torch.empty(B, Hkv, cap, D, device=dev)
+    Kc.normal_(generator=gen)
+    Vc.normal_(generator=gen)
+    lens = torch.from_numpy(lens0.astype(np.int32)).to(dev)
+    oK, oV = Kc[sample].cpu().numpy(), Vc[sample].cpu().numpy()
+    olens = lens0[sample].astype(np.int32)
+    for i, b in enumerate(sample):  # the oracle sees only each sequence's own keys
+        oK[i, :, olens[i]:] = 0
+        oV[i, :, olens[i]:] = 0
+    w = (0.1 * np.random.RandomState(seed).randn(D)).astype(np.float32)
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    ws = q35attn.GqaWorkspace(B, Hq, Hkv, cap)
+    rng = np.random.RandomState(seed + 1)
+    errs = []
+    for t in range(steps):
+        qg = rng.randn(B, Hq, 2 * D).astype(np.float32)
+        kn = rng.randn(B, Hkv, D).astype(np.float32)
+        vn = rng.randn(B, Hkv, D).astype(np.float32)
+        cos, sin = rope(lens0 + t)
+        if arm_first and t == 0:
+            from q35attn import _lib
+            _lib.check(q35attn.load().q35_test_arm_wait_fault(2))
+        out = q35attn.gqa_decode(T(qg), T(kn), T(vn), T(w), T(w), T(cos), T(sin), Kc, Vc, lens,
+                                 workspace=ws).cpu().numpy()
+        ref, oK, oV, olens = oracle.gqa_decode(qg[sample], kn[sample], vn[sample], w, w, cos[sample], sin[sample],
+                                               oK, oV, olens)
+        if arm_first and t == 0:
+            assert ws.status(clear=True) & q35attn.STATUS_WAIT_TIMEOUT
+        else:
+            errs.append(max_rel_err(out[sample], ref))
+    assert ws.status() == 0
+    np.testing.assert_array_equal(lens.cpu().numpy(), lens0 + steps)
+    return max(errs)
+
+
+def test_many_ragged_sequences_even_ranges():
+    """256 sequences of ragged length (1 to 9,200 cached keys, some only a
+    few keys long) at a length hint that selects the even-range schedule: key
+    ranges start and end inside pairs, short pairs lie wholly inside a range,
+    long ones are shared by several CTAs."""
+    B, Hq, Hkv, cap = 256, 8, 2, 9300
+    rng = np.random.RandomState(31)
+    lens0 = rng.randint(1, 9200, size=B)
+    lens0[:8] = [1, 2, 15, 16, 17, 9199, 2048, 2049]
+    sample = np.array([0, 1, 2, 3, 4, 5, 6, 7, 100, 255])
+    err = _ragged_many(B, Hq, Hkv, cap, lens0, sample, 3, seed=32)
+    assert err <= TOL
+
+
+def test_even_ranges_wait_runs_out_then_recovers():
+    """The even-range schedule's first CTA withholds its copies (test hook):
+    the step reports Q35_STATUS_WAIT_TIMEOUT, every sequence still advances
+    (its new key is in the cache), and the next step matches the oracle."""
+    B, Hq, Hkv, cap = 256, 8, 2, 9300
+    rng = np.random.RandomState(41)
+    lens0 = rng.randint(1, 9200, size=B)
+    sample = np.array([0, 1, 128, 255])
+    err = _ragged_many(B, Hq, Hkv, cap, lens0, sample, 2, seed=42, arm_first=True)
+    assert err <= TOL
