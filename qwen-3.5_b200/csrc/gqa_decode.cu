@@ -1020,7 +1020,7 @@ int gqa_keys_per_split(int B, int Hkv, long long max_len, int sms) {
   if (pairs * ((max_len + long_kps - 1) / long_kps) >= 8 * slots) return (int)long_kps;
   long long per = (max_len * pairs + slots - 1) / slots;
   per = (per + kTK - 1) / kTK * kTK;
-  if (per < 4 * kTK) per = 4 * kTK;
+  if (per < 2 * kTK) per = 2 * kTK;  // 2 tiles: both in flight at once (config 1: 13.2 -> 13.0 us per step)
   if (per > long_kps) per = long_kps;
   return (int)per;
 }
