@@ -21,7 +21,8 @@
 //      they carry the epoch, then merges: the flash-decode combine of every
 //      rank's partial, times sigmoid(gate), and the GDN outputs in rank order.
 // No CTA waits for another CTA of its own grid: the work is spread so that a
-// thread has about one pair of values to send and one to receive.
+// thread has about one (pair of values, destination) to send and one pair to
+// receive.
 // The receive buffer has two halves selected by the epoch's parity: a rank can
 // only start step e+1 after it read every rank's step-e words, and every rank
 // wrote those only after finishing step e-1, so the half of step e-1 that a
@@ -126,12 +127,11 @@ __global__ void __launch_bounds__(kCpThreads) cp_exchange_kernel(const CpParams 
     const float2 *q2 = reinterpret_cast<const float2 *>(p.gqa_part);
     const long long ng2 = ng >> 1, n2 = (ng + np) >> 1;
     const long long slot = ((long long)half * p.world + p.rank) * pay;
-    for (long long i = gt; i < n2; i += nthr) {
+    for (long long j = gt; j < n2 * p.world; j += nthr) {  // one (pair, destination) per thread step
+      const long long i = j % n2;
+      const int r = (p.rank + 1 + (int)(j / n2)) % p.world;  // peers first, this rank's own slot last
       const float2 v = i < ng2 ? g2[i] : q2[i - ng2];
-      for (int k = 0; k < p.world; ++k) {
-        const int r = (p.rank + 1 + k) % p.world;  // peers first, this rank's own slot last
-        st_words2(p.peer_data[r] + slot + 2 * i, v, epoch);
-      }
+      st_words2(p.peer_data[r] + slot + 2 * i, v, epoch);
     }
   }
   // 2. receive from this rank's own buffer as the words arrive: first the
@@ -212,8 +212,8 @@ int q35_cp_create(int32_t world, int32_t rank, int32_t batch, int32_t n_gdn, int
   c->hq = num_q_heads;
   c->payload = (size_t)batch * n_gdn + (size_t)batch * num_q_heads * (kD + 2);
   {
-    // about one pair of values per thread to send and to receive
-    const long long pairs = std::max<long long>((long long)c->payload / 2,
+    // about one pair of values per thread to send (to every rank) and to receive
+    const long long pairs = std::max<long long>((long long)c->payload / 2 * world,
                                                 (long long)batch * num_q_heads * (kD / 2) +
                                                     (long long)batch * world * n_gdn / 2);
     c->blocks = (int)std::min<long long>(kCpMaxBlocks, std::max<long long>(1, (pairs + kCpThreads - 1) / kCpThreads));
