@@ -44,9 +44,6 @@ constexpr int kNS = 3;            // pipeline stages
 constexpr int kKPW = kTK / kNW;   // keys per consumer warp per stage
 constexpr int kFanIn = 8;         // partials merged per node of the combine tree
 
-// CTAs of the even-range schedule: one resident wave.
-inline int gqa_sk_ctas(int G, int sms) { return (G <= 4 ? 2 : 1) * sms; }
-
 struct GqaParams {
   const float *q_gate, *k_new, *v_new, *qn_w, *kn_w, *cos, *sin;
   float *k_cache, *v_cache;
@@ -61,13 +58,10 @@ struct GqaParams {
   uint32_t *pair_cnt;  // [B * Hkv]
   uint32_t *seq_cnt;   // [B]
   int32_t *lsnap;      // [B]: keys attended this step (-1: the step was refused), for the split combine
-  uint32_t *done;      // even-range schedule: CTAs finished this step (the last one advances lens)
   uint32_t *status;
   long long cap;
   int B, Hq, Hkv, rot, nsplit, kps, ngroups;
   int tree;  // 1: merge the splits in-kernel (ticket tree); 0: gqa_split_combine_kernel does
-  int sk;    // 1 (with tree): key ranges of gqa_decode_sk_kernel
-  int sk_nb, sk_ns;  // its long and short units (CTAs)
   int fault;  // test hook: CTA (0, 0, 0) issues none of its copies, so its waits run out
   uint64_t wait_ns;  // limit of every bounded wait
   float eps, qscale_log2;
@@ -595,390 +589,8 @@ __global__ void gqa_combine_kernel(int B, int Hq, int n_parts, const float *__re
   out[(size_t)bh * kD + d] = (O / Ls) * sigmoidf_dev(gate);
 }
 
-
-// ---------------------------------------------------------------------------
-// Many-sequence schedule over key ranges.  The keys of every (sequence, kv
-// head) pair of the step are laid end to end (pair order b-major) and cut into
-// units: long ones first (about 2048 keys each at the length hint), then three
-// waves of short ones (256 keys).  The hardware hands units to free SM slots in
-// grid order, so a CTA that streams slower than others (their rates differ by
-// about 15 % on B200) just takes fewer units, and the work still left when the
-// first SMs fall idle is short: no partial last wave of long splits.  A range
-// covers the end of one pair, whole pairs and the start of another; the CTA
-// walks them as segments through one continuous K/V ring.  Per segment the
-// CTA's warps are merged (the ring, drained, is the scratch), and the result
-// is either final (the pair lies inside this range) or one piece of the pair;
-// the last piece of a pair to arrive (atomic ticket, no spin-wait) merges the
-// pair's pieces, held at consecutive slots unit rank + pair, and writes the
-// output.  Every CTA reads lens at its start; the last CTA of the grid to
-// finish (a second ticket) advances lens, so no CTA sees a length of the next
-// step.
-constexpr int kSkMaxPairs = 512;
-constexpr int kSkTailKeys = 256;  // keys per unit of the short tail
-
-template <int G>
-__global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1)) gqa_decode_sk_kernel(const GqaParams p) {
-  constexpr int V = kKPW * G;  // (key, head) dots per warp per stage
-  constexpr int LOGV = V == 1 ? 0 : V == 2 ? 1 : V == 4 ? 2 : V == 8 ? 3 : V == 16 ? 4 : 5;
-  static_assert((1 << LOGV) == V && V <= 32, "V must be a power of two <= 32");
-
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  GqaSmem &sm = *reinterpret_cast<GqaSmem *>(smem_raw);
-  __shared__ __align__(16) float q_s[G][kD];
-  __shared__ __align__(16) float tmp_s[kNW + 1][kD];
-  __shared__ __align__(8) uint64_t full_bar[kNS], empty_bar[kNS];
-  __shared__ int pre_s[kSkMaxPairs + 1];  // prefix sums of the pairs' key counts
-  __shared__ int flag_s, fail_s;
-
-  const int c = blockIdx.x, P = gridDim.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int pairs = p.B * p.Hkv;
-  const bool append = p.k_new != nullptr;
-  const int cap_keys = p.nsplit * p.kps;  // the caller's length hint, rounded up to whole splits
-
-  if (tid == 0) {
-    for (int i = 0; i < kNS; ++i) {
-      mbar_init(&full_bar[i], 1);
-      mbar_init(&empty_bar[i], kNW);
-    }
-    fence_mbar_init();
-    fail_s = 0;
-  }
-  __syncthreads();
-  pdl_entry();
-
-  // keys of every pair this step (a refused sequence has none)
-  for (int b = tid; b < p.B; b += kThreads) {
-    const int len = p.lens[b];
-    const int L = append ? len + 1 : len;
-    const bool full = append && len >= p.cap, over = !full && L > cap_keys;
-    if (c == 0) {
-      if (full) atomicOr(p.status, Q35_STATUS_CACHE_FULL);
-      if (over) atomicOr(p.status, Q35_STATUS_LEN_HINT);
-      if (!(full || over) && L == 0 && p.part_out != nullptr)  // an empty shard: the neutral partial
-        for (int i = 0; i < p.Hkv * G; ++i) {
-          float *dst = p.part_out + ((size_t)b * p.Hq + i) * (kD + 2);
-          for (int d = 0; d < kD; ++d) dst[d] = 0.0f;
-          dst[kD] = -INFINITY;
-          dst[kD + 1] = 0.0f;
-        }
-    }
-    for (int h = 0; h < p.Hkv; ++h) pre_s[1 + b * p.Hkv + h] = (full || over) ? 0 : L;
-  }
-  __syncthreads();
-  if (warp == 0) {  // inclusive scan: each lane one contiguous block, then a warp scan of the block sums
-    const int per = (pairs + 31) / 32;
-    const int lo = 1 + lane * per, hi = min(lo + per, pairs + 1);
-    int sum = 0;
-    for (int i = lo; i < hi; ++i) sum += pre_s[i];
-    int incl = sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    int run = incl - sum;
-    for (int i = lo; i < hi; ++i) {
-      run += pre_s[i];
-      pre_s[i] = run;
-    }
-    if (lane == 0) pre_s[0] = 0;
-  }
-  __syncthreads();
-
-  // Units: the first sk_nb CTAs split the keys before Ts from the end evenly
-  // (about 2048 keys each at the length hint), the last sk_ns CTAs split the
-  // final Ts = min(T, sk_ns * kSkTailKeys) keys evenly, so the units the
-  // hardware dispatches last are short.  Units without keys (when the step
-  // has fewer keys than the hint) are skipped; the others are ranked
-  // contiguously, and rank r + pair indexes a piece.
-  const long long T = pre_s[pairs];
-  const long long Ts = min(T, (long long)p.sk_ns * kSkTailKeys), Tb = T - Ts;
-  const long long nbe = min((long long)p.sk_nb, Tb), nse = min((long long)p.sk_ns, Ts);
-  long long rank = -1;
-  if (c < p.sk_nb) {
-    if (c < nbe) rank = c;
-  } else if (c - p.sk_nb < nse) {
-    rank = nbe + (c - p.sk_nb);
-  }
-  auto start_of = [&](long long r) {
-    return r < nbe ? r * Tb / nbe : Tb + (r - nbe) * Ts / nse;
-  };
-  const long long s0 = rank >= 0 ? start_of(rank) : T, s1 = rank >= 0 ? start_of(rank + 1) : T;
-  auto cta_of = [&](long long k) {  // the rank of the unit whose range holds key k
-    return k < Tb ? ((k + 1) * nbe + Tb - 1) / Tb - 1 : nbe + ((k - Tb + 1) * nse + Ts - 1) / Ts - 1;
-  };
-  int pr = 0;
-  {
-    int lo = 0, hi = pairs;  // first pair whose keys end after s0
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (pre_s[mid + 1] > s0) hi = mid; else lo = mid + 1;
-    }
-    pr = lo;
-  }
-  float *scratch = &sm.k[0][0][0];  // [NW][G][D] + [NW][G][2], or merge_partials' scratch
-  uint32_t gt0 = 0;                 // ring tiles used by earlier segments
-  for (long long k = s0; k < s1;) {
-    while (pre_s[pr + 1] <= k) ++pr;  // skip pairs without keys
-    const long long e = min(s1, (long long)pre_s[pr + 1]);
-    const int kk0 = (int)(k - pre_s[pr]), kk1 = (int)(e - pre_s[pr]);
-    const int b = pr / p.Hkv, kvh = pr % p.Hkv;
-    float *Kc = p.k_cache + (size_t)pr * (size_t)p.cap * kD;
-    float *Vc = p.v_cache + (size_t)pr * (size_t)p.cap * kD;
-    const int ntiles = (kk1 - kk0 + kTK - 1) / kTK;
-    const bool skip = fail_s != 0;  // a wait of this CTA gave up: no more keys, the protocol continues
-
-    if (warp == kNW) {
-      // ------------------------------------------------------ producer
-      const int len = p.lens[b];
-      if (append && len >= kk0 && len < kk1) {  // this segment holds the new position (written even after a
-                                                 // give-up, so cache and lens stay consistent)
-        const float *kin = p.k_new + (size_t)pr * kD;
-        const float *vin = p.v_new + (size_t)pr * kD;
-        float4 x0 = *reinterpret_cast<const float4 *>(kin + 4 * lane);
-        float4 x1 = *reinterpret_cast<const float4 *>(kin + 128 + 4 * lane);
-        norm_rope(x0, x1, p.kn_w, p.cos + (size_t)b * p.rot, p.sin + (size_t)b * p.rot, p.rot, p.eps,
-                  tmp_s[kNW], lane);
-        float *kd = Kc + (size_t)len * kD;
-        float *vd = Vc + (size_t)len * kD;
-        *reinterpret_cast<float4 *>(kd + 4 * lane) = x0;
-        *reinterpret_cast<float4 *>(kd + 128 + 4 * lane) = x1;
-        *reinterpret_cast<float4 *>(vd + 4 * lane) = *reinterpret_cast<const float4 *>(vin + 4 * lane);
-        *reinterpret_cast<float4 *>(vd + 128 + 4 * lane) = *reinterpret_cast<const float4 *>(vin + 128 + 4 * lane);
-        fence_proxy_async_global();
-        __syncwarp();
-      }
-      if (lane == 0 && !skip) {
-        const uint64_t pol = l2_policy_evict_first();
-        const bool withhold = p.fault && c == 0;
-        int issued = 0;
-        for (int t = 0; t < ntiles && !withhold; ++t) {
-          const uint32_t g = gt0 + t;
-          const int st = (int)(g % kNS);
-          if (g >= kNS && !mbar_wait_ns(&empty_bar[st], ((g / kNS) - 1) & 1, p.wait_ns)) {
-            atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
-            break;
-          }
-          const int k0 = kk0 + t * kTK;
-          const int nk = min(kTK, kk1 - k0);
-          const uint32_t bytes = (uint32_t)nk * kD * sizeof(float);
-          mbar_arrive_expect_tx(&full_bar[st], 2 * bytes);
-          bulk_g2s(&sm.k[st][0][0], Kc + (size_t)k0 * kD, bytes, &full_bar[st], pol);
-          bulk_g2s(&sm.v[st][0][0], Vc + (size_t)k0 * kD, bytes, &full_bar[st], pol);
-          issued = t + 1;
-        }
-        // every copy this thread started has landed before the ring becomes scratch
-        for (int t = max(0, issued - kNS); t < issued; ++t) {
-          const uint32_t g = gt0 + t;
-          (void)mbar_wait_ns(&full_bar[g % kNS], (g / kNS) & 1, p.wait_ns);
-        }
-      }
-      __syncwarp();
-      named_bar_sync(2, kThreads);  // this segment's copies have landed (or been given up)
-    } else {
-      // ------------------------------------------------------ consumers
-      if (warp < G) {
-        const int h = kvh * G + warp;
-        const float *qin = p.q_gate + ((size_t)b * p.Hq + h) * 2 * kD;
-        float4 x0 = *reinterpret_cast<const float4 *>(qin + 4 * lane);
-        float4 x1 = *reinterpret_cast<const float4 *>(qin + 128 + 4 * lane);
-        norm_rope(x0, x1, p.qn_w, p.cos + (size_t)b * p.rot, p.sin + (size_t)b * p.rot, p.rot, p.eps,
-                  tmp_s[warp], lane);
-        const float sc = p.qscale_log2;
-        *reinterpret_cast<float4 *>(&q_s[warp][4 * lane]) = make_float4(x0.x * sc, x0.y * sc, x0.z * sc, x0.w * sc);
-        *reinterpret_cast<float4 *>(&q_s[warp][128 + 4 * lane]) =
-            make_float4(x1.x * sc, x1.y * sc, x1.z * sc, x1.w * sc);
-      }
-      named_bar_sync(1, kNW * 32);
-      float4 q0[G], q1[G], a0[G], a1[G];
-      float m_run[G], l_run[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        q0[g] = *reinterpret_cast<const float4 *>(&q_s[g][4 * lane]);
-        q1[g] = *reinterpret_cast<const float4 *>(&q_s[g][128 + 4 * lane]);
-        a0[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-        a1[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-        m_run[g] = -INFINITY;
-        l_run[g] = 0.0f;
-      }
-      bool ok = !skip;
-      for (int t = 0; t < ntiles && ok; ++t) {
-        const uint32_t gg = gt0 + t;
-        const int st = (int)(gg % kNS);
-        if (!__all_sync(0xffffffffu, mbar_wait_ns(&full_bar[st], (gg / kNS) & 1, p.wait_ns))) {
-          if (lane == 0) {
-            atomicOr(p.status, Q35_STATUS_WAIT_TIMEOUT);
-            fail_s = 1;
-          }
-          ok = false;
-          break;
-        }
-        const int nk = min(kTK, kk1 - (kk0 + t * kTK));
-        float sv[V];
-#pragma unroll
-        for (int kk = 0; kk < kKPW; ++kk) {
-          const int j = warp * kKPW + kk;
-          if (j < nk) {
-            const float4 k0 = *reinterpret_cast<const float4 *>(&sm.k[st][j][4 * lane]);
-            const float4 k1 = *reinterpret_cast<const float4 *>(&sm.k[st][j][128 + 4 * lane]);
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-              float d = q0[g].x * k0.x;
-              d = fmaf(q0[g].y, k0.y, d); d = fmaf(q0[g].z, k0.z, d); d = fmaf(q0[g].w, k0.w, d);
-              d = fmaf(q1[g].x, k1.x, d); d = fmaf(q1[g].y, k1.y, d); d = fmaf(q1[g].z, k1.z, d);
-              d = fmaf(q1[g].w, k1.w, d);
-              sv[kk * G + g] = d;
-            }
-          } else {
-#pragma unroll
-            for (int g = 0; g < G; ++g) sv[kk * G + g] = 0.0f;
-          }
-        }
-        reduce_scatter<V>(sv, lane);
-        float sc[V];
-#pragma unroll
-        for (int i = 0; i < V; ++i) {
-          sc[i] = __shfl_sync(0xffffffffu, sv[0], i << (5 - LOGV));
-          if (warp * kKPW + i / G >= nk) sc[i] = -INFINITY;
-        }
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          float mt = sc[g];
-#pragma unroll
-          for (int kk = 1; kk < kKPW; ++kk) mt = fmaxf(mt, sc[kk * G + g]);
-          if (mt > m_run[g]) {
-            const float alpha = exp2f(m_run[g] - mt);
-            l_run[g] *= alpha;
-            a0[g].x *= alpha; a0[g].y *= alpha; a0[g].z *= alpha; a0[g].w *= alpha;
-            a1[g].x *= alpha; a1[g].y *= alpha; a1[g].z *= alpha; a1[g].w *= alpha;
-            m_run[g] = mt;
-          }
-        }
-#pragma unroll
-        for (int kk = 0; kk < kKPW; ++kk) {
-          const int j = warp * kKPW + kk;
-          if (j < nk) {
-            const float4 v0 = *reinterpret_cast<const float4 *>(&sm.v[st][j][4 * lane]);
-            const float4 v1 = *reinterpret_cast<const float4 *>(&sm.v[st][j][128 + 4 * lane]);
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-              const float pw = exp2f(sc[kk * G + g] - m_run[g]);
-              l_run[g] += pw;
-              a0[g] = f4_fma(pw, v0, a0[g]);
-              a1[g] = f4_fma(pw, v1, a1[g]);
-            }
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[st]);
-      }
-      if (!ok) {  // this warp contributes nothing (m = -inf); the status word says why
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          m_run[g] = -INFINITY;
-          l_run[g] = 0.0f;
-          a0[g] = a1[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-      named_bar_sync(2, kThreads);  // the producer has seen its copies land: the ring is scratch
-      float *wacc = scratch;                // [NW][G][D]
-      float *wml = wacc + kNW * G * kD;     // [NW][G][2]
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        *reinterpret_cast<float4 *>(wacc + ((size_t)warp * G + g) * kD + 4 * lane) = a0[g];
-        *reinterpret_cast<float4 *>(wacc + ((size_t)warp * G + g) * kD + 128 + 4 * lane) = a1[g];
-        if (lane == 0) {
-          wml[(warp * G + g) * 2 + 0] = m_run[g];
-          wml[(warp * G + g) * 2 + 1] = l_run[g];
-        }
-      }
-      named_bar_sync(1, kNW * 32);
-      const long long cf = cta_of(pre_s[pr]), cl = cta_of((long long)pre_s[pr + 1] - 1);
-      const int n = (int)(cl - cf + 1);
-      const size_t piece = (size_t)rank + pr;
-      float *po = p.part_o + piece * G * kD;
-      float *pml = p.part_ml + piece * G * 2;
-      for (int i = tid; i < G * kD; i += kNW * 32) {
-        const int g = i / kD, d = i % kD;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kNW; ++w) M = fmaxf(M, wml[(w * G + g) * 2]);
-        float Ls = 0.0f, O = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kNW; ++w) {
-          const float mw = wml[(w * G + g) * 2];
-          const float sw = mw == -INFINITY ? 0.0f : exp2f(mw - M);
-          Ls = fmaf(wml[(w * G + g) * 2 + 1], sw, Ls);
-          O = fmaf(wacc[((size_t)w * G + g) * kD + d], sw, O);
-        }
-        if (n == 1) {
-          write_final(p, b, kvh * G + g, d, O, M, Ls);
-        } else {
-          __stcg(po + i, O);
-          if (d == 0) {
-            __stcg(pml + g * 2 + 0, M);
-            __stcg(pml + g * 2 + 1, Ls);
-          }
-        }
-      }
-      if (n > 1) {
-        __threadfence();
-        named_bar_sync(1, kNW * 32);
-        if (tid == 0) flag_s = atomicAdd(&p.pair_cnt[pr], 1u) == (uint32_t)(n - 1);
-        named_bar_sync(1, kNW * 32);
-        if (flag_s) {
-          __threadfence();
-          const size_t first = (size_t)cf + pr;
-          merge_partials<G>(p, p.part_ml + first * G * 2, p.part_o + first * G * kD, n, nullptr, nullptr, kvh, b,
-                            scratch, warp, lane, tid);
-          if (tid == 0) p.pair_cnt[pr] = 0u;
-        }
-      }
-    }
-    named_bar_sync(3, kThreads);  // scratch free: the ring may be refilled
-    gt0 += (uint32_t)ntiles;
-    k = e;
-    ++pr;
-  }
-
-  // the last CTA of the grid advances lens (every CTA has read it by then)
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    flag_s = atomicAdd(p.done, 1u) == (uint32_t)(P - 1);
-    if (flag_s) *p.done = 0u;
-  }
-  __syncthreads();
-  if (flag_s && append) {
-    __threadfence();
-    for (int b = tid; b < p.B; b += kThreads) {
-      const int len = p.lens[b];
-      if (len < p.cap && len + 1 <= cap_keys) p.lens[b] = len + 1;
-    }
-  }
-}
-
-template <int G>
-cudaError_t launch_sk(const GqaParams &p, cudaStream_t st) {
-  const size_t smem = sizeof(GqaSmem);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gqa_decode_sk_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
-  note_launch();
-  (void)launch_kernel_serial(gqa_decode_sk_kernel<G>, dim3(p.sk_nb + p.sk_ns), dim3(kThreads), smem, st, 1, 1, p);
-  return cudaGetLastError();
-}
-
 template <int G>
 cudaError_t launch_g(const GqaParams &p, cudaStream_t st) {
-  if constexpr (G <= 4) {
-    if (p.sk) return launch_sk<G>(p, st);
-  }
   const size_t smem = sizeof(GqaSmem);
   static bool configured = false;  // per-process attribute set-up
   if (!configured) {
@@ -1026,9 +638,8 @@ int gqa_keys_per_split(int B, int Hkv, long long max_len, int sms) {
 }
 
 struct GqaWsLayout {
-  size_t status, done, grp_cnt, pair_cnt, seq_cnt, lsnap, part_o, part_ml, grp_o, grp_ml, total;
-  int kps, nsplit, ngroups, sk_nb, sk_ns;
-  bool tree, sk;
+  size_t status, grp_cnt, pair_cnt, seq_cnt, lsnap, part_o, part_ml, grp_o, grp_ml, total;
+  int kps, nsplit, ngroups;
 };
 
 GqaWsLayout gqa_ws_layout(int B, int Hq, int Hkv, long long max_len, int sms) {
@@ -1037,25 +648,15 @@ GqaWsLayout gqa_ws_layout(int B, int Hq, int Hkv, long long max_len, int sms) {
   l.nsplit = (int)((max_len + l.kps - 1) / l.kps);
   l.ngroups = (l.nsplit + kFanIn - 1) / kFanIn;
   const size_t G = (size_t)(Hq / Hkv), pairs = (size_t)B * Hkv;
-  l.tree = l.kps >= kLongKps;
-  // the even-range schedule: one ticket per pair in shared-memory prefix sums
-  // of int keys, and a group small enough for its two resident CTAs per SM
-  l.sk = l.tree && G <= 4 && pairs <= (size_t)kSkMaxPairs &&
-         (long long)pairs * ((long long)l.nsplit * l.kps + 1) < (1LL << 31);
-  // long units of about kLongKps keys at the hint, then three waves of short ones
-  l.sk_nb = l.sk ? (int)((pairs * ((size_t)l.nsplit * l.kps) + kLongKps - 1) / kLongKps) : 0;
-  l.sk_ns = l.sk ? 3 * gqa_sk_ctas((int)G, sms) : 0;
-  const size_t pieces = std::max(pairs * l.nsplit, l.sk ? (size_t)l.sk_nb + l.sk_ns + pairs : (size_t)0);
   auto up = [](size_t x) { return (x + 255) / 256 * 256; };
   l.status = 0;
-  l.done = sizeof(uint32_t);
   l.grp_cnt = 256;
   l.pair_cnt = l.grp_cnt + pairs * l.ngroups * sizeof(uint32_t);
   l.seq_cnt = l.pair_cnt + pairs * sizeof(uint32_t);
   l.lsnap = l.seq_cnt + (size_t)B * sizeof(uint32_t);
   l.part_o = up(l.lsnap + (size_t)B * sizeof(int32_t));
-  l.part_ml = up(l.part_o + pieces * G * kD * sizeof(float));
-  l.grp_o = up(l.part_ml + pieces * G * 2 * sizeof(float));
+  l.part_ml = up(l.part_o + pairs * l.nsplit * G * kD * sizeof(float));
+  l.grp_o = up(l.part_ml + pairs * l.nsplit * G * 2 * sizeof(float));
   l.grp_ml = up(l.grp_o + pairs * l.ngroups * G * kD * sizeof(float));
   l.total = up(l.grp_ml + pairs * l.ngroups * G * 2 * sizeof(float));
   return l;
@@ -1090,10 +691,7 @@ int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_g
   p.kps = lay.kps;
   p.nsplit = lay.nsplit;
   p.ngroups = lay.ngroups;
-  p.tree = lay.tree ? 1 : 0;
-  p.sk = lay.sk ? 1 : 0;
-  p.sk_nb = lay.sk_nb;
-  p.sk_ns = lay.sk_ns;
+  p.tree = lay.kps >= kLongKps;
   Q35_REQUIRE(ws != nullptr && ws_bytes >= lay.total && (reinterpret_cast<uintptr_t>(ws) & 255u) == 0,
               Q35_ERR_WORKSPACE,
               "gqa_decode: workspace missing, not 256-byte aligned or too small (need " +
@@ -1106,7 +704,6 @@ int gqa_decode_launch(const q35_gqa_dims *d, long long max_len, const float *q_g
   p.wait_ns = p.fault ? kFaultWaitLimitNs : kWaitLimitNs;
   unsigned char *base = static_cast<unsigned char *>(ws);
   p.status = reinterpret_cast<uint32_t *>(base + lay.status);
-  p.done = reinterpret_cast<uint32_t *>(base + lay.done);
   p.grp_cnt = reinterpret_cast<uint32_t *>(base + lay.grp_cnt);
   p.pair_cnt = reinterpret_cast<uint32_t *>(base + lay.pair_cnt);
   p.seq_cnt = reinterpret_cast<uint32_t *>(base + lay.seq_cnt);

@@ -217,8 +217,9 @@ def test_known_answer_equal_scores():
 
 
 def _ragged_many(B, Hq, Hkv, cap, lens0, sample, steps, seed, arm_first=False):
-    """Many sequences of ragged length on the even-range schedule; the sampled
-    sequences are followed by the oracle, every sequence's lens is checked."""
+    """Many sequences of ragged length on the many-sequence schedule (long
+    splits, in-kernel merge tree); the sampled sequences are followed by the
+    oracle, every sequence's lens is checked."""
     D = 256
     dev = torch.device("cuda:0")
     gen = torch.Generator(device=dev)
@@ -259,11 +260,11 @@ def _ragged_many(B, Hq, Hkv, cap, lens0, sample, steps, seed, arm_first=False):
     return max(errs)
 
 
-def test_many_ragged_sequences_even_ranges():
+def test_many_ragged_sequences_long_splits():
     """256 sequences of ragged length (1 to 9,200 cached keys, some only a
-    few keys long) at a length hint that selects the even-range schedule: key
-    ranges start and end inside pairs, short pairs lie wholly inside a range,
-    long ones are shared by several CTAs."""
+    few keys long, some at split boundaries) at a length hint that selects the
+    many-sequence schedule: splits without keys, splits ending inside a tile,
+    pairs merged from one to five splits."""
     B, Hq, Hkv, cap = 256, 8, 2, 9300
     rng = np.random.RandomState(31)
     lens0 = rng.randint(1, 9200, size=B)
@@ -273,10 +274,11 @@ def test_many_ragged_sequences_even_ranges():
     assert err <= TOL
 
 
-def test_even_ranges_wait_runs_out_then_recovers():
-    """The even-range schedule's first CTA withholds its copies (test hook):
-    the step reports Q35_STATUS_WAIT_TIMEOUT, every sequence still advances
-    (its new key is in the cache), and the next step matches the oracle."""
+def test_long_splits_wait_runs_out_then_recovers():
+    """On the many-sequence schedule the first split withholds its copies
+    (test hook): the step reports Q35_STATUS_WAIT_TIMEOUT, every sequence
+    still advances (its new key is in the cache), the merge tree's counters
+    stay consistent, and the next step matches the oracle."""
     B, Hq, Hkv, cap = 256, 8, 2, 9300
     rng = np.random.RandomState(41)
     lens0 = rng.randint(1, 9200, size=B)
