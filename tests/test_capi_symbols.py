@@ -76,6 +76,29 @@ def test_validation_errors_without_device():
     assert lib.q35_gdn_prefill(C.byref(d), 8, *([None] * 7), 2, None, 0, None, None, 0, None) == _lib.ERR_INVALID_ARG
 
 
+def test_peer_exchange_validation_without_device():
+    """q35_cp_* refuse bad shapes and NULL handles before touching a device;
+    a valid request then fails on the missing GPU, never in an allocation."""
+    lib = q35attn.load()
+    ctx, h = C.c_void_p(), (C.c_ubyte * 64)()
+    assert lib.q35_cp_create(0, 0, 1, 256, 8, 256, C.byref(ctx), h) == _lib.ERR_INVALID_ARG   # world 0
+    assert lib.q35_cp_create(9, 0, 1, 256, 8, 256, C.byref(ctx), h) == _lib.ERR_INVALID_ARG   # world > 8
+    assert lib.q35_cp_create(2, 2, 1, 256, 8, 256, C.byref(ctx), h) == _lib.ERR_INVALID_ARG   # rank >= world
+    assert lib.q35_cp_create(2, 0, 0, 256, 8, 256, C.byref(ctx), h) == _lib.ERR_INVALID_ARG   # no sequence
+    assert lib.q35_cp_create(2, 0, 1, 256, 8, 128, C.byref(ctx), h) == _lib.ERR_UNSUPPORTED   # head_dim
+    assert lib.q35_cp_create(2, 0, 1, 255, 8, 256, C.byref(ctx), h) == _lib.ERR_UNSUPPORTED   # odd n_gdn
+    assert lib.q35_cp_create(2, 0, 1, 256, 8, 256, None, h) == _lib.ERR_INVALID_ARG
+    rc = lib.q35_cp_create(2, 0, 1, 256, 8, 256, C.byref(ctx), h)
+    if torch.cuda.is_available():
+        assert rc == _lib.OK and lib.q35_cp_destroy(ctx) == _lib.OK
+    else:
+        assert rc == _lib.ERR_DEVICE  # the shape is valid; the device check comes last
+    assert lib.q35_cp_exchange(None, *([None] * 5), None) == _lib.ERR_INVALID_ARG
+    assert lib.q35_cp_connect(None, h) == _lib.ERR_INVALID_ARG
+    assert lib.q35_cp_disconnect(None) == _lib.ERR_INVALID_ARG
+    assert lib.q35_cp_destroy(None) == _lib.OK
+
+
 def test_workspace_sizes_are_positive_and_monotone():
     lib = q35attn.load()
     g = _lib.GqaDims(256, 8, 2, 256, 64, 0, 40000, 1e-6)
