@@ -88,6 +88,7 @@ def test_peer_exchange_validation_without_device():
     assert lib.q35_cp_create(2, 0, 1, 256, 8, 128, C.byref(ctx), h) == _lib.ERR_UNSUPPORTED   # head_dim
     assert lib.q35_cp_create(2, 0, 1, 255, 8, 256, C.byref(ctx), h) == _lib.ERR_UNSUPPORTED   # odd n_gdn
     assert lib.q35_cp_create(2, 0, 1, 256, 8, 256, None, h) == _lib.ERR_INVALID_ARG
+    import torch
     rc = lib.q35_cp_create(2, 0, 1, 256, 8, 256, C.byref(ctx), h)
     if torch.cuda.is_available():
         assert rc == _lib.OK and lib.q35_cp_destroy(ctx) == _lib.OK
