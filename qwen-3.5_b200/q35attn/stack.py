@@ -69,9 +69,11 @@ class Q8F:
 
 class HybridStack:
     def __init__(self, cfg: StackConfig = QWEN35_2B, capacity: int = 2048, seed: int = 0, device="cuda",
-                 gemv_mode: int = 1, prefill_chunk: int = 2048, fused: bool = True):
+                 gemv_mode: int = 1, prefill_chunk: int = 2048, fused: bool = True, gate_overlap: bool = True):
         self.cfg, self.cap, self.dev, self.gemv_mode = cfg, capacity, torch.device(device), gemv_mode
         self.fused, self._plan = fused, None
+        self.gate_overlap = gate_overlap
+        self._side = torch.cuda.Stream(self.dev) if gate_overlap else None  # created outside any capture
         g = torch.Generator(device=self.dev)
         g.manual_seed(seed)
         c, dev = cfg, self.dev
@@ -126,7 +128,8 @@ class HybridStack:
     def _decode_buffers(self):
         c, dev = self.cfg, self.dev
         e = lambda *s: torch.empty(*s, device=dev)
-        self.b = {"h": e(c.hidden), "h2": e(c.hidden), "x": e(c.hidden), "attn": e(c.hidden), "mlp": e(c.hidden),
+        self.b = {"h": e(c.hidden), "h2": e(c.hidden), "x": e(c.hidden), "xg": e(c.hidden), "attn": e(c.hidden),
+                  "mlp": e(c.hidden),
                   "mixed": e(1, c.conv_dim), "z": e(1, c.gdn_hv * 128), "beta": e(1, c.gdn_hv), "g": e(1, c.gdn_hv),
                   "core": e(1, max(c.gdn_hv * 128, c.gqa_hq * 256)), "qg": e(1, c.gqa_hq, 512),
                   "kk": e(1, c.gqa_hkv, 256), "vv": e(1, c.gqa_hkv, 256), "up": e(c.inter), "gt": e(c.inter),
@@ -219,7 +222,7 @@ class HybridStack:
                                 norm_w=L["post_norm"], eps=c.eps, sum_out=hs[1 - cur], swiglu=True, mode=m)
             cur = 1 - cur
             down = ops.FusedGemv(b["act"], [W(L["down"])], [b["mlp"]], mode=m)
-            plan.append((L, front, out, mlp, down))
+            plan.append((L, front, out, mlp, down, (xin, kw["residual"])))
         return plan, hs[cur]
 
     def _decode_step_fused(self):
@@ -230,11 +233,24 @@ class HybridStack:
         ops.q8_embedding(b["tok"], self.embed.words, self.embed.scales, b["h"].view(1, -1))
         if self.gqa_layers:
             ops.rope_gather(self.gqa_layers[0]["lens"], self.rope_cos, self.rope_sin, b["cos"], b["sin"])
-        for L, front, out, mlp, down in plan:
-            front()
+        main = torch.cuda.current_stream(self.dev)
+        for L, front, out, mlp, down, (xin, res) in plan:
+            if L["kind"] == "linear" and self._side is not None and self.gate_overlap:
+                # The gate projection reads only the layer input: a side branch recomputes the input norm and
+                # runs it while the input projections stream their weights; the core waits for both.
+                self._side.wait_stream(main)
+                with torch.cuda.stream(self._side):
+                    ops.add_rmsnorm(xin, L["in_norm"], b["xg"], residual=res, eps=c.eps)
+                    ops.gdn_gate(b["xg"].view(1, -1), L["w_b"], L["w_a"], L["a_log"], L["dt_bias"], mode=0,
+                                 beta=b["beta"], g=b["g"])
+                front()
+                main.wait_stream(self._side)
+            else:
+                front()
+                if L["kind"] == "linear":
+                    ops.gdn_gate(b["x"].view(1, -1), L["w_b"], L["w_a"], L["a_log"], L["dt_bias"], mode=0,
+                                 beta=b["beta"], g=b["g"])
             if L["kind"] == "linear":
-                ops.gdn_gate(b["x"].view(1, -1), L["w_b"], L["w_a"], L["a_log"], L["dt_bias"], mode=0,
-                             beta=b["beta"], g=b["g"])
                 ops.gdn_decode(b["mixed"], b["z"], b["beta"], b["g"], L["conv_w"], L["norm_w"], L["conv_state"],
                                L["rec_state"], b["core"][:, :c.gdn_hv * 128], num_k_heads=c.gdn_hk,
                                num_v_heads=c.gdn_hv, eps=c.eps)
