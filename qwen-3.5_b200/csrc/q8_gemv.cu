@@ -166,13 +166,16 @@ int launch_nq(const GemvParams &p, cudaStream_t st) {
 // ---------------------------------------------------------------------------
 // TMA path (every out_dim % 256 == 0, x 16-byte aligned): a CTA owns 64
 // output columns (one scale per row) over every row.  A producer thread
-// streams 128-row boxes of the weights ([128 x 64] bytes) and of the scales
-// ([128 x 4] floats: the 16-byte TMA minimum, of which one column is used) from
+// streams 256-row boxes of the weights ([256 x 64] bytes) and of the scales
+// ([256 x 4] floats: the 16-byte TMA minimum, of which one column is used) from
 // 2-D tensor maps over the reference layout into a shared-memory ring -- one
 // instruction per box, so the stream is not capped by the SM's
 // outstanding-load limit that bounds the per-thread LDG kernel above.  Eight
 // consumer warps take 8 rows x 64 bytes per step (lane = row * 4 + 16-byte
-// quarter) and reduce with warp shuffles and one shared-memory pass.  In mode 1
+// quarter), four steps per box between two ring waits (256-row boxes in a
+// 3-stage ring measured 1-2 % faster on the 2B decode step than 128-row boxes
+// in a 6-stage ring of the same 60 KB; deeper or shallower rings were slower),
+// and reduce with warp shuffles and one shared-memory pass.  In mode 1
 // the rows the reference skips get x = 0 in the CTA's shared copy of x (adding
 // exact zeros leaves every f32 sum unchanged), so the inner loop has no row
 // test.  When the column blocks alone give few CTAs, the row boxes are split
@@ -189,14 +192,14 @@ int launch_nq(const GemvParams &p, cudaStream_t st) {
 // :1053-1085) and optionally with the MLP's SwiGLU behind (two segments up and
 // gate streamed by the same CTA, y = up * silu(gate); :999-1011).
 constexpr int kTC = 64;
-constexpr int kTR = 128;
+constexpr int kTR = 256;
 constexpr int kTWarps = 8;
 constexpr int kTThreads = (kTWarps + 1) * 32;
 constexpr int kMaxSeg = 4;
 
 struct alignas(64) GemvSeg {
-  CUtensorMap wmap;  // uint8 [in][out], box {64, 128}
-  CUtensorMap smap;  // f32 [in][out / 64], box {4, 128}
+  CUtensorMap wmap;  // uint8 [in][out], box {64, 256}
+  CUtensorMap smap;  // f32 [in][out / 64], box {4, 256}
   float *y;
   int out_dim, ncb;                  // ncb = out_dim / 64 column blocks
   int chunk, per_split, ref_splits;  // mode 1 row set of this projection
@@ -483,11 +486,11 @@ int launch_tma(GemvTmaParams &p, bool compat, bool norm, bool swiglu, cudaStream
       break;
     }
   if (swiglu) {
-    if (compat) return norm ? launch_tma_t<true, true, 2, 4>(p, ctas, st) : launch_tma_t<true, false, 2, 4>(p, ctas, st);
-    return norm ? launch_tma_t<false, true, 2, 4>(p, ctas, st) : launch_tma_t<false, false, 2, 4>(p, ctas, st);
+    if (compat) return norm ? launch_tma_t<true, true, 2, 2>(p, ctas, st) : launch_tma_t<true, false, 2, 2>(p, ctas, st);
+    return norm ? launch_tma_t<false, true, 2, 2>(p, ctas, st) : launch_tma_t<false, false, 2, 2>(p, ctas, st);
   }
-  if (compat) return norm ? launch_tma_t<true, true, 1, 6>(p, ctas, st) : launch_tma_t<true, false, 1, 6>(p, ctas, st);
-  return norm ? launch_tma_t<false, true, 1, 6>(p, ctas, st) : launch_tma_t<false, false, 1, 6>(p, ctas, st);
+  if (compat) return norm ? launch_tma_t<true, true, 1, 3>(p, ctas, st) : launch_tma_t<true, false, 1, 3>(p, ctas, st);
+  return norm ? launch_tma_t<false, true, 1, 3>(p, ctas, st) : launch_tma_t<false, false, 1, 3>(p, ctas, st);
 }
 
 // Fills segment k from (w, scales, y, out_dim) with the row plan of `mode`.
