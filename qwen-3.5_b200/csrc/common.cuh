@@ -210,6 +210,35 @@ __device__ __forceinline__ float4 f4_fma(float s, float4 a, float4 c) {
   return make_float4(fmaf(s, a.x, c.x), fmaf(s, a.y, c.y), fmaf(s, a.z, c.z), fmaf(s, a.w, c.w));
 }
 
+// Packed pairs of f32 (low word = first element) and the sm_100 f32x2 ops.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// Bytes 2h and 2h + 1 of w (signed int8) as an exact f32 pair: a byte permute
+// puts q + 128 into the low mantissa byte of 2^23 (0x4B0000XX), and one
+// packed subtraction of 2^23 + 128 leaves q in both lanes.
+__device__ __forceinline__ uint64_t s8_pair(uint32_t w, int h) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint64_t m = f2_pack(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u | (2 * h))),
+                             __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u | (2 * h + 1))));
+  return f2_sub(m, 0x4B0000804B000080ull);
+}
+
 }  // namespace q35
 
 namespace q35 {

@@ -138,8 +138,9 @@ __global__ void silu_mul_kernel(size_t n, const float *gate, const float *up, fl
 // logits[v] = sum_c int8(E[v][c]) * x[c] * scales[v][c / 64]; dim == 2048:
 // lane l owns columns 64 l .. 64 l + 63 (four 16-byte loads, one scale).
 constexpr int kHeadDim = 2048;
-// rows in flight per warp; 2 rows leave room for 2 CTAs per SM (vocab 248,320:
-// 97.9 us against 99.5 us for 4 rows at 1 CTA per SM, 102.2 us for 8 rows)
+// rows in flight per warp; 2 rows leave room for 2 CTAs per SM (vocab 248,320,
+// conversion instruction: 97.9 us against 99.5 us for 4 rows at 1 CTA per SM,
+// 102.2 us for 8 rows; with the packed f32x2 form below 92.4 us)
 constexpr int kHeadRows = 2;
 __global__ void __launch_bounds__(256, 2) q8_lm_head_kernel(int vocab, const float *x, const uint4 *table,
                                                          const float *scales, float *logits) {
@@ -168,16 +169,22 @@ __global__ void __launch_bounds__(256, 2) q8_lm_head_kernel(int vocab, const flo
     }
 #pragma unroll
     for (int u = 0; u < kHeadRows; ++u) {
-      float acc = 0.0f;
+      // two packed f32x2 chains: lane 0 sums columns 4j and 4j + 2 of every
+      // word, lane 1 columns 4j + 1 and 4j + 3 (exact int8 via s8_pair)
+      uint64_t a2 = 0;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const uint32_t wv[4] = {q[u][k].x, q[u][k].y, q[u][k].z, q[u][k].w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-          for (int b = 0; b < 4; ++b) acc = fmaf(s8(wv[j], b), xv[16 * k + 4 * j + b], acc);
+        for (int j = 0; j < 4; ++j) {
+          const float *xj = xv + 16 * k + 4 * j;
+          a2 = f2_fma(s8_pair(wv[j], 0), f2_pack(xj[0], xj[1]), a2);
+          a2 = f2_fma(s8_pair(wv[j], 1), f2_pack(xj[2], xj[3]), a2);
+        }
       }
-      acc = warp_sum(acc * sc[u]);  // lane l's 64 columns share scale l
+      float even, odd;
+      f2_unpack(a2, even, odd);
+      const float acc = warp_sum((even + odd) * sc[u]);  // lane l's 64 columns share scale l
       if (lane == 0 && r0 + u < vocab) logits[r0 + u] = acc;
     }
   }
