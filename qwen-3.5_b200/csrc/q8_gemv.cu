@@ -496,12 +496,15 @@ int launch_tma(GemvTmaParams &p, bool compat, bool norm, bool swiglu, cudaStream
   for (int k = 0; k < p.nseg; ++k) ctas += p.seg[k].ncb;
   if (swiglu) ctas = p.seg[0].ncb;
   // row-box split KS: the largest of 8 / 4 / 2 that keeps the grid within two
-  // CTAs per SM (measured on B200 against a split that evens out the CTAs per
-  // SM: the larger split with deeper rings was faster on every decode shape)
+  // CTAs per SM with the fused norm, one without (measured on B200 against a
+  // split that evens out the CTAs per SM: the larger split with deeper rings
+  // was faster on every decode shape; the plain out / down projections of the
+  // 2B decode step were 1 % faster per token at KS 4 than at KS 8, same tokens)
   const int nst = (p.in_dim + kTR - 1) / kTR;
+  const int per_sm = norm ? 2 : 1;
   p.ks = 1;
   for (int k : {8, 4, 2})
-    if (ctas * k <= 2 * device_sm_count() && k <= nst) {
+    if (ctas * k <= per_sm * device_sm_count() && k <= nst) {
       p.ks = k;
       break;
     }
