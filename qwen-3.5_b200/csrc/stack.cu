@@ -169,8 +169,8 @@ __global__ void __launch_bounds__(256, 2) q8_lm_head_kernel(int vocab, const flo
     }
 #pragma unroll
     for (int u = 0; u < kHeadRows; ++u) {
-      // two packed f32x2 chains: lane 0 sums columns 4j and 4j + 2 of every
-      // word, lane 1 columns 4j + 1 and 4j + 3 (exact int8 via s8_pair)
+      // one packed f32x2 accumulator: its low half sums the even columns of
+      // this thread's 64, its high half the odd ones (exact int8 via s8_pair)
       uint64_t a2 = 0;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
